@@ -1,0 +1,164 @@
+/*
+ * nnrcu.h - C ABI of the B200 (sm_100a) backend for nnr's conv/GEMM hot path.
+ *
+ * The entry points are what nnr's backend_t::CUDA operators (a new
+ * src/backend/cuda/ beside src/backend/cpu/) call from operator_t::reshape()
+ * and operator_t::exec(). Plain pointers and sizes only; every function
+ * returns NNRCU_OK (0) or a negative NNRCU_ERR_* code, mirroring nnr's
+ * bool-return convention (reference: src/nnr.h:331-461, operator_t), and
+ * nnrcu_last_error() returns the message of the last failure on the calling
+ * thread.
+ *
+ * Object lifecycle, matching operator_t:
+ *   nnrcu_*_create   <-> operator_t::reshape()  (shape checks, weight packing
+ *                        and upload, requant constants; once per shape)
+ *   nnrcu_*_run      <-> operator_t::exec()     (enqueue on a stream; no
+ *                        allocation, no host synchronisation)
+ *   nnrcu_op_destroy <-> operator_t::~operator_t() (frees device buffers)
+ *   nnrcu_op_workspace_size <-> operator_t::workspace_size(), but for a
+ *                        device workspace that the caller's device arena
+ *                        provides to *_run.
+ *   nnrcu_op_num_ops <-> operator_t::num_ops() (2 * MACs).
+ *
+ * Tensor pointers passed to *_run are device pointers. Activations may be
+ * NCHW (nnr's default) or NHWC (nnr's memory_layout_t::NHWC, the layout the
+ * device prefers); see nnrcu_conv_desc.
+ */
+#ifndef NNRCU_H
+#define NNRCU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NNRCU_OK 0
+#define NNRCU_ERR_INVALID (-1)     /* bad argument or shape */
+#define NNRCU_ERR_UNSUPPORTED (-2) /* valid ONNX, not handled on the device (caller's registry may decline) */
+#define NNRCU_ERR_CUDA (-3)        /* CUDA runtime / driver error */
+#define NNRCU_ERR_DEVICE (-4)      /* a kernel reported a failure through the device status word */
+#define NNRCU_ERR_NOMEM (-5)       /* device allocation failed */
+
+#define NNRCU_LAYOUT_NCHW 0
+#define NNRCU_LAYOUT_NHWC 1
+
+/* Requantisation formula of QLinearConv. nnr's x64 CPU path uses a different
+ * fp32 operation order per kernel; bit-exact parity needs the same one.
+ *   AUTO: the one nnr's dispatch would pick for this shape on an AVX-512
+ *         VNNI host (reference: src/backend/cpu/QLinearConv.cpp:1337-1351):
+ *         R3 for the small-IC stem with NCHW input, R1 when the output is
+ *         NCHW with oH*oW <= 256, R2 otherwise.
+ *   R1: exec_direct_int8 (QLinearConv.cpp:616-646)
+ *   R2: packed NR48 JIT epilogue (backend/x64/jit_conv_int8_ukernel.cpp:950-965)
+ *   R3: first-layer kernel (backend/x64/conv_first_layer_int8_avx512.h:262-270) */
+#define NNRCU_RQ_AUTO 0
+#define NNRCU_RQ_R1 1
+#define NNRCU_RQ_R2 2
+#define NNRCU_RQ_R3 3
+
+/* Fused post-op of Conv/Gemm/MatMul: nnr sets operator_t::post_fn to the
+ * consumer's fusable_apply (graph_optimizer/fuse_post_ops.cpp:69-71); the
+ * device equivalent is this enum plus two parameters. */
+#define NNRCU_POST_NONE 0
+#define NNRCU_POST_RELU 1
+#define NNRCU_POST_CLIP 2      /* a = min, b = max   (backend/cpu/Clip.cpp:20-40) */
+#define NNRCU_POST_HARDSWISH 3 /* x*clamp(x/6+0.5,0,1) (backend/cpu/HardSwish.cpp:18-35) */
+#define NNRCU_POST_SIGMOID 4
+#define NNRCU_POST_LEAKYRELU 5 /* a = alpha */
+#define NNRCU_POST_TANH 6
+
+typedef struct nnrcu_op nnrcu_op; /* opaque: one prepared operator instance */
+
+/* Shape and attributes of a 2-D convolution (ONNX Conv / QLinearConv).
+ * Weights are ONNX OIHW [oc, c/group, kh, kw]. */
+typedef struct nnrcu_conv_desc {
+  int n, c, h, w;        /* input dims (logical NCHW) */
+  int oc, kh, kw;        /* output channels, kernel size */
+  int group;             /* 1, or c == oc == group for depthwise */
+  int stride_h, stride_w;
+  int pad_top, pad_left, pad_bottom, pad_right; /* ONNX pads after auto_pad resolution */
+  int dil_h, dil_w;
+  int in_layout, out_layout; /* NNRCU_LAYOUT_* */
+  int post_op;               /* NNRCU_POST_*; for QLinearConv any non-zero value means a fused
+                                activation exists (qmin = max(lo, y_zp), QLinearConv.cpp:419) */
+  float post_a, post_b;
+  int requant;               /* NNRCU_RQ_* (QLinearConv only) */
+} nnrcu_conv_desc;
+
+/* ---------------------------------------------------------------- runtime */
+int nnrcu_init(int device);             /* select + initialise a device on this thread */
+int nnrcu_last_error(char* buf, size_t len);
+/* Reads and clears the device status word that kernels set instead of
+ * trapping (e.g. a pipeline wait that ran out of time). 0 = clean. */
+int nnrcu_device_status(int* status_out);
+int nnrcu_stream_create(void** stream);
+int nnrcu_stream_destroy(void* stream);
+int nnrcu_stream_sync(void* stream);
+int nnrcu_malloc(void** ptr, size_t bytes);
+int nnrcu_free(void* ptr);
+int nnrcu_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+int nnrcu_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int nnrcu_memset(void* dst, int value, size_t bytes, void* stream);
+/* Stream capture of a run loop into one CUDA graph (replaces nnr's
+ * exec_steps loop, src/nnr.cpp:908-1051, for a fixed batch). */
+int nnrcu_graph_begin(void* stream);
+int nnrcu_graph_end(void* stream, void** graph_exec);
+int nnrcu_graph_launch(void* graph_exec, void* stream);
+int nnrcu_graph_destroy(void* graph_exec);
+
+/* ---------------------------------------------------------------- operators (common) */
+int nnrcu_op_workspace_size(const nnrcu_op* op, size_t* bytes);
+int nnrcu_op_num_ops(const nnrcu_op* op, int64_t* ops);
+int nnrcu_op_destroy(nnrcu_op* op);
+
+/* ---------------------------------------------------------------- QLinearConv (u8 x, s8 w, u8 y)
+ * Replaces QLinearConv_operator::reshape/exec (backend/cpu/QLinearConv_reshape.h:18-340,
+ * backend/cpu/QLinearConv.cpp:1354-1368). w_scale has 1 or oc entries; w_zp has 0, 1 or
+ * oc entries and must be all zero (nnr's VNNI paths require symmetric weights);
+ * bias may be NULL. */
+int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, const float* w_scale,
+                             int n_w_scale, const int8_t* w_zp, int n_w_zp, const int32_t* bias_host,
+                             float x_scale, uint8_t x_zp, float y_scale, uint8_t y_zp, nnrcu_op** op);
+int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream);
+
+/* ---------------------------------------------------------------- QLinearMatMul (u8 a, s8 b, u8 y)
+ * Replaces QLinearMatMul_operator (backend/cpu/QLinearMatMul.cpp:33-232) for a 2-D B
+ * initializer [k, n] (prepacked once, as nnr does when B is constant, :73-92); a is
+ * [m, k] row-major (leading batch dims folded into m). Requant R4 (:188-198). */
+int nnrcu_qlinearmatmul_create(int m, int k, int n, float a_scale, uint8_t a_zp, const int8_t* b_host,
+                               float b_scale, int8_t b_zp, float y_scale, uint8_t y_zp, nnrcu_op** op);
+int nnrcu_qlinearmatmul_run(nnrcu_op* op, const uint8_t* a, uint8_t* y, void* workspace, void* stream);
+
+/* ---------------------------------------------------------------- fp32 Conv (Conv+BN folded + post-op)
+ * Replaces Conv_operator::reshape/exec<float> (backend/cpu/Conv_reshape.h:17-380,
+ * backend/cpu/Conv_exec.h:1163-1192). Dense convs run on the tensor cores as
+ * split-bf16 (3 products, fp32 accumulation); depthwise (group == c == oc) on
+ * CUDA cores. bias may be NULL. */
+int nnrcu_conv_f32_create(const nnrcu_conv_desc* desc, const float* w_host, const float* bias_host,
+                          nnrcu_op** op);
+/* residual (may be NULL) has y's shape and layout and is added after the post-op
+ * (an unfused Conv -> Add, binary_math.cpp:57-77). */
+int nnrcu_conv_f32_run(nnrcu_op* op, const float* x, float* y, const float* residual, void* workspace,
+                       void* stream);
+
+/* ---------------------------------------------------------------- fp32 Gemm / MatMul
+ * Y[m,n] = alpha * op(A)[m,k] * op(B)[k,n] + beta * C, B a constant initializer
+ * (prepacked, Gemm.cpp:72-103), C NULL or a [n] row vector or a full [m,n] matrix
+ * (c_rows = 1 or m), plus a post-op. MatMul is alpha = 1, beta = 0, trans = 0 with
+ * leading batch dims of A folded into m (MatMul.cpp:156-172). */
+int nnrcu_gemm_f32_create(int m, int n, int k, int trans_a, int trans_b, float alpha, float beta,
+                          const float* b_host, const float* c_host, int c_rows, int post_op, float post_a,
+                          float post_b, nnrcu_op** op);
+int nnrcu_gemm_f32_run(nnrcu_op* op, const float* a, float* y, void* workspace, void* stream);
+
+/* ---------------------------------------------------------------- layout helpers
+ * Device versions of nnr's boundary reorders (src/nnr.cpp:953-1031, kernel/layout.h). */
+int nnrcu_nchw_to_nhwc(const void* src, void* dst, int n, int c, int h, int w, int elem_size, void* stream);
+int nnrcu_nhwc_to_nchw(const void* src, void* dst, int n, int c, int h, int w, int elem_size, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NNRCU_H */

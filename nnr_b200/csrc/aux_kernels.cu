@@ -1,0 +1,320 @@
+// Memory-bound helper kernels: layout reorders, the fp32 -> split-bf16
+// operand preparation, row sums for QLinearMatMul zero points, and the
+// depthwise fp32 convolution (CUDA cores, NHWC, 128-bit channel vectors).
+#include <cuda_bf16.h>
+
+#include "internal.h"
+#include "tc_gemm.cuh"
+
+namespace nnrcu {
+
+namespace {
+
+// NCHW u8 -> NHWC u8 with channel stride cs >= c (extra channels = fill).
+// One block transposes a 32-channel x 32-pixel tile through shared memory.
+__global__ void nchw_to_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, int c, int hw,
+                                       int cs, uint8_t fill) {
+  __shared__ uint8_t tile[32][33];
+  const int img = blockIdx.z;
+  const int p0 = blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  const uint8_t* s = src + (size_t)img * c * hw;
+  uint8_t* d = dst + (size_t)img * hw * cs;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int ch = c0 + i, p = p0 + threadIdx.x;
+    tile[i][threadIdx.x] = (ch < c && p < hw) ? s[(size_t)ch * hw + p] : fill;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int p = p0 + i, ch = c0 + threadIdx.x;
+    if (p < hw && ch < cs) d[(size_t)p * cs + ch] = tile[threadIdx.x][i];
+  }
+}
+
+__global__ void pad_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, long long pixels, int c,
+                                   int cs, uint8_t fill) {
+  const long long total = pixels * cs;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long p = i / cs;
+    const int ch = (int)(i - p * cs);
+    dst[i] = ch < c ? src[p * c + ch] : fill;
+  }
+}
+
+__device__ __forceinline__ void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  const __nv_bfloat16 l = __float2bfloat16_rn(v - __bfloat162float(h));
+  hi = __bfloat16_as_ushort(h);
+  lo = __bfloat16_as_ushort(l);
+}
+
+// fp32 activations (NCHW or NHWC) -> two NHWC bf16 planes with channel stride cs.
+__global__ void split_bf16_nhwc_kernel(const float* __restrict src, int src_nchw, uint16_t* __restrict hi,
+                                       uint16_t* __restrict lo, long long pixels, int c, int hw, int cs) {
+  const long long total = pixels * cs;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long p = i / cs;
+    const int ch = (int)(i - p * cs);
+    float v = 0.0f;
+    if (ch < c) {
+      if (src_nchw) {
+        const long long img = p / hw;
+        const long long q = p - img * hw;
+        v = src[(img * c + ch) * hw + q];
+      } else {
+        v = src[p * c + ch];
+      }
+    }
+    uint16_t h, l;
+    split_bf16(v, h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+// Tiled NCHW -> NHWC split for fp32 inputs: coalesced reads along pixels,
+// coalesced writes along channels.
+__global__ void split_bf16_nchw_tiled_kernel(const float* __restrict src, uint16_t* __restrict hi,
+                                             uint16_t* __restrict lo, int c, int hw, int cs) {
+  __shared__ float tile[32][33];
+  const int img = blockIdx.z;
+  const int p0 = blockIdx.x * 32;
+  const int c0 = blockIdx.y * 32;
+  const float* s = src + (size_t)img * c * hw;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int ch = c0 + i, p = p0 + threadIdx.x;
+    tile[i][threadIdx.x] = (ch < c && p < hw) ? s[(size_t)ch * hw + p] : 0.0f;
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int p = p0 + i, ch = c0 + threadIdx.x;
+    if (p < hw && ch < cs) {
+      uint16_t h, l;
+      split_bf16(tile[threadIdx.x][i], h, l);
+      const size_t o = ((size_t)img * hw + p) * cs + ch;
+      hi[o] = h;
+      lo[o] = l;
+    }
+  }
+}
+
+// Rows of A (or columns when trans) -> K-major bf16 planes [m, kp].
+__global__ void split_bf16_rows_kernel(const float* __restrict src, int trans, uint16_t* __restrict hi,
+                                       uint16_t* __restrict lo, int m, int k, int kp) {
+  const long long total = (long long)m * kp;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / kp);
+    const int kk = (int)(i - (long long)r * kp);
+    float v = 0.0f;
+    if (kk < k) v = trans ? src[(size_t)kk * m + r] : src[(size_t)r * k + kk];
+    uint16_t h, l;
+    split_bf16(v, h, l);
+    hi[i] = h;
+    lo[i] = l;
+  }
+}
+
+__global__ void split_bf16_rows_vec_kernel(const float4* __restrict src, uint2* __restrict hi, uint2* __restrict lo,
+                                           long long n4) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const float4 v = src[i];
+    uint16_t h0, l0, h1, l1, h2, l2, h3, l3;
+    split_bf16(v.x, h0, l0);
+    split_bf16(v.y, h1, l1);
+    split_bf16(v.z, h2, l2);
+    split_bf16(v.w, h3, l3);
+    hi[i] = make_uint2(h0 | ((uint32_t)h1 << 16), h2 | ((uint32_t)h3 << 16));
+    lo[i] = make_uint2(l0 | ((uint32_t)l1 << 16), l2 | ((uint32_t)l3 << 16));
+  }
+}
+
+// out[r] = -b_zp * sum_k a[r, k]  (QLinearMatMul row correction for b_zp != 0).
+__global__ void rowcorr_u8_kernel(const uint8_t* __restrict a, int m, int k, int lda, int b_zp,
+                                  int32_t* __restrict out) {
+  const int r = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= m) return;
+  int s = 0;
+  for (int i = lane; i < k; i += 32) s += a[(size_t)r * lda + i];
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if (lane == 0) out[r] = (int32_t)((uint32_t)(-b_zp) * (uint32_t)s);
+}
+
+template <typename T>
+__global__ void transpose_kernel(const T* __restrict src, T* __restrict dst, int c, int hw, int to_nhwc) {
+  __shared__ T tile[32][33];
+  const int img = blockIdx.z;
+  // to_nhwc: src [c][hw] -> dst [hw][c]; else src [hw][c] -> dst [c][hw]
+  const int rows = to_nhwc ? c : hw, cols = to_nhwc ? hw : c;
+  const int r0 = blockIdx.y * 32, c0 = blockIdx.x * 32;
+  const T* s = src + (size_t)img * c * hw;
+  T* d = dst + (size_t)img * c * hw;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, cc = c0 + threadIdx.x;
+    if (r < rows && cc < cols) tile[i][threadIdx.x] = s[(size_t)r * cols + cc];
+  }
+  __syncthreads();
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int cc = c0 + i, r = r0 + threadIdx.x;
+    if (r < rows && cc < cols) d[(size_t)cc * rows + r] = tile[threadIdx.x][i];
+  }
+}
+
+// Depthwise fp32 conv, NHWC in/out. Each thread produces 4 consecutive
+// channels (one float4) of one output pixel; weights are [kh][kw][c].
+__global__ void depthwise_f32_kernel(const float* __restrict x, const float* __restrict w, const float* __restrict bias,
+                                     float* __restrict y, const float* __restrict residual, int n, int h, int wd, int c,
+                                     int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int dh, int dw,
+                                     int act, float act_a, float act_b, int res_mode, float res_scale) {
+  const int c4 = c >> 2;
+  const long long total = (long long)n * oh * ow * c4;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int cv = (int)(i % c4);
+    long long p = i / c4;
+    const int ox = (int)(p % ow);
+    p /= ow;
+    const int oy = (int)(p % oh);
+    const int img = (int)(p / oh);
+    float4 acc = bias ? reinterpret_cast<const float4*>(bias)[cv] : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int ky = 0; ky < kh; ++ky) {
+      const int iy = oy * sh - ph + ky * dh;
+      if ((unsigned)iy >= (unsigned)h) continue;
+      for (int kx = 0; kx < kw; ++kx) {
+        const int ix = ox * sw - pw + kx * dw;
+        if ((unsigned)ix >= (unsigned)wd) continue;
+        const float4 xv = reinterpret_cast<const float4*>(x + (((size_t)img * h + iy) * wd + ix) * c)[cv];
+        const float4 wv = reinterpret_cast<const float4*>(w + ((size_t)ky * kw + kx) * c)[cv];
+        acc.x = fmaf(xv.x, wv.x, acc.x);
+        acc.y = fmaf(xv.y, wv.y, acc.y);
+        acc.z = fmaf(xv.z, wv.z, acc.z);
+        acc.w = fmaf(xv.w, wv.w, acc.w);
+      }
+    }
+    float o[4] = {acc.x, acc.y, acc.z, acc.w};
+    float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (residual) rr = reinterpret_cast<const float4*>(residual)[i];
+    const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      float a = o[u];
+      if (res_mode == 1) a = fmaf(res_scale, rv[u], a);
+      a = apply_act(a, act, act_a, act_b);
+      if (res_mode == 2) a += rv[u];
+      o[u] = a;
+    }
+    reinterpret_cast<float4*>(y)[i] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+int grid_for(long long total, int threads) {
+  long long b = (total + threads - 1) / threads;
+  const long long cap = (long long)num_sms() * 16;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (int)b;
+}
+
+}  // namespace
+
+void host_split_bf16(float v, uint16_t* hi, uint16_t* lo) {
+  const __nv_bfloat16 h = __float2bfloat16_rn(v);
+  const __nv_bfloat16 l = __float2bfloat16_rn(v - __bfloat162float(h));
+  *hi = __bfloat16_as_ushort(h);
+  *lo = __bfloat16_as_ushort(l);
+}
+
+int launch_nchw_to_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int c, int h, int w, int cs, uint8_t fill,
+                           cudaStream_t st) {
+  const int hw = h * w;
+  dim3 grid((hw + 31) / 32, (cs + 31) / 32, n), block(32, 8);
+  nchw_to_nhwc_u8_kernel<<<grid, block, 0, st>>>(src, dst, c, hw, cs, fill);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_pad_nhwc_u8(const uint8_t* src, uint8_t* dst, int pixels, int c, int cs, uint8_t fill, cudaStream_t st) {
+  const long long total = (long long)pixels * cs;
+  pad_nhwc_u8_kernel<<<grid_for(total, 256), 256, 0, st>>>(src, dst, pixels, c, cs, fill);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
+                           int cs, cudaStream_t st) {
+  const int hw = h * w;
+  if (src_nchw) {
+    dim3 grid((hw + 31) / 32, (cs + 31) / 32, n), block(32, 8);
+    split_bf16_nchw_tiled_kernel<<<grid, block, 0, st>>>(src, hi, lo, c, hw, cs);
+  } else if (c == cs && (c % 4) == 0) {
+    const long long n4 = (long long)n * hw * c / 4;
+    split_bf16_rows_vec_kernel<<<grid_for(n4, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(src),
+                                                                   reinterpret_cast<uint2*>(hi),
+                                                                   reinterpret_cast<uint2*>(lo), n4);
+  } else {
+    const long long pixels = (long long)n * hw;
+    split_bf16_nhwc_kernel<<<grid_for(pixels * cs, 256), 256, 0, st>>>(src, 0, hi, lo, pixels, c, hw, cs);
+  }
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_split_bf16_rows(const float* src, int trans, uint16_t* hi, uint16_t* lo, int m, int k, int kp,
+                           cudaStream_t st) {
+  if (!trans && k == kp && (k % 4) == 0) {
+    const long long n4 = (long long)m * k / 4;
+    split_bf16_rows_vec_kernel<<<grid_for(n4, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(src),
+                                                                   reinterpret_cast<uint2*>(hi),
+                                                                   reinterpret_cast<uint2*>(lo), n4);
+  } else {
+    split_bf16_rows_kernel<<<grid_for((long long)m * kp, 256), 256, 0, st>>>(src, trans, hi, lo, m, k, kp);
+  }
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_rowcorr_u8(const uint8_t* a, int m, int k, int lda, int b_zp, int32_t* out, cudaStream_t st) {
+  rowcorr_u8_kernel<<<(m + 7) / 8, 256, 0, st>>>(a, m, k, lda, b_zp, out);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_transpose_generic(const void* src, void* dst, int n, int c, int hw, int elem, int to_nhwc,
+                             cudaStream_t st) {
+  const int rows = to_nhwc ? c : hw, cols = to_nhwc ? hw : c;
+  dim3 grid((cols + 31) / 32, (rows + 31) / 32, n), block(32, 8);
+  switch (elem) {
+    case 1: transpose_kernel<uint8_t><<<grid, block, 0, st>>>((const uint8_t*)src, (uint8_t*)dst, c, hw, to_nhwc); break;
+    case 2: transpose_kernel<uint16_t><<<grid, block, 0, st>>>((const uint16_t*)src, (uint16_t*)dst, c, hw, to_nhwc); break;
+    case 4: transpose_kernel<uint32_t><<<grid, block, 0, st>>>((const uint32_t*)src, (uint32_t*)dst, c, hw, to_nhwc); break;
+    default: return set_error(NNRCU_ERR_INVALID, "element size %d not supported", elem);
+  }
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const float* residual, cudaStream_t st) {
+  const nnrcu_conv_desc& d = op.d;
+  const long long total = (long long)d.n * op.oh * op.ow * (d.c / 4);
+  depthwise_f32_kernel<<<grid_for(total, 256), 256, 0, st>>>(
+      x_nhwc, op.w_dw, op.bias, y, residual, d.n, d.h, d.w, d.c, op.oh, op.ow, d.kh, d.kw, d.stride_h, d.stride_w,
+      d.pad_top, d.pad_left, d.dil_h, d.dil_w, op.act, op.act_a, op.act_b, residual ? 2 : 0, 1.0f);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+}  // namespace nnrcu
+
+extern "C" {
+
+int nnrcu_nchw_to_nhwc(const void* src, void* dst, int n, int c, int h, int w, int elem_size, void* stream) {
+  if (!src || !dst || n <= 0 || c <= 0 || h <= 0 || w <= 0)
+    return nnrcu::set_error(NNRCU_ERR_INVALID, "nnrcu_nchw_to_nhwc: bad arguments");
+  return nnrcu::launch_transpose_generic(src, dst, n, c, h * w, elem_size, 1, static_cast<cudaStream_t>(stream));
+}
+int nnrcu_nhwc_to_nchw(const void* src, void* dst, int n, int c, int h, int w, int elem_size, void* stream) {
+  if (!src || !dst || n <= 0 || c <= 0 || h <= 0 || w <= 0)
+    return nnrcu::set_error(NNRCU_ERR_INVALID, "nnrcu_nhwc_to_nchw: bad arguments");
+  return nnrcu::launch_transpose_generic(src, dst, n, c, h * w, elem_size, 0, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

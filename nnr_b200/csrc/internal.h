@@ -1,0 +1,112 @@
+// Internal declarations shared by the translation units of libnnrcu.so.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdarg>
+#include <cstddef>
+#include <cstdint>
+#include <vector>
+
+#include "../../include/nnrcu.h"
+
+namespace nnrcu {
+
+// Records a formatted message as this thread's last error and returns code.
+int set_error(int code, const char* fmt, ...);
+// Maps a CUDA error to NNRCU_ERR_CUDA with a message; NNRCU_OK on success.
+int cuda_check(cudaError_t e, const char* what);
+#define NNRCU_CUDA(call)                                  \
+  do {                                                    \
+    int _rc = ::nnrcu::cuda_check((call), #call);         \
+    if (_rc != NNRCU_OK) return _rc;                      \
+  } while (0)
+
+// Device address of this device's status word (set up once per device).
+int* status_ptr();
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point.
+int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+
+enum OpKind : int { OP_QCONV = 1, OP_QMATMUL = 2, OP_CONV_F32 = 3, OP_GEMM_F32 = 4, OP_DWCONV_F32 = 5 };
+
+// One prepared operator: packed weights on the device plus everything the
+// launch needs. Created by nnrcu_*_create, consumed by nnrcu_*_run.
+struct Op {
+  int kind = 0;
+  int device = 0;
+  nnrcu_conv_desc d{};
+  // GEMM view
+  int M = 0, N = 0, K = 0;      // K in elements
+  int kbytes = 0;               // real K per plane in bytes
+  int kpad_bytes = 0;           // packed B row length in bytes (multiple of 128)
+  int num_kb = 0;
+  int npad = 0;                 // packed B rows per plane
+  int bn = 128;
+  int amode = 1;                // A_TMA / A_GATHER
+  int epi = 0;
+  int nplane = 1;
+  int oh = 0, ow = 0;
+  int cs = 0;                   // device channel stride (elements) of the NHWC operand
+  bool need_in_copy = false;    // input must be re-laid-out into the workspace first
+  // device buffers (owned)
+  void* wB = nullptr;
+  int32_t* colcorr = nullptr;
+  int32_t* bias_i = nullptr;
+  float* cs_arr = nullptr;
+  float* bias_f = nullptr;
+  float* os = nullptr;
+  float* bias = nullptr;
+  float* cmat = nullptr;        // Gemm C when it is a full matrix
+  float* w_dw = nullptr;        // depthwise weights [kh][kw][c]
+  CUtensorMap tmB{};
+  // requant scalars
+  float inv_y = 0, yzp_f = 0, qmin_f = 0, qmax_f = 0, rq_lo = 0, rq_hi = 0, combined = 0;
+  int yzp = 0;
+  int x_zp = 0;
+  int a_zp = 0, b_zp = 0;
+  // fp32 post-op
+  int act = 0;
+  float act_a = 0, act_b = 0;
+  float beta = 0;
+  int c_rows = 0;
+  int trans_a = 0;
+  size_t ws_bytes = 0;
+  int64_t num_ops = 0;
+};
+
+// Launch of the tcgen05 engine (tc_launch.cu).
+struct TcLaunch {
+  int bn, nplane, amode, epi;
+  int m_tiles, n_tiles;
+  const CUtensorMap* tmA0;
+  const CUtensorMap* tmA1;
+  const CUtensorMap* tmB;
+  int b_plane_rows;
+  int num_kb;
+};
+struct GatherGeom;
+struct EpiParams;
+int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream);
+// Picks the N tile (64/128/256) that minimises the estimated waves x tile cost.
+int pick_bn(int M, int N, int nplane, int num_sms);
+int num_sms();
+
+// Auxiliary kernels (aux_kernels.cu).
+int launch_nchw_to_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int c, int h, int w, int cs, uint8_t fill,
+                           cudaStream_t st);
+int launch_pad_nhwc_u8(const uint8_t* src, uint8_t* dst, int pixels, int c, int cs, uint8_t fill, cudaStream_t st);
+int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
+                           int cs, cudaStream_t st);
+int launch_split_bf16_rows(const float* src, int trans, uint16_t* hi, uint16_t* lo, int m, int k, int kp,
+                           cudaStream_t st);
+int launch_rowcorr_u8(const uint8_t* a, int m, int k, int lda, int b_zp, int32_t* out, cudaStream_t st);
+int launch_transpose_generic(const void* src, void* dst, int n, int c, int hw, int elem, int to_nhwc,
+                             cudaStream_t st);
+int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const float* residual, cudaStream_t st);
+
+void host_split_bf16(float v, uint16_t* hi, uint16_t* lo);
+
+}  // namespace nnrcu
+
+struct nnrcu_op : nnrcu::Op {};

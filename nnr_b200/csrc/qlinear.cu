@@ -1,0 +1,323 @@
+// QLinearConv and QLinearMatMul on the tcgen05 int8 engine.
+//
+// Weight packing and the requantisation constants are computed once here
+// (the device counterpart of QLinearConv_reshape.h:18-340 and
+// QLinearMatMul.cpp:33-94); *_run only enqueues kernels.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "internal.h"
+#include "tc_gemm.cuh"
+
+namespace nnrcu {
+
+template <typename T>
+static int upload(T** dst, const std::vector<T>& src) {
+  NNRCU_CUDA(cudaMalloc(reinterpret_cast<void**>(dst), std::max<size_t>(1, src.size() * sizeof(T))));
+  NNRCU_CUDA(cudaMemcpy(*dst, src.data(), src.size() * sizeof(T), cudaMemcpyHostToDevice));
+  return NNRCU_OK;
+}
+#define NNRCU_TRY(x)          \
+  do {                        \
+    int _r = (x);             \
+    if (_r != NNRCU_OK) {     \
+      nnrcu_op_destroy(op);   \
+      return _r;              \
+    }                         \
+  } while (0)
+
+static inline int round_up(int v, int a) { return (v + a - 1) / a * a; }
+
+int conv_out_dims(const nnrcu_conv_desc& d, int* oh, int* ow) {
+  if (d.n <= 0 || d.c <= 0 || d.h <= 0 || d.w <= 0 || d.oc <= 0 || d.kh <= 0 || d.kw <= 0 || d.stride_h <= 0 ||
+      d.stride_w <= 0 || d.dil_h <= 0 || d.dil_w <= 0 || d.pad_top < 0 || d.pad_left < 0 || d.pad_bottom < 0 ||
+      d.pad_right < 0 || d.group <= 0)
+    return set_error(NNRCU_ERR_INVALID, "conv descriptor has a non-positive dimension or negative pad");
+  if (d.in_layout != NNRCU_LAYOUT_NCHW && d.in_layout != NNRCU_LAYOUT_NHWC)
+    return set_error(NNRCU_ERR_INVALID, "bad input layout %d", d.in_layout);
+  if (d.out_layout != NNRCU_LAYOUT_NCHW && d.out_layout != NNRCU_LAYOUT_NHWC)
+    return set_error(NNRCU_ERR_INVALID, "bad output layout %d", d.out_layout);
+  // ONNX / compute_conv_output_shape (backend/cpu/conv_shape.h:21-79) with explicit pads.
+  const int eh = d.dil_h * (d.kh - 1) + 1, ew = d.dil_w * (d.kw - 1) + 1;
+  const int ph = d.h + d.pad_top + d.pad_bottom - eh, pw = d.w + d.pad_left + d.pad_right - ew;
+  if (ph < 0 || pw < 0) return set_error(NNRCU_ERR_INVALID, "kernel larger than padded input");
+  *oh = ph / d.stride_h + 1;
+  *ow = pw / d.stride_w + 1;
+  return NNRCU_OK;
+}
+
+}  // namespace nnrcu
+
+using namespace nnrcu;
+
+extern "C" {
+
+int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, const float* w_scale, int n_w_scale,
+                             const int8_t* w_zp, int n_w_zp, const int32_t* bias_host, float x_scale, uint8_t x_zp,
+                             float y_scale, uint8_t y_zp, nnrcu_op** out) {
+  if (!desc || !w_host || !w_scale || !out) return set_error(NNRCU_ERR_INVALID, "NULL argument");
+  *out = nullptr;
+  const nnrcu_conv_desc& d = *desc;
+  int oh = 0, ow = 0;
+  int rc = conv_out_dims(d, &oh, &ow);
+  if (rc != NNRCU_OK) return rc;
+  if (d.group != 1)
+    return set_error(NNRCU_ERR_UNSUPPORTED, "QLinearConv with group=%d is not implemented on the device", d.group);
+  if (n_w_scale != 1 && n_w_scale != d.oc)
+    return set_error(NNRCU_ERR_INVALID, "w_scale has %d entries (expected 1 or %d)", n_w_scale, d.oc);
+  for (int i = 0; i < n_w_zp; ++i)
+    if (w_zp && w_zp[i] != 0)
+      return set_error(NNRCU_ERR_UNSUPPORTED, "non-zero weight zero point (nnr's VNNI paths require symmetric weights)");
+  if (!(y_scale > 0.0f) || !(x_scale > 0.0f)) return set_error(NNRCU_ERR_INVALID, "scales must be positive");
+
+  nnrcu_op* op = new nnrcu_op();
+  NNRCU_TRY(cuda_check(cudaGetDevice(&op->device), "cudaGetDevice"));
+  op->kind = OP_QCONV;
+  op->d = d;
+  op->oh = oh;
+  op->ow = ow;
+  op->cs = round_up(d.c, 16);
+  op->M = d.n * oh * ow;
+  op->N = d.oc;
+  op->K = d.kh * d.kw * d.c;
+  op->kbytes = d.kh * d.kw * op->cs;
+  op->kpad_bytes = round_up(op->kbytes, BKB);
+  op->num_kb = op->kpad_bytes / BKB;
+  op->npad = round_up(d.oc, 256);
+  op->nplane = 1;
+  op->bn = pick_bn(op->M, op->N, 1, num_sms());
+  op->num_ops = 2LL * op->M * d.oc * (long long)op->K;
+  op->x_zp = x_zp;
+
+  // Requant formula: what nnr's x64 VNNI dispatch picks for this layer
+  // (QLinearConv.cpp:1337-1351; stem predicate QLinearConv_reshape.h:245-246
+  // and QLinearConv.cpp:668-675; direct predicate :579-583).
+  int rq = d.requant;
+  if (rq == NNRCU_RQ_AUTO) {
+    const bool stem = d.c <= 4 && d.kh >= 3 && d.oc >= 16 && d.dil_h == 1 && d.dil_w == 1 &&
+                      d.pad_top == d.pad_bottom && d.pad_left == d.pad_right && d.in_layout == NNRCU_LAYOUT_NCHW;
+    const bool direct = d.dil_h == 1 && d.dil_w == 1 && oh * ow <= 256 && d.out_layout == NNRCU_LAYOUT_NCHW;
+    rq = stem ? NNRCU_RQ_R3 : (direct ? NNRCU_RQ_R1 : NNRCU_RQ_R2);
+  }
+  if (rq < NNRCU_RQ_R1 || rq > NNRCU_RQ_R3) {
+    nnrcu_op_destroy(op);
+    return set_error(NNRCU_ERR_INVALID, "unknown requant formula %d", rq);
+  }
+  op->epi = rq == NNRCU_RQ_R1 ? EPI_R1 : (rq == NNRCU_RQ_R2 ? EPI_R2 : EPI_R3);
+
+  // A operand: plain TMA tiles for a 1x1/s1/p0 conv over an NHWC input that
+  // needs no channel padding; the implicit-im2col gather otherwise.
+  const bool one_by_one = d.kh == 1 && d.kw == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_top == 0 &&
+                          d.pad_left == 0 && d.pad_bottom == 0 && d.pad_right == 0;
+  op->need_in_copy = d.in_layout == NNRCU_LAYOUT_NCHW || d.c != op->cs;
+  op->amode = (one_by_one && op->kbytes >= BKB && op->epi != EPI_R3) ? A_TMA : A_GATHER;
+  op->ws_bytes = op->need_in_copy ? (size_t)d.n * d.h * d.w * op->cs : 0;
+
+  // Pack B = W as [npad][kpad] K-major with k = (kh, kw, ic); padded channels,
+  // taps and rows are zero. wsum feeds the x_zp compensation.
+  std::vector<int8_t> B((size_t)op->npad * op->kpad_bytes, 0);
+  std::vector<int32_t> colcorr(d.oc), bias_i(d.oc, 0);
+  std::vector<float> csv(d.oc), bias_f(d.oc, 0.0f), osv(d.oc);
+  const float inv_y = 1.0f / y_scale;  // QLinearConv.cpp:420 / QLinearConv_reshape.h:291
+  for (int o = 0; o < d.oc; ++o) {
+    int32_t wsum = 0;
+    for (int ic = 0; ic < d.c; ++ic)
+      for (int y = 0; y < d.kh; ++y)
+        for (int x = 0; x < d.kw; ++x) {
+          const int8_t v = w_host[(((size_t)o * d.c + ic) * d.kh + y) * d.kw + x];
+          B[(size_t)o * op->kpad_bytes + (size_t)(y * d.kw + x) * op->cs + ic] = v;
+          wsum += v;
+        }
+    colcorr[o] = (int32_t)(0u - (uint32_t)x_zp * (uint32_t)wsum);
+    const float ws = n_w_scale > 1 ? w_scale[o] : w_scale[0];
+    csv[o] = x_scale * ws;                                   // combined scale
+    if (bias_host) {
+      bias_i[o] = bias_host[o];
+      bias_f[o] = (float)bias_host[o] * csv[o];
+    }
+    osv[o] = csv[o] * inv_y;                                 // QLinearConv_reshape.h:310
+  }
+  const int lo = 0, hi = 255;
+  const int qmin = d.post_op != NNRCU_POST_NONE ? std::max(lo, (int)y_zp) : lo;
+  op->inv_y = inv_y;
+  op->yzp_f = (float)y_zp;
+  op->qmin_f = (float)qmin;
+  op->qmax_f = (float)hi;
+  op->rq_lo = (float)lo - (float)y_zp;                       // QLinearConv_reshape.h:326-327
+  op->rq_hi = (float)hi - (float)y_zp;
+  op->yzp = y_zp;
+
+  void* wB = nullptr;
+  NNRCU_TRY(cuda_check(cudaMalloc(&wB, B.size()), "cudaMalloc(weights)"));
+  op->wB = wB;
+  NNRCU_TRY(cuda_check(cudaMemcpy(wB, B.data(), B.size(), cudaMemcpyHostToDevice), "upload weights"));
+  NNRCU_TRY(upload(&op->colcorr, colcorr));
+  NNRCU_TRY(upload(&op->bias_i, bias_i));
+  NNRCU_TRY(upload(&op->cs_arr, csv));
+  NNRCU_TRY(upload(&op->bias_f, bias_f));
+  NNRCU_TRY(upload(&op->os, osv));
+  NNRCU_TRY(encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, op->kpad_bytes, op->npad, op->kpad_bytes,
+                           BKB, op->bn));
+  *out = op;
+  return NNRCU_OK;
+}
+
+int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream) {
+  if (!op || op->kind != OP_QCONV) return set_error(NNRCU_ERR_INVALID, "not a QLinearConv operator");
+  if (!x || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
+  if (op->ws_bytes && !workspace)
+    return set_error(NNRCU_ERR_INVALID, "workspace of %zu bytes required", op->ws_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const nnrcu_conv_desc& d = op->d;
+  const uint8_t* xin = x;
+  if (op->need_in_copy) {
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    int rc = d.in_layout == NNRCU_LAYOUT_NCHW
+                 ? launch_nchw_to_nhwc_u8(x, ws, d.n, d.c, d.h, d.w, op->cs, (uint8_t)op->x_zp, st)
+                 : launch_pad_nhwc_u8(x, ws, d.n * d.h * d.w, d.c, op->cs, (uint8_t)op->x_zp, st);
+    if (rc != NNRCU_OK) return rc;
+    xin = ws;
+  }
+  CUtensorMap tmA{};
+  if (op->amode == A_TMA) {
+    int rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, xin, op->cs, (uint64_t)op->M, op->cs, BKB, BM);
+    if (rc != NNRCU_OK) return rc;
+  }
+  GatherGeom g{};
+  g.x = xin;
+  g.x2 = nullptr;
+  g.N = d.n; g.H = d.h; g.W = d.w;
+  g.cbytes = op->cs;
+  g.OH = op->oh; g.OW = op->ow; g.KH = d.kh; g.KW = d.kw;
+  g.sh = d.stride_h; g.sw = d.stride_w; g.ph = d.pad_top; g.pw = d.pad_left; g.dh = d.dil_h; g.dw = d.dil_w;
+  g.kbytes = op->kbytes;
+  g.pad_word = 0x01010101u * (uint32_t)op->x_zp;
+
+  EpiParams e{};
+  e.M = op->M; e.N = op->N;
+  e.colcorr = op->colcorr; e.bias_i = op->bias_i; e.cs = op->cs_arr; e.bias_f = op->bias_f; e.os = op->os;
+  e.inv_y = op->inv_y; e.yzp_f = op->yzp_f; e.qmin_f = op->qmin_f; e.qmax_f = op->qmax_f;
+  e.rq_lo = op->rq_lo; e.rq_hi = op->rq_hi; e.yzp = op->yzp;
+  e.y = y;
+  e.y_layout = d.out_layout == NNRCU_LAYOUT_NCHW ? 1 : 0;
+  e.ldy = d.oc;
+  e.ohw = op->oh * op->ow;
+  e.status = status_ptr();
+
+  TcLaunch L{};
+  L.bn = op->bn; L.nplane = 1; L.amode = op->amode; L.epi = op->epi;
+  L.m_tiles = (op->M + BM - 1) / BM;
+  L.n_tiles = (op->N + op->bn - 1) / op->bn;
+  L.tmA0 = &tmA; L.tmA1 = &tmA; L.tmB = &op->tmB;
+  L.b_plane_rows = op->npad;
+  L.num_kb = op->num_kb;
+  return tc_launch(L, g, e, st);
+}
+
+int nnrcu_qlinearmatmul_create(int m, int k, int n, float a_scale, uint8_t a_zp, const int8_t* b_host, float b_scale,
+                               int8_t b_zp, float y_scale, uint8_t y_zp, nnrcu_op** out) {
+  if (!b_host || !out) return set_error(NNRCU_ERR_INVALID, "NULL argument");
+  *out = nullptr;
+  if (m <= 0 || k <= 0 || n <= 0) return set_error(NNRCU_ERR_INVALID, "QLinearMatMul dims must be positive");
+  nnrcu_op* op = new nnrcu_op();
+  NNRCU_TRY(cuda_check(cudaGetDevice(&op->device), "cudaGetDevice"));
+  op->kind = OP_QMATMUL;
+  op->M = m; op->N = n; op->K = k;
+  op->cs = round_up(k, 16);            // A row stride on the device
+  op->kbytes = op->cs;
+  op->kpad_bytes = round_up(op->kbytes, BKB);
+  op->num_kb = op->kpad_bytes / BKB;
+  op->npad = round_up(n, 256);
+  op->nplane = 1;
+  op->epi = EPI_R4;
+  op->bn = pick_bn(m, n, 1, num_sms());
+  op->num_ops = 2LL * m * n * (long long)k;
+  op->a_zp = a_zp;
+  op->b_zp = b_zp;
+  op->need_in_copy = op->cs != k;
+  op->amode = op->kbytes >= BKB ? A_TMA : A_GATHER;
+  op->ws_bytes = (op->need_in_copy ? round_up(m * op->cs, 256) : 0) + (b_zp != 0 ? (size_t)m * 4 : 0);
+
+  // Combined scale a*b/y in that order (QLinearMatMul.cpp:134).
+  op->combined = a_scale * b_scale / y_scale;
+  op->yzp_f = (float)y_zp;
+
+  std::vector<int8_t> B((size_t)op->npad * op->kpad_bytes, 0);
+  std::vector<int32_t> colcorr(n);
+  for (int j = 0; j < n; ++j) {
+    int32_t s = 0;
+    for (int kk = 0; kk < k; ++kk) {
+      const int8_t v = b_host[(size_t)kk * n + j];
+      B[(size_t)j * op->kpad_bytes + kk] = v;
+      s += v;
+    }
+    // sum (a - a_zp)(b - b_zp) = sum ab - a_zp*colsum - b_zp*rowsum + k*a_zp*b_zp
+    // (zero-point algebra of backend/x64/gemm_int8_avx512.h:1-11)
+    colcorr[j] = (int32_t)(0u - (uint32_t)a_zp * (uint32_t)s + (uint32_t)k * (uint32_t)a_zp * (uint32_t)(int32_t)b_zp);
+  }
+  void* wB = nullptr;
+  NNRCU_TRY(cuda_check(cudaMalloc(&wB, B.size()), "cudaMalloc(weights)"));
+  op->wB = wB;
+  NNRCU_TRY(cuda_check(cudaMemcpy(wB, B.data(), B.size(), cudaMemcpyHostToDevice), "upload weights"));
+  NNRCU_TRY(upload(&op->colcorr, colcorr));
+  NNRCU_TRY(encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, op->kpad_bytes, op->npad, op->kpad_bytes,
+                           BKB, op->bn));
+  *out = op;
+  return NNRCU_OK;
+}
+
+int nnrcu_qlinearmatmul_run(nnrcu_op* op, const uint8_t* a, uint8_t* y, void* workspace, void* stream) {
+  if (!op || op->kind != OP_QMATMUL) return set_error(NNRCU_ERR_INVALID, "not a QLinearMatMul operator");
+  if (!a || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
+  if (op->ws_bytes && !workspace)
+    return set_error(NNRCU_ERR_INVALID, "workspace of %zu bytes required", op->ws_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const uint8_t* ain = a;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* rowcorr = nullptr;
+  if (op->need_in_copy) {
+    int rc = launch_pad_nhwc_u8(a, ws, op->M, op->K, op->cs, (uint8_t)op->a_zp, st);
+    if (rc != NNRCU_OK) return rc;
+    ain = ws;
+    ws += round_up(op->M * op->cs, 256);
+  }
+  if (op->b_zp != 0) {
+    rowcorr = reinterpret_cast<int32_t*>(ws);
+    int rc = launch_rowcorr_u8(ain, op->M, op->K, op->cs, op->b_zp, rowcorr, st);
+    if (rc != NNRCU_OK) return rc;
+  }
+  CUtensorMap tmA{};
+  if (op->amode == A_TMA) {
+    int rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, ain, op->cs, (uint64_t)op->M, op->cs, BKB, BM);
+    if (rc != NNRCU_OK) return rc;
+  }
+  GatherGeom g{};
+  g.x = ain;
+  g.N = 1; g.H = 1; g.W = op->M;
+  g.cbytes = op->cs;
+  g.OH = 1; g.OW = op->M; g.KH = 1; g.KW = 1; g.sh = 1; g.sw = 1; g.ph = 0; g.pw = 0; g.dh = 1; g.dw = 1;
+  g.kbytes = op->kbytes;
+  g.pad_word = 0;
+  EpiParams e{};
+  e.M = op->M; e.N = op->N;
+  e.colcorr = op->colcorr;
+  e.rowcorr = rowcorr;
+  e.combined = op->combined;
+  e.yzp_f = op->yzp_f;
+  e.y = y;
+  e.y_layout = 0;
+  e.ldy = op->N;
+  e.ohw = 1;
+  e.status = status_ptr();
+  TcLaunch L{};
+  L.bn = op->bn; L.nplane = 1; L.amode = op->amode; L.epi = EPI_R4;
+  L.m_tiles = (op->M + BM - 1) / BM;
+  L.n_tiles = (op->N + op->bn - 1) / op->bn;
+  L.tmA0 = &tmA; L.tmA1 = &tmA; L.tmB = &op->tmB;
+  L.b_plane_rows = op->npad;
+  L.num_kb = op->num_kb;
+  return tc_launch(L, g, e, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,439 @@
+// Implicit-GEMM engine on the 5th-generation tensor cores (tcgen05) for the
+// Conv / QLinearConv / QLinearMatMul / Gemm / MatMul operators.
+//
+// GEMM view: D[M, N] = A[M, K] * B[N, K]^T, both operands K-major in bytes.
+//   * conv:   M = output pixels (n, oh, ow), N = output channels,
+//             K = (kh, kw, ic) with ic padded to a 16-byte channel stride.
+//   * matmul: M = rows of A, N = columns of B, K = the reduction dim.
+//
+// One CTA computes a 128 x BN tile of D:
+//   warps 0-3  A producers in gather mode (cp.async from NHWC activations,
+//              padding pixels filled with the input zero point), then the
+//              epilogue (TMEM -> registers -> requant / bias / post-op -> HBM)
+//   warp 4     TMA producer (B tiles always, A tiles in TMA mode)
+//   warp 5     TMEM allocator and single-thread tcgen05.mma issuer
+// Shared memory holds STAGES stages of {A planes, B planes}, each plane a
+// 128-byte-wide K slab in the 128-byte swizzled K-major layout that both TMA
+// (SWIZZLE_128B) and the UMMA descriptors understand.
+//
+// NPLANE = 1: int8 (kind::i8, u8 activations x s8 weights, s32 accumulate).
+// NPLANE = 2: fp32 emulated as split bf16 (kind::f16, f32 accumulate):
+//             a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi with x_hi = bf16(x),
+//             x_lo = bf16(x - x_hi); the dropped a_lo*b_lo term is < 2^-16
+//             relative per product.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include "ptx.cuh"
+
+namespace nnrcu {
+
+enum : int { A_TMA = 0, A_GATHER = 1 };
+enum : int { EPI_R1 = 1, EPI_R2 = 2, EPI_R3 = 3, EPI_R4 = 4, EPI_F32 = 10 };
+enum : int { ACT_NONE = 0, ACT_RELU = 1, ACT_CLIP = 2, ACT_HARDSWISH = 3, ACT_SIGMOID = 4, ACT_LEAKYRELU = 5,
+             ACT_TANH = 6 };
+enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_ACCUM = 3 };
+
+constexpr int BM = 128;       // rows per tile (TMEM lanes)
+constexpr int BKB = 128;      // K bytes per stage per plane (one swizzle row)
+constexpr int NUM_THREADS = 192;
+
+// Geometry of the implicit im2col gather (A_GATHER). All sizes in bytes where noted.
+struct GatherGeom {
+  const uint8_t* x;      // NHWC activations, plane 0
+  const uint8_t* x2;     // plane 1 (bf16 low halves) or null
+  int N, H, W;
+  int cbytes;            // bytes per pixel (channel stride), multiple of 16
+  int OH, OW, KH, KW, sh, sw, ph, pw, dh, dw;
+  int kbytes;            // real K in bytes = KH*KW*cbytes
+  uint32_t pad_word;     // value written for padding pixels (x_zp replicated, or 0)
+};
+
+struct EpiParams {
+  int M, N;              // logical GEMM extent
+  // int8 requantisation (per output channel arrays are indexed by n)
+  const int32_t* colcorr;  // -x_zp * sum(w) (+ K*a_zp*b_zp), or null
+  const int32_t* rowcorr;  // per-row correction (QLinearMatMul with b_zp != 0), or null
+  const int32_t* bias_i;   // R2 int32 bias, or null
+  const float* cs;         // R1/R3 combined scale x_scale*w_scale[n]
+  const float* bias_f;     // R1/R3 float bias = bias*cs, or null
+  const float* os;         // R2 output scale cs*inv_y
+  float inv_y, yzp_f, qmin_f, qmax_f;  // R1/R3/R4
+  float rq_lo, rq_hi;                  // R2 clamp bounds (lo - y_zp, hi - y_zp)
+  float combined;                      // R4 scalar scale a_s*b_s/y_s
+  int yzp;                             // R2 integer zero point
+  // fp32 epilogue
+  const float* bias;       // per-n bias or null
+  const float* residual;   // same layout as y, or null
+  int res_mode;            // 1: v = act(acc + bias + res_scale*res); 2: v = act(acc + bias) + res
+  float res_scale;
+  int act; float act_a, act_b;
+  // output
+  void* y;
+  int y_layout;            // 0: row-major [M, ldy]; 1: NCHW with M = img*ohw + p
+  int ldy, ohw;
+  int* status;             // device status word (first error wins)
+};
+
+template <int BN, int NPLANE>
+struct TileCfg {
+  static constexpr int A_BYTES = BM * BKB;             // 16 KB per plane
+  static constexpr int B_BYTES = BN * BKB;
+  static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + B_BYTES);
+  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;  // power of two >= 32
+  static constexpr int PARAM_BYTES = 6 * BN * 4;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/ + PARAM_BYTES;
+  static_assert(STAGES >= 2, "need at least two pipeline stages");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
+};
+
+__device__ __forceinline__ void record_status(int* status, int code) {
+  if (status) atomicCAS(status, 0, code);
+}
+
+__device__ __forceinline__ float apply_act(float v, int act, float a, float b) {
+  switch (act) {
+    case ACT_RELU: return fmaxf(v, 0.0f);
+    case ACT_CLIP: return fminf(fmaxf(v, a), b);
+    case ACT_HARDSWISH: {
+      // HardSwish(x) = x * max(0, min(1, x/6 + 0.5))
+      float t = fmaf(v, 1.0f / 6.0f, 0.5f);
+      t = fminf(fmaxf(t, 0.0f), 1.0f);
+      return v * t;
+    }
+    case ACT_SIGMOID: return 1.0f / (1.0f + expf(-v));
+    case ACT_LEAKYRELU: return v >= 0.0f ? v : v * a;
+    case ACT_TANH: return tanhf(v);
+    default: return v;
+  }
+}
+
+// Requantise one int32 accumulator to u8 with the formula EPI selects.
+template <int EPI>
+__device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t colc, int32_t rowc, int32_t bias_i, float cs,
+                                               float bias_f, float os, const EpiParams& e) {
+  if constexpr (EPI == EPI_R1) {
+    // f = fma(float(acc), cs, bias_f); f = rne(f * inv_y) + y_zp; min(hi) then max(qmin)
+    int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)colc);
+    float f = __fmaf_rn(__int2float_rn(acc), cs, bias_f);
+    f = rintf(__fmul_rn(f, e.inv_y));
+    f = __fadd_rn(f, e.yzp_f);
+    f = fmaxf(fminf(f, e.qmax_f), e.qmin_f);
+    return (uint32_t)__float2int_rn(f);
+  } else if constexpr (EPI == EPI_R2) {
+    // f = float(acc + bias) * os; max(lo - y_zp) then min(hi - y_zp); rne; + y_zp; saturate
+    int32_t v = (int32_t)((uint32_t)raw + (uint32_t)colc + (uint32_t)bias_i);
+    float f = __fmul_rn(__int2float_rn(v), os);
+    f = fminf(fmaxf(f, e.rq_lo), e.rq_hi);
+    int32_t q = __float2int_rn(f) + e.yzp;
+    q = q < 0 ? 0 : (q > 255 ? 255 : q);
+    return (uint32_t)q;
+  } else if constexpr (EPI == EPI_R3) {
+    // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); min(hi) then max(qmin); rne
+    int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)colc);
+    float f = __fmaf_rn(__int2float_rn(acc), cs, bias_f);
+    f = __fmaf_rn(f, e.inv_y, e.yzp_f);
+    f = fmaxf(fminf(f, e.qmax_f), e.qmin_f);
+    return (uint32_t)__float2int_rn(f);
+  } else {  // EPI_R4
+    // val = fma(float(acc), a_s*b_s/y_s, y_zp); nearbyint; clamp [0, 255]
+    int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)colc + (uint32_t)rowc);
+    float f = __fmaf_rn(__int2float_rn(acc), e.combined, e.yzp_f);
+    int32_t q = __float2int_rn(f);
+    q = q < 0 ? 0 : (q > 255 ? 255 : q);
+    return (uint32_t)q;
+  }
+}
+
+template <int BN, int NPLANE, int AMODE, int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
+               const __grid_constant__ CUtensorMap tmB, int b_plane_rows, GatherGeom g, EpiParams e, int num_kb) {
+  using Cfg = TileCfg<BN, NPLANE>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int A_BYTES = Cfg::A_BYTES;
+  constexpr int B_BYTES = Cfg::B_BYTES;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;                                        // [STAGES][NPLANE][A_BYTES]
+  uint8_t* sB = sA + STAGES * NPLANE * A_BYTES;              // [STAGES][NPLANE][B_BYTES]
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * NPLANE * B_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* accum_bar = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
+  uint8_t* sparam = reinterpret_cast<uint8_t*>(full_bar) + 256;
+  int32_t* s_colc = reinterpret_cast<int32_t*>(sparam);
+  int32_t* s_bias_i = s_colc + BN;
+  float* s_cs = reinterpret_cast<float*>(s_bias_i + BN);
+  float* s_bias_f = s_cs + BN;
+  float* s_os = s_bias_f + BN;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+
+  if (threadIdx.x == 0) {
+    const uint32_t full_count = (AMODE == A_GATHER) ? (128u + 1u) : 1u;
+    for (int s = 0; s < STAGES; ++s) {
+      ptx::mbar_init(&full_bar[s], full_count);
+      ptx::mbar_init(&empty_bar[s], 1);
+    }
+    ptx::mbar_init(accum_bar, 1);
+    ptx::fence_mbar_init();
+    ptx::fence_proxy_async_smem();
+  }
+  if (warp == 4 && lane == 0) {
+    ptx::tma_prefetch_desc(&tmB);
+    if (AMODE == A_TMA) {
+      ptx::tma_prefetch_desc(&tmA0);
+      if (NPLANE == 2) ptx::tma_prefetch_desc(&tmA1);
+    }
+  }
+  if (warp == 5) ptx::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  if (threadIdx.x < 128) {
+    for (int i = threadIdx.x; i < BN; i += 128) {
+      const int n = n0 + i;
+      const bool ok = n < e.N;
+      s_colc[i] = (ok && e.colcorr) ? e.colcorr[n] : 0;
+      s_bias_i[i] = (ok && e.bias_i) ? e.bias_i[n] : 0;
+      s_cs[i] = (ok && e.cs) ? e.cs[n] : 0.0f;
+      s_bias_f[i] = (ok && e.bias_f) ? e.bias_f[n] : ((ok && e.bias) ? e.bias[n] : 0.0f);
+      s_os[i] = (ok && e.os) ? e.os[n] : 0.0f;
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  bool aborted = false;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      constexpr uint32_t tx = (AMODE == A_TMA ? NPLANE * A_BYTES : 0) + NPLANE * B_BYTES;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+        if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1u)) { record_status(e.status, ST_TIMEOUT_EMPTY); aborted = true; break; }
+        ptx::mbar_arrive_expect_tx(&full_bar[s], tx);
+        uint8_t* a_st = sA + (size_t)s * NPLANE * A_BYTES;
+        uint8_t* b_st = sB + (size_t)s * NPLANE * B_BYTES;
+        const int kx = kb * BKB / (NPLANE == 2 ? 2 : 1);  // element coordinate along K
+        for (int p = 0; p < NPLANE; ++p)
+          ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
+        if (AMODE == A_TMA) {
+          ptx::tma_load_2d(a_st, &tmA0, &full_bar[s], kx, m0);
+          if (NPLANE == 2) ptx::tma_load_2d(a_st + A_BYTES, &tmA1, &full_bar[s], kx, m0);
+        }
+      }
+      if (aborted) ptx::settle_ns(200000);  // let copies already in flight land before the CTA exits
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = (NPLANE == 1) ? ptx::umma_idesc(2, 0, 1, BM, BN) : ptx::umma_idesc(1, 1, 1, BM, BN);
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+        if (!ptx::mbar_wait(&full_bar[s], ph)) { record_status(e.status, ST_TIMEOUT_FULL); aborted = true; break; }
+        ptx::tc_fence_after();
+        ptx::fence_proxy_async_smem();
+        const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * NPLANE * A_BYTES);
+        const uint32_t b_addr = ptx::smem_u32(sB + (size_t)s * NPLANE * B_BYTES);
+#pragma unroll
+        for (int k = 0; k < BKB / 32; ++k) {
+          const uint32_t koff = k * 32;
+          if constexpr (NPLANE == 1) {
+            ptx::mma_i8(tmem_base, ptx::umma_desc_sw128(a_addr + koff), ptx::umma_desc_sw128(b_addr + koff), idesc,
+                        (kb | k) != 0);
+          } else {
+            // hi*hi, hi*lo, lo*hi
+            ptx::mma_f16(tmem_base, ptx::umma_desc_sw128(a_addr + koff), ptx::umma_desc_sw128(b_addr + koff), idesc,
+                         (kb | k) != 0);
+            ptx::mma_f16(tmem_base, ptx::umma_desc_sw128(a_addr + koff),
+                         ptx::umma_desc_sw128(b_addr + B_BYTES + koff), idesc, 1u);
+            ptx::mma_f16(tmem_base, ptx::umma_desc_sw128(a_addr + A_BYTES + koff),
+                         ptx::umma_desc_sw128(b_addr + koff), idesc, 1u);
+          }
+        }
+        ptx::mma_commit(&empty_bar[s]);
+      }
+      ptx::mma_commit(accum_bar);  // fires when every MMA above has completed (also after an abort)
+    }
+  } else {
+    // ------------------------------------------------------------ warps 0-3
+    const int t = threadIdx.x;  // 0..127
+    if constexpr (AMODE == A_GATHER) {
+      // Thread t fills chunk (t & 7) of rows (t >> 3) + 16*i, i = 0..7: eight
+      // consecutive threads cover one 128-byte row, so each warp instruction
+      // reads four full rows.
+      const int chunk = t & 7;
+      int r_n[8], r_ih[8], r_iw[8];
+      const int ohw = g.OH * g.OW;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int r = (t >> 3) + 16 * i;
+        const int m = m0 + r;
+        if (m < e.M) {
+          const int img = m / ohw;
+          const int p = m - img * ohw;
+          const int oh = p / g.OW;
+          const int ow = p - oh * g.OW;
+          r_n[i] = img;
+          r_ih[i] = oh * g.sh - g.ph;
+          r_iw[i] = ow * g.sw - g.pw;
+        } else {
+          r_n[i] = -1; r_ih[i] = 0; r_iw[i] = 0;
+        }
+      }
+      constexpr int LAG = (STAGES - 1) < 2 ? (STAGES - 1) : 2;
+      for (int kb = 0; kb < num_kb && !aborted; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+        const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&empty_bar[s], ph ^ 1u));
+        if (!ok) { record_status(e.status, ST_TIMEOUT_EMPTY); aborted = true; break; }
+        uint8_t* a_st = sA + (size_t)s * NPLANE * A_BYTES;
+        const int kbyte = kb * BKB + chunk * 16;
+        const bool kvalid = kbyte < g.kbytes;
+        int tap = 0, cc = 0, kh = 0, kw = 0;
+        if (kvalid) {
+          tap = kbyte / g.cbytes;
+          cc = kbyte - tap * g.cbytes;
+          kh = tap / g.KW;
+          kw = tap - kh * g.KW;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int r = (t >> 3) + 16 * i;
+          uint8_t* dst = a_st + (r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4);
+          if (!kvalid || r_n[i] < 0) {
+#pragma unroll
+            for (int p = 0; p < NPLANE; ++p) ptx::st_shared_v4(dst + p * A_BYTES, 0u, 0u, 0u, 0u);
+            continue;
+          }
+          const int ih = r_ih[i] + kh * g.dh;
+          const int iw = r_iw[i] + kw * g.dw;
+          if ((unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W) {
+            const size_t off = (((size_t)r_n[i] * g.H + ih) * g.W + iw) * (size_t)g.cbytes + cc;
+            ptx::cp_async16(dst, g.x + off, 16);
+            if (NPLANE == 2) ptx::cp_async16(dst + A_BYTES, g.x2 + off, 16);
+          } else {
+            ptx::st_shared_v4(dst, g.pad_word, g.pad_word, g.pad_word, g.pad_word);
+            if (NPLANE == 2) ptx::st_shared_v4(dst + A_BYTES, 0u, 0u, 0u, 0u);
+          }
+        }
+        ptx::cp_async_commit();
+        // Publish the stage issued LAG iterations ago: its copies are done
+        // once at most LAG groups remain in flight.
+        if (kb >= LAG) {
+          ptx::cp_async_wait<LAG>();
+          ptx::fence_proxy_async_smem();
+          ptx::mbar_arrive(&full_bar[(kb - LAG) % STAGES]);
+        }
+      }
+      // Drain: publish the last LAG stages (or whatever was issued before an abort).
+      ptx::cp_async_wait<0>();
+      ptx::fence_proxy_async_smem();
+      if (!aborted) {
+        const int first = num_kb > LAG ? num_kb - LAG : 0;
+        for (int kb = first; kb < num_kb; ++kb) ptx::mbar_arrive(&full_bar[kb % STAGES]);
+      }
+    }
+
+    // ------------------------------------------------------------ epilogue
+    if (!aborted && !__all_sync(0xffffffffu, ptx::mbar_wait(accum_bar, 0))) {
+      record_status(e.status, ST_TIMEOUT_ACCUM);
+      aborted = true;
+    }
+    if (!aborted) {
+      ptx::tc_fence_after();
+      const int row = warp * 32 + lane;  // TMEM lane == tile row
+      const int m = m0 + row;
+      const bool mvalid = m < e.M;
+      int32_t rowc = 0;
+      if (EPI == EPI_R4 && e.rowcorr && mvalid) rowc = e.rowcorr[m];
+      int img = 0, pix = 0;
+      if (e.y_layout == 1 && mvalid) { img = m / e.ohw; pix = m - img * e.ohw; }
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        ptx::tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+        if (!mvalid || n0 + c0 >= e.N) continue;
+        const int nvalid = min(32, e.N - (n0 + c0));
+        if constexpr (EPI == EPI_F32) {
+          float* y = static_cast<float*>(e.y);
+          const bool rowmajor = e.y_layout == 0;
+          float* dst = rowmajor ? y + (size_t)m * e.ldy + n0 + c0 : nullptr;
+          const float* res = (e.residual && rowmajor) ? e.residual + (size_t)m * e.ldy + n0 + c0 : nullptr;
+          if (rowmajor && nvalid == 32 && (e.ldy & 3) == 0 && ((reinterpret_cast<uintptr_t>(e.y) & 15) == 0) &&
+              (!e.residual || (reinterpret_cast<uintptr_t>(e.residual) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float o[4];
+              float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (res) rr = *reinterpret_cast<const float4*>(res + j);
+              const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                float a = __uint_as_float(v[j + u]) + s_bias_f[c0 + j + u];
+                if (e.res_mode == 1) a = fmaf(e.res_scale, rv[u], a);
+                a = apply_act(a, e.act, e.act_a, e.act_b);
+                if (e.res_mode == 2) a += rv[u];
+                o[u] = a;
+              }
+              *reinterpret_cast<float4*>(dst + j) = make_float4(o[0], o[1], o[2], o[3]);
+            }
+          } else {
+            for (int j = 0; j < nvalid; ++j) {
+              const size_t idx = rowmajor ? (size_t)m * e.ldy + n0 + c0 + j
+                                          : ((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix;
+              const float r = e.residual ? e.residual[idx] : 0.0f;
+              float a = __uint_as_float(v[j]) + s_bias_f[c0 + j];
+              if (e.res_mode == 1) a = fmaf(e.res_scale, r, a);
+              a = apply_act(a, e.act, e.act_a, e.act_b);
+              if (e.res_mode == 2) a += r;
+              y[idx] = a;
+            }
+          }
+        } else {
+          uint32_t q[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            q[j] = requant_u8<EPI>((int32_t)v[j], s_colc[c0 + j], rowc, s_bias_i[c0 + j], s_cs[c0 + j],
+                                   s_bias_f[c0 + j], s_os[c0 + j], e);
+          }
+          uint8_t* y = static_cast<uint8_t*>(e.y);
+          if (e.y_layout == 0) {
+            uint8_t* dst = y + (size_t)m * e.ldy + n0 + c0;
+            if (nvalid == 32 && (e.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0) {
+              uint32_t w[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                w[j] = q[4 * j] | (q[4 * j + 1] << 8) | (q[4 * j + 2] << 16) | (q[4 * j + 3] << 24);
+              reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+              reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            } else {
+              for (int j = 0; j < nvalid; ++j) dst[j] = (uint8_t)q[j];
+            }
+          } else {
+            for (int j = 0; j < nvalid; ++j) y[((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix] = (uint8_t)q[j];
+          }
+        }
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace nnrcu

@@ -1,0 +1,92 @@
+// Instantiations of the tcgen05 engine and the runtime dispatch onto them.
+#include "internal.h"
+#include "tc_gemm.cuh"
+
+namespace nnrcu {
+
+namespace {
+
+template <int BN, int NPLANE, int AMODE, int EPI>
+int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
+  using Cfg = TileCfg<BN, NPLANE>;
+  auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI>;
+  // The attribute is per function; setting it is cheap but not free, so do it
+  // once per device.
+  static unsigned long long configured = 0;
+  int dev = 0;
+  NNRCU_CUDA(cudaGetDevice(&dev));
+  if (!(configured & (1ull << dev))) {
+    NNRCU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    configured |= 1ull << dev;
+  }
+  dim3 grid(L.m_tiles, L.n_tiles);
+  kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, L.b_plane_rows, g, e, L.num_kb);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+template <int BN>
+int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t st) {
+  if (L.nplane == 2) {
+    if (L.epi != EPI_F32) return set_error(NNRCU_ERR_INVALID, "split-bf16 engine needs the fp32 epilogue");
+    if (L.amode == A_TMA) return launch_one<BN, 2, A_TMA, EPI_F32>(L, g, e, st);
+    return launch_one<BN, 2, A_GATHER, EPI_F32>(L, g, e, st);
+  }
+  if (L.amode == A_TMA) {
+    switch (L.epi) {
+      case EPI_R1: return launch_one<BN, 1, A_TMA, EPI_R1>(L, g, e, st);
+      case EPI_R2: return launch_one<BN, 1, A_TMA, EPI_R2>(L, g, e, st);
+      case EPI_R4: return launch_one<BN, 1, A_TMA, EPI_R4>(L, g, e, st);
+      default: break;
+    }
+  } else {
+    switch (L.epi) {
+      case EPI_R1: return launch_one<BN, 1, A_GATHER, EPI_R1>(L, g, e, st);
+      case EPI_R2: return launch_one<BN, 1, A_GATHER, EPI_R2>(L, g, e, st);
+      case EPI_R3: return launch_one<BN, 1, A_GATHER, EPI_R3>(L, g, e, st);
+      case EPI_R4: return launch_one<BN, 1, A_GATHER, EPI_R4>(L, g, e, st);
+      default: break;
+    }
+  }
+  return set_error(NNRCU_ERR_INVALID, "no engine instance for amode %d epilogue %d", L.amode, L.epi);
+}
+
+}  // namespace
+
+int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
+  if (L.m_tiles <= 0 || L.n_tiles <= 0 || L.num_kb <= 0) return NNRCU_OK;
+  if (L.m_tiles > 0x7fffffff || L.n_tiles > 65535)
+    return set_error(NNRCU_ERR_INVALID, "grid too large (%d x %d)", L.m_tiles, L.n_tiles);
+  if (L.amode == A_GATHER && ((reinterpret_cast<uintptr_t>(g.x) & 15) || (g.x2 && (reinterpret_cast<uintptr_t>(g.x2) & 15)) ||
+                              (g.cbytes & 15)))
+    return set_error(NNRCU_ERR_INVALID, "gathered operand must be 16-byte aligned with a 16-byte pixel stride");
+  switch (L.bn) {
+    case 64: return dispatch_bn<64>(L, g, e, stream);
+    case 128: return dispatch_bn<128>(L, g, e, stream);
+    case 256: return dispatch_bn<256>(L, g, e, stream);
+    default: return set_error(NNRCU_ERR_INVALID, "unsupported N tile %d", L.bn);
+  }
+}
+
+int pick_bn(int M, int N, int nplane, int sms) {
+  // Estimated time ~ waves * per-tile cost, with the per-tile cost linear in
+  // BN plus a fixed overhead (prologue, epilogue drain) worth ~48 columns.
+  const int cands[3] = {256, 128, 64};
+  int best = 128;
+  double best_cost = 1e30;
+  const int mt = (M + BM - 1) / BM;
+  for (int bn : cands) {
+    if (nplane == 2 && bn == 256) continue;  // two stages only: keep 128 for split-bf16
+    const int nt = (N + bn - 1) / bn;
+    const long long tiles = (long long)mt * nt;
+    const long long waves = (tiles + sms - 1) / sms;
+    const double cost = (double)waves * (bn + 48);
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+}  // namespace nnrcu

@@ -1,0 +1,270 @@
+"""Host-side operators over libnnrcu.so, mirroring nnr's operator_t interface.
+
+Each class corresponds to the nnr operator of the same op_type. Constructing
+one is nnr's init()+reshape(): attributes are validated, weights packed and
+uploaded, requant constants computed (once). exec() is nnr's exec(): it
+enqueues the device work on a stream and returns. Tensors are torch CUDA
+tensors used purely as device buffers; no torch op touches the data.
+
+Reference interface: src/nnr.h:331-461 (operator_t), backend/cpu/Conv.cpp,
+QLinearConv.cpp, QLinearMatMul.cpp, Gemm.cpp, MatMul.cpp.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import (ConvDesc, LAYOUT_NCHW, LAYOUT_NHWC, POST_NONE, RQ_AUTO, call, lib)
+
+_LAYOUTS = {"NCHW": LAYOUT_NCHW, "NHWC": LAYOUT_NHWC}
+_POSTS = {None: 0, "Relu": 1, "Clip": 2, "HardSwish": 3, "Sigmoid": 4, "LeakyRelu": 5, "Tanh": 6}
+
+
+def init(device: int = 0) -> None:
+    """Selects the device on this thread and initialises the library there."""
+    torch.cuda.set_device(device)
+    call("nnrcu_init", device)
+
+
+def device_status() -> int:
+    st = C.c_int(0)
+    call("nnrcu_device_status", C.byref(st))
+    return st.value
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream().cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise ValueError("device operators take CUDA tensors")
+    if not t.is_contiguous():
+        raise ValueError("tensors must be contiguous")
+    return C.c_void_p(t.data_ptr())
+
+
+def _host(a: Optional[np.ndarray], dtype):
+    if a is None:
+        return None, None
+    arr = np.ascontiguousarray(np.asarray(a, dtype=dtype))
+    return arr, arr.ctypes.data_as(C.c_void_p)
+
+
+class DeviceArena:
+    """Bump allocator over one device buffer: the device arena that nnr's
+    memory planner slots map onto (memory_planner.h:13-51). Reset per run."""
+
+    def __init__(self, nbytes: int, device: Optional[int] = None):
+        dev = torch.device("cuda", torch.cuda.current_device() if device is None else device)
+        self.buf = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        self.off = 0
+
+    def alloc(self, nbytes: int) -> Optional[torch.Tensor]:
+        if nbytes == 0:
+            return None
+        start = (self.off + 255) // 256 * 256
+        if start + nbytes > self.buf.numel():
+            raise MemoryError(f"arena of {self.buf.numel()} bytes exhausted")
+        self.off = start + nbytes
+        return self.buf[start:start + nbytes]
+
+    def reset(self) -> None:
+        self.off = 0
+
+
+class Operator:
+    op_type = ""
+
+    def __init__(self):
+        self._op = C.c_void_p()
+
+    def _created(self):
+        if not self._op:
+            raise RuntimeError("operator not created")
+
+    def workspace_size(self) -> int:
+        self._created()
+        n = C.c_size_t(0)
+        call("nnrcu_op_workspace_size", self._op, C.byref(n))
+        return n.value
+
+    def num_ops(self) -> int:
+        self._created()
+        n = C.c_int64(0)
+        call("nnrcu_op_num_ops", self._op, C.byref(n))
+        return n.value
+
+    def _workspace(self, workspace, device):
+        need = self.workspace_size()
+        if need == 0:
+            return None, None
+        if workspace is None:
+            workspace = torch.empty(need, dtype=torch.uint8, device=device)
+        if workspace.numel() * workspace.element_size() < need:
+            raise ValueError(f"workspace too small ({need} bytes needed)")
+        return workspace, _ptr(workspace)
+
+    def close(self):
+        if getattr(self, "_op", None):
+            lib.nnrcu_op_destroy(self._op)
+            self._op = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def conv_desc(x_shape, w_shape, strides, pads, dilations, group, in_layout, out_layout, post, post_a, post_b,
+              requant) -> ConvDesc:
+    n, c, h, w = x_shape
+    oc, _, kh, kw = w_shape
+    pads = list(pads) if pads is not None else [0, 0, 0, 0]
+    return ConvDesc(n=n, c=c, h=h, w=w, oc=oc, kh=kh, kw=kw, group=group,
+                    stride_h=strides[0], stride_w=strides[1],
+                    pad_top=pads[0], pad_left=pads[1], pad_bottom=pads[2], pad_right=pads[3],
+                    dil_h=dilations[0], dil_w=dilations[1],
+                    in_layout=_LAYOUTS[in_layout], out_layout=_LAYOUTS[out_layout],
+                    post_op=_POSTS[post] if not isinstance(post, int) else post,
+                    post_a=post_a, post_b=post_b, requant=requant)
+
+
+def conv_out_hw(h, w, kh, kw, strides, pads, dilations):
+    oh = (h + pads[0] + pads[2] - (dilations[0] * (kh - 1) + 1)) // strides[0] + 1
+    ow = (w + pads[1] + pads[3] - (dilations[1] * (kw - 1) + 1)) // strides[1] + 1
+    return oh, ow
+
+
+class QLinearConv(Operator):
+    """ONNX QLinearConv (u8 activations, s8 weights, u8 output).
+
+    x_shape is the logical NCHW shape [n, c, h, w]; in_layout / out_layout
+    give the physical layout (nnr's memory_layout_t NCHW or NHWC).
+    fused_relu mirrors nnr's post_fn being set by fuse_post_ops, which
+    raises the lower clamp to y_zp (QLinearConv.cpp:419).
+    """
+    op_type = "QLinearConv"
+
+    def __init__(self, x_shape: Sequence[int], w: np.ndarray, w_scale, w_zp, bias, x_scale: float, x_zp: int,
+                 y_scale: float, y_zp: int, strides=(1, 1), pads=(0, 0, 0, 0), dilations=(1, 1), group: int = 1,
+                 in_layout="NCHW", out_layout="NCHW", fused_relu: bool = False, requant: int = RQ_AUTO):
+        super().__init__()
+        w = np.ascontiguousarray(w, dtype=np.int8)
+        self.x_shape = tuple(int(v) for v in x_shape)
+        self.w_shape = w.shape
+        self.strides, self.pads, self.dilations = tuple(strides), tuple(pads), tuple(dilations)
+        self.in_layout, self.out_layout = in_layout, out_layout
+        self.desc = conv_desc(self.x_shape, w.shape, strides, pads, dilations, group, in_layout, out_layout,
+                              1 if fused_relu else 0, 0.0, 0.0, requant)
+        ws_arr, ws_p = _host(np.atleast_1d(w_scale), np.float32)
+        zp_arr, zp_p = _host(None if w_zp is None else np.atleast_1d(w_zp), np.int8)
+        b_arr, b_p = _host(bias, np.int32)
+        call("nnrcu_qlinearconv_create", C.byref(self.desc), w.ctypes.data_as(C.c_void_p), ws_p, ws_arr.size,
+             zp_p, 0 if zp_arr is None else zp_arr.size, b_p, float(x_scale), int(x_zp), float(y_scale), int(y_zp),
+             C.byref(self._op))
+        n, c, h, wd = self.x_shape
+        oh, ow = conv_out_hw(h, wd, w.shape[2], w.shape[3], self.strides, self.pads, self.dilations)
+        self.y_shape = (n, w.shape[0], oh, ow) if out_layout == "NCHW" else (n, oh, ow, w.shape[0])
+
+    def exec(self, x: torch.Tensor, y: Optional[torch.Tensor] = None, workspace=None, stream=None) -> torch.Tensor:
+        if y is None:
+            y = torch.empty(self.y_shape, dtype=torch.uint8, device=x.device)
+        ws, ws_p = self._workspace(workspace, x.device)
+        call("nnrcu_qlinearconv_run", self._op, _ptr(x), _ptr(y), ws_p, C.c_void_p(_stream(stream)))
+        return y
+
+
+class QLinearMatMul(Operator):
+    """ONNX QLinearMatMul with a constant 2-D B [k, n] (u8 A, s8 B, u8 Y).
+    A's leading dims are folded into m (rows)."""
+    op_type = "QLinearMatMul"
+
+    def __init__(self, m: int, b: np.ndarray, a_scale, a_zp, b_scale, b_zp, y_scale, y_zp):
+        super().__init__()
+        b = np.ascontiguousarray(b, dtype=np.int8)
+        k, n = b.shape
+        self.m, self.k, self.n = int(m), int(k), int(n)
+        call("nnrcu_qlinearmatmul_create", self.m, self.k, self.n, float(a_scale), int(a_zp),
+             b.ctypes.data_as(C.c_void_p), float(b_scale), int(b_zp), float(y_scale), int(y_zp), C.byref(self._op))
+
+    def exec(self, a: torch.Tensor, y: Optional[torch.Tensor] = None, workspace=None, stream=None) -> torch.Tensor:
+        if y is None:
+            y = torch.empty((self.m, self.n), dtype=torch.uint8, device=a.device)
+        ws, ws_p = self._workspace(workspace, a.device)
+        call("nnrcu_qlinearmatmul_run", self._op, _ptr(a), _ptr(y), ws_p, C.c_void_p(_stream(stream)))
+        return y
+
+
+class Conv(Operator):
+    """ONNX Conv, fp32 (Conv+BN already folded by nnr's fuse_conv_bn), with
+    the fused post-op (post in Relu/Clip/HardSwish/Sigmoid/LeakyRelu/Tanh)."""
+    op_type = "Conv"
+
+    def __init__(self, x_shape, w: np.ndarray, bias=None, strides=(1, 1), pads=(0, 0, 0, 0), dilations=(1, 1),
+                 group: int = 1, in_layout="NCHW", out_layout="NCHW", post=None, post_a=0.0, post_b=0.0):
+        super().__init__()
+        w = np.ascontiguousarray(w, dtype=np.float32)
+        self.x_shape = tuple(int(v) for v in x_shape)
+        self.desc = conv_desc(self.x_shape, w.shape, strides, pads, dilations, group, in_layout, out_layout, post,
+                              post_a, post_b, 0)
+        b_arr, b_p = _host(bias, np.float32)
+        call("nnrcu_conv_f32_create", C.byref(self.desc), w.ctypes.data_as(C.c_void_p), b_p, C.byref(self._op))
+        n, c, h, wd = self.x_shape
+        oh, ow = conv_out_hw(h, wd, w.shape[2], w.shape[3], tuple(strides), tuple(pads), tuple(dilations))
+        self.y_shape = (n, w.shape[0], oh, ow) if out_layout == "NCHW" else (n, oh, ow, w.shape[0])
+
+    def exec(self, x, y=None, residual=None, workspace=None, stream=None):
+        if y is None:
+            y = torch.empty(self.y_shape, dtype=torch.float32, device=x.device)
+        ws, ws_p = self._workspace(workspace, x.device)
+        call("nnrcu_conv_f32_run", self._op, _ptr(x), _ptr(y), _ptr(residual), ws_p, C.c_void_p(_stream(stream)))
+        return y
+
+
+class Gemm(Operator):
+    """ONNX Gemm with a constant B: Y = post(alpha*op(A)op(B) + beta*C)."""
+    op_type = "Gemm"
+
+    def __init__(self, m, b: np.ndarray, c=None, alpha=1.0, beta=1.0, trans_a=0, trans_b=0, post=None, post_a=0.0,
+                 post_b=0.0):
+        super().__init__()
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        n, k = (b.shape[0], b.shape[1]) if trans_b else (b.shape[1], b.shape[0])
+        self.m, self.n, self.k = int(m), int(n), int(k)
+        c_arr, c_p = _host(c, np.float32)
+        c_rows = 0
+        if c_arr is not None:
+            c_rows = 1 if c_arr.size == n else (self.m if c_arr.size == self.m * n else -1)
+            if c_rows < 0:
+                raise ValueError("Gemm C must be [n] or [m, n]")
+        call("nnrcu_gemm_f32_create", self.m, self.n, self.k, int(trans_a), int(trans_b), float(alpha), float(beta),
+             b.ctypes.data_as(C.c_void_p), c_p, c_rows, _POSTS[post] if not isinstance(post, int) else post,
+             float(post_a), float(post_b), C.byref(self._op))
+
+    def exec(self, a, y=None, workspace=None, stream=None):
+        if y is None:
+            y = torch.empty((self.m, self.n), dtype=torch.float32, device=a.device)
+        ws, ws_p = self._workspace(workspace, a.device)
+        call("nnrcu_gemm_f32_run", self._op, _ptr(a), _ptr(y), ws_p, C.c_void_p(_stream(stream)))
+        return y
+
+
+class MatMul(Gemm):
+    """ONNX MatMul with a constant 2-D B [k, n]: leading dims of A fold into m
+    (MatMul.cpp:156-172)."""
+    op_type = "MatMul"
+
+    def __init__(self, m, b: np.ndarray, post=None, post_a=0.0, post_b=0.0):
+        super().__init__(m, b, None, 1.0, 0.0, 0, 0, post, post_a, post_b)

@@ -1,0 +1,161 @@
+"""Parity of the device QLinearConv / QLinearMatMul with the CPU oracle.
+
+Integer outputs must be bit-exact (nnr's tensor_equal compares integer
+tensors exactly, src/nnr.cpp:503-606). Every call goes through the C ABI
+(libnnrcu.so) via nnr_b200.ops.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from nnr_b200 import workloads as W
+
+pytestmark = pytest.mark.gpu
+
+
+def _to_nhwc(x):
+    return np.ascontiguousarray(x.transpose(0, 2, 3, 1))
+
+
+def run_qconv(dev, case, formula=O.R1, in_layout="NCHW", out_layout="NCHW", fused_relu=False, requant=None):
+    from nnr_b200 import ops
+    from nnr_b200._lib import RQ_AUTO
+    x_dev_np = case.x if in_layout == "NCHW" else _to_nhwc(case.x)
+    op = ops.QLinearConv(case.x.shape, case.w, case.w_scale, case.w_zp, case.bias, case.x_scale, case.x_zp,
+                         case.y_scale, case.y_zp, strides=case.strides, pads=case.pads, dilations=case.dilations,
+                         in_layout=in_layout, out_layout=out_layout, fused_relu=fused_relu,
+                         requant=formula if requant is None else requant)
+    x = torch.from_numpy(x_dev_np).to(dev)
+    y = op.exec(x)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    return y.cpu().numpy(), op
+
+
+def oracle_qconv(case, formula, out_layout="NCHW", fused_relu=False):
+    return O.qlinearconv(case.x, case.w, case.w_scale, case.bias, case.x_scale, case.x_zp, case.y_scale, case.y_zp,
+                         strides=case.strides, pads=case.pads, dilations=case.dilations, formula=formula,
+                         has_post=fused_relu, out_layout=out_layout)
+
+
+def test_config2_bit_exact(cuda_dev):
+    """BASELINE config 2 at full size; nnr dispatches exec_direct_int8 (R1)."""
+    case = W.config2_qlinearconv()
+    y, op = run_qconv(cuda_dev, case, requant=0)
+    ref = oracle_qconv(case, O.R1)
+    assert np.array_equal(y, ref), f"{(y != ref).sum()} mismatches"
+    assert op.num_ops() == 7_398_752_256
+
+
+def test_config2_nhwc_r2(cuda_dev):
+    """Same layer inside an NHWC chain: nnr's packed NR48 path (R2)."""
+    case = W.config2_qlinearconv(n=4)
+    y, _ = run_qconv(cuda_dev, case, in_layout="NHWC", out_layout="NHWC", requant=0)
+    ref = oracle_qconv(case, O.R2, out_layout="NHWC")
+    assert np.array_equal(y, ref)
+
+
+SHAPES = [
+    # n, c, h, w, oc, kh, kw, strides, pads, dilations
+    (2, 64, 13, 11, 96, 3, 3, (1, 1), (1, 1, 1, 1), (1, 1)),
+    (3, 128, 28, 28, 128, 3, 3, (2, 2), (1, 1, 1, 1), (1, 1)),
+    (2, 256, 14, 14, 64, 1, 1, (1, 1), (0, 0, 0, 0), (1, 1)),   # 1x1 -> TMA A path when NHWC
+    (2, 64, 28, 28, 256, 1, 1, (2, 2), (0, 0, 0, 0), (1, 1)),   # 1x1 stride 2 (downsample)
+    (1, 5, 9, 7, 17, 3, 3, (1, 1), (2, 0, 1, 1), (1, 1)),       # ragged channels, asymmetric pads
+    (2, 32, 16, 16, 48, 3, 3, (1, 1), (2, 2, 2, 2), (2, 2)),    # dilation 2
+    (1, 512, 7, 7, 512, 3, 3, (1, 1), (1, 1, 1, 1), (1, 1)),    # ResNet stage 4 3x3
+    (1, 16, 5, 5, 256, 5, 5, (1, 1), (0, 0, 0, 0), (1, 1)),     # single output pixel
+]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("formula", [O.R1, O.R2, O.R3])
+@pytest.mark.parametrize("layouts", [("NCHW", "NCHW"), ("NHWC", "NHWC")])
+def test_random_shapes(cuda_dev, shape, formula, layouts):
+    n, c, h, w, oc, kh, kw, s, p, d = shape
+    rng = np.random.default_rng(hash((shape, formula)) & 0xffff)
+    case = W.random_qconv(rng, n, c, h, w, oc, kh, kw, s, p, d)
+    y, _ = run_qconv(cuda_dev, case, formula, layouts[0], layouts[1])
+    ref = oracle_qconv(case, formula, layouts[1])
+    assert np.array_equal(y, ref), f"{(y != ref).sum()} / {y.size} mismatches"
+
+
+@pytest.mark.parametrize("formula", [O.R1, O.R2, O.R3])
+def test_fused_relu_and_zero_points(cuda_dev, formula):
+    """A fused Relu raises the lower clamp to y_zp for R1/R3; R2 ignores it
+    (QLinearConv_reshape.h:326). x_zp = 0 (post-Relu activations) and odd zps."""
+    rng = np.random.default_rng(7)
+    for xz, yz in [(0, 0), (0, 37), (200, 3)]:
+        case = W.random_qconv(rng, 2, 64, 12, 12, 64, 3, 3, (1, 1), (1, 1, 1, 1), x_zp=xz, y_zp=yz)
+        y, _ = run_qconv(cuda_dev, case, formula, fused_relu=True)
+        ref = oracle_qconv(case, formula, fused_relu=True)
+        assert np.array_equal(y, ref)
+
+
+def test_stem_auto_r3(cuda_dev):
+    """ResNet stem 7x7/2 on a 3-channel NCHW input: nnr's first-layer path (R3)."""
+    rng = np.random.default_rng(3)
+    case = W.random_qconv(rng, 2, 3, 64, 64, 64, 7, 7, (2, 2), (3, 3, 3, 3), x_zp=128, y_zp=0)
+    y, _ = run_qconv(cuda_dev, case, in_layout="NCHW", out_layout="NHWC", requant=0)
+    ref = oracle_qconv(case, O.R3, out_layout="NHWC")
+    assert np.array_equal(y, ref)
+
+
+def test_no_bias_per_tensor_scale(cuda_dev):
+    rng = np.random.default_rng(11)
+    case = W.random_qconv(rng, 1, 32, 10, 10, 32, 3, 3, (1, 1), (1, 1, 1, 1), per_channel=False, bias=False)
+    for f in (O.R1, O.R2, O.R3):
+        y, _ = run_qconv(cuda_dev, case, f)
+        assert np.array_equal(y, oracle_qconv(case, f))
+
+
+def test_repeat_and_graph_capture(cuda_dev):
+    """Same op launched repeatedly and replayed from a captured CUDA graph."""
+    from nnr_b200 import ops
+    rng = np.random.default_rng(5)
+    case = W.random_qconv(rng, 4, 64, 14, 14, 128, 3, 3, (1, 1), (1, 1, 1, 1))
+    op = ops.QLinearConv(case.x.shape, case.w, case.w_scale, case.w_zp, case.bias, case.x_scale, case.x_zp,
+                         case.y_scale, case.y_zp, pads=case.pads, requant=O.R1)
+    x = torch.from_numpy(case.x).to(cuda_dev)
+    y = torch.empty(op.y_shape, dtype=torch.uint8, device=cuda_dev)
+    ws = torch.empty(max(op.workspace_size(), 1), dtype=torch.uint8, device=cuda_dev)
+    s = torch.cuda.Stream()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        op.exec(x, y, ws, stream=s)
+    for _ in range(3):
+        y.zero_()
+        g.replay()
+    torch.cuda.synchronize()
+    assert np.array_equal(y.cpu().numpy(), oracle_qconv(case, O.R1))
+
+
+# ------------------------------------------------------------------ QLinearMatMul
+
+def run_qmm(dev, a, b, a_scale, a_zp, b_scale, b_zp, y_scale, y_zp):
+    from nnr_b200 import ops
+    op = ops.QLinearMatMul(a.shape[0], b, a_scale, a_zp, b_scale, b_zp, y_scale, y_zp)
+    y = op.exec(torch.from_numpy(a).to(dev))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    return y.cpu().numpy()
+
+
+def test_config3_qlinearmatmul_bit_exact(cuda_dev):
+    c = W.config3_matmul()
+    y = run_qmm(cuda_dev, c.a_u8, c.b_s8, c.a_scale, c.a_zp, c.b_scale, c.b_zp, c.y_scale, c.y_zp)
+    ref = O.qlinearmatmul(c.a_u8, c.b_s8, c.a_scale, c.a_zp, c.b_scale, c.b_zp, c.y_scale, c.y_zp)
+    assert np.array_equal(y, ref), f"{(y != ref).sum()} mismatches"
+
+
+@pytest.mark.parametrize("m,k,n,b_zp", [(32, 2048, 1000, 0), (200, 100, 70, 0), (129, 256, 300, -3),
+                                        (1, 768, 64, 5), (257, 48, 33, 0)])
+def test_qlinearmatmul_shapes(cuda_dev, m, k, n, b_zp):
+    rng = np.random.default_rng(m * 7 + k)
+    a = rng.integers(0, 256, size=(m, k)).astype(np.uint8)
+    b = rng.integers(-127, 128, size=(k, n)).astype(np.int8)
+    ys = 0.03 * 0.004 * 30.0 * np.sqrt(k)
+    y = run_qmm(cuda_dev, a, b, 0.03, 117, 0.004, b_zp, ys, 100)
+    ref = O.qlinearmatmul(a, b, 0.03, 117, 0.004, b_zp, ys, 100)
+    assert np.array_equal(y, ref)
