@@ -131,6 +131,26 @@ int nnrcu_qlinearmatmul_create(int m, int k, int n, float a_scale, uint8_t a_zp,
                                float b_scale, int8_t b_zp, float y_scale, uint8_t y_zp, nnrcu_op** op);
 int nnrcu_qlinearmatmul_run(nnrcu_op* op, const uint8_t* a, uint8_t* y, void* workspace, void* stream);
 
+/* QLinearMatMul that allocates no device memory. No counterpart in the
+ * reference: nnr runs on the CPU and has no device allocations to avoid.
+ * For callers that cannot call cudaMalloc when they run an operator (device
+ * memory reserved up front by another allocator, a policy of no allocation
+ * after start-up). a u8 [m,k], b s8 [k,n] (raw ONNX layout) and y u8 [m,n]
+ * are device pointers the caller owns; k must be a multiple of 16 and a
+ * 16-byte aligned. Everything derived from b (transposed tiles, zero-point
+ * sums) goes to one static device array of NNRCU_NOALLOC_SCRATCH_BYTES per
+ * device, held until the process exits; calls needing more
+ * (round_up(n,256)*round_up(k,128) + 4n (+ 4m when b_zp != 0) bytes, each
+ * rounded to 256) fail with NNRCU_ERR_INVALID. The first call on a device
+ * looks up the array's device address, so make that first call before any
+ * stream capture. Calls share the array: calls that overlap on the GPU race
+ * and must be serialised by the caller. Same requant (R4) and results as
+ * nnrcu_qlinearmatmul_create/_run. */
+#define NNRCU_NOALLOC_SCRATCH_BYTES (8u << 20)
+int nnrcu_qlinearmatmul_noalloc(const uint8_t* a, const int8_t* b, uint8_t* y, int m, int k, int n, float a_scale,
+                                uint8_t a_zp, float b_scale, int8_t b_zp, float y_scale, uint8_t y_zp,
+                                void* stream);
+
 /* ---------------------------------------------------------------- fp32 Conv (Conv+BN folded + post-op)
  * Replaces Conv_operator::reshape/exec<float> (backend/cpu/Conv_reshape.h:17-380,
  * backend/cpu/Conv_exec.h:1163-1192). Dense convs run on the tensor cores as

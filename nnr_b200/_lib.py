@@ -67,6 +67,7 @@ SIGNATURES = {
     "nnrcu_qlinearconv_run": [P, P, P, P, P],
     "nnrcu_qlinearmatmul_create": [I, I, I, F, U8, P, F, I8, F, U8, PP],
     "nnrcu_qlinearmatmul_run": [P, P, P, P, P],
+    "nnrcu_qlinearmatmul_noalloc": [P, P, P, I, I, I, F, U8, F, I8, F, U8, P],
     "nnrcu_conv_f32_create": [C.POINTER(ConvDesc), P, P, PP],
     "nnrcu_conv_f32_run": [P, P, P, P, P, P],
     "nnrcu_gemm_f32_create": [I, I, I, I, I, F, F, P, P, I, I, F, F, PP],
