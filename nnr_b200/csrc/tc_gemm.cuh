@@ -7,11 +7,13 @@
 //   * matmul: M = rows of A, N = columns of B, K = the reduction dim.
 //
 // One CTA computes a 128 x BN tile of D:
-//   warps 0-3  A producers in gather mode (cp.async from NHWC activations,
-//              padding pixels filled with the input zero point), then the
-//              epilogue (TMEM -> registers -> requant / bias / post-op -> HBM)
-//   warp 4     TMA producer (B tiles always, A tiles in TMA mode)
-//   warp 5     TMEM allocator and single-thread tcgen05.mma issuer
+//   warps 0-3  epilogue (TMEM -> registers -> requant / bias / post-op -> HBM)
+//   warps 4-7  A producers in gather mode (cp.async from NHWC activations,
+//              padding pixels filled with the input zero point)
+//   warp 8     TMA producer (B tiles always, A tiles in TMA mode)
+//   warp 9     TMEM allocator and single-thread tcgen05.mma issuer
+// The kernel is persistent: one CTA per SM loops over tiles, with the
+// accumulator double-buffered in TMEM.
 // Shared memory holds STAGES stages of {A planes, B planes}, each plane a
 // 128-byte-wide K slab in the 128-byte swizzled K-major layout that both TMA
 // (SWIZZLE_128B) and the UMMA descriptors understand.
@@ -36,7 +38,7 @@ enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_AC
 
 constexpr int BM = 128;       // rows per tile (TMEM lanes)
 constexpr int BKB = 128;      // K bytes per stage per plane (one swizzle row)
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 320;  // 4 epilogue + 4 gather + TMA + MMA warps
 
 // Geometry of the implicit im2col gather (A_GATHER). All sizes in bytes where noted.
 struct GatherGeom {
@@ -82,8 +84,8 @@ struct TileCfg {
   static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + B_BYTES);
   static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;  // power of two >= 32
-  static constexpr int PARAM_BYTES = 6 * BN * 4;
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (power of two)
+  static constexpr int PARAM_BYTES = 4 /*epilogue warps*/ * 5 * BN * 4;
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/ + PARAM_BYTES;
   static_assert(STAGES >= 2, "need at least two pipeline stages");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
@@ -147,10 +149,21 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t colc, int32_
   }
 }
 
+// Persistent warp-specialised kernel. One CTA per SM walks the tiles
+// blockIdx.x, blockIdx.x + gridDim.x, ...; tile t covers rows
+// [(t / n_tiles) * 128, +128) and columns [(t % n_tiles) * BN, +BN).
+//   warps 0-3  epilogue: TMEM -> registers -> requant / bias / post-op -> HBM
+//   warps 4-7  A producers in gather mode (implicit im2col with cp.async)
+//   warp 8     TMA producer (B always, A in TMA mode)
+//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer
+// The smem stage ring runs continuously across tiles, and the accumulator is
+// double-buffered in TMEM (2 x BN columns), so the epilogue of tile i overlaps
+// the loads and MMAs of tile i + 1.
 template <int BN, int NPLANE, int AMODE, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
-               const __grid_constant__ CUtensorMap tmB, int b_plane_rows, GatherGeom g, EpiParams e, int num_kb) {
+               const __grid_constant__ CUtensorMap tmB, int b_plane_rows, GatherGeom g, EpiParams e, int num_kb,
+               int m_tiles, int n_tiles) {
   using Cfg = TileCfg<BN, NPLANE>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int A_BYTES = Cfg::A_BYTES;
@@ -162,19 +175,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   uint8_t* sB = sA + STAGES * NPLANE * A_BYTES;              // [STAGES][NPLANE][B_BYTES]
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * NPLANE * B_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* accum_bar = empty_bar + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(accum_bar + 1);
-  uint8_t* sparam = reinterpret_cast<uint8_t*>(full_bar) + 256;
+  uint64_t* tfull_bar = empty_bar + STAGES;                  // [2] accumulator ready
+  uint64_t* tempty_bar = tfull_bar + 2;                      // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = m_tiles * n_tiles;
+  // per-column constants, one private copy per epilogue warp (no cross-warp sync)
+  uint8_t* sparam = reinterpret_cast<uint8_t*>(full_bar) + 256 + (warp & 3) * (5 * BN * 4);
   int32_t* s_colc = reinterpret_cast<int32_t*>(sparam);
   int32_t* s_bias_i = s_colc + BN;
   float* s_cs = reinterpret_cast<float*>(s_bias_i + BN);
   float* s_bias_f = s_cs + BN;
   float* s_os = s_bias_f + BN;
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM;
-  const int n0 = blockIdx.y * BN;
 
   if (threadIdx.x == 0) {
     const uint32_t full_count = (AMODE == A_GATHER) ? (128u + 1u) : 1u;
@@ -182,187 +197,224 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       ptx::mbar_init(&full_bar[s], full_count);
       ptx::mbar_init(&empty_bar[s], 1);
     }
-    ptx::mbar_init(accum_bar, 1);
+    for (int a = 0; a < 2; ++a) {
+      ptx::mbar_init(&tfull_bar[a], 1);
+      ptx::mbar_init(&tempty_bar[a], 4);
+    }
+    *abort_flag = 0;
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == 8 && lane == 0) {
     ptx::tma_prefetch_desc(&tmB);
     if (AMODE == A_TMA) {
       ptx::tma_prefetch_desc(&tmA0);
       if (NPLANE == 2) ptx::tma_prefetch_desc(&tmA1);
     }
   }
-  if (warp == 5) ptx::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-  if (threadIdx.x < 128) {
-    for (int i = threadIdx.x; i < BN; i += 128) {
-      const int n = n0 + i;
-      const bool ok = n < e.N;
-      s_colc[i] = (ok && e.colcorr) ? e.colcorr[n] : 0;
-      s_bias_i[i] = (ok && e.bias_i) ? e.bias_i[n] : 0;
-      s_cs[i] = (ok && e.cs) ? e.cs[n] : 0.0f;
-      s_bias_f[i] = (ok && e.bias_f) ? e.bias_f[n] : ((ok && e.bias) ? e.bias[n] : 0.0f);
-      s_os[i] = (ok && e.os) ? e.os[n] : 0.0f;
-    }
-  }
+  if (warp == 9) ptx::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  bool aborted = false;
+  auto fail = [&](int code) {
+    record_status(e.status, code);
+    *abort_flag = 1;
+  };
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       constexpr uint32_t tx = (AMODE == A_TMA ? NPLANE * A_BYTES : 0) + NPLANE * B_BYTES;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-        if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1u)) { record_status(e.status, ST_TIMEOUT_EMPTY); aborted = true; break; }
-        ptx::mbar_arrive_expect_tx(&full_bar[s], tx);
-        uint8_t* a_st = sA + (size_t)s * NPLANE * A_BYTES;
-        uint8_t* b_st = sB + (size_t)s * NPLANE * B_BYTES;
-        const int kx = kb * BKB / (NPLANE == 2 ? 2 : 1);  // element coordinate along K
-        for (int p = 0; p < NPLANE; ++p)
-          ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
-        if (AMODE == A_TMA) {
-          ptx::tma_load_2d(a_st, &tmA0, &full_bar[s], kx, m0);
-          if (NPLANE == 2) ptx::tma_load_2d(a_st + A_BYTES, &tmA1, &full_bar[s], kx, m0);
+      bool aborted = false;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag)) { fail(ST_TIMEOUT_EMPTY); aborted = true; break; }
+          ptx::mbar_arrive_expect_tx(&full_bar[s], tx);
+          uint8_t* a_st = sA + (size_t)s * NPLANE * A_BYTES;
+          uint8_t* b_st = sB + (size_t)s * NPLANE * B_BYTES;
+          const int kx = kb * BKB / (NPLANE == 2 ? 2 : 1);  // element coordinate along K
+          for (int p = 0; p < NPLANE; ++p)
+            ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
+          if (AMODE == A_TMA) {
+            ptx::tma_load_2d(a_st, &tmA0, &full_bar[s], kx, m0);
+            if (NPLANE == 2) ptx::tma_load_2d(a_st + A_BYTES, &tmA1, &full_bar[s], kx, m0);
+          }
         }
       }
       if (aborted) ptx::settle_ns(200000);  // let copies already in flight land before the CTA exits
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = (NPLANE == 1) ? ptx::umma_idesc(2, 0, 1, BM, BN) : ptx::umma_idesc(1, 1, 1, BM, BN);
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-        if (!ptx::mbar_wait(&full_bar[s], ph)) { record_status(e.status, ST_TIMEOUT_FULL); aborted = true; break; }
+      bool aborted = false;
+      int it = 0, lt = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x, ++lt) {
+        const int acc = lt & 1;
+        const uint32_t use_ph = (uint32_t)(lt >> 1) & 1u;
+        if (!ptx::mbar_wait(&tempty_bar[acc], use_ph ^ 1u, abort_flag)) { fail(ST_TIMEOUT_ACCUM); aborted = true; break; }
         ptx::tc_fence_after();
-        ptx::fence_proxy_async_smem();
-        const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * NPLANE * A_BYTES);
-        const uint32_t b_addr = ptx::smem_u32(sB + (size_t)s * NPLANE * B_BYTES);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          if (!ptx::mbar_wait(&full_bar[s], ph, abort_flag)) { fail(ST_TIMEOUT_FULL); aborted = true; break; }
+          ptx::tc_fence_after();
+          ptx::fence_proxy_async_smem();
+          const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * NPLANE * A_BYTES);
+          const uint32_t b_addr = ptx::smem_u32(sB + (size_t)s * NPLANE * B_BYTES);
 #pragma unroll
-        for (int k = 0; k < BKB / 32; ++k) {
-          const uint32_t koff = k * 32;
-          if constexpr (NPLANE == 1) {
-            ptx::mma_i8(tmem_base, ptx::umma_desc_sw128(a_addr + koff), ptx::umma_desc_sw128(b_addr + koff), idesc,
-                        (kb | k) != 0);
-          } else {
-            // hi*hi, hi*lo, lo*hi
-            ptx::mma_f16(tmem_base, ptx::umma_desc_sw128(a_addr + koff), ptx::umma_desc_sw128(b_addr + koff), idesc,
-                         (kb | k) != 0);
-            ptx::mma_f16(tmem_base, ptx::umma_desc_sw128(a_addr + koff),
-                         ptx::umma_desc_sw128(b_addr + B_BYTES + koff), idesc, 1u);
-            ptx::mma_f16(tmem_base, ptx::umma_desc_sw128(a_addr + A_BYTES + koff),
-                         ptx::umma_desc_sw128(b_addr + koff), idesc, 1u);
+          for (int k = 0; k < BKB / 32; ++k) {
+            const uint32_t koff = k * 32;
+            if constexpr (NPLANE == 1) {
+              ptx::mma_i8(d_tmem, ptx::umma_desc_sw128(a_addr + koff), ptx::umma_desc_sw128(b_addr + koff), idesc,
+                          (kb | k) != 0);
+            } else {
+              // hi*hi, hi*lo, lo*hi
+              ptx::mma_f16(d_tmem, ptx::umma_desc_sw128(a_addr + koff), ptx::umma_desc_sw128(b_addr + koff), idesc,
+                           (kb | k) != 0);
+              ptx::mma_f16(d_tmem, ptx::umma_desc_sw128(a_addr + koff),
+                           ptx::umma_desc_sw128(b_addr + B_BYTES + koff), idesc, 1u);
+              ptx::mma_f16(d_tmem, ptx::umma_desc_sw128(a_addr + A_BYTES + koff),
+                           ptx::umma_desc_sw128(b_addr + koff), idesc, 1u);
+            }
           }
+          ptx::mma_commit(&empty_bar[s]);
         }
-        ptx::mma_commit(&empty_bar[s]);
+        if (!aborted) ptx::mma_commit(&tfull_bar[acc]);  // fires when this tile's MMAs have completed
       }
-      ptx::mma_commit(accum_bar);  // fires when every MMA above has completed (also after an abort)
+      if (aborted) ptx::settle_ns(200000);  // MMAs already issued finish before TMEM is freed
     }
-  } else {
-    // ------------------------------------------------------------ warps 0-3
-    const int t = threadIdx.x;  // 0..127
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ gather producers (warps 4-7)
     if constexpr (AMODE == A_GATHER) {
-      // Thread t fills chunk (t & 7) of rows (t >> 3) + 16*i, i = 0..7: eight
-      // consecutive threads cover one 128-byte row, so each warp instruction
-      // reads four full rows.
-      const int chunk = t & 7;
-      int r_n[8], r_ih[8], r_iw[8];
+      // Thread t owns tile row t (one output pixel) and copies its whole
+      // 128-byte K slab per stage: one address per filter tap touched, then
+      // consecutive 16-byte cp.async chunks into the swizzled row.
+      const int r = threadIdx.x - 128;
+      uint8_t* const row_dst0 = sA + (r >> 3) * 1024 + (r & 7) * 128;
+      const int rsw = r & 7;
       const int ohw = g.OH * g.OW;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int r = (t >> 3) + 16 * i;
-        const int m = m0 + r;
-        if (m < e.M) {
+      constexpr int LAG = STAGES - 1;  // keep every free stage in flight
+      bool aborted = false;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
+        const int m = (tile / n_tiles) * BM + r;
+        const bool rvalid = m < e.M;
+        int r_n = 0, r_ih = 0, r_iw = 0;
+        if (rvalid) {
           const int img = m / ohw;
           const int p = m - img * ohw;
           const int oh = p / g.OW;
           const int ow = p - oh * g.OW;
-          r_n[i] = img;
-          r_ih[i] = oh * g.sh - g.ph;
-          r_iw[i] = ow * g.sw - g.pw;
-        } else {
-          r_n[i] = -1; r_ih[i] = 0; r_iw[i] = 0;
+          r_n = img;
+          r_ih = oh * g.sh - g.ph;
+          r_iw = ow * g.sw - g.pw;
+        }
+        const size_t img_base = (size_t)r_n * g.H;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
+          const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag));
+          if (!ok) { fail(ST_TIMEOUT_EMPTY); aborted = true; break; }
+          uint8_t* const row_dst = row_dst0 + (size_t)s * NPLANE * A_BYTES;
+          int kbyte = kb * BKB;
+          int tap = kbyte / g.cbytes;
+          int cc = kbyte - tap * g.cbytes;
+          int j = 0;
+          while (j < 8) {
+            // chunks [j, j + run) lie in one filter tap
+            const int run = min(8 - j, (g.cbytes - cc) >> 4);
+            const bool kvalid = kbyte < g.kbytes;
+            const uint8_t* src = nullptr;
+            bool inb = false;
+            if (kvalid && rvalid) {
+              const int kh = tap / g.KW;
+              const int kw = tap - kh * g.KW;
+              const int ih = r_ih + kh * g.dh;
+              const int iw = r_iw + kw * g.dw;
+              inb = (unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W;
+              if (inb) src = g.x + ((img_base + ih) * g.W + iw) * (size_t)g.cbytes + cc;
+            }
+            for (int u = 0; u < run; ++u) {
+              uint8_t* dst = row_dst + (((j + u) ^ rsw) << 4);
+              if (inb) {
+                ptx::cp_async16(dst, src + u * 16, 16);
+                if (NPLANE == 2) ptx::cp_async16(dst + A_BYTES, g.x2 + (src - g.x) + u * 16, 16);
+              } else {
+                // padding pixel (x_zp pattern), K tail or row beyond M (zeros)
+                const uint32_t wv = (kvalid && rvalid) ? g.pad_word : 0u;
+                ptx::st_shared_v4(dst, wv, wv, wv, wv);
+                if (NPLANE == 2) ptx::st_shared_v4(dst + A_BYTES, 0u, 0u, 0u, 0u);
+              }
+            }
+            j += run;
+            kbyte += run * 16;
+            cc += run * 16;
+            if (cc >= g.cbytes) { cc = 0; ++tap; }
+          }
+          ptx::cp_async_commit();
+          // Publish the stage issued LAG iterations ago: its copies are done
+          // once at most LAG groups remain in flight. LAG = STAGES - 1 cannot
+          // deadlock: refilling stage it needs stage it - STAGES consumed,
+          // which was published at iteration it - STAGES + LAG < it.
+          if (it >= LAG) {
+            ptx::cp_async_wait<LAG>();
+            ptx::fence_proxy_async_smem();
+            ptx::mbar_arrive(&full_bar[(it - LAG) % STAGES]);
+          }
         }
       }
-      constexpr int LAG = (STAGES - 1) < 2 ? (STAGES - 1) : 2;
-      for (int kb = 0; kb < num_kb && !aborted; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-        const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&empty_bar[s], ph ^ 1u));
-        if (!ok) { record_status(e.status, ST_TIMEOUT_EMPTY); aborted = true; break; }
-        uint8_t* a_st = sA + (size_t)s * NPLANE * A_BYTES;
-        const int kbyte = kb * BKB + chunk * 16;
-        const bool kvalid = kbyte < g.kbytes;
-        int tap = 0, cc = 0, kh = 0, kw = 0;
-        if (kvalid) {
-          tap = kbyte / g.cbytes;
-          cc = kbyte - tap * g.cbytes;
-          kh = tap / g.KW;
-          kw = tap - kh * g.KW;
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int r = (t >> 3) + 16 * i;
-          uint8_t* dst = a_st + (r >> 3) * 1024 + (r & 7) * 128 + ((chunk ^ (r & 7)) << 4);
-          if (!kvalid || r_n[i] < 0) {
-#pragma unroll
-            for (int p = 0; p < NPLANE; ++p) ptx::st_shared_v4(dst + p * A_BYTES, 0u, 0u, 0u, 0u);
-            continue;
-          }
-          const int ih = r_ih[i] + kh * g.dh;
-          const int iw = r_iw[i] + kw * g.dw;
-          if ((unsigned)ih < (unsigned)g.H && (unsigned)iw < (unsigned)g.W) {
-            const size_t off = (((size_t)r_n[i] * g.H + ih) * g.W + iw) * (size_t)g.cbytes + cc;
-            ptx::cp_async16(dst, g.x + off, 16);
-            if (NPLANE == 2) ptx::cp_async16(dst + A_BYTES, g.x2 + off, 16);
-          } else {
-            ptx::st_shared_v4(dst, g.pad_word, g.pad_word, g.pad_word, g.pad_word);
-            if (NPLANE == 2) ptx::st_shared_v4(dst + A_BYTES, 0u, 0u, 0u, 0u);
-          }
-        }
-        ptx::cp_async_commit();
-        // Publish the stage issued LAG iterations ago: its copies are done
-        // once at most LAG groups remain in flight.
-        if (kb >= LAG) {
-          ptx::cp_async_wait<LAG>();
-          ptx::fence_proxy_async_smem();
-          ptx::mbar_arrive(&full_bar[(kb - LAG) % STAGES]);
-        }
-      }
-      // Drain: publish the last LAG stages (or whatever was issued before an abort).
+      // Drain: publish the last LAG stages.
       ptx::cp_async_wait<0>();
       ptx::fence_proxy_async_smem();
       if (!aborted) {
-        const int first = num_kb > LAG ? num_kb - LAG : 0;
-        for (int kb = first; kb < num_kb; ++kb) ptx::mbar_arrive(&full_bar[kb % STAGES]);
+        const int first = it > LAG ? it - LAG : 0;
+        for (int q = first; q < it; ++q) ptx::mbar_arrive(&full_bar[q % STAGES]);
       }
     }
-
-    // ------------------------------------------------------------ epilogue
-    if (!aborted && !__all_sync(0xffffffffu, ptx::mbar_wait(accum_bar, 0))) {
-      record_status(e.status, ST_TIMEOUT_ACCUM);
-      aborted = true;
-    }
-    if (!aborted) {
+  } else {
+    // ------------------------------------------------------------ epilogue (warps 0-3)
+    const int row = warp * 32 + lane;  // TMEM lane == tile row
+    int lt = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
+      const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+      const int acc = lt & 1;
+      const uint32_t use_ph = (uint32_t)(lt >> 1) & 1u;
+      // per-column constants of this tile's columns (this warp's copy)
+      __syncwarp();
+      for (int i = lane; i < BN; i += 32) {
+        const int n = n0 + i;
+        const bool ok = n < e.N;
+        s_colc[i] = (ok && e.colcorr) ? e.colcorr[n] : 0;
+        s_bias_i[i] = (ok && e.bias_i) ? e.bias_i[n] : 0;
+        s_cs[i] = (ok && e.cs) ? e.cs[n] : 0.0f;
+        s_bias_f[i] = (ok && e.bias_f) ? e.bias_f[n] : ((ok && e.bias) ? e.bias[n] : 0.0f);
+        s_os[i] = (ok && e.os) ? e.os[n] : 0.0f;
+      }
+      __syncwarp();
+      if (!__all_sync(0xffffffffu, ptx::mbar_wait(&tfull_bar[acc], use_ph, abort_flag))) {
+        fail(ST_TIMEOUT_ACCUM);
+        break;
+      }
       ptx::tc_fence_after();
-      const int row = warp * 32 + lane;  // TMEM lane == tile row
       const int m = m0 + row;
       const bool mvalid = m < e.M;
       int32_t rowc = 0;
       if (EPI == EPI_R4 && e.rowcorr && mvalid) rowc = e.rowcorr[m];
       int img = 0, pix = 0;
       if (e.y_layout == 1 && mvalid) { img = m / e.ohw; pix = m - img * e.ohw; }
+      const uint32_t t_addr = tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 32) {
         uint32_t v[32];
-        ptx::tmem_ld32(tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0, v);
+        ptx::tmem_ld32(t_addr + (uint32_t)c0, v);
         if (!mvalid || n0 + c0 >= e.N) continue;
         const int nvalid = min(32, e.N - (n0 + c0));
         if constexpr (EPI == EPI_F32) {
@@ -389,14 +441,16 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
               *reinterpret_cast<float4*>(dst + j) = make_float4(o[0], o[1], o[2], o[3]);
             }
           } else {
-            for (int j = 0; j < nvalid; ++j) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j >= nvalid) break;
               const size_t idx = rowmajor ? (size_t)m * e.ldy + n0 + c0 + j
                                           : ((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix;
-              const float r = e.residual ? e.residual[idx] : 0.0f;
+              const float rr = e.residual ? e.residual[idx] : 0.0f;
               float a = __uint_as_float(v[j]) + s_bias_f[c0 + j];
-              if (e.res_mode == 1) a = fmaf(e.res_scale, r, a);
+              if (e.res_mode == 1) a = fmaf(e.res_scale, rr, a);
               a = apply_act(a, e.act, e.act_a, e.act_b);
-              if (e.res_mode == 2) a += r;
+              if (e.res_mode == 2) a += rr;
               y[idx] = a;
             }
           }
@@ -418,19 +472,27 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
               reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
               reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
             } else {
-              for (int j = 0; j < nvalid; ++j) dst[j] = (uint8_t)q[j];
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nvalid) dst[j] = (uint8_t)q[j];
             }
           } else {
-            for (int j = 0; j < nvalid; ++j) y[((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix] = (uint8_t)q[j];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < nvalid) y[((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix] = (uint8_t)q[j];
           }
         }
       }
+      // hand the accumulator back to the MMA warp
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
     }
   }
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }

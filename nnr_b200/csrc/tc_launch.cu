@@ -1,4 +1,6 @@
 // Instantiations of the tcgen05 engine and the runtime dispatch onto them.
+#include <algorithm>
+
 #include "internal.h"
 #include "tc_gemm.cuh"
 
@@ -19,8 +21,10 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
     NNRCU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     configured |= 1ull << dev;
   }
-  dim3 grid(L.m_tiles, L.n_tiles);
-  kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, L.b_plane_rows, g, e, L.num_kb);
+  const long long tiles = (long long)L.m_tiles * L.n_tiles;
+  const int grid = (int)std::min<long long>(tiles, (long long)num_sms());
+  kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, L.b_plane_rows, g, e, L.num_kb,
+                                                       L.m_tiles, L.n_tiles);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }
@@ -55,8 +59,8 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
 
 int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
   if (L.m_tiles <= 0 || L.n_tiles <= 0 || L.num_kb <= 0) return NNRCU_OK;
-  if (L.m_tiles > 0x7fffffff || L.n_tiles > 65535)
-    return set_error(NNRCU_ERR_INVALID, "grid too large (%d x %d)", L.m_tiles, L.n_tiles);
+  if ((long long)L.m_tiles * L.n_tiles > 0x7fffffffLL)
+    return set_error(NNRCU_ERR_INVALID, "too many tiles (%d x %d)", L.m_tiles, L.n_tiles);
   if (L.amode == A_GATHER && ((reinterpret_cast<uintptr_t>(g.x) & 15) || (g.x2 && (reinterpret_cast<uintptr_t>(g.x2) & 15)) ||
                               (g.cbytes & 15)))
     return set_error(NNRCU_ERR_INVALID, "gathered operand must be 16-byte aligned with a 16-byte pixel stride");
