@@ -61,6 +61,33 @@ __global__ void nchw_to_nhwc_u8_vec_kernel(const uint8_t* __restrict src, uint8_
   }
 }
 
+// NCHW u8 -> spatially padded NHWC u8 [n][hp][wp][cs]: pixel (y, x) lands at
+// (y + pt, x + pl). The border and the channel padding must already hold
+// fill (the caller memsets the buffer); 64-channel x 128-pixel tiles.
+__global__ void nchw_to_nhwc_u8_padded_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, int c, int h,
+                                              int w, int hp, int wp, int pt, int pl, int cs) {
+  __shared__ uint8_t tile[64][128 + 4];
+  const int hw = h * w;
+  const int img = blockIdx.z;
+  const int p0 = blockIdx.x * 128;
+  const int c0 = blockIdx.y * 64;
+  const uint8_t* s = src + (size_t)img * c * hw;
+  uint8_t* d = dst + (size_t)img * hp * wp * cs;
+  for (int idx = threadIdx.x; idx < 64 * 128; idx += blockDim.x) {
+    const int ch = idx >> 7, pp = idx & 127;
+    const int p = p0 + pp;
+    tile[ch][pp] = (c0 + ch < c && p < hw) ? s[(size_t)(c0 + ch) * hw + p] : 0;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 128 * 64; idx += blockDim.x) {
+    const int pp = idx >> 6, cl = idx & 63;
+    const int p = p0 + pp, ch = c0 + cl;
+    if (p >= hw || ch >= c) continue;
+    const int y = p / w, x = p - y * w;
+    d[((size_t)(y + pt) * wp + (x + pl)) * cs + ch] = tile[cl][pp];
+  }
+}
+
 __global__ void pad_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, long long pixels, int c,
                                    int cs, uint8_t fill) {
   const long long total = pixels * cs;
@@ -265,6 +292,16 @@ int launch_nchw_to_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int c, int h
   }
   dim3 grid((hw + 31) / 32, (cs + 31) / 32, n), block(32, 8);
   nchw_to_nhwc_u8_kernel<<<grid, block, 0, st>>>(src, dst, c, hw, cs, fill);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_nchw_to_nhwc_u8_padded(const uint8_t* src, uint8_t* dst, int n, int c, int h, int w, int pt, int pl,
+                                  int pb, int pr, int cs, uint8_t fill, cudaStream_t st) {
+  const int hp = h + pt + pb, wp = w + pl + pr;
+  NNRCU_CUDA(cudaMemsetAsync(dst, fill, (size_t)n * hp * wp * cs, st));
+  dim3 grid((h * w + 127) / 128, (c + 63) / 64, n);
+  nchw_to_nhwc_u8_padded_kernel<<<grid, 256, 0, st>>>(src, dst, c, h, w, hp, wp, pt, pl, cs);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

@@ -7,7 +7,7 @@
 #include <cstdint>
 #include <vector>
 
-#include "../../include/nnrcu.h"
+#include "nnrcu.h"
 
 namespace nnrcu {
 
@@ -26,7 +26,14 @@ int* status_ptr();
 
 // cuTensorMapEncodeTiled through the runtime's driver entry point.
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
-                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer);
+                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B);
+
+// cuTensorMapEncodeIm2col over an NHWC tensor [n][h][w][c] (c in elements,
+// row of c*elem bytes): boxes of 128 pixels x (128 bytes of channels), with
+// the bounding box of a conv with the given pads/kernel/dilation/stride.
+int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, int n, int h,
+                       int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw);
 
 enum OpKind : int { OP_QCONV = 1, OP_QMATMUL = 2, OP_CONV_F32 = 3, OP_GEMM_F32 = 4, OP_DWCONV_F32 = 5 };
 
@@ -49,6 +56,7 @@ struct Op {
   int oh = 0, ow = 0;
   int cs = 0;                   // device channel stride (elements) of the NHWC operand
   bool need_in_copy = false;    // input must be re-laid-out into the workspace first
+  bool pad_in = false;          // ... spatially padded with x_zp (im2col path with x_zp != 0)
   // device buffers (owned)
   void* wB = nullptr;
   int32_t* colcorr = nullptr;
@@ -95,6 +103,8 @@ int num_sms();
 // Auxiliary kernels (aux_kernels.cu).
 int launch_nchw_to_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int c, int h, int w, int cs, uint8_t fill,
                            cudaStream_t st);
+int launch_nchw_to_nhwc_u8_padded(const uint8_t* src, uint8_t* dst, int n, int c, int h, int w, int pt, int pl,
+                                  int pb, int pr, int cs, uint8_t fill, cudaStream_t st);
 int launch_pad_nhwc_u8(const uint8_t* src, uint8_t* dst, int pixels, int c, int cs, uint8_t fill, cudaStream_t st);
 int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
                            int cs, cudaStream_t st);

@@ -53,14 +53,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 // Bounded wait on the phase with the given parity. Returns false on timeout,
 // or as soon as *abort_flag (shared memory, optional) is set by another role.
+// The limit is counted in SM clock cycles (clock64 is local and cheap; the
+// global nanosecond timer is slow to read and would add latency to every
+// pipeline hand-off): NNRCU_WAIT_NS * 2 cycles is >= NNRCU_WAIT_NS ns at any
+// clock up to 2 GHz.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const long long t0 = clock64();
   for (uint32_t it = 0;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 15u) == 15u) {
       if (abort_flag && *abort_flag) return false;
-      if (globaltimer() - t0 > NNRCU_WAIT_NS) return false;
+      if (clock64() - t0 > (long long)(2 * NNRCU_WAIT_NS)) return false;
     }
   }
 }
@@ -91,9 +95,32 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+// im2col-mode load: pixelsPerColumn pixels x channelsPerPixel channels,
+// starting at input position (w, h, n) plus the filter-tap offsets.
+__device__ __forceinline__ void tma_load_im2col_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c, int w, int h,
+                                                   int n, uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c), "r"(w), "r"(h), "r"(n), "h"(off_w), "h"(off_h)
+      : "memory");
+}
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
+
+// TMA tensor store from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the source smem of every committed bulk store may be reused.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until every committed bulk store has completed.
+__device__ __forceinline__ void bulk_wait0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---------------------------------------------------------------- cp.async (16 B, zero-fill when src_bytes = 0)
 // .ca keeps the line in L1: neighbouring filter taps of an implicit-im2col

@@ -112,7 +112,23 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
                           d.pad_left == 0 && d.pad_bottom == 0 && d.pad_right == 0;
   op->need_in_copy = d.in_layout == NNRCU_LAYOUT_NCHW || d.c != op->cs;
   op->amode = (one_by_one && op->kbytes >= BKB && op->epi != EPI_R3) ? A_TMA : A_GATHER;
-  op->ws_bytes = op->need_in_copy ? (size_t)d.n * d.h * d.w * op->cs : 0;
+  // Hardware im2col (TMA) when the channel stride is whole 128-byte slabs.
+  // Its out-of-bounds fill is zero, which equals the padding value when
+  // x_zp = 0 or there is no padding; an NCHW input with x_zp != 0 is instead
+  // reordered into a spatially padded copy whose border holds x_zp. Tensors
+  // under 128 KB keep the gather path.
+  const bool has_pad = d.pad_top || d.pad_left || d.pad_bottom || d.pad_right;
+  const bool im2col_shape = op->amode == A_GATHER && op->epi != EPI_R3 && op->cs % BKB == 0 &&
+                            (size_t)d.n * d.h * d.w * op->cs >= 128 * 1024;
+  if (im2col_shape && (x_zp == 0 || !has_pad)) {
+    op->amode = A_IM2COL;
+  } else if (im2col_shape && d.in_layout == NNRCU_LAYOUT_NCHW) {
+    op->amode = A_IM2COL;
+    op->pad_in = true;
+  }
+  const size_t hp = d.h + (op->pad_in ? d.pad_top + d.pad_bottom : 0);
+  const size_t wp = d.w + (op->pad_in ? d.pad_left + d.pad_right : 0);
+  op->ws_bytes = op->need_in_copy ? (size_t)d.n * hp * wp * op->cs : 0;
 
   // Pack B = W as [npad][kpad] K-major with k = (kh, kw, ic); padded channels,
   // taps and rows are zero. wsum feeds the x_zp compensation.
@@ -173,7 +189,9 @@ int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* work
   const uint8_t* xin = x;
   if (op->need_in_copy) {
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    int rc = d.in_layout == NNRCU_LAYOUT_NCHW
+    int rc = op->pad_in ? launch_nchw_to_nhwc_u8_padded(x, ws, d.n, d.c, d.h, d.w, d.pad_top, d.pad_left,
+                                                         d.pad_bottom, d.pad_right, op->cs, (uint8_t)op->x_zp, st)
+             : d.in_layout == NNRCU_LAYOUT_NCHW
                  ? launch_nchw_to_nhwc_u8(x, ws, d.n, d.c, d.h, d.w, op->cs, (uint8_t)op->x_zp, st)
                  : launch_pad_nhwc_u8(x, ws, d.n * d.h * d.w, d.c, op->cs, (uint8_t)op->x_zp, st);
     if (rc != NNRCU_OK) return rc;
@@ -187,10 +205,20 @@ int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* work
   GatherGeom g{};
   g.x = xin;
   g.x2 = nullptr;
-  g.N = d.n; g.H = d.h; g.W = d.w;
+  // a spatially pre-padded input is convolved with zero pads
+  const int pt = op->pad_in ? 0 : d.pad_top, pl = op->pad_in ? 0 : d.pad_left;
+  const int pb = op->pad_in ? 0 : d.pad_bottom, pr = op->pad_in ? 0 : d.pad_right;
+  g.N = d.n;
+  g.H = d.h + (op->pad_in ? d.pad_top + d.pad_bottom : 0);
+  g.W = d.w + (op->pad_in ? d.pad_left + d.pad_right : 0);
   g.cbytes = op->cs;
   g.OH = op->oh; g.OW = op->ow; g.KH = d.kh; g.KW = d.kw;
-  g.sh = d.stride_h; g.sw = d.stride_w; g.ph = d.pad_top; g.pw = d.pad_left; g.dh = d.dil_h; g.dw = d.dil_w;
+  g.sh = d.stride_h; g.sw = d.stride_w; g.ph = pt; g.pw = pl; g.dh = d.dil_h; g.dw = d.dil_w;
+  if (op->amode == A_IM2COL) {
+    int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, op->cs, pt, pl, pb, pr,
+                                d.kh, d.kw, d.dil_h, d.dil_w, d.stride_h, d.stride_w);
+    if (rc != NNRCU_OK) return rc;
+  }
   g.kbytes = op->kbytes;
   g.pad_word = 0x01010101u * (uint32_t)op->x_zp;
 

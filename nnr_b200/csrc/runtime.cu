@@ -21,6 +21,7 @@ int g_num_sms[kMaxDevices] = {};
 std::mutex g_mu;
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+PFN_cuTensorMapEncodeIm2col_v12000 g_encode_im2col = nullptr;
 }  // namespace
 
 int set_error(int code, const char* fmt, ...) {
@@ -59,6 +60,11 @@ static int device_setup(int dev) {
     if (q != cudaDriverEntryPointSuccess || !fn)
       return set_error(NNRCU_ERR_CUDA, "cuTensorMapEncodeTiled entry point not found");
     g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    fn = nullptr;
+    NNRCU_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q));
+    if (q != cudaDriverEntryPointSuccess || !fn)
+      return set_error(NNRCU_ERR_CUDA, "cuTensorMapEncodeIm2col entry point not found");
+    g_encode_im2col = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(fn);
   }
   g_num_sms[dev] = sms;
   g_status_addr[dev] = static_cast<int*>(p);
@@ -83,7 +89,7 @@ int num_sms() {
 }
 
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
-                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer) {
+                   uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   int dev = 0;
   int rc = current_device(&dev);
   if (rc != NNRCU_OK) return rc;
@@ -95,11 +101,33 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
   const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
-                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(NNRCU_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) dims %llu x %llu box %u x %u", (int)r,
                      (unsigned long long)inner, (unsigned long long)outer, box_inner, box_outer);
+  return NNRCU_OK;
+}
+
+int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, int n, int h,
+                       int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NNRCU_OK) return rc;
+  const uint64_t row = (uint64_t)c * elem_bytes;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row % 128) != 0)
+    return set_error(NNRCU_ERR_INVALID, "im2col operand must be 16-byte aligned with a 128-byte multiple channel stride");
+  const cuuint64_t dims[4] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
+  const cuuint64_t strides[3] = {row, row * (uint64_t)w, row * (uint64_t)w * (uint64_t)h};
+  const int lower[2] = {-pl, -pt};
+  const int upper[2] = {pr - (kw - 1) * dw, pb - (kh - 1) * dh};
+  const cuuint32_t estr[4] = {1, (cuuint32_t)sw, (cuuint32_t)sh, 1};
+  CUresult r = g_encode_im2col(map, dtype, 4, const_cast<void*>(base), dims, strides, lower, upper,
+                               (cuuint32_t)(128 / elem_bytes), 128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(NNRCU_ERR_CUDA, "cuTensorMapEncodeIm2col failed (%d) n=%d h=%d w=%d c=%d", (int)r, n, h, w, c);
   return NNRCU_OK;
 }
 

@@ -10,7 +10,9 @@
 //   warps 0-3  epilogue (TMEM -> registers -> requant / bias / post-op -> HBM)
 //   warps 4-7  A producers in gather mode (cp.async from NHWC activations,
 //              padding pixels filled with the input zero point)
-//   warp 8     TMA producer (B tiles always, A tiles in TMA mode)
+//   warp 8     TMA producer (B tiles always; A tiles in TMA mode, i.e. plain
+//              2-D tiles, and in im2col mode, i.e. hardware implicit im2col
+//              over an NHWC tensor whose channel stride is a multiple of 128 B)
 //   warp 9     TMEM allocator and single-thread tcgen05.mma issuer
 // The kernel is persistent: one CTA per SM loops over tiles, with the
 // accumulator double-buffered in TMEM.
@@ -30,7 +32,7 @@
 
 namespace nnrcu {
 
-enum : int { A_TMA = 0, A_GATHER = 1 };
+enum : int { A_TMA = 0, A_GATHER = 1, A_IM2COL = 2 };
 enum : int { EPI_R1 = 1, EPI_R2 = 2, EPI_R3 = 3, EPI_R4 = 4, EPI_F32 = 10 };
 enum : int { ACT_NONE = 0, ACT_RELU = 1, ACT_CLIP = 2, ACT_HARDSWISH = 3, ACT_SIGMOID = 4, ACT_LEAKYRELU = 5,
              ACT_TANH = 6 };
@@ -77,18 +79,26 @@ struct EpiParams {
   int* status;             // device status word (first error wins)
 };
 
-template <int BN, int NPLANE>
+template <int BN, int NPLANE, int EPI>
 struct TileCfg {
   static constexpr int A_BYTES = BM * BKB;             // 16 KB per plane
   static constexpr int B_BYTES = BN * BKB;
   static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + B_BYTES);
-  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  // u8 epilogues stage each warp's 32 x BN output block for a TMA store
+  static constexpr int OUT_BYTES = (EPI == EPI_F32) ? 0 : 4 * 32 * BN;
+  static constexpr int OUT_SEG = BN >= 128 ? 128 : 64;  // bytes per staged row segment (= TMA box width)
+  static constexpr int STAGES_RAW = (200 * 1024 - OUT_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  // Gather producers publish a stage LAG iterations after issuing it: LAG
+  // stages of copies in flight, STAGES - 1 - LAG stages of slack for the MMA.
+  static constexpr int LAG = (STAGES - 1) / 2 > 1 ? (STAGES - 1) / 2 : 1;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (power of two)
-  static constexpr int PARAM_BYTES = 4 /*epilogue warps*/ * 5 * BN * 4;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/ + PARAM_BYTES;
+  static constexpr int PARAM_BYTES = 4 /*epilogue warps*/ * 3 * BN * 4;
+  static constexpr int SMEM_BYTES =
+      1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + 256 /*barriers*/ + PARAM_BYTES;
   static_assert(STAGES >= 2, "need at least two pipeline stages");
-  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
+  static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
 __device__ __forceinline__ void record_status(int* status, int code) {
@@ -113,35 +123,37 @@ __device__ __forceinline__ float apply_act(float v, int act, float a, float b) {
 }
 
 // Requantise one int32 accumulator to u8 with the formula EPI selects.
+// ci is the per-column int32 correction (-x_zp*sum(w), plus the int32 bias
+// for R2); f1/f2 are the per-column floats (R1/R3: cs, bias_f; R2: os).
 template <int EPI>
-__device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t colc, int32_t rowc, int32_t bias_i, float cs,
-                                               float bias_f, float os, const EpiParams& e) {
+__device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t rowc, float f1, float f2,
+                                               const EpiParams& e) {
   if constexpr (EPI == EPI_R1) {
     // f = fma(float(acc), cs, bias_f); f = rne(f * inv_y) + y_zp; min(hi) then max(qmin)
-    int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)colc);
-    float f = __fmaf_rn(__int2float_rn(acc), cs, bias_f);
+    int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci);
+    float f = __fmaf_rn(__int2float_rn(acc), f1, f2);
     f = rintf(__fmul_rn(f, e.inv_y));
     f = __fadd_rn(f, e.yzp_f);
     f = fmaxf(fminf(f, e.qmax_f), e.qmin_f);
     return (uint32_t)__float2int_rn(f);
   } else if constexpr (EPI == EPI_R2) {
     // f = float(acc + bias) * os; max(lo - y_zp) then min(hi - y_zp); rne; + y_zp; saturate
-    int32_t v = (int32_t)((uint32_t)raw + (uint32_t)colc + (uint32_t)bias_i);
-    float f = __fmul_rn(__int2float_rn(v), os);
+    int32_t v = (int32_t)((uint32_t)raw + (uint32_t)ci);
+    float f = __fmul_rn(__int2float_rn(v), f1);
     f = fminf(fmaxf(f, e.rq_lo), e.rq_hi);
     int32_t q = __float2int_rn(f) + e.yzp;
     q = q < 0 ? 0 : (q > 255 ? 255 : q);
     return (uint32_t)q;
   } else if constexpr (EPI == EPI_R3) {
     // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); min(hi) then max(qmin); rne
-    int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)colc);
-    float f = __fmaf_rn(__int2float_rn(acc), cs, bias_f);
+    int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci);
+    float f = __fmaf_rn(__int2float_rn(acc), f1, f2);
     f = __fmaf_rn(f, e.inv_y, e.yzp_f);
     f = fmaxf(fminf(f, e.qmax_f), e.qmin_f);
     return (uint32_t)__float2int_rn(f);
   } else {  // EPI_R4
     // val = fma(float(acc), a_s*b_s/y_s, y_zp); nearbyint; clamp [0, 255]
-    int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)colc + (uint32_t)rowc);
+    int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci + (uint32_t)rowc);
     float f = __fmaf_rn(__int2float_rn(acc), e.combined, e.yzp_f);
     int32_t q = __float2int_rn(f);
     q = q < 0 ? 0 : (q > 255 ? 255 : q);
@@ -162,9 +174,9 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t colc, int32_
 template <int BN, int NPLANE, int AMODE, int EPI>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
-               const __grid_constant__ CUtensorMap tmB, int b_plane_rows, GatherGeom g, EpiParams e, int num_kb,
-               int m_tiles, int n_tiles) {
-  using Cfg = TileCfg<BN, NPLANE>;
+               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY, int y_tma,
+               int b_plane_rows, GatherGeom g, EpiParams e, int num_kb, int m_tiles, int n_tiles) {
+  using Cfg = TileCfg<BN, NPLANE, EPI>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr int A_BYTES = Cfg::A_BYTES;
   constexpr int B_BYTES = Cfg::B_BYTES;
@@ -173,7 +185,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;                                        // [STAGES][NPLANE][A_BYTES]
   uint8_t* sB = sA + STAGES * NPLANE * A_BYTES;              // [STAGES][NPLANE][B_BYTES]
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sB + STAGES * NPLANE * B_BYTES);
+  uint8_t* sOut = sB + STAGES * NPLANE * B_BYTES;            // [4 warps][32 rows][BN] (u8 epilogues)
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + Cfg::OUT_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;                  // [2] accumulator ready
   uint64_t* tempty_bar = tfull_bar + 2;                      // [2] accumulator drained
@@ -184,15 +197,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   const int lane = threadIdx.x & 31;
   const int num_tiles = m_tiles * n_tiles;
   // per-column constants, one private copy per epilogue warp (no cross-warp sync)
-  uint8_t* sparam = reinterpret_cast<uint8_t*>(full_bar) + 256 + (warp & 3) * (5 * BN * 4);
-  int32_t* s_colc = reinterpret_cast<int32_t*>(sparam);
-  int32_t* s_bias_i = s_colc + BN;
-  float* s_cs = reinterpret_cast<float*>(s_bias_i + BN);
-  float* s_bias_f = s_cs + BN;
-  float* s_os = s_bias_f + BN;
+  int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + 256 + (warp & 3) * (3 * BN * 4));
+  float* s_f1 = reinterpret_cast<float*>(s_ci + BN);
+  float* s_f2 = s_f1 + BN;
 
   if (threadIdx.x == 0) {
-    const uint32_t full_count = (AMODE == A_GATHER) ? (128u + 1u) : 1u;
+    const uint32_t full_count = (AMODE == A_GATHER) ? (4u + 1u) : 1u;  // 4 gather warps + TMA
     for (int s = 0; s < STAGES; ++s) {
       ptx::mbar_init(&full_bar[s], full_count);
       ptx::mbar_init(&empty_bar[s], 1);
@@ -207,7 +217,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   }
   if (warp == 8 && lane == 0) {
     ptx::tma_prefetch_desc(&tmB);
-    if (AMODE == A_TMA) {
+    if (AMODE != A_GATHER) {
       ptx::tma_prefetch_desc(&tmA0);
       if (NPLANE == 2) ptx::tma_prefetch_desc(&tmA1);
     }
@@ -226,11 +236,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   if (warp == 8) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      constexpr uint32_t tx = (AMODE == A_TMA ? NPLANE * A_BYTES : 0) + NPLANE * B_BYTES;
+      constexpr uint32_t tx = (AMODE != A_GATHER ? NPLANE * A_BYTES : 0) + NPLANE * B_BYTES;
       bool aborted = false;
       int it = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
         const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+        // im2col: input position of the tile's first output pixel
+        int i_n = 0, i_h = 0, i_w = 0;
+        if (AMODE == A_IM2COL) {
+          const int ohw = g.OH * g.OW;
+          i_n = m0 / ohw;
+          const int p = m0 - i_n * ohw;
+          const int oh = p / g.OW;
+          i_h = oh * g.sh - g.ph;
+          i_w = (p - oh * g.OW) * g.sw - g.pw;
+        }
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
@@ -244,6 +264,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           if (AMODE == A_TMA) {
             ptx::tma_load_2d(a_st, &tmA0, &full_bar[s], kx, m0);
             if (NPLANE == 2) ptx::tma_load_2d(a_st + A_BYTES, &tmA1, &full_bar[s], kx, m0);
+          } else if (AMODE == A_IM2COL) {
+            // one K slab = 128 bytes of channels of a single filter tap
+            const int kbyte = kb * BKB;
+            const int tap = kbyte / g.cbytes;
+            const int cc = (kbyte - tap * g.cbytes) / (NPLANE == 2 ? 2 : 1);
+            const int kh = tap / g.KW, kw = tap - kh * g.KW;
+            const uint16_t ow_off = (uint16_t)(kw * g.dw), oh_off = (uint16_t)(kh * g.dh);
+            ptx::tma_load_im2col_4d(a_st, &tmA0, &full_bar[s], cc, i_w, i_h, i_n, ow_off, oh_off);
+            if (NPLANE == 2) ptx::tma_load_im2col_4d(a_st + A_BYTES, &tmA1, &full_bar[s], cc, i_w, i_h, i_n, ow_off, oh_off);
           }
         }
       }
@@ -301,7 +330,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       uint8_t* const row_dst0 = sA + (r >> 3) * 1024 + (r & 7) * 128;
       const int rsw = r & 7;
       const int ohw = g.OH * g.OW;
-      constexpr int LAG = STAGES - 1;  // keep every free stage in flight
+      constexpr int LAG = Cfg::LAG;
       bool aborted = false;
       int it = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
@@ -361,20 +390,26 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           }
           ptx::cp_async_commit();
           // Publish the stage issued LAG iterations ago: its copies are done
-          // once at most LAG groups remain in flight. LAG = STAGES - 1 cannot
-          // deadlock: refilling stage it needs stage it - STAGES consumed,
-          // which was published at iteration it - STAGES + LAG < it.
+          // once at most LAG groups remain in flight. Refilling stage it needs
+          // stage it - STAGES consumed, which was published at iteration
+          // it - STAGES + LAG <= it - 1, leaving STAGES - 1 - LAG iterations of
+          // slack for the MMA (LAG = STAGES - 1 would lock the two in step).
+          // Each lane waits for its own copies and fences them for the async
+          // proxy; one arrival per warp (after __syncwarp) then publishes the
+          // warp's 32 rows, instead of 32 serialised arrivals.
           if (it >= LAG) {
             ptx::cp_async_wait<LAG>();
             ptx::fence_proxy_async_smem();
-            ptx::mbar_arrive(&full_bar[(it - LAG) % STAGES]);
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(&full_bar[(it - LAG) % STAGES]);
           }
         }
       }
       // Drain: publish the last LAG stages.
       ptx::cp_async_wait<0>();
       ptx::fence_proxy_async_smem();
-      if (!aborted) {
+      __syncwarp();
+      if (!aborted && lane == 0) {
         const int first = it > LAG ? it - LAG : 0;
         for (int q = first; q < it; ++q) ptx::mbar_arrive(&full_bar[q % STAGES]);
       }
@@ -383,27 +418,46 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     // ------------------------------------------------------------ epilogue (warps 0-3)
     const int row = warp * 32 + lane;  // TMEM lane == tile row
     int lt = 0;
+    int cached_n0 = -1;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
       const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
       const int acc = lt & 1;
       const uint32_t use_ph = (uint32_t)(lt >> 1) & 1u;
-      // per-column constants of this tile's columns (this warp's copy)
-      __syncwarp();
-      for (int i = lane; i < BN; i += 32) {
-        const int n = n0 + i;
-        const bool ok = n < e.N;
-        s_colc[i] = (ok && e.colcorr) ? e.colcorr[n] : 0;
-        s_bias_i[i] = (ok && e.bias_i) ? e.bias_i[n] : 0;
-        s_cs[i] = (ok && e.cs) ? e.cs[n] : 0.0f;
-        s_bias_f[i] = (ok && e.bias_f) ? e.bias_f[n] : ((ok && e.bias) ? e.bias[n] : 0.0f);
-        s_os[i] = (ok && e.os) ? e.os[n] : 0.0f;
+      if (n0 != cached_n0) {
+        // per-column constants of this column block (this warp's copy)
+        __syncwarp();
+        for (int i = lane; i < BN; i += 32) {
+          const int n = n0 + i;
+          const bool ok = n < e.N;
+          int32_t ci = (ok && e.colcorr) ? e.colcorr[n] : 0;
+          float f1 = 0.0f, f2 = 0.0f;
+          if (EPI == EPI_R2) {
+            if (ok && e.bias_i) ci = (int32_t)((uint32_t)ci + (uint32_t)e.bias_i[n]);
+            f1 = (ok && e.os) ? e.os[n] : 0.0f;
+          } else if (EPI == EPI_F32) {
+            f2 = (ok && e.bias) ? e.bias[n] : 0.0f;
+          } else {
+            f1 = (ok && e.cs) ? e.cs[n] : 0.0f;
+            f2 = (ok && e.bias_f) ? e.bias_f[n] : 0.0f;
+          }
+          s_ci[i] = ci;
+          s_f1[i] = f1;
+          s_f2[i] = f2;
+        }
+        __syncwarp();
+        cached_n0 = n0;
       }
-      __syncwarp();
       if (!__all_sync(0xffffffffu, ptx::mbar_wait(&tfull_bar[acc], use_ph, abort_flag))) {
         fail(ST_TIMEOUT_ACCUM);
         break;
       }
       ptx::tc_fence_after();
+      // the staging block may be rewritten once the previous tile's stores have read it
+      uint8_t* const stg = sOut + warp * (32 * BN);
+      if (EPI != EPI_F32 && y_tma) {
+        if (lane == 0) ptx::bulk_wait_read0();
+        __syncwarp();
+      }
       const int m = m0 + row;
       const bool mvalid = m < e.M;
       int32_t rowc = 0;
@@ -432,7 +486,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
               const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
-                float a = __uint_as_float(v[j + u]) + s_bias_f[c0 + j + u];
+                float a = __uint_as_float(v[j + u]) + s_f2[c0 + j + u];
                 if (e.res_mode == 1) a = fmaf(e.res_scale, rv[u], a);
                 a = apply_act(a, e.act, e.act_a, e.act_b);
                 if (e.res_mode == 2) a += rv[u];
@@ -447,7 +501,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
               const size_t idx = rowmajor ? (size_t)m * e.ldy + n0 + c0 + j
                                           : ((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix;
               const float rr = e.residual ? e.residual[idx] : 0.0f;
-              float a = __uint_as_float(v[j]) + s_bias_f[c0 + j];
+              float a = __uint_as_float(v[j]) + s_f2[c0 + j];
               if (e.res_mode == 1) a = fmaf(e.res_scale, rr, a);
               a = apply_act(a, e.act, e.act_a, e.act_b);
               if (e.res_mode == 2) a += rr;
@@ -457,18 +511,32 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         } else {
           uint32_t q[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            q[j] = requant_u8<EPI>((int32_t)v[j], s_colc[c0 + j], rowc, s_bias_i[c0 + j], s_cs[c0 + j],
-                                   s_bias_f[c0 + j], s_os[c0 + j], e);
+          for (int j = 0; j < 32; j += 4) {
+            const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + c0 + j);
+            const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + c0 + j);
+            const float4 b4 = *reinterpret_cast<const float4*>(s_f2 + c0 + j);
+            q[j + 0] = requant_u8<EPI>((int32_t)v[j + 0], ci4.x, rowc, a4.x, b4.x, e);
+            q[j + 1] = requant_u8<EPI>((int32_t)v[j + 1], ci4.y, rowc, a4.y, b4.y, e);
+            q[j + 2] = requant_u8<EPI>((int32_t)v[j + 2], ci4.z, rowc, a4.z, b4.z, e);
+            q[j + 3] = requant_u8<EPI>((int32_t)v[j + 3], ci4.w, rowc, a4.w, b4.w, e);
           }
           uint8_t* y = static_cast<uint8_t*>(e.y);
-          if (e.y_layout == 0) {
+          uint32_t w[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            w[j] = q[4 * j] | (q[4 * j + 1] << 8) | (q[4 * j + 2] << 16) | (q[4 * j + 3] << 24);
+          if (y_tma) {
+            // swizzled staging (matches the store map's 128B / 64B swizzle):
+            // row r, 16-byte chunk c of a segment lives at r*SEG + ((c ^ f(r)) << 4)
+            constexpr int SEG = Cfg::OUT_SEG;
+            const int h = c0 / SEG, cc = (c0 % SEG) >> 4;
+            const int f = SEG == 128 ? (lane & 7) : ((lane >> 1) & 3);
+            uint8_t* seg = stg + h * (32 * SEG) + lane * SEG;
+            ptx::st_shared_v4(seg + ((cc ^ f) << 4), w[0], w[1], w[2], w[3]);
+            ptx::st_shared_v4(seg + (((cc + 1) ^ f) << 4), w[4], w[5], w[6], w[7]);
+          } else if (e.y_layout == 0) {
             uint8_t* dst = y + (size_t)m * e.ldy + n0 + c0;
             if (nvalid == 32 && (e.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0) {
-              uint32_t w[8];
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                w[j] = q[4 * j] | (q[4 * j + 1] << 8) | (q[4 * j + 2] << 16) | (q[4 * j + 3] << 24);
               reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
               reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
             } else {
@@ -487,7 +555,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+      if (EPI != EPI_F32 && y_tma) {
+        // publish the staged block: rows >= M and columns >= N are clipped by the map
+        ptx::fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          constexpr int SEG = Cfg::OUT_SEG;
+          if (m0 + warp * 32 < e.M)
+            for (int h = 0; h < BN / SEG; ++h)
+              if (n0 + h * SEG < e.N) ptx::tma_store_2d(&tmY, stg + h * (32 * SEG), n0 + h * SEG, m0 + warp * 32);
+          ptx::bulk_commit();
+        }
+      }
     }
+    if (EPI != EPI_F32 && y_tma && lane == 0) ptx::bulk_wait0();  // stores complete before smem is released
   }
 
   ptx::tc_fence_before();

@@ -10,7 +10,7 @@ namespace {
 
 template <int BN, int NPLANE, int AMODE, int EPI>
 int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
-  using Cfg = TileCfg<BN, NPLANE>;
+  using Cfg = TileCfg<BN, NPLANE, EPI>;
   auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI>;
   // The attribute is per function; setting it is cheap but not free, so do it
   // once per device.
@@ -23,8 +23,19 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
   }
   const long long tiles = (long long)L.m_tiles * L.n_tiles;
   const int grid = (int)std::min<long long>(tiles, (long long)num_sms());
-  kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, L.b_plane_rows, g, e, L.num_kb,
-                                                       L.m_tiles, L.n_tiles);
+  // u8 outputs in row-major [M, ldy] leave through a TMA store of each
+  // warp's staged 32 x BN block (coalesced rows instead of per-lane pieces).
+  CUtensorMap tmY{};
+  int y_tma = 0;
+  if (EPI != EPI_F32 && e.y_layout == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 && (e.ldy & 15) == 0) {
+    const int seg = Cfg::OUT_SEG;
+    int rc = encode_tmap_2d(&tmY, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.y, (uint64_t)e.N, (uint64_t)e.M, (uint64_t)e.ldy,
+                            seg, 32, seg == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != NNRCU_OK) return rc;
+    y_tma = 1;
+  }
+  kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, tmY, y_tma, L.b_plane_rows, g, e,
+                                                       L.num_kb, L.m_tiles, L.n_tiles);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }
@@ -34,9 +45,16 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
   if (L.nplane == 2) {
     if (L.epi != EPI_F32) return set_error(NNRCU_ERR_INVALID, "split-bf16 engine needs the fp32 epilogue");
     if (L.amode == A_TMA) return launch_one<BN, 2, A_TMA, EPI_F32>(L, g, e, st);
+    if (L.amode == A_IM2COL) return launch_one<BN, 2, A_IM2COL, EPI_F32>(L, g, e, st);
     return launch_one<BN, 2, A_GATHER, EPI_F32>(L, g, e, st);
   }
-  if (L.amode == A_TMA) {
+  if (L.amode == A_IM2COL) {
+    switch (L.epi) {
+      case EPI_R1: return launch_one<BN, 1, A_IM2COL, EPI_R1>(L, g, e, st);
+      case EPI_R2: return launch_one<BN, 1, A_IM2COL, EPI_R2>(L, g, e, st);
+      default: break;
+    }
+  } else if (L.amode == A_TMA) {
     switch (L.epi) {
       case EPI_R1: return launch_one<BN, 1, A_TMA, EPI_R1>(L, g, e, st);
       case EPI_R2: return launch_one<BN, 1, A_TMA, EPI_R2>(L, g, e, st);

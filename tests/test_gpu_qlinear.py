@@ -159,3 +159,36 @@ def test_qlinearmatmul_shapes(cuda_dev, m, k, n, b_zp):
     y = run_qmm(cuda_dev, a, b, 0.03, 117, 0.004, b_zp, ys, 100)
     ref = O.qlinearmatmul(a, b, 0.03, 117, 0.004, b_zp, ys, 100)
     assert np.array_equal(y, ref)
+
+
+# Hardware-im2col path: NHWC inputs with a 128-byte multiple channel stride
+# and >= 128 KB; x_zp = 0 so the TMA zero fill equals the padding value.
+IM2COL_SHAPES = [
+    (2, 128, 28, 28, 128, 3, 3, (1, 1), (1, 1, 1, 1), (1, 1)),
+    (2, 256, 20, 18, 96, 3, 3, (2, 2), (1, 0, 1, 1), (1, 1)),
+    (1, 128, 40, 40, 64, 3, 3, (1, 1), (2, 2, 2, 2), (2, 2)),
+    (4, 128, 13, 15, 160, 5, 5, (2, 1), (2, 2, 2, 2), (1, 1)),
+]
+
+
+@pytest.mark.parametrize("shape", IM2COL_SHAPES)
+@pytest.mark.parametrize("formula", [O.R1, O.R2])
+def test_im2col_zero_zp(cuda_dev, shape, formula):
+    n, c, h, w, oc, kh, kw, s, p, d = shape
+    rng = np.random.default_rng(sum(shape[:7]) + formula)
+    case = W.random_qconv(rng, n, c, h, w, oc, kh, kw, s, p, d, x_zp=0)
+    for lay in (("NHWC", "NHWC"), ("NCHW", "NCHW")):
+        y, _ = run_qconv(cuda_dev, case, formula, lay[0], lay[1])
+        ref = oracle_qconv(case, formula, lay[1])
+        assert np.array_equal(y, ref), f"{lay}: {(y != ref).sum()} / {y.size} mismatches"
+
+
+@pytest.mark.parametrize("shape", IM2COL_SHAPES[:2])
+def test_im2col_padded_copy_nonzero_zp(cuda_dev, shape):
+    """NCHW input with x_zp != 0: reordered into an x_zp-bordered NHWC copy."""
+    n, c, h, w, oc, kh, kw, s, p, d = shape
+    rng = np.random.default_rng(77)
+    case = W.random_qconv(rng, n, c, h, w, oc, kh, kw, s, p, d, x_zp=201)
+    for f in (O.R1, O.R2):
+        y, _ = run_qconv(cuda_dev, case, f, "NCHW", "NCHW")
+        assert np.array_equal(y, oracle_qconv(case, f))
