@@ -33,15 +33,17 @@ __global__ void nchw_to_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* _
 
 // Vectorised variant for hw % 4 == 0 and cs % 4 == 0: a 64-channel x
 // 128-pixel tile is read as 32-bit words along pixels and written as 32-bit
-// words along channels.
-__global__ void nchw_to_nhwc_u8_vec_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, int c, int hw,
-                                           int cs, uint8_t fill) {
+// words along channels. The destination may be spatially padded
+// ([n][hp][wp][cs], pixel (y, x) stored at (y + pt, x + pl)); its border is
+// filled by the caller.
+__global__ void nchw_to_nhwc_u8_vec_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, int c, int w,
+                                           int hw, int hp, int wp, int pt, int pl, int cs, uint8_t fill) {
   __shared__ uint8_t tile[64][128 + 4];
   const int img = blockIdx.z;
   const int p0 = blockIdx.x * 128;
   const int c0 = blockIdx.y * 64;
   const uint8_t* s = src + (size_t)img * c * hw;
-  uint8_t* d = dst + (size_t)img * hw * cs;
+  uint8_t* d = dst + (size_t)img * hp * wp * cs;
   const uint32_t fill4 = 0x01010101u * fill;
   for (int idx = threadIdx.x; idx < 64 * 32; idx += blockDim.x) {
     const int ch = idx >> 5, wd = idx & 31;
@@ -55,36 +57,10 @@ __global__ void nchw_to_nhwc_u8_vec_kernel(const uint8_t* __restrict src, uint8_
     const int pp = idx >> 4, wd = idx & 15;
     const int p = p0 + pp, ch = c0 + wd * 4;
     if (p >= hw || ch >= cs) continue;
+    const int y = p / w, x = p - y * w;
     const uint32_t v = (uint32_t)tile[wd * 4][pp] | ((uint32_t)tile[wd * 4 + 1][pp] << 8) |
                        ((uint32_t)tile[wd * 4 + 2][pp] << 16) | ((uint32_t)tile[wd * 4 + 3][pp] << 24);
-    *reinterpret_cast<uint32_t*>(d + (size_t)p * cs + ch) = v;
-  }
-}
-
-// NCHW u8 -> spatially padded NHWC u8 [n][hp][wp][cs]: pixel (y, x) lands at
-// (y + pt, x + pl). The border and the channel padding must already hold
-// fill (the caller memsets the buffer); 64-channel x 128-pixel tiles.
-__global__ void nchw_to_nhwc_u8_padded_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, int c, int h,
-                                              int w, int hp, int wp, int pt, int pl, int cs) {
-  __shared__ uint8_t tile[64][128 + 4];
-  const int hw = h * w;
-  const int img = blockIdx.z;
-  const int p0 = blockIdx.x * 128;
-  const int c0 = blockIdx.y * 64;
-  const uint8_t* s = src + (size_t)img * c * hw;
-  uint8_t* d = dst + (size_t)img * hp * wp * cs;
-  for (int idx = threadIdx.x; idx < 64 * 128; idx += blockDim.x) {
-    const int ch = idx >> 7, pp = idx & 127;
-    const int p = p0 + pp;
-    tile[ch][pp] = (c0 + ch < c && p < hw) ? s[(size_t)(c0 + ch) * hw + p] : 0;
-  }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < 128 * 64; idx += blockDim.x) {
-    const int pp = idx >> 6, cl = idx & 63;
-    const int p = p0 + pp, ch = c0 + cl;
-    if (p >= hw || ch >= c) continue;
-    const int y = p / w, x = p - y * w;
-    d[((size_t)(y + pt) * wp + (x + pl)) * cs + ch] = tile[cl][pp];
+    *reinterpret_cast<uint32_t*>(d + ((size_t)(y + pt) * wp + (x + pl)) * cs + ch) = v;
   }
 }
 
@@ -286,7 +262,7 @@ int launch_nchw_to_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int c, int h
   if ((hw & 3) == 0 && (cs & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 3) == 0 &&
       (reinterpret_cast<uintptr_t>(dst) & 3) == 0) {
     dim3 grid((hw + 127) / 128, (cs + 63) / 64, n);
-    nchw_to_nhwc_u8_vec_kernel<<<grid, 256, 0, st>>>(src, dst, c, hw, cs, fill);
+    nchw_to_nhwc_u8_vec_kernel<<<grid, 256, 0, st>>>(src, dst, c, w, hw, h, w, 0, 0, cs, fill);
     NNRCU_CUDA(cudaGetLastError());
     return NNRCU_OK;
   }
@@ -299,9 +275,11 @@ int launch_nchw_to_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int c, int h
 int launch_nchw_to_nhwc_u8_padded(const uint8_t* src, uint8_t* dst, int n, int c, int h, int w, int pt, int pl,
                                   int pb, int pr, int cs, uint8_t fill, cudaStream_t st) {
   const int hp = h + pt + pb, wp = w + pl + pr;
+  if ((h * w) % 4 != 0 || cs % 4 != 0 || (reinterpret_cast<uintptr_t>(src) & 3) || (reinterpret_cast<uintptr_t>(dst) & 3))
+    return set_error(NNRCU_ERR_INVALID, "padded reorder needs h*w %% 4 == 0 and 4-byte aligned buffers");
   NNRCU_CUDA(cudaMemsetAsync(dst, fill, (size_t)n * hp * wp * cs, st));
-  dim3 grid((h * w + 127) / 128, (c + 63) / 64, n);
-  nchw_to_nhwc_u8_padded_kernel<<<grid, 256, 0, st>>>(src, dst, c, h, w, hp, wp, pt, pl, cs);
+  dim3 grid((h * w + 127) / 128, (cs + 63) / 64, n);
+  nchw_to_nhwc_u8_vec_kernel<<<grid, 256, 0, st>>>(src, dst, c, w, h * w, hp, wp, pt, pl, cs, fill);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

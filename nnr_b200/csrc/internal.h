@@ -33,7 +33,8 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 // row of c*elem bytes): boxes of 128 pixels x (128 bytes of channels), with
 // the bounding box of a conv with the given pads/kernel/dilation/stride.
 int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, int n, int h,
-                       int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw);
+                       int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw,
+                       int kslab = 128);
 
 enum OpKind : int { OP_QCONV = 1, OP_QMATMUL = 2, OP_CONV_F32 = 3, OP_GEMM_F32 = 4, OP_DWCONV_F32 = 5 };
 
@@ -50,6 +51,7 @@ struct Op {
   int num_kb = 0;
   int npad = 0;                 // packed B rows per plane
   int bn = 128;
+  int kslab = 128;              // K bytes per pipeline stage (128 or 64)
   int amode = 1;                // A_TMA / A_GATHER
   int epi = 0;
   int nplane = 1;
@@ -92,6 +94,7 @@ struct TcLaunch {
   const CUtensorMap* tmB;
   int b_plane_rows;
   int num_kb;
+  int kb_bytes = 128;  // K bytes per pipeline stage (128, or 64 for 64-byte channel strides)
 };
 struct GatherGeom;
 struct EpiParams;

@@ -151,16 +151,20 @@ __device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
 }
 
 // Shared-memory matrix descriptor for a K-major operand tile stored with the
-// 128-byte swizzle: rows of 128 bytes, 8-row groups 1024 bytes apart.
-__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+// 128-byte swizzle (rows of 128 bytes, 8-row groups 1024 bytes apart) or the
+// 64-byte swizzle (rows of 64 bytes, 8-row groups 512 bytes apart).
+template <int KB = 128>
+__device__ __forceinline__ uint64_t umma_desc_sw(uint32_t saddr) {
+  static_assert(KB == 128 || KB == 64, "128- or 64-byte K slabs");
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);      // start address
   d |= (uint64_t)1 << 16;                         // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024u >> 4) << 32;              // stride byte offset: 8 rows * 128 B
+  d |= (uint64_t)((8u * KB) >> 4) << 32;          // stride byte offset: 8 rows
   d |= (uint64_t)1 << 46;                         // descriptor version (sm_100)
-  d |= (uint64_t)2 << 61;                         // layout: 128-byte swizzle
+  d |= (uint64_t)(KB == 128 ? 2 : 4) << 61;       // layout: 128-byte / 64-byte swizzle
   return d;
 }
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) { return umma_desc_sw<128>(saddr); }
 
 // Instruction descriptor. dtype: 1 = f32, 2 = s32. atype/btype: for kind::i8
 // 0 = u8, 1 = s8; for kind::f16 1 = bf16. Both operands K-major.

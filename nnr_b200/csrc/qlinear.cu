@@ -111,21 +111,25 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   const bool one_by_one = d.kh == 1 && d.kw == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_top == 0 &&
                           d.pad_left == 0 && d.pad_bottom == 0 && d.pad_right == 0;
   op->need_in_copy = d.in_layout == NNRCU_LAYOUT_NCHW || d.c != op->cs;
-  op->amode = (one_by_one && op->kbytes >= BKB && op->epi != EPI_R3) ? A_TMA : A_GATHER;
+  // K-slab width for TMA-fed A: 128 bytes, or 64 for 64-byte channel strides
+  const int kslab = op->cs % 128 == 0 ? 128 : (op->cs % 64 == 0 ? 64 : 0);
+  op->amode = (one_by_one && kslab && op->kbytes >= kslab && op->epi != EPI_R3) ? A_TMA : A_GATHER;
   // Hardware im2col (TMA) when the channel stride is whole 128-byte slabs.
   // Its out-of-bounds fill is zero, which equals the padding value when
   // x_zp = 0 or there is no padding; an NCHW input with x_zp != 0 is instead
   // reordered into a spatially padded copy whose border holds x_zp. Tensors
   // under 128 KB keep the gather path.
   const bool has_pad = d.pad_top || d.pad_left || d.pad_bottom || d.pad_right;
-  const bool im2col_shape = op->amode == A_GATHER && op->epi != EPI_R3 && op->cs % BKB == 0 &&
+  const bool im2col_shape = op->amode == A_GATHER && op->epi != EPI_R3 && kslab != 0 &&
                             (size_t)d.n * d.h * d.w * op->cs >= 128 * 1024;
   if (im2col_shape && (x_zp == 0 || !has_pad)) {
     op->amode = A_IM2COL;
-  } else if (im2col_shape && d.in_layout == NNRCU_LAYOUT_NCHW) {
+  } else if (im2col_shape && d.in_layout == NNRCU_LAYOUT_NCHW && (d.h * d.w) % 4 == 0) {
     op->amode = A_IM2COL;
     op->pad_in = true;
   }
+  op->kslab = op->amode == A_GATHER ? BKB : kslab;
+  op->num_kb = (op->kbytes + op->kslab - 1) / op->kslab;
   const size_t hp = d.h + (op->pad_in ? d.pad_top + d.pad_bottom : 0);
   const size_t wp = d.w + (op->pad_in ? d.pad_left + d.pad_right : 0);
   op->ws_bytes = op->need_in_copy ? (size_t)d.n * hp * wp * op->cs : 0;
@@ -174,7 +178,8 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   NNRCU_TRY(upload(&op->bias_f, bias_f));
   NNRCU_TRY(upload(&op->os, osv));
   NNRCU_TRY(encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, op->kpad_bytes, op->npad, op->kpad_bytes,
-                           BKB, op->bn));
+                           op->kslab, op->bn,
+                           op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
   *out = op;
   return NNRCU_OK;
 }
@@ -199,7 +204,8 @@ int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* work
   }
   CUtensorMap tmA{};
   if (op->amode == A_TMA) {
-    int rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, xin, op->cs, (uint64_t)op->M, op->cs, BKB, BM);
+    int rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, xin, op->cs, (uint64_t)op->M, op->cs, op->kslab, BM,
+                            op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc != NNRCU_OK) return rc;
   }
   GatherGeom g{};
@@ -216,7 +222,7 @@ int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* work
   g.sh = d.stride_h; g.sw = d.stride_w; g.ph = pt; g.pw = pl; g.dh = d.dil_h; g.dw = d.dil_w;
   if (op->amode == A_IM2COL) {
     int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, op->cs, pt, pl, pb, pr,
-                                d.kh, d.kw, d.dil_h, d.dil_w, d.stride_h, d.stride_w);
+                                d.kh, d.kw, d.dil_h, d.dil_w, d.stride_h, d.stride_w, op->kslab);
     if (rc != NNRCU_OK) return rc;
   }
   g.kbytes = op->kbytes;
@@ -240,6 +246,7 @@ int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* work
   L.tmA0 = &tmA; L.tmA1 = &tmA; L.tmB = &op->tmB;
   L.b_plane_rows = op->npad;
   L.num_kb = op->num_kb;
+  L.kb_bytes = op->kslab;
   return tc_launch(L, g, e, st);
 }
 

@@ -110,12 +110,13 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 }
 
 int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, int n, int h,
-                       int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw) {
+                       int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw,
+                       int kslab) {
   int dev = 0;
   int rc = current_device(&dev);
   if (rc != NNRCU_OK) return rc;
   const uint64_t row = (uint64_t)c * elem_bytes;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (row % 128) != 0)
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (kslab != 128 && kslab != 64) || (row % kslab) != 0)
     return set_error(NNRCU_ERR_INVALID, "im2col operand must be 16-byte aligned with a 128-byte multiple channel stride");
   const cuuint64_t dims[4] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
   const cuuint64_t strides[3] = {row, row * (uint64_t)w, row * (uint64_t)w * (uint64_t)h};
@@ -123,8 +124,9 @@ int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
   const int upper[2] = {pr - (kw - 1) * dw, pb - (kh - 1) * dh};
   const cuuint32_t estr[4] = {1, (cuuint32_t)sw, (cuuint32_t)sh, 1};
   CUresult r = g_encode_im2col(map, dtype, 4, const_cast<void*>(base), dims, strides, lower, upper,
-                               (cuuint32_t)(128 / elem_bytes), 128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               (cuuint32_t)(kslab / elem_bytes), 128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(NNRCU_ERR_CUDA, "cuTensorMapEncodeIm2col failed (%d) n=%d h=%d w=%d c=%d", (int)r, n, h, w, c);

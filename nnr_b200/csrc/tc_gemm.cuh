@@ -39,7 +39,7 @@ enum : int { ACT_NONE = 0, ACT_RELU = 1, ACT_CLIP = 2, ACT_HARDSWISH = 3, ACT_SI
 enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_ACCUM = 3 };
 
 constexpr int BM = 128;       // rows per tile (TMEM lanes)
-constexpr int BKB = 128;      // K bytes per stage per plane (one swizzle row)
+constexpr int BKB = 128;      // K bytes per stage per plane (one swizzle row); 64 for the 64-byte-slab variant
 constexpr int NUM_THREADS = 320;  // 4 epilogue + 4 gather + TMA + MMA warps
 
 // Geometry of the implicit im2col gather (A_GATHER). All sizes in bytes where noted.
@@ -79,16 +79,16 @@ struct EpiParams {
   int* status;             // device status word (first error wins)
 };
 
-template <int BN, int NPLANE, int EPI>
+template <int BN, int NPLANE, int EPI, int KB = BKB>
 struct TileCfg {
-  static constexpr int A_BYTES = BM * BKB;             // 16 KB per plane
-  static constexpr int B_BYTES = BN * BKB;
+  static constexpr int A_BYTES = BM * KB;              // 16 KB per plane (8 KB with 64-byte slabs)
+  static constexpr int B_BYTES = BN * KB;
   static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + B_BYTES);
   // u8 epilogues stage each warp's 32 x BN output block for a TMA store
   static constexpr int OUT_BYTES = (EPI == EPI_F32) ? 0 : 4 * 32 * BN;
   static constexpr int OUT_SEG = BN >= 128 ? 128 : 64;  // bytes per staged row segment (= TMA box width)
   static constexpr int STAGES_RAW = (200 * 1024 - OUT_BYTES) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
   // Gather producers publish a stage LAG iterations after issuing it: LAG
   // stages of copies in flight, STAGES - 1 - LAG stages of slack for the MMA.
   static constexpr int LAG = (STAGES - 1) / 2 > 1 ? (STAGES - 1) / 2 : 1;
@@ -171,12 +171,13 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t 
 // The smem stage ring runs continuously across tiles, and the accumulator is
 // double-buffered in TMEM (2 x BN columns), so the epilogue of tile i overlaps
 // the loads and MMAs of tile i + 1.
-template <int BN, int NPLANE, int AMODE, int EPI>
+template <int BN, int NPLANE, int AMODE, int EPI, int KB>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY, int y_tma,
                int b_plane_rows, GatherGeom g, EpiParams e, int num_kb, int m_tiles, int n_tiles) {
-  using Cfg = TileCfg<BN, NPLANE, EPI>;
+  using Cfg = TileCfg<BN, NPLANE, EPI, KB>;
+  static_assert(KB == BKB || AMODE != A_GATHER, "the gather producers fill 128-byte slabs");
   constexpr int STAGES = Cfg::STAGES;
   constexpr int A_BYTES = Cfg::A_BYTES;
   constexpr int B_BYTES = Cfg::B_BYTES;
@@ -258,7 +259,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           ptx::mbar_arrive_expect_tx(&full_bar[s], tx);
           uint8_t* a_st = sA + (size_t)s * NPLANE * A_BYTES;
           uint8_t* b_st = sB + (size_t)s * NPLANE * B_BYTES;
-          const int kx = kb * BKB / (NPLANE == 2 ? 2 : 1);  // element coordinate along K
+          const int kx = kb * KB / (NPLANE == 2 ? 2 : 1);  // element coordinate along K
           for (int p = 0; p < NPLANE; ++p)
             ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
           if (AMODE == A_TMA) {
@@ -266,7 +267,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             if (NPLANE == 2) ptx::tma_load_2d(a_st + A_BYTES, &tmA1, &full_bar[s], kx, m0);
           } else if (AMODE == A_IM2COL) {
             // one K slab = 128 bytes of channels of a single filter tap
-            const int kbyte = kb * BKB;
+            const int kbyte = kb * KB;
             const int tap = kbyte / g.cbytes;
             const int cc = (kbyte - tap * g.cbytes) / (NPLANE == 2 ? 2 : 1);
             const int kh = tap / g.KW, kw = tap - kh * g.KW;
@@ -299,19 +300,19 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * NPLANE * A_BYTES);
           const uint32_t b_addr = ptx::smem_u32(sB + (size_t)s * NPLANE * B_BYTES);
 #pragma unroll
-          for (int k = 0; k < BKB / 32; ++k) {
+          for (int k = 0; k < KB / 32; ++k) {
             const uint32_t koff = k * 32;
             if constexpr (NPLANE == 1) {
-              ptx::mma_i8(d_tmem, ptx::umma_desc_sw128(a_addr + koff), ptx::umma_desc_sw128(b_addr + koff), idesc,
+              ptx::mma_i8(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff), ptx::umma_desc_sw<KB>(b_addr + koff), idesc,
                           (kb | k) != 0);
             } else {
               // hi*hi, hi*lo, lo*hi
-              ptx::mma_f16(d_tmem, ptx::umma_desc_sw128(a_addr + koff), ptx::umma_desc_sw128(b_addr + koff), idesc,
+              ptx::mma_f16(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff), ptx::umma_desc_sw<KB>(b_addr + koff), idesc,
                            (kb | k) != 0);
-              ptx::mma_f16(d_tmem, ptx::umma_desc_sw128(a_addr + koff),
-                           ptx::umma_desc_sw128(b_addr + B_BYTES + koff), idesc, 1u);
-              ptx::mma_f16(d_tmem, ptx::umma_desc_sw128(a_addr + A_BYTES + koff),
-                           ptx::umma_desc_sw128(b_addr + koff), idesc, 1u);
+              ptx::mma_f16(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff),
+                           ptx::umma_desc_sw<KB>(b_addr + B_BYTES + koff), idesc, 1u);
+              ptx::mma_f16(d_tmem, ptx::umma_desc_sw<KB>(a_addr + A_BYTES + koff),
+                           ptx::umma_desc_sw<KB>(b_addr + koff), idesc, 1u);
             }
           }
           ptx::mma_commit(&empty_bar[s]);

@@ -8,10 +8,10 @@ namespace nnrcu {
 
 namespace {
 
-template <int BN, int NPLANE, int AMODE, int EPI>
+template <int BN, int NPLANE, int AMODE, int EPI, int KB = BKB>
 int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
-  using Cfg = TileCfg<BN, NPLANE, EPI>;
-  auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI>;
+  using Cfg = TileCfg<BN, NPLANE, EPI, KB>;
+  auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI, KB>;
   // The attribute is per function; setting it is cheap but not free, so do it
   // once per device.
   static unsigned long long configured = 0;
@@ -42,6 +42,20 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
 
 template <int BN>
 int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t st) {
+  if (L.kb_bytes == 64) {
+    // 64-byte K slabs (channel strides of 64 bytes): int8, TMA-fed A only
+    if (L.nplane != 1 || L.amode == A_GATHER)
+      return set_error(NNRCU_ERR_INVALID, "64-byte K slabs need int8 with a TMA-fed A operand");
+    if (L.amode == A_IM2COL) {
+      if (L.epi == EPI_R1) return launch_one<BN, 1, A_IM2COL, EPI_R1, 64>(L, g, e, st);
+      if (L.epi == EPI_R2) return launch_one<BN, 1, A_IM2COL, EPI_R2, 64>(L, g, e, st);
+    } else {
+      if (L.epi == EPI_R1) return launch_one<BN, 1, A_TMA, EPI_R1, 64>(L, g, e, st);
+      if (L.epi == EPI_R2) return launch_one<BN, 1, A_TMA, EPI_R2, 64>(L, g, e, st);
+      if (L.epi == EPI_R4) return launch_one<BN, 1, A_TMA, EPI_R4, 64>(L, g, e, st);
+    }
+    return set_error(NNRCU_ERR_INVALID, "no 64-byte-slab engine instance for amode %d epilogue %d", L.amode, L.epi);
+  }
   if (L.nplane == 2) {
     if (L.epi != EPI_F32) return set_error(NNRCU_ERR_INVALID, "split-bf16 engine needs the fp32 epilogue");
     if (L.amode == A_TMA) return launch_one<BN, 2, A_TMA, EPI_F32>(L, g, e, st);

@@ -168,6 +168,9 @@ IM2COL_SHAPES = [
     (2, 256, 20, 18, 96, 3, 3, (2, 2), (1, 0, 1, 1), (1, 1)),
     (1, 128, 40, 40, 64, 3, 3, (1, 1), (2, 2, 2, 2), (2, 2)),
     (4, 128, 13, 15, 160, 5, 5, (2, 1), (2, 2, 2, 2), (1, 1)),
+    (2, 64, 32, 32, 64, 3, 3, (1, 1), (1, 1, 1, 1), (1, 1)),     # 64-byte K slabs (SWIZZLE_64B)
+    (3, 64, 30, 30, 128, 3, 3, (2, 2), (1, 1, 1, 1), (1, 1)),
+    (2, 64, 24, 24, 256, 1, 1, (1, 1), (0, 0, 0, 0), (1, 1)),     # 1x1, 64-byte slabs, plain TMA
 ]
 
 
