@@ -173,6 +173,29 @@ int nnrcu_gemm_f32_create(int m, int n, int k, int trans_a, int trans_b, float a
                           float post_b, nnrcu_op** op);
 int nnrcu_gemm_f32_run(nnrcu_op* op, const float* a, float* y, void* workspace, void* stream);
 
+/* ---------------------------------------------------------------- QDQ glue of int8 networks
+ * Device versions of the ops around QLinearConv/QLinearMatMul in a QDQ graph,
+ * so that a whole int8 network stays on the device. Same float operation
+ * order as nnr's x64 paths (bit-exact u8 results). */
+/* QuantizeLinear fp32 NCHW -> u8, per-tensor (backend/cpu/QuantizeLinear.cpp:128-160);
+ * out_layout NCHW, or NHWC with channel stride out_cs >= c (extra channels = zp). */
+int nnrcu_quantize_linear_u8(const float* x, uint8_t* y, int n, int c, int h, int w, float scale, uint8_t zp,
+                             int out_layout, int out_cs, void* stream);
+/* MaxPool on u8 NHWC (backend/cpu/MaxPool.cpp:279, dilation 1). */
+int nnrcu_maxpool_u8_nhwc(const uint8_t* x, uint8_t* y, int n, int h, int w, int c, int kh, int kw, int sh, int sw,
+                          int pt, int pl, int pb, int pr, void* stream);
+/* QLinearAdd of two same-shape u8 tensors (backend/cpu/QLinearAdd.cpp:46-104). */
+int nnrcu_qlinearadd_u8(const uint8_t* a, float a_scale, uint8_t a_zp, const uint8_t* b, float b_scale, uint8_t b_zp,
+                        float y_scale, uint8_t y_zp, uint8_t* y, size_t n, void* stream);
+/* DequantizeLinear -> GlobalAveragePool -> QuantizeLinear on u8 NHWC [n, hw, c] -> u8 [n, c]
+ * (DequantizeLinear.cpp:135-160, kernel/pool.h:109-125, QuantizeLinear.cpp:128-160). */
+int nnrcu_dq_gap_q_u8_nhwc(const uint8_t* x, int n, int hw, int c, float x_scale, uint8_t x_zp, float y_scale,
+                           uint8_t y_zp, uint8_t* y, void* stream);
+/* DequantizeLinear of u8 [rows, cols] followed by an fp32 Add of bias[cols] (bias may be NULL)
+ * (DequantizeLinear.cpp:135-160, binary_math.cpp:57-77). */
+int nnrcu_dequantize_linear_u8(const uint8_t* x, float scale, uint8_t zp, const float* bias, int rows, int cols,
+                               float* y, void* stream);
+
 /* ---------------------------------------------------------------- layout helpers
  * Device versions of nnr's boundary reorders (src/nnr.cpp:953-1031, kernel/layout.h). */
 int nnrcu_nchw_to_nhwc(const void* src, void* dst, int n, int c, int h, int w, int elem_size, void* stream);

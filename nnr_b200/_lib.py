@@ -72,6 +72,11 @@ SIGNATURES = {
     "nnrcu_conv_f32_run": [P, P, P, P, P, P],
     "nnrcu_gemm_f32_create": [I, I, I, I, I, F, F, P, P, I, I, F, F, PP],
     "nnrcu_gemm_f32_run": [P, P, P, P, P],
+    "nnrcu_quantize_linear_u8": [P, P, I, I, I, I, F, U8, I, I, P],
+    "nnrcu_maxpool_u8_nhwc": [P, P, I, I, I, I, I, I, I, I, I, I, I, I, P],
+    "nnrcu_qlinearadd_u8": [P, F, U8, P, F, U8, F, U8, P, SZ, P],
+    "nnrcu_dq_gap_q_u8_nhwc": [P, I, I, I, F, U8, F, U8, P, P],
+    "nnrcu_dequantize_linear_u8": [P, F, U8, P, I, I, P, P],
     "nnrcu_nchw_to_nhwc": [P, P, I, I, I, I, I, P],
     "nnrcu_nhwc_to_nchw": [P, P, I, I, I, I, I, P],
 }

@@ -1,0 +1,227 @@
+"""Device execution of a quantised network through libnnrcu.so.
+
+This is the device side of nnr's context run loop for a graph whose nodes
+all live on the device:
+  * plan_arena() is the device arena of nnr's memory planner
+    (memory_planner.cpp:33-337): tensor lifetimes (producer step .. last
+    consumer step) packed into one device allocation, best fit by size,
+    operator workspaces included as one-step lifetimes;
+  * DeviceNetwork.run() enqueues every node on one stream, in order
+    (nnr.cpp:908-1051's exec_steps loop);
+  * DeviceNetwork.capture() records that sequence once into a CUDA graph
+    (nnrcu_graph_begin/_end) that later runs replay with one launch.
+All compute goes through the C ABI; torch only provides the arena buffer,
+streams and host staging.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+
+ALIGN = 256
+
+
+@dataclass
+class Interval:
+    name: str
+    nbytes: int
+    first: int      # first step that writes or reads it
+    last: int       # last step that reads it
+
+
+def plan_arena(items: Sequence[Interval]) -> Tuple[Dict[str, int], int]:
+    """Assigns byte offsets so that tensors whose lifetimes overlap never
+    share bytes. Largest first, each at the lowest offset that fits between
+    the already-placed intervals it overlaps in time. Returns (offsets, size)."""
+    placed: List[Tuple[int, int, Interval]] = []  # (offset, end, item)
+    offsets: Dict[str, int] = {}
+    for it in sorted(items, key=lambda i: (-i.nbytes, i.first, i.name)):
+        size = (it.nbytes + ALIGN - 1) // ALIGN * ALIGN
+        busy = sorted((o, e) for o, e, other in placed if not (other.last < it.first or it.last < other.first))
+        off = 0
+        for o, e in busy:
+            if off + size <= o:
+                break
+            off = max(off, e)
+        placed.append((off, off + size, it))
+        offsets[it.name] = off
+    total = max((e for _, e, _ in placed), default=0)
+    return offsets, total
+
+
+def check_plan(items: Sequence[Interval], offsets: Dict[str, int]) -> None:
+    """Raises if two time-overlapping intervals share bytes (planner self-check)."""
+    lst = list(items)
+    for i, a in enumerate(lst):
+        for b in lst[i + 1:]:
+            if a.last < b.first or b.last < a.first:
+                continue
+            a0, a1 = offsets[a.name], offsets[a.name] + a.nbytes
+            b0, b1 = offsets[b.name], offsets[b.name] + b.nbytes
+            if a0 < b1 and b0 < a1:
+                raise AssertionError(f"arena overlap: {a.name} and {b.name}")
+
+
+class DeviceNetwork:
+    """A nnr_b200.resnet50.QModel prepared on one device."""
+
+    def __init__(self, model, device: int = 0, reuse: bool = True):
+        import torch
+        from . import ops
+        from ._lib import ConvDesc, call  # noqa: F401
+
+        self.torch = torch
+        self.model = model
+        self.device = device
+        ops.init(device)
+        self.dev = torch.device("cuda", device)
+        self.ops = []      # per node: prepared operator or None
+        self.ws = []       # per node: workspace bytes
+        qp = model.qparams
+        for nd in model.nodes:
+            a = nd.attrs
+            if nd.op == "QLinearConv":
+                x = nd.inputs[0]
+                shp = model.shapes[x]
+                lay = a["in_layout"]
+                logical = shp if lay == "NCHW" else (shp[0], shp[3], shp[1], shp[2])
+                xq, yq = qp[x], qp[nd.output]
+                op = ops.QLinearConv(logical, a["w"], a["w_scale"], None, a["bias"], xq.scale, xq.zp, yq.scale, yq.zp,
+                                     strides=(a["stride"],) * 2, pads=(a["pad"],) * 4, in_layout=lay,
+                                     out_layout="NHWC", requant=a["requant"])
+                self.ops.append(op)
+                self.ws.append(op.workspace_size())
+            elif nd.op == "QLinearMatMul":
+                xq, yq = qp[nd.inputs[0]], qp[nd.output]
+                op = ops.QLinearMatMul(model.shapes[nd.inputs[0]][0], a["b"], xq.scale, xq.zp, a["b_scale"],
+                                       a["b_zp"], yq.scale, yq.zp)
+                self.ops.append(op)
+                self.ws.append(op.workspace_size())
+            else:
+                self.ops.append(None)
+                self.ws.append(0)
+        self.bias = {}
+        for i, nd in enumerate(model.nodes):
+            if nd.op == "DequantizeLinear" and nd.attrs.get("bias") is not None:
+                self.bias[i] = torch.from_numpy(np.ascontiguousarray(nd.attrs["bias"], np.float32)).to(self.dev)
+        self._plan(reuse)
+        self.stream = torch.cuda.Stream(device=self.dev)
+        self.graph_exec = None
+
+    # ------------------------------------------------------------------ memory
+    def _nbytes(self, name: str) -> int:
+        elem = 4 if name in ("input", "logits") else 1
+        return int(np.prod(self.model.shapes[name])) * elem
+
+    def _plan(self, reuse: bool = True):
+        nodes = self.model.nodes
+        first: Dict[str, int] = {"input": -1}
+        last: Dict[str, int] = {}
+        for i, nd in enumerate(nodes):
+            first.setdefault(nd.output, i)
+            for x in nd.inputs:
+                last[x] = i
+        last["logits"] = len(nodes)  # graph output lives to the end
+        items = [Interval(name, self._nbytes(name), first[name], last.get(name, first[name])) for name in first]
+        items += [Interval(f"ws{i}", b, i, i) for i, b in enumerate(self.ws) if b]
+        if not reuse:  # every tensor keeps its own slot (for inspecting intermediates)
+            items = [Interval(it.name, it.nbytes, -1, len(nodes)) for it in items]
+        self.offsets, self.arena_bytes = plan_arena(items)
+        check_plan(items, self.offsets)
+        self.intervals = items
+        self.arena = self.torch.empty(max(self.arena_bytes, ALIGN), dtype=self.torch.uint8, device=self.dev)
+        base = self.arena.data_ptr()
+        self.ptr = {k: base + v for k, v in self.offsets.items()}
+
+    def view(self, name: str):
+        """A torch view of a tensor's arena slot (for inputs and inspection)."""
+        t = self.torch
+        shape = self.model.shapes[name]
+        dtype = t.float32 if name in ("input", "logits") else t.uint8
+        off = self.offsets[name]
+        return self.arena[off:off + self._nbytes(name)].view(dtype).view(shape)
+
+    # ------------------------------------------------------------------ execution
+    def run(self, stream=None) -> None:
+        """Enqueues every node on the stream (no synchronisation)."""
+        from ._lib import LAYOUT_NCHW, call
+        st = C.c_void_p(self.stream.cuda_stream if stream is None else stream)
+        qp, m, P = self.model.qparams, self.model, self.ptr
+        for i, nd in enumerate(m.nodes):
+            a = nd.attrs
+            out = C.c_void_p(P[nd.output])
+            if nd.op == "QuantizeLinear":
+                n, c, h, w = m.shapes[nd.inputs[0]]
+                q = qp[nd.output]
+                call("nnrcu_quantize_linear_u8", C.c_void_p(P[nd.inputs[0]]), out, n, c, h, w, q.scale, q.zp,
+                     LAYOUT_NCHW, 0, st)
+            elif nd.op in ("QLinearConv", "QLinearMatMul"):
+                ws = C.c_void_p(P[f"ws{i}"]) if self.ws[i] else None
+                fn = "nnrcu_qlinearconv_run" if nd.op == "QLinearConv" else "nnrcu_qlinearmatmul_run"
+                call(fn, self.ops[i]._op, C.c_void_p(P[nd.inputs[0]]), out, ws, st)
+            elif nd.op == "MaxPool":
+                n, h, w, c = m.shapes[nd.inputs[0]]
+                k, s, p = a["k"], a["s"], a["pad"]
+                call("nnrcu_maxpool_u8_nhwc", C.c_void_p(P[nd.inputs[0]]), out, n, h, w, c, k, k, s, s, p, p, p, p, st)
+            elif nd.op == "QLinearAdd":
+                qa, qb, qy = qp[nd.inputs[0]], qp[nd.inputs[1]], qp[nd.output]
+                call("nnrcu_qlinearadd_u8", C.c_void_p(P[nd.inputs[0]]), qa.scale, qa.zp, C.c_void_p(P[nd.inputs[1]]),
+                     qb.scale, qb.zp, qy.scale, qy.zp, out, int(np.prod(m.shapes[nd.output])), st)
+            elif nd.op == "DqGapQ":
+                n, h, w, c = m.shapes[nd.inputs[0]]
+                qx, qy = qp[nd.inputs[0]], qp[nd.output]
+                call("nnrcu_dq_gap_q_u8_nhwc", C.c_void_p(P[nd.inputs[0]]), n, h * w, c, qx.scale, qx.zp, qy.scale,
+                     qy.zp, out, st)
+            elif nd.op == "DequantizeLinear":
+                rows, cols = m.shapes[nd.inputs[0]]
+                qx = qp[nd.inputs[0]]
+                b = C.c_void_p(self.bias[i].data_ptr()) if i in self.bias else None
+                call("nnrcu_dequantize_linear_u8", C.c_void_p(P[nd.inputs[0]]), qx.scale, qx.zp, b, rows, cols, out, st)
+            else:
+                raise ValueError(f"unknown node {nd.op}")
+
+    def capture(self) -> None:
+        """Records run() once into a CUDA graph (nnrcu_graph_begin/_end)."""
+        from ._lib import call
+        self.run()           # first launches outside capture (module load, attribute set-up)
+        self.stream.synchronize()
+        st = C.c_void_p(self.stream.cuda_stream)
+        call("nnrcu_graph_begin", st)
+        try:
+            self.run()
+        finally:
+            g = C.c_void_p()
+            call("nnrcu_graph_end", st, C.byref(g))
+        self.graph_exec = g
+
+    def launch(self) -> None:
+        """One forward pass: the captured graph if any, else the node loop."""
+        from ._lib import call
+        if self.graph_exec is not None:
+            call("nnrcu_graph_launch", self.graph_exec, C.c_void_p(self.stream.cuda_stream))
+        else:
+            self.run()
+
+    def forward(self, x_host, out_host=None):
+        """Host fp32 NCHW input -> host fp32 logits: H2D, one forward, D2H."""
+        t = self.torch
+        xin = self.view("input")
+        with t.cuda.stream(self.stream):
+            xin.copy_(x_host, non_blocking=True)
+            self.launch()
+            if out_host is None:
+                out_host = t.empty(self.model.shapes["logits"], dtype=t.float32, pin_memory=True)
+            out_host.copy_(self.view("logits"), non_blocking=True)
+        return out_host
+
+    def close(self):
+        from ._lib import lib
+        if self.graph_exec is not None:
+            lib.nnrcu_graph_destroy(self.graph_exec)
+            self.graph_exec = None
+        for op in self.ops:
+            if op is not None:
+                op.close()

@@ -324,3 +324,103 @@ int oracle_num_threads(void) {
   return 1;
 #endif
 }
+
+/* ------------------------------------------------------------------ QDQ glue (int8 networks) */
+
+static inline uint8_t sat_u8(int v) { return (uint8_t)(v < 0 ? 0 : (v > 255 ? 255 : v)); }
+
+/* QuantizeLinear fp32 -> u8, per tensor (QuantizeLinear.cpp:128-160). Element
+ * i in the 16-wide body: rne(x * (1/scale)) + zp, min 255 then max 0; the
+ * final partial 16-group (and tensors under 64 elements): nearbyint(x/scale)
+ * + zp, integer clamp. x and y share the element order. */
+int oracle_quantize_u8(const float* x, uint8_t* y, long long total, float scale, uint8_t zp) {
+  const float inv = 1.0f / scale;
+  const long long vec_end = total >= 64 ? total / 16 * 16 : 0;
+  for (long long i = 0; i < total; ++i) {
+    if (i < vec_end) {
+      float f = nearbyintf(x[i] * inv) + (float)zp;
+      f = fmaxf(fminf(f, 255.0f), 0.0f);
+      y[i] = (uint8_t)(int)f;
+    } else {
+      y[i] = sat_u8((int)nearbyintf(x[i] / scale) + zp);
+    }
+  }
+  return ORACLE_OK;
+}
+
+/* MaxPool on u8 NHWC (MaxPool.cpp:279): padding skipped. */
+int oracle_maxpool_u8_nhwc(const uint8_t* x, uint8_t* y, int n, int h, int w, int c, int kh, int kw, int sh, int sw,
+                           int pt, int pl, int pb, int pr) {
+  const int oh = out_dim(h, pt, pb, kh, sh, 1), ow = out_dim(w, pl, pr, kw, sw, 1);
+  if (oh <= 0 || ow <= 0) return ORACLE_ERR;
+  for (int img = 0; img < n; ++img)
+    for (int oy = 0; oy < oh; ++oy)
+      for (int ox = 0; ox < ow; ++ox)
+        for (int ch = 0; ch < c; ++ch) {
+          int m = 0;
+          for (int a = 0; a < kh; ++a) {
+            const int iy = oy * sh - pt + a;
+            if (iy < 0 || iy >= h) continue;
+            for (int b = 0; b < kw; ++b) {
+              const int ix = ox * sw - pl + b;
+              if (ix < 0 || ix >= w) continue;
+              const int t = x[(((size_t)img * h + iy) * w + ix) * c + ch];
+              if (t > m) m = t;
+            }
+          }
+          y[(((size_t)img * oh + oy) * ow + ox) * c + ch] = (uint8_t)m;
+        }
+  return ORACLE_OK;
+}
+
+/* QLinearAdd, same shape (QLinearAdd.cpp:46-104). sa = a_s/y_s, sb = b_s/y_s,
+ * fixed = y_zp - (sa*a_zp + sb*b_zp) as GCC contracts it with FMA
+ * (fma(sa, a_zp, sb*b_zp)). Body: v = fma(a, sa, fma(b, sb, fixed)), rne,
+ * max 0, unsigned saturate. Tail (final n % 16):
+ * fma(sa, a - a_zp, sb*(b - b_zp)) + y_zp, nearbyint, clamp. */
+int oracle_qlinearadd_u8(const uint8_t* a, float a_scale, uint8_t a_zp, const uint8_t* b, float b_scale, uint8_t b_zp,
+                         float y_scale, uint8_t y_zp, uint8_t* y, long long n) {
+  const float sa = a_scale / y_scale, sb = b_scale / y_scale;
+  const float fixed = (float)y_zp - fmaf(sa, (float)a_zp, sb * (float)b_zp);
+  const long long vec_end = n / 16 * 16;
+  for (long long i = 0; i < n; ++i) {
+    if (i < vec_end) {
+      float v = fmaf((float)b[i], sb, fixed);
+      v = fmaf((float)a[i], sa, v);
+      y[i] = sat_u8((int)nearbyintf(v));
+    } else {
+      const float da = (float)((int)a[i] - a_zp), db = (float)((int)b[i] - b_zp);
+      y[i] = sat_u8((int)nearbyintf(fmaf(sa, da, sb * db) + (float)y_zp));
+    }
+  }
+  return ORACLE_OK;
+}
+
+/* DequantizeLinear -> GlobalAveragePool (NHWC, per-channel sum from 0 over
+ * the spatial positions in order, times 1/spatial; kernel/pool.h:109-125)
+ * -> QuantizeLinear, on u8 [n, hw, c] -> u8 [n, c]. */
+int oracle_dq_gap_q_u8_nhwc(const uint8_t* x, int n, int hw, int c, float xs, uint8_t xzp, float ys, uint8_t yzp,
+                            uint8_t* y) {
+  const float inv_hw = 1.0f / (float)hw;
+  float* v = (float*)malloc(sizeof(float) * (size_t)n * c);
+  if (!v) return ORACLE_ERR;
+  for (int img = 0; img < n; ++img)
+    for (int ch = 0; ch < c; ++ch) {
+      float sum = 0.0f;
+      for (int s = 0; s < hw; ++s) sum += ((float)x[((size_t)img * hw + s) * c + ch] - (float)xzp) * xs;
+      v[(size_t)img * c + ch] = sum * inv_hw;
+    }
+  const int rc = oracle_quantize_u8(v, y, (long long)n * c, ys, yzp);
+  free(v);
+  return rc;
+}
+
+/* DequantizeLinear of u8 [rows, cols] then + bias[cols] (fp32 Add). */
+int oracle_dequantize_u8(const uint8_t* x, float scale, uint8_t zp, const float* bias, int rows, int cols, float* y) {
+  for (long long i = 0; i < (long long)rows * cols; ++i) {
+    float v = ((float)x[i] - (float)zp) * scale;
+    if (bias) v = v + bias[i % cols];
+    y[i] = v;
+  }
+  return ORACLE_OK;
+}

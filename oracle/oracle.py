@@ -177,3 +177,94 @@ def ref_qlinearconv_direct(x, w, w_scale, bias, x_scale, x_zp, y_scale, y_zp, st
 
 def num_threads() -> int:
     return lib().oracle_num_threads()
+
+
+# ------------------------------------------------------------------ QDQ glue
+def quantize_u8(x, scale, zp):
+    x = np.ascontiguousarray(x, np.float32)
+    y = np.empty(x.shape, np.uint8)
+    lib().oracle_quantize_u8(_p(x), _p(y), C.c_longlong(x.size), _f(scale), C.c_uint8(zp))
+    return y
+
+
+def maxpool_u8_nhwc(x, k=3, s=2, pads=(1, 1, 1, 1)):
+    x = np.ascontiguousarray(x, np.uint8)
+    n, h, w, c = x.shape
+    oh = (h + pads[0] + pads[2] - k) // s + 1
+    ow = (w + pads[1] + pads[3] - k) // s + 1
+    y = np.empty((n, oh, ow, c), np.uint8)
+    rc = lib().oracle_maxpool_u8_nhwc(_p(x), _p(y), n, h, w, c, k, k, s, s, *pads)
+    if rc != 0:
+        raise RuntimeError("oracle_maxpool_u8_nhwc failed")
+    return y
+
+
+def qlinearadd_u8(a, a_scale, a_zp, b, b_scale, b_zp, y_scale, y_zp):
+    a = np.ascontiguousarray(a, np.uint8)
+    b = np.ascontiguousarray(b, np.uint8)
+    y = np.empty(a.shape, np.uint8)
+    lib().oracle_qlinearadd_u8(_p(a), _f(a_scale), C.c_uint8(a_zp), _p(b), _f(b_scale), C.c_uint8(b_zp),
+                               _f(y_scale), C.c_uint8(y_zp), _p(y), C.c_longlong(a.size))
+    return y
+
+
+def dq_gap_q_u8_nhwc(x, x_scale, x_zp, y_scale, y_zp):
+    x = np.ascontiguousarray(x, np.uint8)
+    n, h, w, c = x.shape
+    y = np.empty((n, c), np.uint8)
+    rc = lib().oracle_dq_gap_q_u8_nhwc(_p(x), n, h * w, c, _f(x_scale), C.c_uint8(x_zp), _f(y_scale),
+                                       C.c_uint8(y_zp), _p(y))
+    if rc != 0:
+        raise RuntimeError("oracle_dq_gap_q_u8_nhwc failed")
+    return y
+
+
+def dequantize_u8(x, scale, zp, bias=None):
+    x = np.ascontiguousarray(x, np.uint8)
+    rows, cols = x.shape
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    y = np.empty(x.shape, np.float32)
+    lib().oracle_dequantize_u8(_p(x), _f(scale), C.c_uint8(zp), _p(b), rows, cols, _p(y))
+    return y
+
+
+# ------------------------------------------------------------------ whole int8 network
+def run_qmodel(model, x, keep=False):
+    """Runs a quantised network (nnr_b200.resnet50.QModel) node by node on the
+    CPU with the restated operators. x: fp32 NCHW input. Returns the fp32
+    logits, plus every intermediate tensor when keep is set."""
+    t = {"input": np.ascontiguousarray(x, np.float32)}
+    qp = model.qparams
+    for nd in model.nodes:
+        a = nd.attrs
+        if nd.op == "QuantizeLinear":
+            t[nd.output] = quantize_u8(t[nd.inputs[0]], qp[nd.output].scale, qp[nd.output].zp)
+        elif nd.op == "QLinearConv":
+            xin = t[nd.inputs[0]]
+            xq, yq = qp[nd.inputs[0]], qp[nd.output]
+            t[nd.output] = qlinearconv(xin, a["w"], a["w_scale"], a["bias"], xq.scale, xq.zp, yq.scale, yq.zp,
+                                       strides=(a["stride"],) * 2, pads=(a["pad"],) * 4, formula=a["requant"],
+                                       in_layout=a["in_layout"], out_layout="NHWC")
+        elif nd.op == "MaxPool":
+            t[nd.output] = maxpool_u8_nhwc(t[nd.inputs[0]], a["k"], a["s"], (a["pad"],) * 4)
+        elif nd.op == "QLinearAdd":
+            qa, qb, qy = qp[nd.inputs[0]], qp[nd.inputs[1]], qp[nd.output]
+            t[nd.output] = qlinearadd_u8(t[nd.inputs[0]], qa.scale, qa.zp, t[nd.inputs[1]], qb.scale, qb.zp,
+                                         qy.scale, qy.zp)
+        elif nd.op == "DqGapQ":
+            qx, qy = qp[nd.inputs[0]], qp[nd.output]
+            t[nd.output] = dq_gap_q_u8_nhwc(t[nd.inputs[0]], qx.scale, qx.zp, qy.scale, qy.zp)
+        elif nd.op == "QLinearMatMul":
+            qa, qy = qp[nd.inputs[0]], qp[nd.output]
+            t[nd.output] = qlinearmatmul(t[nd.inputs[0]], a["b"], qa.scale, qa.zp, a["b_scale"], a["b_zp"],
+                                         qy.scale, qy.zp)
+        elif nd.op == "DequantizeLinear":
+            qx = qp[nd.inputs[0]]
+            t[nd.output] = dequantize_u8(t[nd.inputs[0]], qx.scale, qx.zp, a.get("bias"))
+        else:
+            raise ValueError(f"unknown node {nd.op}")
+        if not keep:
+            for name in nd.inputs:
+                if name != "input" and all(name not in n2.inputs for n2 in model.nodes[model.nodes.index(nd) + 1:]):
+                    t.pop(name, None)
+    return (t["logits"], t) if keep else t["logits"]

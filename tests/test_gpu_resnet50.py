@@ -1,0 +1,51 @@
+"""ResNet-50 v1 QDQ int8 end to end on the device vs the
+CPU oracle: the fp32 logits after the last DequantizeLinear + Add must be
+identical (every op on the path is integer or performs nnr's float
+operations in nnr's order), and so must every intermediate u8 tensor."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def model4():
+    from nnr_b200 import resnet50
+    return resnet50.build(batch=4)
+
+
+def test_resnet50_qdq_bit_exact(cuda_dev, model4):
+    from nnr_b200 import graph, ops, resnet50
+    x = resnet50.input_batch(0, 4)
+    ref, tensors = O.run_qmodel(model4, x, keep=True)
+    net = graph.DeviceNetwork(model4, 0, reuse=False)
+    net.view("input").copy_(torch.from_numpy(x))
+    net.run()
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    for nd in model4.nodes:  # first divergent layer, if any
+        if nd.output == "logits":
+            continue
+        got = net.view(nd.output).cpu().numpy()
+        want = tensors[nd.output]
+        assert np.array_equal(got, want), f"{nd.op} {nd.output}: {(got != want).sum()} of {want.size} differ"
+    got = net.view("logits").cpu().numpy()
+    assert np.array_equal(got, ref)
+
+
+def test_resnet50_graph_replay_and_host_path(cuda_dev, model4):
+    """Captured CUDA graph + host input/output path give the same logits."""
+    from nnr_b200 import graph, resnet50
+    x = resnet50.input_batch(4, 4)
+    ref = O.run_qmodel(model4, x)
+    net = graph.DeviceNetwork(model4, 0)
+    net.capture()
+    xh = torch.from_numpy(x).pin_memory()
+    for _ in range(2):
+        out = net.forward(xh)
+        net.stream.synchronize()
+        assert np.array_equal(out.numpy(), ref)
+    net.close()
