@@ -64,6 +64,47 @@ __global__ void nchw_to_nhwc_u8_vec_kernel(const uint8_t* __restrict src, uint8_
   }
 }
 
+// Explicit im2col for small-channel convs (the 3-channel stem): row m (output
+// pixel) of A[M][kp] holds x[(kh, kw, ic)] densely, k = (kh*KW + kw)*C + ic;
+// padding pixels hold x_zp, k >= KH*KW*C holds 0. Input NCHW or NHWC u8.
+// One thread writes 16 bytes of one row.
+__global__ void im2col_u8_kernel(const uint8_t* __restrict x, uint8_t* __restrict a, int nchw, int n, int c, int h,
+                                 int w, int oh, int ow, int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw,
+                                 int kp, uint8_t x_zp) {
+  const int chunks = kp / 16;
+  const long long total = (long long)n * oh * ow * chunks;
+  const int kreal = kh * kw * c;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const long long m = i / chunks;
+    const int ck = (int)(i - m * chunks);
+    const int img = (int)(m / ((long long)oh * ow));
+    const int p = (int)(m - (long long)img * oh * ow);
+    const int oy = p / ow, ox = p - oy * ow;
+    uint32_t wv[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t word = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int k = ck * 16 + q * 4 + b;
+        uint32_t v = 0;
+        if (k < kreal) {
+          const int tap = k / c, ic = k - tap * c;
+          const int ky = tap / kw, kx = tap - ky * kw;
+          const int iy = oy * sh - pt + ky * dh, ix = ox * sw - pl + kx * dw;
+          if ((unsigned)iy < (unsigned)h && (unsigned)ix < (unsigned)w)
+            v = nchw ? x[(((size_t)img * c + ic) * h + iy) * w + ix] : x[(((size_t)img * h + iy) * w + ix) * c + ic];
+          else
+            v = x_zp;
+        }
+        word |= v << (8 * b);
+      }
+      wv[q] = word;
+    }
+    reinterpret_cast<uint4*>(a + (size_t)m * kp)[ck] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  }
+}
+
 __global__ void pad_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, long long pixels, int c,
                                    int cs, uint8_t fill) {
   const long long total = pixels * cs;
@@ -239,6 +280,95 @@ __global__ void depthwise_f32_kernel(const float* __restrict x, const float* __r
   }
 }
 
+// Explicit im2col of one output row (oy) of one image per block: the kh input
+// rows it needs (all c channels, full width, x_zp outside the image) are first
+// staged in shared memory with coalesced reads, then rows of A are written as
+// 16-byte chunks. NCHW or NHWC input; smem = c * kh * w bytes.
+__global__ void im2col_rows_u8_kernel(const uint8_t* __restrict x, uint8_t* __restrict a, int nchw, int c, int h,
+                                      int w, int oh, int ow, int kh, int kw, int sh, int sw, int pt, int pl, int dh,
+                                      int dw, int kp, uint8_t x_zp) {
+  extern __shared__ uint8_t smem_dyn[];
+  // per-k table: row offset (ic * kh + ky) * w into the staged rows (-1 for the
+  // K padding) and the tap's column offset kx * dw
+  int* koff = reinterpret_cast<int*>(smem_dyn);
+  int* kcol = koff + kp;
+  uint8_t* rows = reinterpret_cast<uint8_t*>(kcol + kp);  // [c][kh][w]
+  const int oy = blockIdx.x, img = blockIdx.y;
+  const int kreal = kh * kw * c;
+  for (int k = threadIdx.x; k < kp; k += blockDim.x) {
+    if (k < kreal) {
+      const int tap = k / c, ic = k - tap * c;
+      const int ky = tap / kw, kx = tap - ky * kw;
+      koff[k] = (ic * kh + ky) * w;
+      kcol[k] = kx * dw;
+    } else {
+      koff[k] = -1;
+      kcol[k] = 0;
+    }
+  }
+  const int nwarps = blockDim.x >> 5, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // stage the c * kh input rows (warp per row, lanes along the row)
+  for (int rr = warp; rr < c * kh; rr += nwarps) {
+    const int ic = rr / kh, r = rr - ic * kh;
+    const int iy = oy * sh - pt + r * dh;
+    uint8_t* dstrow = rows + rr * w;
+    if ((unsigned)iy >= (unsigned)h) {
+      for (int ix = lane; ix < w; ix += 32) dstrow[ix] = x_zp;
+    } else if (nchw) {
+      const uint8_t* src = x + (((size_t)img * c + ic) * h + iy) * w;
+      if ((w & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 3) == 0) {
+        for (int q = lane; q < (w >> 2); q += 32)
+          reinterpret_cast<uint32_t*>(dstrow)[q] = reinterpret_cast<const uint32_t*>(src)[q];
+      } else {
+        for (int ix = lane; ix < w; ix += 32) dstrow[ix] = src[ix];
+      }
+    } else {
+      const uint8_t* src = x + (((size_t)img * h + iy) * w) * c + ic;
+      for (int ix = lane; ix < w; ix += 32) dstrow[ix] = src[(size_t)ix * c];
+    }
+  }
+  __syncthreads();
+  // Rows of A are assembled in shared memory (row pitch kp + 16 to spread
+  // banks). Each warp owns fixed 16-byte K chunks and keeps their table
+  // entries in registers while its lanes sweep the output pixels; the
+  // block's contiguous output is then copied out coalesced.
+  const int chunks = kp / 16;
+  const int pitch = kp + 16;
+  uint8_t* sout = rows + ((c * kh * w + 15) & ~15);
+  for (int ck = warp; ck < chunks; ck += nwarps) {
+    int toff[16], tcol[16];
+#pragma unroll
+    for (int b = 0; b < 16; ++b) {
+      toff[b] = koff[ck * 16 + b];
+      tcol[b] = kcol[ck * 16 + b];
+    }
+    for (int ox = lane; ox < ow; ox += 32) {
+      const int ix0 = ox * sw - pl;
+      uint32_t wv[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int off = toff[q * 4 + b];
+          const int ix = ix0 + tcol[q * 4 + b];
+          uint32_t v = 0;
+          if (off >= 0) v = (unsigned)ix < (unsigned)w ? rows[off + ix] : x_zp;
+          word |= v << (8 * b);
+        }
+        wv[q] = word;
+      }
+      *reinterpret_cast<uint4*>(sout + ox * pitch + ck * 16) = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+    }
+  }
+  __syncthreads();
+  uint4* dst = reinterpret_cast<uint4*>(a + ((size_t)img * oh + oy) * ow * kp);
+  for (int i = threadIdx.x; i < ow * chunks; i += blockDim.x) {
+    const int ox = i / chunks, ck = i - ox * chunks;
+    dst[i] = *reinterpret_cast<const uint4*>(sout + ox * pitch + ck * 16);
+  }
+}
+
 int grid_for(long long total, int threads) {
   long long b = (total + threads - 1) / threads;
   const long long cap = (long long)num_sms() * 16;
@@ -280,6 +410,22 @@ int launch_nchw_to_nhwc_u8_padded(const uint8_t* src, uint8_t* dst, int n, int c
   NNRCU_CUDA(cudaMemsetAsync(dst, fill, (size_t)n * hp * wp * cs, st));
   dim3 grid((h * w + 127) / 128, (cs + 63) / 64, n);
   nchw_to_nhwc_u8_vec_kernel<<<grid, 256, 0, st>>>(src, dst, c, w, h * w, hp, wp, pt, pl, cs, fill);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_im2col_u8(const uint8_t* x, uint8_t* a, int nchw, int n, int c, int h, int w, int oh, int ow, int kh,
+                     int kw, int sh, int sw, int pt, int pl, int dh, int dw, int kp, uint8_t x_zp, cudaStream_t st) {
+  const size_t smem = (size_t)kp * 8 + (((size_t)c * kh * w + 15) & ~(size_t)15) + (size_t)ow * (kp + 16);
+  if (smem <= 48 * 1024 && n <= 65535) {
+    im2col_rows_u8_kernel<<<dim3(oh, n), 256, smem, st>>>(x, a, nchw, c, h, w, oh, ow, kh, kw, sh, sw, pt, pl, dh, dw,
+                                                          kp, x_zp);
+    NNRCU_CUDA(cudaGetLastError());
+    return NNRCU_OK;
+  }
+  const long long total = (long long)n * oh * ow * (kp / 16);
+  im2col_u8_kernel<<<grid_for(total, 256), 256, 0, st>>>(x, a, nchw, n, c, h, w, oh, ow, kh, kw, sh, sw, pt, pl, dh, dw,
+                                                          kp, x_zp);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

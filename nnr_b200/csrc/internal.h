@@ -58,7 +58,8 @@ struct Op {
   int oh = 0, ow = 0;
   int cs = 0;                   // device channel stride (elements) of the NHWC operand
   bool need_in_copy = false;    // input must be re-laid-out into the workspace first
-  bool pad_in = false;          // ... spatially padded with x_zp (im2col path with x_zp != 0)
+  bool pad_in = false;
+  bool explicit_im2col = false; // small-C conv: A materialised densely as [M][kpad] in the workspace          // ... spatially padded with x_zp (im2col path with x_zp != 0)
   // device buffers (owned)
   void* wB = nullptr;
   int32_t* colcorr = nullptr;
@@ -108,6 +109,8 @@ int launch_nchw_to_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int c, int h
                            cudaStream_t st);
 int launch_nchw_to_nhwc_u8_padded(const uint8_t* src, uint8_t* dst, int n, int c, int h, int w, int pt, int pl,
                                   int pb, int pr, int cs, uint8_t fill, cudaStream_t st);
+int launch_im2col_u8(const uint8_t* x, uint8_t* a, int nchw, int n, int c, int h, int w, int oh, int ow, int kh,
+                     int kw, int sh, int sw, int pt, int pl, int dh, int dw, int kp, uint8_t x_zp, cudaStream_t st);
 int launch_pad_nhwc_u8(const uint8_t* src, uint8_t* dst, int pixels, int c, int cs, uint8_t fill, cudaStream_t st);
 int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
                            int cs, cudaStream_t st);

@@ -130,9 +130,24 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   }
   op->kslab = op->amode == A_GATHER ? BKB : kslab;
   op->num_kb = (op->kbytes + op->kslab - 1) / op->kslab;
+  // Small-channel convs with a spatial kernel (the 3-channel stem): padding
+  // every pixel to a 16-byte channel stride would waste most of K and the
+  // gather would touch many taps per slab; materialise a dense im2col matrix
+  // [M][round_up(KH*KW*C, 64)] instead and feed it to the engine by TMA.
+  if (d.c < 16 && d.kh * d.kw > 1) {
+    op->explicit_im2col = true;
+    op->amode = A_TMA;
+    op->need_in_copy = false;
+    op->pad_in = false;
+    op->kslab = 64;
+    op->kbytes = round_up(d.kh * d.kw * d.c, 64);
+    op->kpad_bytes = round_up(op->kbytes, BKB);
+    op->num_kb = op->kbytes / 64;
+  }
   const size_t hp = d.h + (op->pad_in ? d.pad_top + d.pad_bottom : 0);
   const size_t wp = d.w + (op->pad_in ? d.pad_left + d.pad_right : 0);
   op->ws_bytes = op->need_in_copy ? (size_t)d.n * hp * wp * op->cs : 0;
+  if (op->explicit_im2col) op->ws_bytes = (size_t)op->M * op->kbytes;
 
   // Pack B = W as [npad][kpad] K-major with k = (kh, kw, ic); padded channels,
   // taps and rows are zero. wsum feeds the x_zp compensation.
@@ -146,7 +161,8 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
       for (int y = 0; y < d.kh; ++y)
         for (int x = 0; x < d.kw; ++x) {
           const int8_t v = w_host[(((size_t)o * d.c + ic) * d.kh + y) * d.kw + x];
-          B[(size_t)o * op->kpad_bytes + (size_t)(y * d.kw + x) * op->cs + ic] = v;
+          const int tap_stride = op->explicit_im2col ? d.c : op->cs;  // dense K for explicit im2col
+          B[(size_t)o * op->kpad_bytes + (size_t)(y * d.kw + x) * tap_stride + ic] = v;
           wsum += v;
         }
     colcorr[o] = (int32_t)(0u - (uint32_t)x_zp * (uint32_t)wsum);
@@ -192,7 +208,13 @@ int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* work
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const nnrcu_conv_desc& d = op->d;
   const uint8_t* xin = x;
-  if (op->need_in_copy) {
+  if (op->explicit_im2col) {
+    int rc = launch_im2col_u8(x, static_cast<uint8_t*>(workspace), d.in_layout == NNRCU_LAYOUT_NCHW, d.n, d.c, d.h,
+                              d.w, op->oh, op->ow, d.kh, d.kw, d.stride_h, d.stride_w, d.pad_top, d.pad_left, d.dil_h,
+                              d.dil_w, op->kbytes, (uint8_t)op->x_zp, st);
+    if (rc != NNRCU_OK) return rc;
+    xin = static_cast<const uint8_t*>(workspace);
+  } else if (op->need_in_copy) {
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     int rc = op->pad_in ? launch_nchw_to_nhwc_u8_padded(x, ws, d.n, d.c, d.h, d.w, d.pad_top, d.pad_left,
                                                          d.pad_bottom, d.pad_right, op->cs, (uint8_t)op->x_zp, st)
@@ -204,7 +226,8 @@ int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* work
   }
   CUtensorMap tmA{};
   if (op->amode == A_TMA) {
-    int rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, xin, op->cs, (uint64_t)op->M, op->cs, op->kslab, BM,
+    const int arow = op->explicit_im2col ? op->kbytes : op->cs;  // bytes per A row
+    int rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, xin, arow, (uint64_t)op->M, arow, op->kslab, BM,
                             op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
     if (rc != NNRCU_OK) return rc;
   }

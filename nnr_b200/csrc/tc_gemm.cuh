@@ -79,21 +79,23 @@ struct EpiParams {
   int* status;             // device status word (first error wins)
 };
 
-template <int BN, int NPLANE, int EPI, int KB = BKB>
+template <int BN, int NPLANE, int EPI, int KB = BKB, int SPLIT = 1>
 struct TileCfg {
   static constexpr int A_BYTES = BM * KB;              // 16 KB per plane (8 KB with 64-byte slabs)
   static constexpr int B_BYTES = BN * KB;
   static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + B_BYTES);
   // u8 epilogues stage each warp's 32 x BN output block for a TMA store
   static constexpr int OUT_BYTES = (EPI == EPI_F32) ? 0 : 4 * 32 * BN;
-  static constexpr int OUT_SEG = BN >= 128 ? 128 : 64;  // bytes per staged row segment (= TMA box width)
+  // Epilogue warps: 4 x SPLIT, each covering 32 TMEM lanes x BN / SPLIT columns.
+  static constexpr int HB = BN / SPLIT;
+  static constexpr int OUT_SEG = HB >= 128 ? 128 : HB;  // bytes per staged row segment (= TMA box width)
   static constexpr int STAGES_RAW = (200 * 1024 - OUT_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
   // Gather producers publish a stage LAG iterations after issuing it: LAG
   // stages of copies in flight, STAGES - 1 - LAG stages of slack for the MMA.
   static constexpr int LAG = (STAGES - 1) / 2 > 1 ? (STAGES - 1) / 2 : 1;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (power of two)
-  static constexpr int PARAM_BYTES = 4 /*epilogue warps*/ * 3 * BN * 4;
+  static constexpr int PARAM_BYTES = 4 * SPLIT /*epilogue warps*/ * 3 * HB * 4;
   static constexpr int SMEM_BYTES =
       1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + 256 /*barriers*/ + PARAM_BYTES;
   static_assert(STAGES >= 2, "need at least two pipeline stages");
@@ -176,7 +178,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY, int y_tma,
                int b_plane_rows, GatherGeom g, EpiParams e, int num_kb, int m_tiles, int n_tiles) {
-  using Cfg = TileCfg<BN, NPLANE, EPI, KB>;
+  // In TMA / im2col modes the gather warps 4-7 are free and join the epilogue:
+  // warps w and w + 4 drain the same 32 TMEM lanes, each half of the columns.
+  constexpr int SPLIT = (AMODE == A_GATHER) ? 1 : 2;
+  constexpr int HB = BN / SPLIT;
+  using Cfg = TileCfg<BN, NPLANE, EPI, KB, SPLIT>;
   static_assert(KB == BKB || AMODE != A_GATHER, "the gather producers fill 128-byte slabs");
   constexpr int STAGES = Cfg::STAGES;
   constexpr int A_BYTES = Cfg::A_BYTES;
@@ -198,9 +204,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   const int lane = threadIdx.x & 31;
   const int num_tiles = m_tiles * n_tiles;
   // per-column constants, one private copy per epilogue warp (no cross-warp sync)
-  int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + 256 + (warp & 3) * (3 * BN * 4));
-  float* s_f1 = reinterpret_cast<float*>(s_ci + BN);
-  float* s_f2 = s_f1 + BN;
+  int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + 256 +
+                                             (warp & (4 * SPLIT - 1)) * (3 * HB * 4));
+  float* s_f1 = reinterpret_cast<float*>(s_ci + HB);
+  float* s_f2 = s_f1 + HB;
 
   if (threadIdx.x == 0) {
     const uint32_t full_count = (AMODE == A_GATHER) ? (4u + 1u) : 1u;  // 4 gather warps + TMA
@@ -210,7 +217,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     }
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull_bar[a], 1);
-      ptx::mbar_init(&tempty_bar[a], 4);
+      ptx::mbar_init(&tempty_bar[a], 4 * SPLIT);
     }
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -321,7 +328,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       }
       if (aborted) ptx::settle_ns(200000);  // MMAs already issued finish before TMEM is freed
     }
-  } else if (warp >= 4) {
+  } else if (warp >= 4 && AMODE == A_GATHER) {
     // ------------------------------------------------------------ gather producers (warps 4-7)
     if constexpr (AMODE == A_GATHER) {
       // Thread t owns tile row t (one output pixel) and copies its whole
@@ -415,9 +422,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         for (int q = first; q < it; ++q) ptx::mbar_arrive(&full_bar[q % STAGES]);
       }
     }
-  } else {
-    // ------------------------------------------------------------ epilogue (warps 0-3)
-    const int row = warp * 32 + lane;  // TMEM lane == tile row
+  } else if (warp < 4 * SPLIT) {
+    // ------------------------------------------------------------ epilogue (warps 0-3, and 4-7 when SPLIT = 2)
+    const int eq = warp & 3;           // TMEM lane quarter
+    const int col0 = (warp >> 2) * HB; // this warp's columns [col0, col0 + HB) of the tile
+    const int row = eq * 32 + lane;    // TMEM lane == tile row
     int lt = 0;
     int cached_n0 = -1;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
@@ -427,8 +436,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       if (n0 != cached_n0) {
         // per-column constants of this column block (this warp's copy)
         __syncwarp();
-        for (int i = lane; i < BN; i += 32) {
-          const int n = n0 + i;
+        for (int i = lane; i < HB; i += 32) {
+          const int n = n0 + col0 + i;
           const bool ok = n < e.N;
           int32_t ci = (ok && e.colcorr) ? e.colcorr[n] : 0;
           float f1 = 0.0f, f2 = 0.0f;
@@ -454,7 +463,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       }
       ptx::tc_fence_after();
       // the staging block may be rewritten once the previous tile's stores have read it
-      uint8_t* const stg = sOut + warp * (32 * BN);
+      uint8_t* const stg = sOut + warp * (32 * HB);
       if (EPI != EPI_F32 && y_tma) {
         if (lane == 0) ptx::bulk_wait_read0();
         __syncwarp();
@@ -465,9 +474,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       if (EPI == EPI_R4 && e.rowcorr && mvalid) rowc = e.rowcorr[m];
       int img = 0, pix = 0;
       if (e.y_layout == 1 && mvalid) { img = m / e.ohw; pix = m - img * e.ohw; }
-      const uint32_t t_addr = tmem_base + ((uint32_t)(warp * 32) << 16) + (uint32_t)(acc * BN);
+      const uint32_t t_addr = tmem_base + ((uint32_t)(eq * 32) << 16) + (uint32_t)(acc * BN);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 32) {
+      for (int c0 = col0; c0 < col0 + HB; c0 += 32) {
+        const int pc = c0 - col0;  // column within this warp's parameter copy
         uint32_t v[32];
         ptx::tmem_ld32(t_addr + (uint32_t)c0, v);
         if (!mvalid || n0 + c0 >= e.N) continue;
@@ -487,7 +497,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
               const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
-                float a = __uint_as_float(v[j + u]) + s_f2[c0 + j + u];
+                float a = __uint_as_float(v[j + u]) + s_f2[pc + j + u];
                 if (e.res_mode == 1) a = fmaf(e.res_scale, rv[u], a);
                 a = apply_act(a, e.act, e.act_a, e.act_b);
                 if (e.res_mode == 2) a += rv[u];
@@ -502,7 +512,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
               const size_t idx = rowmajor ? (size_t)m * e.ldy + n0 + c0 + j
                                           : ((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix;
               const float rr = e.residual ? e.residual[idx] : 0.0f;
-              float a = __uint_as_float(v[j]) + s_f2[c0 + j];
+              float a = __uint_as_float(v[j]) + s_f2[pc + j];
               if (e.res_mode == 1) a = fmaf(e.res_scale, rr, a);
               a = apply_act(a, e.act, e.act_a, e.act_b);
               if (e.res_mode == 2) a += rr;
@@ -513,9 +523,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           uint32_t q[32];
 #pragma unroll
           for (int j = 0; j < 32; j += 4) {
-            const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + c0 + j);
-            const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + c0 + j);
-            const float4 b4 = *reinterpret_cast<const float4*>(s_f2 + c0 + j);
+            const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
+            const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
+            const float4 b4 = *reinterpret_cast<const float4*>(s_f2 + pc + j);
             q[j + 0] = requant_u8<EPI>((int32_t)v[j + 0], ci4.x, rowc, a4.x, b4.x, e);
             q[j + 1] = requant_u8<EPI>((int32_t)v[j + 1], ci4.y, rowc, a4.y, b4.y, e);
             q[j + 2] = requant_u8<EPI>((int32_t)v[j + 2], ci4.z, rowc, a4.z, b4.z, e);
@@ -530,8 +540,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             // swizzled staging (matches the store map's 128B / 64B swizzle):
             // row r, 16-byte chunk c of a segment lives at r*SEG + ((c ^ f(r)) << 4)
             constexpr int SEG = Cfg::OUT_SEG;
-            const int h = c0 / SEG, cc = (c0 % SEG) >> 4;
-            const int f = SEG == 128 ? (lane & 7) : ((lane >> 1) & 3);
+            const int h = pc / SEG, cc = (pc % SEG) >> 4;
+            const int f = SEG == 128 ? (lane & 7) : (SEG == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
             uint8_t* seg = stg + h * (32 * SEG) + lane * SEG;
             ptx::st_shared_v4(seg + ((cc ^ f) << 4), w[0], w[1], w[2], w[3]);
             ptx::st_shared_v4(seg + (((cc + 1) ^ f) << 4), w[4], w[5], w[6], w[7]);
@@ -562,9 +572,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         __syncwarp();
         if (lane == 0) {
           constexpr int SEG = Cfg::OUT_SEG;
-          if (m0 + warp * 32 < e.M)
-            for (int h = 0; h < BN / SEG; ++h)
-              if (n0 + h * SEG < e.N) ptx::tma_store_2d(&tmY, stg + h * (32 * SEG), n0 + h * SEG, m0 + warp * 32);
+          if (m0 + eq * 32 < e.M)
+            for (int h = 0; h < HB / SEG; ++h)
+              if (n0 + col0 + h * SEG < e.N)
+                ptx::tma_store_2d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEG, m0 + eq * 32);
           ptx::bulk_commit();
         }
       }

@@ -10,7 +10,7 @@ namespace {
 
 template <int BN, int NPLANE, int AMODE, int EPI, int KB = BKB>
 int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
-  using Cfg = TileCfg<BN, NPLANE, EPI, KB>;
+  using Cfg = TileCfg<BN, NPLANE, EPI, KB, (AMODE == A_GATHER ? 1 : 2)>;
   auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI, KB>;
   // The attribute is per function; setting it is cheap but not free, so do it
   // once per device.
@@ -30,7 +30,9 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
   if (EPI != EPI_F32 && e.y_layout == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 && (e.ldy & 15) == 0) {
     const int seg = Cfg::OUT_SEG;
     int rc = encode_tmap_2d(&tmY, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.y, (uint64_t)e.N, (uint64_t)e.M, (uint64_t)e.ldy,
-                            seg, 32, seg == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+                            seg, 32,
+                            seg == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                       : (seg == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B));
     if (rc != NNRCU_OK) return rc;
     y_tma = 1;
   }
@@ -52,6 +54,7 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
     } else {
       if (L.epi == EPI_R1) return launch_one<BN, 1, A_TMA, EPI_R1, 64>(L, g, e, st);
       if (L.epi == EPI_R2) return launch_one<BN, 1, A_TMA, EPI_R2, 64>(L, g, e, st);
+      if (L.epi == EPI_R3) return launch_one<BN, 1, A_TMA, EPI_R3, 64>(L, g, e, st);
       if (L.epi == EPI_R4) return launch_one<BN, 1, A_TMA, EPI_R4, 64>(L, g, e, st);
     }
     return set_error(NNRCU_ERR_INVALID, "no 64-byte-slab engine instance for amode %d epilogue %d", L.amode, L.epi);
