@@ -186,18 +186,8 @@ def reference_arm(args, rank, world):
 
 
 # ------------------------------------------------------------------ B200 arm
-def run_node(net, i):
-    """Enqueues tensor-core node i of the network alone (same operator, same
-    arena slots) on the network's stream."""
-    from nnr_b200._lib import call
-    nd = net.model.nodes[i]
-    st = C.c_void_p(net.stream.cuda_stream)
-    ws = C.c_void_p(net.ptr[f"ws{i}"]) if net.ws[i] else None
-    fn = "nnrcu_qlinearconv_run" if nd.op == "QLinearConv" else "nnrcu_qlinearmatmul_run"
-    call(fn, net.ops[i]._op, C.c_void_p(net.ptr[nd.inputs[0]]), C.c_void_p(net.ptr[nd.output]), ws, st)
-
-
 def node_ops(model, i):
+    """Algorithmic int8 ops (2 x MACs) of tensor-core node i."""
     nd = model.nodes[i]
     if nd.op == "QLinearConv":
         n, oh, ow, oc = model.shapes[nd.output]
@@ -273,7 +263,9 @@ def main():
     net.view("input").copy_(x_host)
     stream = net.stream
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    tc_nodes = [i for i, nd in enumerate(model.nodes) if nd.op in ("QLinearConv", "QLinearMatMul")]
+    # steps that launch the tcgen05 engine (conv, conv + fused add, matmul): (step, node)
+    tc_steps = [(t, st_[4]) for t, st_ in enumerate(net.steps) if st_[0] in ("QLinearConv", "QLinearMatMul", "QConvAdd")]
+    tc_nodes = [i for _, i in tc_steps]
 
     net.capture()
     for _ in range(args.warmup):
@@ -296,10 +288,10 @@ def main():
     def node_times(reps=3):
         evs = []
         for _ in range(reps):
-            for i in tc_nodes:
+            for t_, i in tc_steps:
                 e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 e0.record(stream)
-                run_node(net, i)
+                net.run_step(t_)
                 e1.record(stream)
                 evs.append((i, e0, e1))
         stream.synchronize()
@@ -364,11 +356,11 @@ def main():
                     "d2h_bytes_per_step": int(np.prod(model.shapes["logits"]) * 4)},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
                          "frac": round(achieved / peak, 4), "traffic": None,
-                         "kernel": "tc_gemm_kernel: all 53 QLinearConv + the QLinearMatMul of one forward",
+                         "kernel": "tc_gemm_kernel: all 53 QLinearConv (16 with the residual QLinearAdd fused) + the QLinearMatMul of one forward",
                          "kernel_ms_per_forward": round(k_ms, 4), "ops_per_forward": int(k_ops),
                          "conv3x3_tops": round(three_tops, 1), "peak_source": peak_note},
             "qlinearconv_config2": c2,
-            "gpu_launches": (len(model.nodes) + 1) * args.steps,  # 74 nodes + the stem input reorder
+            "gpu_launches": (len(net.steps) + 1) * args.steps,  # steps + the stem im2col
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline and world == 1:

@@ -122,6 +122,17 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
                              int n_w_scale, const int8_t* w_zp, int n_w_zp, const int32_t* bias_host,
                              float x_scale, uint8_t x_zp, float y_scale, uint8_t y_zp, nnrcu_op** op);
 int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream);
+/* QLinearConv followed by QLinearAdd(conv_out, residual) in one kernel: the
+ * conv output is requantised to u8 exactly as above, then combined with the
+ * u8 residual (same NHWC shape, scale res_scale, zero point res_zp) into y
+ * (out_scale, out_zp) with QLinearAdd's float sequence
+ * (backend/cpu/QLinearAdd.cpp:46-104). Results equal the two unfused
+ * operators; the conv output never reaches HBM. NHWC output only. (The
+ * reference's binary post-op fusion is unused, fuse_post_ops.cpp:67; this
+ * is its device form.) */
+int nnrcu_qlinearconv_run_add(nnrcu_op* op, const uint8_t* x, const uint8_t* residual, float res_scale,
+                              uint8_t res_zp, float out_scale, uint8_t out_zp, uint8_t* y, void* workspace,
+                              void* stream);
 
 /* ---------------------------------------------------------------- QLinearMatMul (u8 a, s8 b, u8 y)
  * Replaces QLinearMatMul_operator (backend/cpu/QLinearMatMul.cpp:33-232) for a 2-D B

@@ -74,6 +74,7 @@ struct Op {
   // requant scalars
   float inv_y = 0, yzp_f = 0, qmin_f = 0, qmax_f = 0, rq_lo = 0, rq_hi = 0, combined = 0;
   int yzp = 0;
+  float y_scale = 0;
   int x_zp = 0;
   int a_zp = 0, b_zp = 0;
   // fp32 post-op

@@ -183,6 +183,7 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   op->rq_lo = (float)lo - (float)y_zp;                       // QLinearConv_reshape.h:326-327
   op->rq_hi = (float)hi - (float)y_zp;
   op->yzp = y_zp;
+  op->y_scale = y_scale;
 
   void* wB = nullptr;
   NNRCU_TRY(cuda_check(cudaMalloc(&wB, B.size()), "cudaMalloc(weights)"));
@@ -200,7 +201,8 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   return NNRCU_OK;
 }
 
-int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream) {
+static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream, const uint8_t* res,
+                     float res_scale, uint8_t res_zp, float out_scale, uint8_t out_zp) {
   if (!op || op->kind != OP_QCONV) return set_error(NNRCU_ERR_INVALID, "not a QLinearConv operator");
   if (!x || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
   if (op->ws_bytes && !workspace)
@@ -261,6 +263,22 @@ int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* work
   e.ldy = d.oc;
   e.ohw = op->oh * op->ow;
   e.status = status_ptr();
+  if (res) {
+    if (d.out_layout != NNRCU_LAYOUT_NHWC)
+      return set_error(NNRCU_ERR_UNSUPPORTED, "a fused residual add needs an NHWC output");
+    if (!(out_scale > 0.0f)) return set_error(NNRCU_ERR_INVALID, "add output scale must be positive");
+    // QLinearAdd constants in nnr's order (QLinearAdd.cpp:46-66); GCC
+    // contracts sa*a_zp + sb*b_zp into fma(sa, a_zp, sb*b_zp)
+    e.qres = res;
+    e.qa_sa = op->y_scale / out_scale;
+    e.qa_sb = res_scale / out_scale;
+    e.qa_fixed = (float)out_zp - std::fma(e.qa_sa, (float)op->yzp, e.qa_sb * (float)res_zp);
+    e.qa_azp = op->yzp;
+    e.qa_bzp = res_zp;
+    e.qa_yzp = out_zp;
+    const long long n = (long long)op->M * op->N;
+    e.qa_vec_end = n / 16 * 16;
+  }
 
   TcLaunch L{};
   L.bn = op->bn; L.nplane = 1; L.amode = op->amode; L.epi = op->epi;
@@ -271,6 +289,17 @@ int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* work
   L.num_kb = op->num_kb;
   L.kb_bytes = op->kslab;
   return tc_launch(L, g, e, st);
+}
+
+int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream) {
+  return qconv_run(op, x, y, workspace, stream, nullptr, 0.0f, 0, 0.0f, 0);
+}
+
+int nnrcu_qlinearconv_run_add(nnrcu_op* op, const uint8_t* x, const uint8_t* residual, float res_scale,
+                              uint8_t res_zp, float out_scale, uint8_t out_zp, uint8_t* y, void* workspace,
+                              void* stream) {
+  if (!residual) return set_error(NNRCU_ERR_INVALID, "NULL residual");
+  return qconv_run(op, x, y, workspace, stream, residual, res_scale, res_zp, out_scale, out_zp);
 }
 
 int nnrcu_qlinearmatmul_create(int m, int k, int n, float a_scale, uint8_t a_zp, const int8_t* b_host, float b_scale,

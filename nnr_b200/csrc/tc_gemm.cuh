@@ -66,6 +66,12 @@ struct EpiParams {
   float rq_lo, rq_hi;                  // R2 clamp bounds (lo - y_zp, hi - y_zp)
   float combined;                      // R4 scalar scale a_s*b_s/y_s
   int yzp;                             // R2 integer zero point
+  // Fused QLinearAdd after the requant (u8 epilogues): y = QLinearAdd(q, qres)
+  // with qres laid out like y. Same float sequence as the standalone op.
+  const uint8_t* qres;                 // residual operand b, or null
+  float qa_sa, qa_sb, qa_fixed;        // a_s / y_s, b_s / y_s, y_zp - fma(sa, a_zp, sb * b_zp)
+  int qa_azp, qa_bzp, qa_yzp;
+  long long qa_vec_end;                // elements below use the 16-wide body, the rest the scalar tail
   // fp32 epilogue
   const float* bias;       // per-n bias or null
   const float* residual;   // same layout as y, or null
@@ -97,7 +103,7 @@ struct TileCfg {
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (power of two)
   static constexpr int PARAM_BYTES = 4 * SPLIT /*epilogue warps*/ * 3 * HB * 4;
   static constexpr int SMEM_BYTES =
-      1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + 256 /*barriers*/ + PARAM_BYTES;
+      1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + 512 /*barriers*/ + PARAM_BYTES;
   static_assert(STAGES >= 2, "need at least two pipeline stages");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -176,7 +182,8 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t 
 template <int BN, int NPLANE, int AMODE, int EPI, int KB>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
-               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY, int y_tma,
+               const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY,
+               const __grid_constant__ CUtensorMap tmR, int y_tma,
                int b_plane_rows, GatherGeom g, EpiParams e, int num_kb, int m_tiles, int n_tiles) {
   // In TMA / im2col modes the gather warps 4-7 are free and join the epilogue:
   // warps w and w + 4 drain the same 32 TMEM lanes, each half of the columns.
@@ -197,14 +204,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;                  // [2] accumulator ready
   uint64_t* tempty_bar = tfull_bar + 2;                      // [2] accumulator drained
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  uint64_t* res_bar = tempty_bar + 2;                        // [8] residual tile landed (per epilogue warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_tiles = m_tiles * n_tiles;
   // per-column constants, one private copy per epilogue warp (no cross-warp sync)
-  int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + 256 +
+  int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + 512 +
                                              (warp & (4 * SPLIT - 1)) * (3 * HB * 4));
   float* s_f1 = reinterpret_cast<float*>(s_ci + HB);
   float* s_f2 = s_f1 + HB;
@@ -215,6 +223,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       ptx::mbar_init(&full_bar[s], full_count);
       ptx::mbar_init(&empty_bar[s], 1);
     }
+    for (int a = 0; a < 8; ++a) ptx::mbar_init(&res_bar[a], 1);
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull_bar[a], 1);
       ptx::mbar_init(&tempty_bar[a], 4 * SPLIT);
@@ -457,16 +466,32 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         __syncwarp();
         cached_n0 = n0;
       }
+      // the staging block may be rewritten once the previous tile's stores have read it
+      uint8_t* const stg = sOut + warp * (32 * HB);
+      // fused residual add: the residual block lands in the staging buffer
+      // (same box and swizzle as the output store), loaded while the MMAs
+      // run, and is combined with the requantised tile in place
+      const bool res_tma = EPI != EPI_F32 && y_tma && e.qres != nullptr;
+      if (EPI != EPI_F32 && y_tma) {
+        if (lane == 0) {
+          ptx::bulk_wait_read0();
+          if (res_tma) {
+            constexpr int SEG = Cfg::OUT_SEG;
+            ptx::mbar_arrive_expect_tx(&res_bar[warp], 32 * HB);
+            for (int h = 0; h < HB / SEG; ++h)
+              ptx::tma_load_2d(stg + h * (32 * SEG), &tmR, &res_bar[warp], n0 + col0 + h * SEG, m0 + eq * 32);
+          }
+        }
+        __syncwarp();
+      }
       if (!__all_sync(0xffffffffu, ptx::mbar_wait(&tfull_bar[acc], use_ph, abort_flag))) {
         fail(ST_TIMEOUT_ACCUM);
         break;
       }
       ptx::tc_fence_after();
-      // the staging block may be rewritten once the previous tile's stores have read it
-      uint8_t* const stg = sOut + warp * (32 * HB);
-      if (EPI != EPI_F32 && y_tma) {
-        if (lane == 0) ptx::bulk_wait_read0();
-        __syncwarp();
+      if (res_tma && !__all_sync(0xffffffffu, ptx::mbar_wait(&res_bar[warp], (uint32_t)lt & 1u, abort_flag))) {
+        fail(ST_TIMEOUT_ACCUM);
+        break;
       }
       const int m = m0 + row;
       const bool mvalid = m < e.M;
@@ -530,6 +555,49 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             q[j + 1] = requant_u8<EPI>((int32_t)v[j + 1], ci4.y, rowc, a4.y, b4.y, e);
             q[j + 2] = requant_u8<EPI>((int32_t)v[j + 2], ci4.z, rowc, a4.z, b4.z, e);
             q[j + 3] = requant_u8<EPI>((int32_t)v[j + 3], ci4.w, rowc, a4.w, b4.w, e);
+          }
+          if (e.qres) {
+            // QLinearAdd(q, residual) (QLinearAdd.cpp:46-104): body
+            // fma(a, sa, fma(b, sb, fixed)), rne, saturate; tail elements
+            // fma(sa, a - a_zp, sb * (b - b_zp)) + y_zp.
+            const uint8_t* rp = e.qres + (size_t)m * e.ldy + n0 + c0;
+            uint8_t rb[32];
+            if (res_tma) {
+              constexpr int SEG = Cfg::OUT_SEG;
+              const int h = pc / SEG, cc = (pc % SEG) >> 4;
+              const int f = SEG == 128 ? (lane & 7) : (SEG == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
+              const uint8_t* seg = stg + h * (32 * SEG) + lane * SEG;
+              *reinterpret_cast<uint4*>(rb) = *reinterpret_cast<const uint4*>(seg + ((cc ^ f) << 4));
+              *reinterpret_cast<uint4*>(rb + 16) = *reinterpret_cast<const uint4*>(seg + (((cc + 1) ^ f) << 4));
+            } else if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
+              *reinterpret_cast<uint4*>(rb) = reinterpret_cast<const uint4*>(rp)[0];
+              *reinterpret_cast<uint4*>(rb + 16) = reinterpret_cast<const uint4*>(rp)[1];
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) rb[j] = j < nvalid ? rp[j] : 0;
+            }
+            const long long ebase = (long long)m * e.N + n0 + c0;
+            if (ebase + 32 <= e.qa_vec_end) {  // whole chunk in the 16-wide body (the common case)
+              const float sa = e.qa_sa, sb = e.qa_sb, fx = e.qa_fixed;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int r = __float2int_rn(__fmaf_rn((float)q[j], sa, __fmaf_rn((float)rb[j], sb, fx)));
+                q[j] = (uint32_t)min(max(r, 0), 255);
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float fa = (float)q[j], fb = (float)rb[j];
+                int r;
+                if (ebase + j < e.qa_vec_end) {
+                  r = __float2int_rn(__fmaf_rn(fa, e.qa_sa, __fmaf_rn(fb, e.qa_sb, e.qa_fixed)));
+                } else {
+                  const float da = (float)((int)q[j] - e.qa_azp), db = (float)((int)rb[j] - e.qa_bzp);
+                  r = __float2int_rn(__fadd_rn(__fmaf_rn(e.qa_sa, da, __fmul_rn(e.qa_sb, db)), (float)e.qa_yzp));
+                }
+                q[j] = (uint32_t)(r < 0 ? 0 : (r > 255 ? 255 : r));
+              }
+            }
           }
           uint8_t* y = static_cast<uint8_t*>(e.y);
           uint32_t w[8];

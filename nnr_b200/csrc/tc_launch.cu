@@ -36,8 +36,18 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
     if (rc != NNRCU_OK) return rc;
     y_tma = 1;
   }
-  kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, tmY, y_tma, L.b_plane_rows, g, e,
-                                                       L.num_kb, L.m_tiles, L.n_tiles);
+  CUtensorMap tmR{};
+  if (y_tma && e.qres) {
+    if (reinterpret_cast<uintptr_t>(e.qres) & 15) return set_error(NNRCU_ERR_INVALID, "residual must be 16-byte aligned");
+    const int seg = Cfg::OUT_SEG;
+    int rc = encode_tmap_2d(&tmR, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.qres, (uint64_t)e.N, (uint64_t)e.M,
+                            (uint64_t)e.ldy, seg, 32,
+                            seg == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                       : (seg == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B));
+    if (rc != NNRCU_OK) return rc;
+  }
+  kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, tmY, tmR, y_tma, L.b_plane_rows, g,
+                                                       e, L.num_kb, L.m_tiles, L.n_tiles);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

@@ -68,7 +68,7 @@ def check_plan(items: Sequence[Interval], offsets: Dict[str, int]) -> None:
 class DeviceNetwork:
     """A nnr_b200.resnet50.QModel prepared on one device."""
 
-    def __init__(self, model, device: int = 0, reuse: bool = True):
+    def __init__(self, model, device: int = 0, reuse: bool = True, fuse_add: bool = True):
         import torch
         from . import ops
         from ._lib import ConvDesc, call  # noqa: F401
@@ -107,9 +107,44 @@ class DeviceNetwork:
         for i, nd in enumerate(model.nodes):
             if nd.op == "DequantizeLinear" and nd.attrs.get("bias") is not None:
                 self.bias[i] = torch.from_numpy(np.ascontiguousarray(nd.attrs["bias"], np.float32)).to(self.dev)
+        self._schedule(fuse_add)
         self._plan(reuse)
         self.stream = torch.cuda.Stream(device=self.dev)
         self.graph_exec = None
+
+    # ------------------------------------------------------------------ schedule
+    def _schedule(self, fuse_add: bool):
+        """Steps to run: one per node, except that a QLinearAdd whose first
+        operand is produced by a QLinearConv with no other consumer becomes one
+        fused step (nnrcu_qlinearconv_run_add) at the add's position (its
+        residual may come from a later node, e.g. the downsample conv)."""
+        nodes = self.model.nodes
+        consumers: Dict[str, int] = {}
+        for nd in nodes:
+            for x in nd.inputs:
+                consumers[x] = consumers.get(x, 0) + 1
+        producer = {nd.output: i for i, nd in enumerate(nodes)}
+        fused_conv = {}
+        if fuse_add:
+            for j, nd in enumerate(nodes):
+                if nd.op != "QLinearAdd":
+                    continue
+                a = nd.inputs[0]
+                i = producer.get(a)
+                if i is not None and nodes[i].op == "QLinearConv" and consumers.get(a, 0) == 1:
+                    fused_conv[i] = j
+        self.steps = []  # (kind, node index, inputs, output, conv node index)
+        folded = set(fused_conv)
+        add_of = {j: i for i, j in fused_conv.items()}
+        for j, nd in enumerate(nodes):
+            if j in folded:
+                continue
+            if j in add_of:
+                i = add_of[j]
+                self.steps.append(("QConvAdd", j, [nodes[i].inputs[0], nd.inputs[1]], nd.output, i))
+            else:
+                self.steps.append((nd.op, j, list(nd.inputs), nd.output, j))
+        self.fused_away = {nodes[i].output for i in fused_conv}
 
     # ------------------------------------------------------------------ memory
     def _nbytes(self, name: str) -> int:
@@ -117,18 +152,20 @@ class DeviceNetwork:
         return int(np.prod(self.model.shapes[name])) * elem
 
     def _plan(self, reuse: bool = True):
-        nodes = self.model.nodes
+        steps = self.steps
         first: Dict[str, int] = {"input": -1}
         last: Dict[str, int] = {}
-        for i, nd in enumerate(nodes):
-            first.setdefault(nd.output, i)
-            for x in nd.inputs:
-                last[x] = i
-        last["logits"] = len(nodes)  # graph output lives to the end
+        for t, (_, _, ins, out, _) in enumerate(steps):
+            first.setdefault(out, t)
+            for x in ins:
+                last[x] = t
+        last["logits"] = len(steps)  # graph output lives to the end
         items = [Interval(name, self._nbytes(name), first[name], last.get(name, first[name])) for name in first]
-        items += [Interval(f"ws{i}", b, i, i) for i, b in enumerate(self.ws) if b]
+        for t, (_, _, _, _, ci) in enumerate(steps):
+            if self.ws[ci]:
+                items.append(Interval(f"ws{ci}", self.ws[ci], t, t))
         if not reuse:  # every tensor keeps its own slot (for inspecting intermediates)
-            items = [Interval(it.name, it.nbytes, -1, len(nodes)) for it in items]
+            items = [Interval(it.name, it.nbytes, -1, len(steps)) for it in items]
         self.offsets, self.arena_bytes = plan_arena(items)
         check_plan(items, self.offsets)
         self.intervals = items
@@ -146,42 +183,54 @@ class DeviceNetwork:
 
     # ------------------------------------------------------------------ execution
     def run(self, stream=None) -> None:
-        """Enqueues every node on the stream (no synchronisation)."""
+        """Enqueues every step on the stream (no synchronisation)."""
+        for t in range(len(self.steps)):
+            self.run_step(t, stream)
+
+    def run_step(self, t: int, stream=None) -> None:
+        """Enqueues step t alone (same operators, same arena slots)."""
         from ._lib import LAYOUT_NCHW, call
         st = C.c_void_p(self.stream.cuda_stream if stream is None else stream)
         qp, m, P = self.model.qparams, self.model, self.ptr
-        for i, nd in enumerate(m.nodes):
-            a = nd.attrs
-            out = C.c_void_p(P[nd.output])
-            if nd.op == "QuantizeLinear":
-                n, c, h, w = m.shapes[nd.inputs[0]]
-                q = qp[nd.output]
-                call("nnrcu_quantize_linear_u8", C.c_void_p(P[nd.inputs[0]]), out, n, c, h, w, q.scale, q.zp,
-                     LAYOUT_NCHW, 0, st)
-            elif nd.op in ("QLinearConv", "QLinearMatMul"):
-                ws = C.c_void_p(P[f"ws{i}"]) if self.ws[i] else None
-                fn = "nnrcu_qlinearconv_run" if nd.op == "QLinearConv" else "nnrcu_qlinearmatmul_run"
-                call(fn, self.ops[i]._op, C.c_void_p(P[nd.inputs[0]]), out, ws, st)
-            elif nd.op == "MaxPool":
-                n, h, w, c = m.shapes[nd.inputs[0]]
-                k, s, p = a["k"], a["s"], a["pad"]
-                call("nnrcu_maxpool_u8_nhwc", C.c_void_p(P[nd.inputs[0]]), out, n, h, w, c, k, k, s, s, p, p, p, p, st)
-            elif nd.op == "QLinearAdd":
-                qa, qb, qy = qp[nd.inputs[0]], qp[nd.inputs[1]], qp[nd.output]
-                call("nnrcu_qlinearadd_u8", C.c_void_p(P[nd.inputs[0]]), qa.scale, qa.zp, C.c_void_p(P[nd.inputs[1]]),
-                     qb.scale, qb.zp, qy.scale, qy.zp, out, int(np.prod(m.shapes[nd.output])), st)
-            elif nd.op == "DqGapQ":
-                n, h, w, c = m.shapes[nd.inputs[0]]
-                qx, qy = qp[nd.inputs[0]], qp[nd.output]
-                call("nnrcu_dq_gap_q_u8_nhwc", C.c_void_p(P[nd.inputs[0]]), n, h * w, c, qx.scale, qx.zp, qy.scale,
-                     qy.zp, out, st)
-            elif nd.op == "DequantizeLinear":
-                rows, cols = m.shapes[nd.inputs[0]]
-                qx = qp[nd.inputs[0]]
-                b = C.c_void_p(self.bias[i].data_ptr()) if i in self.bias else None
-                call("nnrcu_dequantize_linear_u8", C.c_void_p(P[nd.inputs[0]]), qx.scale, qx.zp, b, rows, cols, out, st)
-            else:
-                raise ValueError(f"unknown node {nd.op}")
+        kind, j, ins, output, i = self.steps[t]
+        nd = m.nodes[i]
+        a = nd.attrs
+        out = C.c_void_p(P[output])
+        if kind == "QConvAdd":
+            add = m.nodes[j]
+            qb, qy = qp[add.inputs[1]], qp[add.output]
+            ws = C.c_void_p(P[f"ws{i}"]) if self.ws[i] else None
+            call("nnrcu_qlinearconv_run_add", self.ops[i]._op, C.c_void_p(P[ins[0]]), C.c_void_p(P[ins[1]]),
+                 qb.scale, qb.zp, qy.scale, qy.zp, out, ws, st)
+        elif nd.op == "QuantizeLinear":
+            n, c, h, w = m.shapes[nd.inputs[0]]
+            q = qp[nd.output]
+            call("nnrcu_quantize_linear_u8", C.c_void_p(P[nd.inputs[0]]), out, n, c, h, w, q.scale, q.zp,
+                 LAYOUT_NCHW, 0, st)
+        elif nd.op in ("QLinearConv", "QLinearMatMul"):
+            ws = C.c_void_p(P[f"ws{i}"]) if self.ws[i] else None
+            fn = "nnrcu_qlinearconv_run" if nd.op == "QLinearConv" else "nnrcu_qlinearmatmul_run"
+            call(fn, self.ops[i]._op, C.c_void_p(P[nd.inputs[0]]), out, ws, st)
+        elif nd.op == "MaxPool":
+            n, h, w, c = m.shapes[nd.inputs[0]]
+            k, s_, p = a["k"], a["s"], a["pad"]
+            call("nnrcu_maxpool_u8_nhwc", C.c_void_p(P[nd.inputs[0]]), out, n, h, w, c, k, k, s_, s_, p, p, p, p, st)
+        elif nd.op == "QLinearAdd":
+            qa, qb, qy = qp[nd.inputs[0]], qp[nd.inputs[1]], qp[nd.output]
+            call("nnrcu_qlinearadd_u8", C.c_void_p(P[nd.inputs[0]]), qa.scale, qa.zp, C.c_void_p(P[nd.inputs[1]]),
+                 qb.scale, qb.zp, qy.scale, qy.zp, out, int(np.prod(m.shapes[nd.output])), st)
+        elif nd.op == "DqGapQ":
+            n, h, w, c = m.shapes[nd.inputs[0]]
+            qx, qy = qp[nd.inputs[0]], qp[nd.output]
+            call("nnrcu_dq_gap_q_u8_nhwc", C.c_void_p(P[nd.inputs[0]]), n, h * w, c, qx.scale, qx.zp, qy.scale,
+                 qy.zp, out, st)
+        elif nd.op == "DequantizeLinear":
+            rows, cols = m.shapes[nd.inputs[0]]
+            qx = qp[nd.inputs[0]]
+            b = C.c_void_p(self.bias[i].data_ptr()) if i in self.bias else None
+            call("nnrcu_dequantize_linear_u8", C.c_void_p(P[nd.inputs[0]]), qx.scale, qx.zp, b, rows, cols, out, st)
+        else:
+            raise ValueError(f"unknown node {nd.op}")
 
     def capture(self) -> None:
         """Records run() once into a CUDA graph (nnrcu_graph_begin/_end)."""

@@ -195,3 +195,31 @@ def test_im2col_padded_copy_nonzero_zp(cuda_dev, shape):
     for f in (O.R1, O.R2):
         y, _ = run_qconv(cuda_dev, case, f, "NCHW", "NCHW")
         assert np.array_equal(y, oracle_qconv(case, f))
+
+
+@pytest.mark.parametrize("shape", [(2, 64, 14, 14, 256, 1, 0), (1, 32, 7, 9, 17, 3, 1), (3, 128, 10, 10, 48, 3, 1)])
+def test_conv_with_fused_residual_add(cuda_dev, shape):
+    """nnrcu_qlinearconv_run_add == QLinearConv then QLinearAdd(conv, residual);
+    odd element counts exercise QLinearAdd's scalar tail."""
+    import ctypes as C
+    from nnr_b200 import ops
+    from nnr_b200._lib import check, lib
+    n, c, h, w, oc, k, p = shape
+    rng = np.random.default_rng(oc + k)
+    case = W.random_qconv(rng, n, c, h, w, oc, k, k, (1, 1), (p,) * 4, x_zp=0)
+    op = ops.QLinearConv(case.x.shape, case.w, case.w_scale, case.w_zp, case.bias, case.x_scale, case.x_zp,
+                         case.y_scale, case.y_zp, pads=case.pads, in_layout="NHWC", out_layout="NHWC", requant=O.R2)
+    conv = oracle_qconv(case, O.R2, out_layout="NHWC")
+    res = rng.integers(0, 256, size=conv.shape).astype(np.uint8)
+    rs, rz, ys, yz = 0.037, 101, 0.05, 7
+    ref = O.qlinearadd_u8(conv, case.y_scale, case.y_zp, res, rs, rz, ys, yz)
+    x = torch.from_numpy(_to_nhwc(case.x)).to(cuda_dev)
+    r = torch.from_numpy(res).to(cuda_dev)
+    y = torch.empty(conv.shape, dtype=torch.uint8, device=cuda_dev)
+    ws = torch.empty(max(op.workspace_size(), 1), dtype=torch.uint8, device=cuda_dev)
+    check(lib.nnrcu_qlinearconv_run_add(op._op, C.c_void_p(x.data_ptr()), C.c_void_p(r.data_ptr()), rs, rz, ys, yz,
+                                        C.c_void_p(y.data_ptr()), C.c_void_p(ws.data_ptr()),
+                                        C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert np.array_equal(y.cpu().numpy(), ref)

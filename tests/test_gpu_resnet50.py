@@ -27,13 +27,26 @@ def test_resnet50_qdq_bit_exact(cuda_dev, model4):
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     for nd in model4.nodes:  # first divergent layer, if any
-        if nd.output == "logits":
+        if nd.output == "logits" or nd.output in net.fused_away:
             continue
         got = net.view(nd.output).cpu().numpy()
         want = tensors[nd.output]
         assert np.array_equal(got, want), f"{nd.op} {nd.output}: {(got != want).sum()} of {want.size} differ"
     got = net.view("logits").cpu().numpy()
     assert np.array_equal(got, ref)
+
+
+def test_resnet50_unfused_add_path(cuda_dev, model4):
+    """Without the conv+add fusion (separate QLinearAdd kernels) the logits are the same."""
+    from nnr_b200 import graph, resnet50
+    x = resnet50.input_batch(0, 4)
+    ref = O.run_qmodel(model4, x)
+    net = graph.DeviceNetwork(model4, 0, fuse_add=False)
+    net.view("input").copy_(torch.from_numpy(x))
+    net.run()
+    torch.cuda.synchronize()
+    assert not net.fused_away
+    assert np.array_equal(net.view("logits").cpu().numpy(), ref)
 
 
 def test_resnet50_graph_replay_and_host_path(cuda_dev, model4):
