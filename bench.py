@@ -16,9 +16,10 @@ one captured CUDA graph.
             the launching stream, max over ranks.
   e2e       the same forward through the public API with host buffers:
             pinned H2D of the fp32 input, forward, D2H of the fp32 logits.
-  roofline  the tcgen05 conv/matmul kernels of the forward, each launch timed
-            with CUDA events in an un-captured pass: algorithmic int8 ops /
-            kernel time vs the int8 tensor peak.
+  roofline  the tcgen05 conv/matmul kernels of the forward: each engine step
+            timed as 10 launches replayed from a CUDA graph (CUDA events on
+            the launching stream); algorithmic int8 ops / summed kernel time
+            vs the int8 tensor peak.
   qlinearconv_config2  BASELINE config 2 (one QLinearConv layer, NCHW in/out,
             requant R1): operator and kernel TOPS.
 
@@ -285,19 +286,25 @@ def main():
         stream.synchronize()
         return sum(a.elapsed_time(b) for a, b in ev)
 
-    def node_times(reps=3):
-        evs = []
-        for _ in range(reps):
-            for t_, i in tc_steps:
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                e0.record(stream)
-                net.run_step(t_)
-                e1.record(stream)
-                evs.append((i, e0, e1))
-        stream.synchronize()
-        times = {i: 0.0 for i in tc_nodes}
-        for i, e0, e1 in evs:
-            times[i] += e0.elapsed_time(e1) / reps
+    def node_times(reps=5):
+        """Device time of each engine step: 10 launches captured in a CUDA
+        graph, replayed `reps` times, CUDA events on the network's stream
+        (no host gaps between launches; L2 warm)."""
+        times = {}
+        for t_, i in tc_steps:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for _ in range(10):
+                    net.run_step(t_)
+            g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                with torch.cuda.stream(stream):
+                    g.replay()
+            e1.record(stream)
+            stream.synchronize()
+            times[i] = e0.elapsed_time(e1) / (10 * reps)
         return times
 
     with ClockSampler(local) as clk:

@@ -149,9 +149,9 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t 
     int32_t v = (int32_t)((uint32_t)raw + (uint32_t)ci);
     float f = __fmul_rn(__int2float_rn(v), f1);
     f = fminf(fmaxf(f, e.rq_lo), e.rq_hi);
-    int32_t q = __float2int_rn(f) + e.yzp;
-    q = q < 0 ? 0 : (q > 255 ? 255 : q);
-    return (uint32_t)q;
+    // f lies in [-y_zp, 255 - y_zp] (integral bounds), so rne(f) + y_zp is
+    // already in [0, 255]: the unsigned saturation of the reference is a no-op
+    return (uint32_t)(__float2int_rn(f) + e.yzp);
   } else if constexpr (EPI == EPI_R3) {
     // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); min(hi) then max(qmin); rne
     int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci);
@@ -500,12 +500,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       int img = 0, pix = 0;
       if (e.y_layout == 1 && mvalid) { img = m / e.ohw; pix = m - img * e.ohw; }
       const uint32_t t_addr = tmem_base + ((uint32_t)(eq * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int c0 = col0; c0 < col0 + HB; c0 += 32) {
+      // one 32-column chunk: requant / bias / post-op / stores
+      auto chunk = [&](const int c0, uint32_t (&v)[32]) {
         const int pc = c0 - col0;  // column within this warp's parameter copy
-        uint32_t v[32];
-        ptx::tmem_ld32(t_addr + (uint32_t)c0, v);
-        if (!mvalid || n0 + c0 >= e.N) continue;
+        if (!mvalid || n0 + c0 >= e.N) return;
         const int nvalid = min(32, e.N - (n0 + c0));
         if constexpr (EPI == EPI_F32) {
           float* y = static_cast<float*>(e.y);
@@ -628,6 +626,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             for (int j = 0; j < 32; ++j)
               if (j < nvalid) y[((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix] = (uint8_t)q[j];
           }
+        }
+            };
+      // TMEM loads are double-buffered: chunk i + 1 is in flight while i is processed
+      uint32_t va[32], vb[32];
+      ptx::tmem_ld32_async(t_addr + (uint32_t)col0, va);
+      ptx::tmem_wait_ld(va);
+#pragma unroll 1
+      for (int c0 = col0; c0 < col0 + HB; c0 += 64) {
+        const bool has_b = c0 + 32 < col0 + HB;
+        if (has_b) ptx::tmem_ld32_async(t_addr + (uint32_t)(c0 + 32), vb);
+        chunk(c0, va);
+        if (has_b) {
+          ptx::tmem_wait_ld(vb);
+          const bool has_a = c0 + 64 < col0 + HB;
+          if (has_a) ptx::tmem_ld32_async(t_addr + (uint32_t)(c0 + 64), va);
+          chunk(c0 + 32, vb);
+          if (has_a) ptx::tmem_wait_ld(va);
         }
       }
       // hand the accumulator back to the MMA warp

@@ -1,0 +1,99 @@
+"""Per-step timing of the ResNet-50 QDQ forward on one GPU.
+
+    python -m nnr_b200.profile_steps [--batch 32] [--json out.json]
+        times every step of the forward: each step is captured 10x into its
+        own CUDA graph and replayed (back to back, L2 warm), CUDA events on the
+        network's stream; prints per-kind totals and the slowest steps.
+
+    python -m nnr_b200.profile_steps --only b0.out --repeat 3
+        launches only the step producing tensor b0.out, 3 times (a target
+        for an ncu capture: -k regex:tc_gemm -s 1 -c 1).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+
+def step_ops(model, node_index: int) -> int:
+    nd = model.nodes[node_index]
+    if nd.op == "QLinearConv":
+        n, oh, ow, oc = model.shapes[nd.output]
+        w = nd.attrs["w"]
+        return 2 * n * oh * ow * oc * w.shape[1] * w.shape[2] * w.shape[3]
+    if nd.op == "QLinearMatMul":
+        b = nd.attrs["b"]
+        return 2 * model.shapes[nd.output][0] * b.shape[0] * b.shape[1]
+    return 0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--only", default=None, help="output tensor of the one step to launch")
+    ap.add_argument("--repeat", type=int, default=3)
+    ap.add_argument("--json", default=None)
+    a = ap.parse_args(argv)
+
+    import torch
+    from . import graph, resnet50
+
+    m = resnet50.build(batch=a.batch)
+    net = graph.DeviceNetwork(m, 0)
+    net.view("input").copy_(torch.from_numpy(resnet50.input_batch(0, a.batch)))
+    st = net.stream
+    if a.only:
+        t = [k for k, s in enumerate(net.steps) if s[3] == a.only][0]
+        for _ in range(a.repeat):
+            net.run_step(t)
+        torch.cuda.synchronize()
+        print(f"launched step {t} ({net.steps[t][0]} -> {a.only}) x{a.repeat}")
+        return 0
+
+    net.run()
+    torch.cuda.synchronize()
+    rows = []
+    for t, (kind, _, _, out, i) in enumerate(net.steps):
+        g = torch.cuda.CUDAGraph()
+        for _ in range(2):
+            net.run_step(t)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(10):
+                net.run_step(t)
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(5):
+            with torch.cuda.stream(st):
+                g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / 50
+        nd = m.nodes[i]
+        ops = step_ops(m, i)
+        k = nd.attrs["w"].shape[2] if nd.op == "QLinearConv" else None
+        label = kind + (f" {k}x{k}" if k else "")
+        rows.append(dict(step=t, kind=label, output=out, us=round(us, 2),
+                         tops=round(ops / us / 1e6, 1) if ops else None))
+    total = sum(r["us"] for r in rows)
+    by = {}
+    for r in rows:
+        c = by.setdefault(r["kind"], [0, 0.0])
+        c[0] += 1
+        c[1] += r["us"]
+    summary = {k: {"steps": v[0], "us": round(v[1], 1), "share": round(v[1] / total, 3)} for k, v in by.items()}
+    print(json.dumps({"batch": a.batch, "total_us": round(total, 1), "steps": len(rows)}))
+    print(json.dumps(summary, indent=1))
+    for r in sorted(rows, key=lambda r: -r["us"])[:15]:
+        print(json.dumps(r))
+    if a.json:
+        with open(a.json, "w") as f:
+            json.dump({"total_us": total, "by_kind": summary, "steps": rows}, f, indent=1)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
