@@ -33,14 +33,52 @@
 namespace nnrcu {
 
 enum : int { A_TMA = 0, A_GATHER = 1, A_IM2COL = 2 };
-enum : int { EPI_R1 = 1, EPI_R2 = 2, EPI_R3 = 3, EPI_R4 = 4, EPI_F32 = 10 };
+// EPI_R2A: the R2 requant followed by a fused QLinearAdd whose residual
+// tiles are TMA-prefetched one tile ahead (u8 row-major output via TMA store).
+enum : int { EPI_R1 = 1, EPI_R2 = 2, EPI_R3 = 3, EPI_R4 = 4, EPI_R2A = 5, EPI_F32 = 10 };
 enum : int { ACT_NONE = 0, ACT_RELU = 1, ACT_CLIP = 2, ACT_HARDSWISH = 3, ACT_SIGMOID = 4, ACT_LEAKYRELU = 5,
              ACT_TANH = 6 };
 enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_ACCUM = 3 };
 
+// Opt-in phase trace for performance analysis (built only with -DNNRCU_TRACE):
+// clock64 stamps of CTAs 0-3, per warp, per local tile (first 16), 4 events.
+#ifdef NNRCU_TRACE
+__device__ unsigned long long g_trace[4 * 18 * 16 * 4];
+#define NNRCU_TRACE_AT(w, t, ev)                                                       \
+  do {                                                                                 \
+    if (blockIdx.x < 4 && (t) < 16) g_trace[((blockIdx.x * 18 + (w)) * 16 + (t)) * 4 + (ev)] = clock64(); \
+  } while (0)
+// finer stamps inside a tile's epilogue: CTAs 0-1, first 4 tiles, 16 events
+__device__ unsigned long long g_trace2[2 * 18 * 4 * 16];
+#define NNRCU_TRACE2_AT(w, t, ev)                                                       \
+  do {                                                                                  \
+    if (blockIdx.x < 2 && (t) < 4 && (ev) < 16) g_trace2[((blockIdx.x * 18 + (w)) * 4 + (t)) * 16 + (ev)] = clock64(); \
+  } while (0)
+#else
+#define NNRCU_TRACE2_AT(w, t, ev) \
+  do {                            \
+  } while (0)
+#define NNRCU_TRACE_AT(w, t, ev) \
+  do {                           \
+  } while (0)
+#endif
+
 constexpr int BM = 128;       // rows per tile (TMEM lanes)
 constexpr int BKB = 128;      // K bytes per stage per plane (one swizzle row); 64 for the 64-byte-slab variant
-constexpr int NUM_THREADS = 320;  // 4 epilogue + 4 gather + TMA + MMA warps
+// Warp roles per A-operand mode and N tile:
+//   gather mode:    warps 0-3 epilogue, 4-7 gather producers, 8 TMA, 9 MMA
+//   TMA / im2col:   warps 0 .. 4*SPLIT-1 epilogue, then TMA, then MMA, with
+//                   SPLIT epilogue warps per TMEM lane quarter, each draining
+//                   BN / SPLIT columns (16 warps for BN >= 128: the epilogue,
+//                   not the tensor core, bounds the small-K layers)
+template <int AMODE, int BN>
+struct Roles {
+  static constexpr int SPLIT = AMODE == A_GATHER ? 1 : (BN >= 128 ? 4 : 2);
+  static constexpr int TMA_WARP = AMODE == A_GATHER ? 8 : 4 * SPLIT;
+  static constexpr int MMA_WARP = TMA_WARP + 1;
+  static constexpr int THREADS = (MMA_WARP + 1) * 32;
+  static constexpr int CW = 32;  // accumulator columns per TMEM load
+};
 
 // Geometry of the implicit im2col gather (A_GATHER). All sizes in bytes where noted.
 struct GatherGeom {
@@ -91,19 +129,26 @@ struct TileCfg {
   static constexpr int B_BYTES = BN * KB;
   static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + B_BYTES);
   // u8 epilogues stage each warp's 32 x BN output block for a TMA store
-  static constexpr int OUT_BYTES = (EPI == EPI_F32) ? 0 : 4 * 32 * BN;
+  static constexpr int OUT_BLOCK = (EPI == EPI_F32) ? 0 : 4 * 32 * BN;  // one 32 x HB block per epilogue warp
+  // EPI_R2A: two residual blocks per epilogue warp (tile i in use, tile i+1 landing)
+  static constexpr int RES_BYTES = (EPI == EPI_R2A) ? 2 * OUT_BLOCK : 0;
+  // Output staging is double-buffered (the store of tile i drains while tile
+  // i+1 is requantised) when that still leaves three pipeline stages.
+  static constexpr int OUT_BUFS = (200 * 1024 - 2 * OUT_BLOCK - RES_BYTES) / STAGE_BYTES >= 3 ? 2 : 1;
+  static constexpr int OUT_BYTES = OUT_BUFS * OUT_BLOCK;
   // Epilogue warps: 4 x SPLIT, each covering 32 TMEM lanes x BN / SPLIT columns.
   static constexpr int HB = BN / SPLIT;
   static constexpr int OUT_SEG = HB >= 128 ? 128 : HB;  // bytes per staged row segment (= TMA box width)
-  static constexpr int STAGES_RAW = (200 * 1024 - OUT_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES_RAW = (200 * 1024 - OUT_BYTES - RES_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
   // Gather producers publish a stage LAG iterations after issuing it: LAG
   // stages of copies in flight, STAGES - 1 - LAG stages of slack for the MMA.
   static constexpr int LAG = (STAGES - 1) / 2 > 1 ? (STAGES - 1) / 2 : 1;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (power of two)
   static constexpr int PARAM_BYTES = 4 * SPLIT /*epilogue warps*/ * 3 * HB * 4;
+  static constexpr int BAR_BYTES = 1024;  // mbarriers, TMEM slot, abort flag
   static constexpr int SMEM_BYTES =
-      1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + 512 /*barriers*/ + PARAM_BYTES;
+      1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + RES_BYTES + BAR_BYTES + PARAM_BYTES;
   static_assert(STAGES >= 2, "need at least two pipeline stages");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -130,7 +175,25 @@ __device__ __forceinline__ float apply_act(float v, int act, float a, float b) {
   }
 }
 
-// Requantise one int32 accumulator to u8 with the formula EPI selects.
+// Rounding through the float adder: for |x| <= 2^22, x + 1.5 * 2^23 is
+// rounded to an integer (ulp 1 in [2^23, 2^24)) with ties to even, because
+// 1.5 * 2^23 is even; the integer rne(x) then sits in the low mantissa bits
+// (bits = 0x4B400000 + rne(x), two's complement offset). This is exact
+// round-to-nearest-even, done on the FMA pipe instead of the conversion unit.
+constexpr float RND_MAGIC = 12582912.0f;   // 1.5 * 2^23, bits 0x4B400000
+constexpr float BYTE_MAGIC = 8388608.0f;   // 2^23, bits 0x4B000000: 0x4B0000bb = 2^23 + bb
+
+// R2 requant up to the rounding: returns RND_MAGIC + rne(f) as a float,
+// where f = clamp(float(acc + bias) * os, lo - y_zp, hi - y_zp) (|f| <= 255).
+__device__ __forceinline__ float r2_magic(int32_t raw, int32_t ci, float os, const EpiParams& e) {
+  const int32_t v = (int32_t)((uint32_t)raw + (uint32_t)ci);
+  float f = __fmul_rn(__int2float_rn(v), os);
+  f = fminf(fmaxf(f, e.rq_lo), e.rq_hi);
+  return __fadd_rn(f, RND_MAGIC);
+}
+
+// Requantise one int32 accumulator to u8 with the formula EPI selects; the
+// result is in the low byte of the returned word (upper bytes unspecified).
 // ci is the per-column int32 correction (-x_zp*sum(w), plus the int32 bias
 // for R2); f1/f2 are the per-column floats (R1/R3: cs, bias_f; R2: os).
 template <int EPI>
@@ -144,29 +207,37 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t 
     f = __fadd_rn(f, e.yzp_f);
     f = fmaxf(fminf(f, e.qmax_f), e.qmin_f);
     return (uint32_t)__float2int_rn(f);
-  } else if constexpr (EPI == EPI_R2) {
-    // f = float(acc + bias) * os; max(lo - y_zp) then min(hi - y_zp); rne; + y_zp; saturate
-    int32_t v = (int32_t)((uint32_t)raw + (uint32_t)ci);
-    float f = __fmul_rn(__int2float_rn(v), f1);
-    f = fminf(fmaxf(f, e.rq_lo), e.rq_hi);
+  } else if constexpr (EPI == EPI_R2 || EPI == EPI_R2A) {
+    // f = float(acc + bias) * os; max(lo - y_zp) then min(hi - y_zp); rne; + y_zp.
     // f lies in [-y_zp, 255 - y_zp] (integral bounds), so rne(f) + y_zp is
     // already in [0, 255]: the unsigned saturation of the reference is a no-op
-    return (uint32_t)(__float2int_rn(f) + e.yzp);
+    return __float_as_uint(r2_magic(raw, ci, f1, e)) + (uint32_t)e.yzp;
   } else if constexpr (EPI == EPI_R3) {
     // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); min(hi) then max(qmin); rne
+    // (the clamp bounds are integers in [0, 255], so rne commutes with the clamp)
     int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci);
     float f = __fmaf_rn(__int2float_rn(acc), f1, f2);
     f = __fmaf_rn(f, e.inv_y, e.yzp_f);
     f = fmaxf(fminf(f, e.qmax_f), e.qmin_f);
-    return (uint32_t)__float2int_rn(f);
+    return __float_as_uint(__fadd_rn(f, RND_MAGIC));
   } else {  // EPI_R4
     // val = fma(float(acc), a_s*b_s/y_s, y_zp); nearbyint; clamp [0, 255]
+    // == rne(clamp(val, 0, 255)), the clamp bounds being integers
     int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci + (uint32_t)rowc);
     float f = __fmaf_rn(__int2float_rn(acc), e.combined, e.yzp_f);
-    int32_t q = __float2int_rn(f);
-    q = q < 0 ? 0 : (q > 255 ? 255 : q);
-    return (uint32_t)q;
+    f = fminf(fmaxf(f, 0.0f), 255.0f);
+    return __float_as_uint(__fadd_rn(f, RND_MAGIC));
   }
+}
+
+// Low bytes of four words packed into one (byte j from word j).
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
+// Byte j of w as an exact float: bits 0x4B0000bb = 2^23 + bb, minus 2^23.
+__device__ __forceinline__ float byte_to_float(uint32_t w, int j) {
+  return __fsub_rn(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650 | j)), BYTE_MAGIC);
 }
 
 // Persistent warp-specialised kernel. One CTA per SM walks the tiles
@@ -180,14 +251,16 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t 
 // double-buffered in TMEM (2 x BN columns), so the epilogue of tile i overlaps
 // the loads and MMAs of tile i + 1.
 template <int BN, int NPLANE, int AMODE, int EPI, int KB>
-__global__ void __launch_bounds__(NUM_THREADS, 1)
+__global__ void __launch_bounds__(Roles<AMODE, BN>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY,
                const __grid_constant__ CUtensorMap tmR, int y_tma,
                int b_plane_rows, GatherGeom g, EpiParams e, int num_kb, int m_tiles, int n_tiles) {
   // In TMA / im2col modes the gather warps 4-7 are free and join the epilogue:
   // warps w and w + 4 drain the same 32 TMEM lanes, each half of the columns.
-  constexpr int SPLIT = (AMODE == A_GATHER) ? 1 : 2;
+  using R = Roles<AMODE, BN>;
+  constexpr int SPLIT = R::SPLIT;
+  constexpr int CW = R::CW;
   constexpr int HB = BN / SPLIT;
   using Cfg = TileCfg<BN, NPLANE, EPI, KB, SPLIT>;
   static_assert(KB == BKB || AMODE != A_GATHER, "the gather producers fill 128-byte slabs");
@@ -196,23 +269,28 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   constexpr int B_BYTES = Cfg::B_BYTES;
 
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base, derived by pointer arithmetic on the shared array
+  // so that accesses through it stay shared-memory (not generic) accesses
+  uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;                                        // [STAGES][NPLANE][A_BYTES]
   uint8_t* sB = sA + STAGES * NPLANE * A_BYTES;              // [STAGES][NPLANE][B_BYTES]
   uint8_t* sOut = sB + STAGES * NPLANE * B_BYTES;            // [4 warps][32 rows][BN] (u8 epilogues)
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sOut + Cfg::OUT_BYTES);
+  uint8_t* sRes = sOut + Cfg::OUT_BYTES;                      // [2][8 warps][32 rows][HB] (EPI_R2A)
+  // sOut: [OUT_BUFS][8 warps][32 rows][HB]
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(sRes + Cfg::RES_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* tfull_bar = empty_bar + STAGES;                  // [2] accumulator ready
   uint64_t* tempty_bar = tfull_bar + 2;                      // [2] accumulator drained
-  uint64_t* res_bar = tempty_bar + 2;                        // [8] residual tile landed (per epilogue warp)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 8);
+  uint64_t* res_bar = tempty_bar + 2;                        // [2][16] residual block landed (buffer, warp)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 32);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_tiles = m_tiles * n_tiles;
+  if (threadIdx.x == 0) NNRCU_TRACE_AT(17, 15, 3);  // CTA start
   // per-column constants, one private copy per epilogue warp (no cross-warp sync)
-  int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + 512 +
+  int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + Cfg::BAR_BYTES +
                                              (warp & (4 * SPLIT - 1)) * (3 * HB * 4));
   float* s_f1 = reinterpret_cast<float*>(s_ci + HB);
   float* s_f2 = s_f1 + HB;
@@ -223,7 +301,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       ptx::mbar_init(&full_bar[s], full_count);
       ptx::mbar_init(&empty_bar[s], 1);
     }
-    for (int a = 0; a < 8; ++a) ptx::mbar_init(&res_bar[a], 1);
+    for (int a = 0; a < 32; ++a) ptx::mbar_init(&res_bar[a], 1);
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull_bar[a], 1);
       ptx::mbar_init(&tempty_bar[a], 4 * SPLIT);
@@ -232,14 +310,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     ptx::fence_mbar_init();
     ptx::fence_proxy_async_smem();
   }
-  if (warp == 8 && lane == 0) {
+  if (warp == R::TMA_WARP && lane == 0) {
     ptx::tma_prefetch_desc(&tmB);
     if (AMODE != A_GATHER) {
       ptx::tma_prefetch_desc(&tmA0);
       if (NPLANE == 2) ptx::tma_prefetch_desc(&tmA1);
     }
   }
-  if (warp == 9) ptx::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  if (warp == R::MMA_WARP) ptx::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -250,13 +328,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     *abort_flag = 1;
   };
 
-  if (warp == 8) {
+  if (warp == R::TMA_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
       constexpr uint32_t tx = (AMODE != A_GATHER ? NPLANE * A_BYTES : 0) + NPLANE * B_BYTES;
       bool aborted = false;
-      int it = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
+      int it = 0, tlt = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x, ++tlt) {
+        NNRCU_TRACE_AT(warp, tlt, 0);
         const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
         // im2col: input position of the tile's first output pixel
         int i_n = 0, i_h = 0, i_w = 0;
@@ -292,10 +371,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             if (NPLANE == 2) ptx::tma_load_im2col_4d(a_st + A_BYTES, &tmA1, &full_bar[s], cc, i_w, i_h, i_n, ow_off, oh_off);
           }
         }
+        NNRCU_TRACE_AT(warp, tlt, 1);
       }
       if (aborted) ptx::settle_ns(200000);  // let copies already in flight land before the CTA exits
     }
-  } else if (warp == 9) {
+  } else if (warp == R::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = (NPLANE == 1) ? ptx::umma_idesc(2, 0, 1, BM, BN) : ptx::umma_idesc(1, 1, 1, BM, BN);
@@ -305,12 +385,14 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         const int acc = lt & 1;
         const uint32_t use_ph = (uint32_t)(lt >> 1) & 1u;
         if (!ptx::mbar_wait(&tempty_bar[acc], use_ph ^ 1u, abort_flag)) { fail(ST_TIMEOUT_ACCUM); aborted = true; break; }
+        NNRCU_TRACE_AT(warp, lt, 0);
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!ptx::mbar_wait(&full_bar[s], ph, abort_flag)) { fail(ST_TIMEOUT_FULL); aborted = true; break; }
+          if (kb == 0) NNRCU_TRACE_AT(warp, lt, 1);
           ptx::tc_fence_after();
           ptx::fence_proxy_async_smem();
           const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * NPLANE * A_BYTES);
@@ -334,6 +416,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           ptx::mma_commit(&empty_bar[s]);
         }
         if (!aborted) ptx::mma_commit(&tfull_bar[acc]);  // fires when this tile's MMAs have completed
+        NNRCU_TRACE_AT(warp, lt, 2);
       }
       if (aborted) ptx::settle_ns(200000);  // MMAs already issued finish before TMEM is freed
     }
@@ -438,6 +521,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const int row = eq * 32 + lane;    // TMEM lane == tile row
     int lt = 0;
     int cached_n0 = -1;
+    // EPI_R2A: TMA load of this warp's 32 x HB residual block of tile t into buffer buf
+    auto issue_res = [&](const int t, const int buf) {
+      constexpr int SEG = Cfg::OUT_SEG;
+      const int rm0 = (t / n_tiles) * BM, rn0 = (t % n_tiles) * BN;
+      uint64_t* bar = &res_bar[buf * 16 + warp];
+      uint8_t* dst = sRes + buf * Cfg::OUT_BLOCK + warp * (32 * HB);
+      ptx::mbar_arrive_expect_tx(bar, 32 * HB);
+      for (int h = 0; h < HB / SEG; ++h) ptx::tma_load_2d(dst + h * (32 * SEG), &tmR, bar, rn0 + col0 + h * SEG, rm0 + eq * 32);
+    };
+    if (EPI == EPI_R2A && lane == 0 && (int)blockIdx.x < num_tiles) issue_res(blockIdx.x, 0);
+    bool res_failed = false;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
       const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
       const int acc = lt & 1;
@@ -450,7 +544,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           const bool ok = n < e.N;
           int32_t ci = (ok && e.colcorr) ? e.colcorr[n] : 0;
           float f1 = 0.0f, f2 = 0.0f;
-          if (EPI == EPI_R2) {
+          if (EPI == EPI_R2 || EPI == EPI_R2A) {
             if (ok && e.bias_i) ci = (int32_t)((uint32_t)ci + (uint32_t)e.bias_i[n]);
             f1 = (ok && e.os) ? e.os[n] : 0.0f;
           } else if (EPI == EPI_F32) {
@@ -467,32 +561,39 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         cached_n0 = n0;
       }
       // the staging block may be rewritten once the previous tile's stores have read it
-      uint8_t* const stg = sOut + warp * (32 * HB);
-      // fused residual add: the residual block lands in the staging buffer
-      // (same box and swizzle as the output store), loaded while the MMAs
-      // run, and is combined with the requantised tile in place
-      const bool res_tma = EPI != EPI_F32 && y_tma && e.qres != nullptr;
+      if (lane == 0) NNRCU_TRACE_AT(warp, lt, 0);
+      uint8_t* const stg = sOut + (Cfg::OUT_BUFS == 2 ? (lt & 1) * Cfg::OUT_BLOCK : 0) + warp * (32 * HB);
+      constexpr int SEG = Cfg::OUT_SEG;
+      // swizzle of a staged row (the store / residual maps' 128B, 64B or 32B
+      // swizzle): row r, 16-byte chunk c of a segment lives at r*SEG + ((c ^ f(r)) << 4)
+      const int swz = SEG == 128 ? (lane & 7) : (SEG == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
       if (EPI != EPI_F32 && y_tma) {
         if (lane == 0) {
-          ptx::bulk_wait_read0();
-          if (res_tma) {
-            constexpr int SEG = Cfg::OUT_SEG;
-            ptx::mbar_arrive_expect_tx(&res_bar[warp], 32 * HB);
-            for (int h = 0; h < HB / SEG; ++h)
-              ptx::tma_load_2d(stg + h * (32 * SEG), &tmR, &res_bar[warp], n0 + col0 + h * SEG, m0 + eq * 32);
+          ptx::bulk_wait_read<Cfg::OUT_BUFS - 1>();  // the store that last used this buffer has read it
+          if constexpr (EPI == EPI_R2A) {
+            // prefetch the residual block of this warp's next tile into the
+            // other buffer (its previous contents were consumed by tile lt - 1)
+            const int nxt = tile + gridDim.x;
+            if (nxt < num_tiles) issue_res(nxt, (lt + 1) & 1);
           }
         }
         __syncwarp();
       }
       if (!__all_sync(0xffffffffu, ptx::mbar_wait(&tfull_bar[acc], use_ph, abort_flag))) {
         fail(ST_TIMEOUT_ACCUM);
+        res_failed = true;
         break;
       }
       ptx::tc_fence_after();
-      if (res_tma && !__all_sync(0xffffffffu, ptx::mbar_wait(&res_bar[warp], (uint32_t)lt & 1u, abort_flag))) {
+      if (lane == 0) NNRCU_TRACE_AT(warp, lt, 1);
+      const uint8_t* rstg = sRes + (lt & 1) * Cfg::OUT_BLOCK + warp * (32 * HB);
+      if (EPI == EPI_R2A &&
+          !__all_sync(0xffffffffu, ptx::mbar_wait(&res_bar[(lt & 1) * 16 + warp], (uint32_t)(lt >> 1) & 1u, abort_flag))) {
         fail(ST_TIMEOUT_ACCUM);
+        res_failed = true;
         break;
       }
+      if (lane == 0) NNRCU_TRACE_AT(warp, lt, 2);
       const int m = m0 + row;
       const bool mvalid = m < e.M;
       int32_t rowc = 0;
@@ -500,20 +601,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       int img = 0, pix = 0;
       if (e.y_layout == 1 && mvalid) { img = m / e.ohw; pix = m - img * e.ohw; }
       const uint32_t t_addr = tmem_base + ((uint32_t)(eq * 32) << 16) + (uint32_t)(acc * BN);
-      // one 32-column chunk: requant / bias / post-op / stores
-      auto chunk = [&](const int c0, uint32_t (&v)[32]) {
+      // one CW-column chunk: requant / bias / post-op / stores
+      auto chunk = [&](const int c0, uint32_t (&v)[CW]) {
         const int pc = c0 - col0;  // column within this warp's parameter copy
         if (!mvalid || n0 + c0 >= e.N) return;
-        const int nvalid = min(32, e.N - (n0 + c0));
+        const int nvalid = min(CW, e.N - (n0 + c0));
         if constexpr (EPI == EPI_F32) {
           float* y = static_cast<float*>(e.y);
           const bool rowmajor = e.y_layout == 0;
           float* dst = rowmajor ? y + (size_t)m * e.ldy + n0 + c0 : nullptr;
           const float* res = (e.residual && rowmajor) ? e.residual + (size_t)m * e.ldy + n0 + c0 : nullptr;
-          if (rowmajor && nvalid == 32 && (e.ldy & 3) == 0 && ((reinterpret_cast<uintptr_t>(e.y) & 15) == 0) &&
+          if (rowmajor && nvalid == CW && (e.ldy & 3) == 0 && ((reinterpret_cast<uintptr_t>(e.y) & 15) == 0) &&
               (!e.residual || (reinterpret_cast<uintptr_t>(e.residual) & 15) == 0)) {
 #pragma unroll
-            for (int j = 0; j < 32; j += 4) {
+            for (int j = 0; j < CW; j += 4) {
               float o[4];
               float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
               if (res) rr = *reinterpret_cast<const float4*>(res + j);
@@ -530,7 +631,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
+            for (int j = 0; j < CW; ++j) {
               if (j >= nvalid) break;
               const size_t idx = rowmajor ? (size_t)m * e.ldy + n0 + c0 + j
                                           : ((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix;
@@ -543,108 +644,236 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             }
           }
         } else {
-          uint32_t q[32];
-#pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
-            const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
-            const float4 b4 = *reinterpret_cast<const float4*>(s_f2 + pc + j);
-            q[j + 0] = requant_u8<EPI>((int32_t)v[j + 0], ci4.x, rowc, a4.x, b4.x, e);
-            q[j + 1] = requant_u8<EPI>((int32_t)v[j + 1], ci4.y, rowc, a4.y, b4.y, e);
-            q[j + 2] = requant_u8<EPI>((int32_t)v[j + 2], ci4.z, rowc, a4.z, b4.z, e);
-            q[j + 3] = requant_u8<EPI>((int32_t)v[j + 3], ci4.w, rowc, a4.w, b4.w, e);
-          }
-          if (e.qres) {
-            // QLinearAdd(q, residual) (QLinearAdd.cpp:46-104): body
-            // fma(a, sa, fma(b, sb, fixed)), rne, saturate; tail elements
-            // fma(sa, a - a_zp, sb * (b - b_zp)) + y_zp.
-            const uint8_t* rp = e.qres + (size_t)m * e.ldy + n0 + c0;
-            uint8_t rb[32];
-            if (res_tma) {
-              constexpr int SEG = Cfg::OUT_SEG;
+          // q[j]: the requantised value in the low byte
+          uint32_t q[CW];
+          const bool fused = (EPI == EPI_R2A) || e.qres != nullptr;
+          // residual words (4 bytes each) of this row's CW columns
+          uint32_t rw[CW / 4];
+          if (fused) {
+            if constexpr (EPI == EPI_R2A) {
               const int h = pc / SEG, cc = (pc % SEG) >> 4;
-              const int f = SEG == 128 ? (lane & 7) : (SEG == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
-              const uint8_t* seg = stg + h * (32 * SEG) + lane * SEG;
-              *reinterpret_cast<uint4*>(rb) = *reinterpret_cast<const uint4*>(seg + ((cc ^ f) << 4));
-              *reinterpret_cast<uint4*>(rb + 16) = *reinterpret_cast<const uint4*>(seg + (((cc + 1) ^ f) << 4));
-            } else if (nvalid == 32 && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
-              *reinterpret_cast<uint4*>(rb) = reinterpret_cast<const uint4*>(rp)[0];
-              *reinterpret_cast<uint4*>(rb + 16) = reinterpret_cast<const uint4*>(rp)[1];
-            } else {
+              const uint8_t* seg = rstg + h * (32 * SEG) + lane * SEG;
 #pragma unroll
-              for (int j = 0; j < 32; ++j) rb[j] = j < nvalid ? rp[j] : 0;
-            }
-            const long long ebase = (long long)m * e.N + n0 + c0;
-            if (ebase + 32 <= e.qa_vec_end) {  // whole chunk in the 16-wide body (the common case)
-              const float sa = e.qa_sa, sb = e.qa_sb, fx = e.qa_fixed;
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int r = __float2int_rn(__fmaf_rn((float)q[j], sa, __fmaf_rn((float)rb[j], sb, fx)));
-                q[j] = (uint32_t)min(max(r, 0), 255);
+              for (int k = 0; k < CW / 16; ++k) {
+                const uint4 r0 = *reinterpret_cast<const uint4*>(seg + (((cc + k) ^ swz) << 4));
+                rw[4 * k] = r0.x; rw[4 * k + 1] = r0.y; rw[4 * k + 2] = r0.z; rw[4 * k + 3] = r0.w;
               }
             } else {
+              const uint8_t* rp = e.qres + (size_t)m * e.ldy + n0 + c0;
+              if (nvalid == CW && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float fa = (float)q[j], fb = (float)rb[j];
+                for (int k = 0; k < CW / 16; ++k) {
+                  const uint4 r0 = reinterpret_cast<const uint4*>(rp)[k];
+                  rw[4 * k] = r0.x; rw[4 * k + 1] = r0.y; rw[4 * k + 2] = r0.z; rw[4 * k + 3] = r0.w;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < CW / 4; ++j) {
+                  uint32_t x = 0;
+#pragma unroll
+                  for (int u = 0; u < 4; ++u)
+                    if (4 * j + u < nvalid) x |= (uint32_t)rp[4 * j + u] << (8 * u);
+                  rw[j] = x;
+                }
+              }
+            }
+          }
+          const long long ebase = (long long)m * e.N + n0 + c0;
+          bool scalar_add = fused;  // cleared when the vectorised body below covers the chunk
+          if (EPI == EPI_R2 || EPI == EPI_R2A) {
+            float t[CW];  // RND_MAGIC + rne(f)
+#pragma unroll
+            for (int j = 0; j < CW; j += 4) {
+              const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
+              const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
+              t[j + 0] = r2_magic((int32_t)v[j + 0], ci4.x, a4.x, e);
+              t[j + 1] = r2_magic((int32_t)v[j + 1], ci4.y, a4.y, e);
+              t[j + 2] = r2_magic((int32_t)v[j + 2], ci4.z, a4.z, e);
+              t[j + 3] = r2_magic((int32_t)v[j + 3], ci4.w, a4.w, e);
+            }
+            if (fused && ebase + CW <= e.qa_vec_end) {
+              // QLinearAdd(q, residual) body (QLinearAdd.cpp:46-104):
+              // fma(a, sa, fma(b, sb, fixed)), rne, saturate; a = rne(f) + y_zp
+              // is t - (RND_MAGIC - y_zp), exact (integers below 2^24)
+              const float sa = e.qa_sa, sb = e.qa_sb, fx = e.qa_fixed;
+              const float ca = __fsub_rn(e.yzp_f, RND_MAGIC);
+#pragma unroll
+              for (int j = 0; j < CW; ++j) {
+                const float fa = __fadd_rn(t[j], ca);
+                const float fb = byte_to_float(rw[j >> 2], j & 3);
+                float r = __fmaf_rn(fa, sa, __fmaf_rn(fb, sb, fx));
+                r = fminf(fmaxf(r, 0.0f), 255.0f);
+                q[j] = __float_as_uint(__fadd_rn(r, RND_MAGIC));
+              }
+              scalar_add = false;
+            } else {
+#pragma unroll
+              for (int j = 0; j < CW; ++j) q[j] = __float_as_uint(t[j]) + (uint32_t)e.yzp;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < CW; j += 4) {
+              const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
+              const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
+              const float4 b4 = *reinterpret_cast<const float4*>(s_f2 + pc + j);
+              q[j + 0] = requant_u8<EPI>((int32_t)v[j + 0], ci4.x, rowc, a4.x, b4.x, e);
+              q[j + 1] = requant_u8<EPI>((int32_t)v[j + 1], ci4.y, rowc, a4.y, b4.y, e);
+              q[j + 2] = requant_u8<EPI>((int32_t)v[j + 2], ci4.z, rowc, a4.z, b4.z, e);
+              q[j + 3] = requant_u8<EPI>((int32_t)v[j + 3], ci4.w, rowc, a4.w, b4.w, e);
+            }
+          }
+          if (scalar_add) {
+              // element-wise QLinearAdd: the 16-wide body for elements below
+              // qa_vec_end, nnr's scalar tail formula
+              // fma(sa, a - a_zp, sb * (b - b_zp)) + y_zp for the rest
+#pragma unroll
+              for (int j = 0; j < CW; ++j) {
+                const int qa = (int)(q[j] & 0xFFu), qb = (int)((rw[j >> 2] >> (8 * (j & 3))) & 0xFFu);
                 int r;
                 if (ebase + j < e.qa_vec_end) {
-                  r = __float2int_rn(__fmaf_rn(fa, e.qa_sa, __fmaf_rn(fb, e.qa_sb, e.qa_fixed)));
+                  r = __float2int_rn(__fmaf_rn((float)qa, e.qa_sa, __fmaf_rn((float)qb, e.qa_sb, e.qa_fixed)));
                 } else {
-                  const float da = (float)((int)q[j] - e.qa_azp), db = (float)((int)rb[j] - e.qa_bzp);
+                  const float da = (float)(qa - e.qa_azp), db = (float)(qb - e.qa_bzp);
                   r = __float2int_rn(__fadd_rn(__fmaf_rn(e.qa_sa, da, __fmul_rn(e.qa_sb, db)), (float)e.qa_yzp));
                 }
                 q[j] = (uint32_t)(r < 0 ? 0 : (r > 255 ? 255 : r));
               }
-            }
           }
           uint8_t* y = static_cast<uint8_t*>(e.y);
-          uint32_t w[8];
+          uint32_t w[CW / 4];
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            w[j] = q[4 * j] | (q[4 * j + 1] << 8) | (q[4 * j + 2] << 16) | (q[4 * j + 3] << 24);
+          for (int j = 0; j < CW / 4; ++j) w[j] = pack_low_bytes(q[4 * j], q[4 * j + 1], q[4 * j + 2], q[4 * j + 3]);
           if (y_tma) {
-            // swizzled staging (matches the store map's 128B / 64B swizzle):
-            // row r, 16-byte chunk c of a segment lives at r*SEG + ((c ^ f(r)) << 4)
-            constexpr int SEG = Cfg::OUT_SEG;
             const int h = pc / SEG, cc = (pc % SEG) >> 4;
-            const int f = SEG == 128 ? (lane & 7) : (SEG == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
             uint8_t* seg = stg + h * (32 * SEG) + lane * SEG;
-            ptx::st_shared_v4(seg + ((cc ^ f) << 4), w[0], w[1], w[2], w[3]);
-            ptx::st_shared_v4(seg + (((cc + 1) ^ f) << 4), w[4], w[5], w[6], w[7]);
+#pragma unroll
+            for (int k = 0; k < CW / 16; ++k)
+              ptx::st_shared_v4(seg + (((cc + k) ^ swz) << 4), w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
           } else if (e.y_layout == 0) {
             uint8_t* dst = y + (size_t)m * e.ldy + n0 + c0;
-            if (nvalid == 32 && (e.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0) {
-              reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-              reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+            if (nvalid == CW && (e.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0) {
+#pragma unroll
+              for (int k = 0; k < CW / 16; ++k)
+                reinterpret_cast<uint4*>(dst)[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
             } else {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
+              for (int j = 0; j < CW; ++j)
                 if (j < nvalid) dst[j] = (uint8_t)q[j];
             }
           } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
+            for (int j = 0; j < CW; ++j)
               if (j < nvalid) y[((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix] = (uint8_t)q[j];
           }
         }
-            };
-      // TMEM loads are double-buffered: chunk i + 1 is in flight while i is processed
-      uint32_t va[32], vb[32];
-      ptx::tmem_ld32_async(t_addr + (uint32_t)col0, va);
-      ptx::tmem_wait_ld(va);
+      };
+      // Interior tiles of u8 epilogues with a TMA-stored output take a lean
+      // path: no row / column / tail checks, one inlined copy in the loop.
+      bool fast = false;
+      if constexpr (EPI != EPI_F32)
+        fast = y_tma && m0 + BM <= e.M && n0 + BN <= e.N &&
+               (EPI == EPI_R2A ? (long long)(m0 + BM) * e.N <= e.qa_vec_end : e.qres == nullptr);
+      auto chunk_fast = [&](const int c0, uint32_t (&v)[CW]) {
+        if constexpr (EPI != EPI_F32) {
+          const int pc = c0 - col0;
+          uint32_t q[CW];
+          if constexpr (EPI == EPI_R2 || EPI == EPI_R2A) {
+#pragma unroll
+            for (int j = 0; j < CW; j += 4) {
+              const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
+              const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
+              q[j + 0] = __float_as_uint(r2_magic((int32_t)v[j + 0], ci4.x, a4.x, e));
+              q[j + 1] = __float_as_uint(r2_magic((int32_t)v[j + 1], ci4.y, a4.y, e));
+              q[j + 2] = __float_as_uint(r2_magic((int32_t)v[j + 2], ci4.z, a4.z, e));
+              q[j + 3] = __float_as_uint(r2_magic((int32_t)v[j + 3], ci4.w, a4.w, e));
+            }
+            if constexpr (EPI == EPI_R2A) {
+              const int h = pc / SEG, cc = (pc % SEG) >> 4;
+              const uint8_t* seg = rstg + h * (32 * SEG) + lane * SEG;
+              uint32_t rw[CW / 4];
+#pragma unroll
+              for (int k = 0; k < CW / 16; ++k) {
+                const uint4 r0 = *reinterpret_cast<const uint4*>(seg + (((cc + k) ^ swz) << 4));
+                rw[4 * k] = r0.x; rw[4 * k + 1] = r0.y; rw[4 * k + 2] = r0.z; rw[4 * k + 3] = r0.w;
+              }
+              const float sa = e.qa_sa, sb = e.qa_sb, fx = e.qa_fixed;
+              const float ca = __fsub_rn(e.yzp_f, RND_MAGIC);
+#pragma unroll
+              for (int j = 0; j < CW; ++j) {
+                const float fa = __fadd_rn(__uint_as_float(q[j]), ca);
+                const float fb = byte_to_float(rw[j >> 2], j & 3);
+                float r = __fmaf_rn(fa, sa, __fmaf_rn(fb, sb, fx));
+                r = fminf(fmaxf(r, 0.0f), 255.0f);
+                q[j] = __float_as_uint(__fadd_rn(r, RND_MAGIC));
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < CW; ++j) q[j] += (uint32_t)e.yzp;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < CW; j += 4) {
+              const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
+              const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
+              const float4 b4 = *reinterpret_cast<const float4*>(s_f2 + pc + j);
+              q[j + 0] = requant_u8<EPI>((int32_t)v[j + 0], ci4.x, rowc, a4.x, b4.x, e);
+              q[j + 1] = requant_u8<EPI>((int32_t)v[j + 1], ci4.y, rowc, a4.y, b4.y, e);
+              q[j + 2] = requant_u8<EPI>((int32_t)v[j + 2], ci4.z, rowc, a4.z, b4.z, e);
+              q[j + 3] = requant_u8<EPI>((int32_t)v[j + 3], ci4.w, rowc, a4.w, b4.w, e);
+            }
+          }
+          const int h = pc / SEG, cc = (pc % SEG) >> 4;
+          uint8_t* seg = stg + h * (32 * SEG) + lane * SEG;
+#pragma unroll
+          for (int k = 0; k < CW / 16; ++k)
+            ptx::st_shared_v4(seg + (((cc + k) ^ swz) << 4), pack_low_bytes(q[16 * k], q[16 * k + 1], q[16 * k + 2], q[16 * k + 3]),
+                              pack_low_bytes(q[16 * k + 4], q[16 * k + 5], q[16 * k + 6], q[16 * k + 7]),
+                              pack_low_bytes(q[16 * k + 8], q[16 * k + 9], q[16 * k + 10], q[16 * k + 11]),
+                              pack_low_bytes(q[16 * k + 12], q[16 * k + 13], q[16 * k + 14], q[16 * k + 15]));
+        }
+      };
+      uint32_t va[CW], vb[CW];
+      int tev = 0;
+      if (fast) {
+        // many epilogue warps per SM hide the TMEM load latency: one buffer
 #pragma unroll 1
-      for (int c0 = col0; c0 < col0 + HB; c0 += 64) {
-        const bool has_b = c0 + 32 < col0 + HB;
-        if (has_b) ptx::tmem_ld32_async(t_addr + (uint32_t)(c0 + 32), vb);
+        for (int c0 = col0; c0 < col0 + HB; c0 += CW) {
+          ptx::tmem_ld_async(t_addr + (uint32_t)c0, va);
+          ptx::tmem_wait_ld(va);
+          chunk_fast(c0, va);
+          if (lane == 0) NNRCU_TRACE2_AT(warp, lt, tev++);
+        }
+      } else if (SPLIT == 4) {
+#pragma unroll 1
+        for (int c0 = col0; c0 < col0 + HB; c0 += CW) {
+          ptx::tmem_ld_async(t_addr + (uint32_t)c0, va);
+          ptx::tmem_wait_ld(va);
+          chunk(c0, va);
+        }
+      } else {
+      // few epilogue warps: TMEM loads double-buffered, chunk i + 1 in flight while i is processed
+      ptx::tmem_ld_async(t_addr + (uint32_t)col0, va);
+      ptx::tmem_wait_ld(va);
+      if (lane == 0) NNRCU_TRACE2_AT(warp, lt, tev++);
+#pragma unroll 1
+      for (int c0 = col0; c0 < col0 + HB; c0 += 2 * CW) {
+        const bool has_b = c0 + CW < col0 + HB;
+        if (has_b) ptx::tmem_ld_async(t_addr + (uint32_t)(c0 + CW), vb);
         chunk(c0, va);
+        if (lane == 0) NNRCU_TRACE2_AT(warp, lt, tev++);
         if (has_b) {
           ptx::tmem_wait_ld(vb);
-          const bool has_a = c0 + 64 < col0 + HB;
-          if (has_a) ptx::tmem_ld32_async(t_addr + (uint32_t)(c0 + 64), va);
-          chunk(c0 + 32, vb);
+          if (lane == 0) NNRCU_TRACE2_AT(warp, lt, tev++);
+          const bool has_a = c0 + 2 * CW < col0 + HB;
+          if (has_a) ptx::tmem_ld_async(t_addr + (uint32_t)(c0 + 2 * CW), va);
+          chunk(c0 + CW, vb);
+          if (lane == 0) NNRCU_TRACE2_AT(warp, lt, tev++);
           if (has_a) ptx::tmem_wait_ld(va);
+          if (lane == 0) NNRCU_TRACE2_AT(warp, lt, tev++);
         }
       }
+      }
+      if (lane == 0) NNRCU_TRACE_AT(warp, lt, 3);
       // hand the accumulator back to the MMA warp
       ptx::tc_fence_before();
       __syncwarp();
@@ -664,11 +893,12 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       }
     }
     if (EPI != EPI_F32 && y_tma && lane == 0) ptx::bulk_wait0();  // stores complete before smem is released
+    if (EPI == EPI_R2A && res_failed) ptx::settle_ns(200000);      // residual loads still in flight land first
   }
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == 9) {
+  if (warp == R::MMA_WARP) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }

@@ -10,7 +10,7 @@ namespace {
 
 template <int BN, int NPLANE, int AMODE, int EPI, int KB = BKB>
 int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
-  using Cfg = TileCfg<BN, NPLANE, EPI, KB, (AMODE == A_GATHER ? 1 : 2)>;
+  using Cfg = TileCfg<BN, NPLANE, EPI, KB, Roles<AMODE, BN>::SPLIT>;
   auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI, KB>;
   // The attribute is per function; setting it is cheap but not free, so do it
   // once per device.
@@ -37,7 +37,8 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
     y_tma = 1;
   }
   CUtensorMap tmR{};
-  if (y_tma && e.qres) {
+  if (EPI == EPI_R2A) {
+    if (!y_tma) return set_error(NNRCU_ERR_INVALID, "the prefetched residual add needs a TMA-stored output");
     if (reinterpret_cast<uintptr_t>(e.qres) & 15) return set_error(NNRCU_ERR_INVALID, "residual must be 16-byte aligned");
     const int seg = Cfg::OUT_SEG;
     int rc = encode_tmap_2d(&tmR, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.qres, (uint64_t)e.N, (uint64_t)e.M,
@@ -46,7 +47,7 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
                                        : (seg == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B));
     if (rc != NNRCU_OK) return rc;
   }
-  kern<<<grid, NUM_THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, tmY, tmR, y_tma, L.b_plane_rows, g,
+  kern<<<grid, Roles<AMODE, BN>::THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, tmY, tmR, y_tma, L.b_plane_rows, g,
                                                        e, L.num_kb, L.m_tiles, L.n_tiles);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
@@ -58,6 +59,7 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
     // 64-byte K slabs (channel strides of 64 bytes): int8, TMA-fed A only
     if (L.nplane != 1 || L.amode == A_GATHER)
       return set_error(NNRCU_ERR_INVALID, "64-byte K slabs need int8 with a TMA-fed A operand");
+    if (L.epi == EPI_R2A && L.amode == A_TMA) return launch_one<BN, 1, A_TMA, EPI_R2A, 64>(L, g, e, st);
     if (L.amode == A_IM2COL) {
       if (L.epi == EPI_R1) return launch_one<BN, 1, A_IM2COL, EPI_R1, 64>(L, g, e, st);
       if (L.epi == EPI_R2) return launch_one<BN, 1, A_IM2COL, EPI_R2, 64>(L, g, e, st);
@@ -85,6 +87,7 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
     switch (L.epi) {
       case EPI_R1: return launch_one<BN, 1, A_TMA, EPI_R1>(L, g, e, st);
       case EPI_R2: return launch_one<BN, 1, A_TMA, EPI_R2>(L, g, e, st);
+      case EPI_R2A: return launch_one<BN, 1, A_TMA, EPI_R2A>(L, g, e, st);
       case EPI_R4: return launch_one<BN, 1, A_TMA, EPI_R4>(L, g, e, st);
       default: break;
     }
@@ -102,6 +105,25 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
 
 }  // namespace
 
+#ifdef NNRCU_TRACE
+extern "C" int nnrcu_trace_read(void* host, size_t bytes) {
+  NNRCU_CUDA(cudaDeviceSynchronize());
+  NNRCU_CUDA(cudaMemcpyFromSymbol(host, g_trace, bytes < sizeof(g_trace) ? bytes : sizeof(g_trace)));
+  void* dev = nullptr;
+  NNRCU_CUDA(cudaGetSymbolAddress(&dev, g_trace));
+  NNRCU_CUDA(cudaMemset(dev, 0, sizeof(g_trace)));
+  return NNRCU_OK;
+}
+extern "C" int nnrcu_trace2_read(void* host, size_t bytes) {
+  NNRCU_CUDA(cudaDeviceSynchronize());
+  NNRCU_CUDA(cudaMemcpyFromSymbol(host, g_trace2, bytes < sizeof(g_trace2) ? bytes : sizeof(g_trace2)));
+  void* dev = nullptr;
+  NNRCU_CUDA(cudaGetSymbolAddress(&dev, g_trace2));
+  NNRCU_CUDA(cudaMemset(dev, 0, sizeof(g_trace2)));
+  return NNRCU_OK;
+}
+#endif
+
 int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
   if (L.m_tiles <= 0 || L.n_tiles <= 0 || L.num_kb <= 0) return NNRCU_OK;
   if ((long long)L.m_tiles * L.n_tiles > 0x7fffffffLL)
@@ -109,10 +131,16 @@ int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaSt
   if (L.amode == A_GATHER && ((reinterpret_cast<uintptr_t>(g.x) & 15) || (g.x2 && (reinterpret_cast<uintptr_t>(g.x2) & 15)) ||
                               (g.cbytes & 15)))
     return set_error(NNRCU_ERR_INVALID, "gathered operand must be 16-byte aligned with a 16-byte pixel stride");
+  // an R2 requant with a fused add whose output and residual can move by
+  // TMA (16-byte aligned NHWC rows) runs the residual-prefetching instance
+  TcLaunch L2 = L;
+  if (L.epi == EPI_R2 && L.amode == A_TMA && e.qres && e.y_layout == 0 && (e.ldy & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 && (reinterpret_cast<uintptr_t>(e.qres) & 15) == 0)
+    L2.epi = EPI_R2A;
   switch (L.bn) {
-    case 64: return dispatch_bn<64>(L, g, e, stream);
-    case 128: return dispatch_bn<128>(L, g, e, stream);
-    case 256: return dispatch_bn<256>(L, g, e, stream);
+    case 64: return dispatch_bn<64>(L2, g, e, stream);
+    case 128: return dispatch_bn<128>(L2, g, e, stream);
+    case 256: return dispatch_bn<256>(L2, g, e, stream);
     default: return set_error(NNRCU_ERR_INVALID, "unsupported N tile %d", L.bn);
   }
 }
