@@ -105,6 +105,38 @@ __global__ void im2col_u8_kernel(const uint8_t* __restrict x, uint8_t* __restric
   }
 }
 
+// Space-to-depth reorder of a small-channel image into 16-byte s2d pixels
+// inside a fill border (the s2d conv path). One thread per padded pixel.
+__global__ void s2d_u8_kernel(const uint8_t* __restrict x, int nchw, uint8_t* __restrict dst, int n, int c, int h,
+                              int w, int hp, int wp, int pt, int pl, uint8_t fill) {
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const long long total = (long long)n * hp * wp;
+  if (idx >= total) return;
+  const int X = (int)(idx % wp);
+  const int Y = (int)((idx / wp) % hp);
+  const int b = (int)(idx / ((long long)wp * hp));
+  uint32_t wv[4];
+  const uint32_t f4 = 0x01010101u * fill;
+  wv[0] = wv[1] = wv[2] = wv[3] = f4;
+#pragma unroll
+  for (int dy = 0; dy < 2; ++dy) {
+    const int ih = 2 * (Y - pt) + dy;
+    if (ih < 0 || ih >= h) continue;
+#pragma unroll
+    for (int dx = 0; dx < 2; ++dx) {
+      const int iw = 2 * (X - pl) + dx;
+      if (iw < 0 || iw >= w) continue;
+      for (int ci = 0; ci < c; ++ci) {
+        const uint8_t v = nchw ? x[(((size_t)b * c + ci) * h + ih) * w + iw] : x[(((size_t)b * h + ih) * w + iw) * c + ci];
+        const int byte = (dy * 2 + dx) * c + ci;
+        const int sh = 8 * (byte & 3);
+        wv[byte >> 2] = (wv[byte >> 2] & ~(0xFFu << sh)) | ((uint32_t)v << sh);
+      }
+    }
+  }
+  reinterpret_cast<uint4*>(dst)[idx] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+}
+
 __global__ void pad_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, long long pixels, int c,
                                    int cs, uint8_t fill) {
   const long long total = pixels * cs;
@@ -426,6 +458,16 @@ int launch_im2col_u8(const uint8_t* x, uint8_t* a, int nchw, int n, int c, int h
   const long long total = (long long)n * oh * ow * (kp / 16);
   im2col_u8_kernel<<<grid_for(total, 256), 256, 0, st>>>(x, a, nchw, n, c, h, w, oh, ow, kh, kw, sh, sw, pt, pl, dh, dw,
                                                           kp, x_zp);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_s2d_u8(const uint8_t* x, int nchw, uint8_t* dst, int n, int c, int h, int w, int hp, int wp, int pt, int pl,
+                  uint8_t fill, cudaStream_t st) {
+  if (c * 4 > 16 || (reinterpret_cast<uintptr_t>(dst) & 15))
+    return set_error(NNRCU_ERR_INVALID, "space-to-depth needs 4c <= 16 and a 16-byte aligned destination");
+  const long long total = (long long)n * hp * wp;
+  s2d_u8_kernel<<<grid_for(total, 256), 256, 0, st>>>(x, nchw, dst, n, c, h, w, hp, wp, pt, pl, fill);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

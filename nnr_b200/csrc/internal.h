@@ -36,6 +36,10 @@ int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
                        int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw,
                        int kslab = 128);
 
+// cuTensorMapEncodeTiled of a 3-d tensor (dims innermost first, unswizzled).
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
+                   const uint64_t strides_bytes[2], const uint32_t box[3]);
+
 enum OpKind : int { OP_QCONV = 1, OP_QMATMUL = 2, OP_CONV_F32 = 3, OP_GEMM_F32 = 4, OP_DWCONV_F32 = 5 };
 
 // One prepared operator: packed weights on the device plus everything the
@@ -59,7 +63,13 @@ struct Op {
   int cs = 0;                   // device channel stride (elements) of the NHWC operand
   bool need_in_copy = false;    // input must be re-laid-out into the workspace first
   bool pad_in = false;
-  bool explicit_im2col = false; // small-C conv: A materialised densely as [M][kpad] in the workspace          // ... spatially padded with x_zp (im2col path with x_zp != 0)
+  bool explicit_im2col = false; // small-C conv: A materialised densely as [M][kpad] in the workspace
+  // Space-to-depth form of a stride-2 small-channel conv (the stem): the
+  // input is reordered into s2d pixels of 16 bytes ((dy, dx, c) for 4c <= 16)
+  // inside an x_zp border, and convolved at stride 1 with an s2d kernel
+  // s2d_kh x s2d_kw (taps of 16 bytes, 8 per 128-byte K slab).
+  bool s2d = false;
+  int s2d_kh = 0, s2d_kw = 0, s2d_pt = 0, s2d_pl = 0, s2d_hp = 0, s2d_wp = 0;
   // device buffers (owned)
   void* wB = nullptr;
   int32_t* colcorr = nullptr;
@@ -96,7 +106,8 @@ struct TcLaunch {
   const CUtensorMap* tmB;
   int b_plane_rows;
   int num_kb;
-  int kb_bytes = 128;  // K bytes per pipeline stage (128, or 64 for 64-byte channel strides)
+  int kb_bytes = 128;  // K bytes per pipeline stage (128, or 64 for 64-byte channel strides);
+                       // 16: 128-byte stages of eight 16-byte taps (the s2d path)
 };
 struct GatherGeom;
 struct EpiParams;
@@ -112,6 +123,12 @@ int launch_nchw_to_nhwc_u8_padded(const uint8_t* src, uint8_t* dst, int n, int c
                                   int pb, int pr, int cs, uint8_t fill, cudaStream_t st);
 int launch_im2col_u8(const uint8_t* x, uint8_t* a, int nchw, int n, int c, int h, int w, int oh, int ow, int kh,
                      int kw, int sh, int sw, int pt, int pl, int dh, int dw, int kp, uint8_t x_zp, cudaStream_t st);
+// Space-to-depth reorder into the padded layout of the s2d conv path:
+// dst[n][hp][wp][16], pixel (Y, X) holds input (2(Y - pt) + dy, 2(X - pl) + dx)
+// channels c at byte (dy * 2 + dx) * C + c; out-of-image bytes and the bytes
+// past 4C hold fill.
+int launch_s2d_u8(const uint8_t* x, int nchw, uint8_t* dst, int n, int c, int h, int w, int hp, int wp, int pt, int pl,
+                  uint8_t fill, cudaStream_t st);
 int launch_pad_nhwc_u8(const uint8_t* src, uint8_t* dst, int pixels, int c, int cs, uint8_t fill, cudaStream_t st);
 int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
                            int cs, cudaStream_t st);

@@ -95,6 +95,13 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 // im2col-mode load: pixelsPerColumn pixels x channelsPerPixel channels,
 // starting at input position (w, h, n) plus the filter-tap offsets.
 __device__ __forceinline__ void tma_load_im2col_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c, int w, int h,
@@ -168,6 +175,18 @@ __device__ __forceinline__ uint64_t umma_desc_sw(uint32_t saddr) {
   return d;
 }
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) { return umma_desc_sw<128>(saddr); }
+// Descriptor of a K-major operand without swizzle, built from 16-byte wide
+// core-matrix columns: 8 rows x 16 bytes per core matrix (128 contiguous
+// bytes), row groups `sbo` bytes apart, K-adjacent 16-byte columns `lbo`
+// bytes apart.
+__device__ __forceinline__ uint64_t umma_desc_interleaved(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100); layout type 0 = no swizzle
+  return d;
+}
 
 // Instruction descriptor. dtype: 1 = f32, 2 = s32. atype/btype: for kind::i8
 // 0 = u8, 1 = s8; for kind::f16 1 = bf16. Both operands K-major.

@@ -144,10 +144,37 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
     op->kpad_bytes = round_up(op->kbytes, BKB);
     op->num_kb = op->kbytes / 64;
   }
+  // Stride-2 convs over at most 4 channels (the stem): space-to-depth. Input
+  // row 2*oh - pt + kh lands in s2d row oh + floor((kh - pt) / 2) at parity
+  // dy, so the conv becomes a stride-1 conv over 16-byte s2d pixels with an
+  // s2d kernel of s2d_kh x s2d_kw taps; weights of kernel positions outside
+  // the original kernel are zero, so the integer accumulators are unchanged.
+  if (d.c * 4 <= 16 && d.stride_h == 2 && d.stride_w == 2 && d.dil_h == 1 && d.dil_w == 1 && d.kh * d.kw > 1) {
+    auto fdiv2 = [](int a) { return a >= 0 ? a / 2 : -((1 - a) / 2); };  // floor(a / 2)
+    op->s2d = true;
+    op->explicit_im2col = false;
+    op->s2d_pt = -fdiv2(-d.pad_top);
+    op->s2d_pl = -fdiv2(-d.pad_left);
+    op->s2d_kh = fdiv2(d.kh - 1 - d.pad_top) - fdiv2(-d.pad_top) + 1;
+    op->s2d_kw = fdiv2(d.kw - 1 - d.pad_left) - fdiv2(-d.pad_left) + 1;
+    op->s2d_hp = oh + op->s2d_kh - 1;  // exactly the rows the stride-1 conv reads
+    op->s2d_wp = ow + op->s2d_kw - 1;
+    op->amode = A_IM2COL;
+    op->need_in_copy = false;
+    op->pad_in = false;
+    op->cs = 16;
+    op->kslab = 16;
+    const int taps = op->s2d_kh * op->s2d_kw;
+    op->num_kb = (taps + 7) / 8;
+    op->kbytes = taps * 16;
+    op->kpad_bytes = op->num_kb * 128;
+    op->bn = std::min(op->bn, 128);
+  }
   const size_t hp = d.h + (op->pad_in ? d.pad_top + d.pad_bottom : 0);
   const size_t wp = d.w + (op->pad_in ? d.pad_left + d.pad_right : 0);
   op->ws_bytes = op->need_in_copy ? (size_t)d.n * hp * wp * op->cs : 0;
   if (op->explicit_im2col) op->ws_bytes = (size_t)op->M * op->kbytes;
+  if (op->s2d) op->ws_bytes = (size_t)d.n * op->s2d_hp * op->s2d_wp * 16;
 
   // Pack B = W as [npad][kpad] K-major with k = (kh, kw, ic); padded channels,
   // taps and rows are zero. wsum feeds the x_zp compensation.
@@ -161,8 +188,15 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
       for (int y = 0; y < d.kh; ++y)
         for (int x = 0; x < d.kw; ++x) {
           const int8_t v = w_host[(((size_t)o * d.c + ic) * d.kh + y) * d.kw + x];
-          const int tap_stride = op->explicit_im2col ? d.c : op->cs;  // dense K for explicit im2col
-          B[(size_t)o * op->kpad_bytes + (size_t)(y * d.kw + x) * tap_stride + ic] = v;
+          if (op->s2d) {
+            // [tap][npad][16]: s2d tap (ky, kx), byte (dy * 2 + dx) * C + ic
+            const int ry = y + 2 * op->s2d_pt - d.pad_top, rx = x + 2 * op->s2d_pl - d.pad_left;
+            const int tap = (ry >> 1) * op->s2d_kw + (rx >> 1);
+            B[((size_t)tap * op->npad + o) * 16 + ((ry & 1) * 2 + (rx & 1)) * d.c + ic] = v;
+          } else {
+            const int tap_stride = op->explicit_im2col ? d.c : op->cs;  // dense K for explicit im2col
+            B[(size_t)o * op->kpad_bytes + (size_t)(y * d.kw + x) * tap_stride + ic] = v;
+          }
           wsum += v;
         }
     colcorr[o] = (int32_t)(0u - (uint32_t)x_zp * (uint32_t)wsum);
@@ -194,9 +228,16 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   NNRCU_TRY(upload(&op->cs_arr, csv));
   NNRCU_TRY(upload(&op->bias_f, bias_f));
   NNRCU_TRY(upload(&op->os, osv));
-  NNRCU_TRY(encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, op->kpad_bytes, op->npad, op->kpad_bytes,
-                           op->kslab, op->bn,
-                           op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
+  if (op->s2d) {
+    const uint64_t dims[3] = {16, (uint64_t)op->npad, (uint64_t)op->num_kb * 8};
+    const uint64_t strides[2] = {16, (uint64_t)op->npad * 16};
+    const uint32_t box[3] = {16, (uint32_t)op->bn, 8};
+    NNRCU_TRY(encode_tmap_3d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, dims, strides, box));
+  } else {
+    NNRCU_TRY(encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, op->kpad_bytes, op->npad, op->kpad_bytes,
+                             op->kslab, op->bn,
+                             op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
+  }
   *out = op;
   return NNRCU_OK;
 }
@@ -210,7 +251,12 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const nnrcu_conv_desc& d = op->d;
   const uint8_t* xin = x;
-  if (op->explicit_im2col) {
+  if (op->s2d) {
+    int rc = launch_s2d_u8(x, d.in_layout == NNRCU_LAYOUT_NCHW, static_cast<uint8_t*>(workspace), d.n, d.c, d.h, d.w,
+                           op->s2d_hp, op->s2d_wp, op->s2d_pt, op->s2d_pl, (uint8_t)op->x_zp, st);
+    if (rc != NNRCU_OK) return rc;
+    xin = static_cast<const uint8_t*>(workspace);
+  } else if (op->explicit_im2col) {
     int rc = launch_im2col_u8(x, static_cast<uint8_t*>(workspace), d.in_layout == NNRCU_LAYOUT_NCHW, d.n, d.c, d.h,
                               d.w, op->oh, op->ow, d.kh, d.kw, d.stride_h, d.stride_w, d.pad_top, d.pad_left, d.dil_h,
                               d.dil_w, op->kbytes, (uint8_t)op->x_zp, st);
@@ -245,7 +291,13 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   g.cbytes = op->cs;
   g.OH = op->oh; g.OW = op->ow; g.KH = d.kh; g.KW = d.kw;
   g.sh = d.stride_h; g.sw = d.stride_w; g.ph = pt; g.pw = pl; g.dh = d.dil_h; g.dw = d.dil_w;
-  if (op->amode == A_IM2COL) {
+  if (op->s2d) {
+    g.H = op->s2d_hp; g.W = op->s2d_wp; g.KH = op->s2d_kh; g.KW = op->s2d_kw;
+    g.sh = g.sw = 1; g.ph = g.pw = 0; g.dh = g.dw = 1;
+    int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, 16, 0, 0, 0, 0, g.KH, g.KW,
+                                1, 1, 1, 1, 16);
+    if (rc != NNRCU_OK) return rc;
+  } else if (op->amode == A_IM2COL) {
     int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, op->cs, pt, pl, pb, pr,
                                 d.kh, d.kw, d.dil_h, d.dil_w, d.stride_h, d.stride_w, op->kslab);
     if (rc != NNRCU_OK) return rc;

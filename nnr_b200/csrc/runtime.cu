@@ -109,6 +109,23 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
   return NNRCU_OK;
 }
 
+int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
+                   const uint64_t strides_bytes[2], const uint32_t box[3]) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NNRCU_OK) return rc;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (strides_bytes[0] & 15) != 0 || (strides_bytes[1] & 15) != 0)
+    return set_error(NNRCU_ERR_INVALID, "TMA operand must be 16-byte aligned");
+  const cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  const cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+  const cuuint32_t b[3] = {box[0], box[1], box[2]};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(NNRCU_ERR_CUDA, "cuTensorMapEncodeTiled (3-d) failed (%d)", (int)r);
+  return NNRCU_OK;
+}
+
 int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_bytes, const void* base, int n, int h,
                        int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw,
                        int kslab) {
@@ -116,8 +133,10 @@ int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
   int rc = current_device(&dev);
   if (rc != NNRCU_OK) return rc;
   const uint64_t row = (uint64_t)c * elem_bytes;
-  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (kslab != 128 && kslab != 64) || (row % kslab) != 0)
-    return set_error(NNRCU_ERR_INVALID, "im2col operand must be 16-byte aligned with a 128-byte multiple channel stride");
+  // kslab: bytes of channels per pixel in one copy (128 / 64 with the
+  // matching swizzle; 16 = one whole 16-byte pixel, unswizzled)
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0 || (kslab != 128 && kslab != 64 && kslab != 16) || (row % kslab) != 0)
+    return set_error(NNRCU_ERR_INVALID, "im2col operand must be 16-byte aligned with a channel stride in whole copies");
   const cuuint64_t dims[4] = {(cuuint64_t)c, (cuuint64_t)w, (cuuint64_t)h, (cuuint64_t)n};
   const cuuint64_t strides[3] = {row, row * (uint64_t)w, row * (uint64_t)w * (uint64_t)h};
   const int lower[2] = {-pl, -pt};
@@ -125,7 +144,8 @@ int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
   const cuuint32_t estr[4] = {1, (cuuint32_t)sw, (cuuint32_t)sh, 1};
   CUresult r = g_encode_im2col(map, dtype, 4, const_cast<void*>(base), dims, strides, lower, upper,
                                (cuuint32_t)(kslab / elem_bytes), 128, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                               kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                               kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                            : (kslab == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE),
                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)

@@ -125,8 +125,10 @@ struct EpiParams {
 
 template <int BN, int NPLANE, int EPI, int KB = BKB, int SPLIT = 1>
 struct TileCfg {
-  static constexpr int A_BYTES = BM * KB;              // 16 KB per plane (8 KB with 64-byte slabs)
-  static constexpr int B_BYTES = BN * KB;
+  // K bytes per stage: KB, except KB = 16 (eight 16-byte taps per 128-byte stage)
+  static constexpr int SLAB = KB == 16 ? 128 : KB;
+  static constexpr int A_BYTES = BM * SLAB;            // 16 KB per plane (8 KB with 64-byte slabs)
+  static constexpr int B_BYTES = BN * SLAB;
   static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + B_BYTES);
   // u8 epilogues stage each warp's 32 x BN output block for a TMA store
   static constexpr int OUT_BLOCK = (EPI == EPI_F32) ? 0 : 4 * 32 * BN;  // one 32 x HB block per epilogue warp
@@ -355,6 +357,20 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           uint8_t* a_st = sA + (size_t)s * NPLANE * A_BYTES;
           uint8_t* b_st = sB + (size_t)s * NPLANE * B_BYTES;
           const int kx = kb * KB / (NPLANE == 2 ? 2 : 1);  // element coordinate along K
+          if constexpr (KB == 16) {
+            // B: [tap][row][16 B] -> eight taps x BN rows x 16 B; A: one
+            // hardware im2col copy (128 pixels x 16 B) per tap. Taps past the
+            // kernel (zero weights) re-read the last tap to keep the byte count.
+            ptx::tma_load_3d(b_st, &tmB, &full_bar[s], 0, n0, kb * 8);
+            const int taps = g.KH * g.KW;
+#pragma unroll 1
+            for (int j = 0; j < 8; ++j) {
+              const int tap = min(kb * 8 + j, taps - 1);
+              const int kh = tap / g.KW, kw = tap - kh * g.KW;
+              ptx::tma_load_im2col_4d(a_st + j * (BM * 16), &tmA0, &full_bar[s], 0, i_w, i_h, i_n,
+                                      (uint16_t)(kw * g.dw), (uint16_t)(kh * g.dh));
+            }
+          } else {
           for (int p = 0; p < NPLANE; ++p)
             ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
           if (AMODE == A_TMA) {
@@ -369,6 +385,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             const uint16_t ow_off = (uint16_t)(kw * g.dw), oh_off = (uint16_t)(kh * g.dh);
             ptx::tma_load_im2col_4d(a_st, &tmA0, &full_bar[s], cc, i_w, i_h, i_n, ow_off, oh_off);
             if (NPLANE == 2) ptx::tma_load_im2col_4d(a_st + A_BYTES, &tmA1, &full_bar[s], cc, i_w, i_h, i_n, ow_off, oh_off);
+          }
           }
         }
         NNRCU_TRACE_AT(warp, tlt, 1);
@@ -398,9 +415,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * NPLANE * A_BYTES);
           const uint32_t b_addr = ptx::smem_u32(sB + (size_t)s * NPLANE * B_BYTES);
 #pragma unroll
-          for (int k = 0; k < KB / 32; ++k) {
+          for (int k = 0; k < Cfg::SLAB / 32; ++k) {
             const uint32_t koff = k * 32;
-            if constexpr (NPLANE == 1) {
+            if constexpr (KB == 16) {
+              // two 16-byte tap columns per K step
+              ptx::mma_i8(d_tmem, ptx::umma_desc_interleaved(a_addr + k * 2 * (BM * 16), BM * 16, 128),
+                          ptx::umma_desc_interleaved(b_addr + k * 2 * (BN * 16), BN * 16, 128), idesc, (kb | k) != 0);
+            } else if constexpr (NPLANE == 1) {
               ptx::mma_i8(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff), ptx::umma_desc_sw<KB>(b_addr + koff), idesc,
                           (kb | k) != 0);
             } else {

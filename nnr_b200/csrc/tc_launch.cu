@@ -55,6 +55,18 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
 
 template <int BN>
 int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t st) {
+  if (L.kb_bytes == 16) {
+    // eight 16-byte taps per stage (space-to-depth convs): int8 im2col, N tile <= 128
+    if constexpr (BN <= 128) {
+      if (L.nplane == 1 && L.amode == A_IM2COL) {
+        if (L.epi == EPI_R1) return launch_one<BN, 1, A_IM2COL, EPI_R1, 16>(L, g, e, st);
+        if (L.epi == EPI_R2) return launch_one<BN, 1, A_IM2COL, EPI_R2, 16>(L, g, e, st);
+        if (L.epi == EPI_R3) return launch_one<BN, 1, A_IM2COL, EPI_R3, 16>(L, g, e, st);
+      }
+    }
+    return set_error(NNRCU_ERR_INVALID, "no 16-byte-tap engine instance for bn %d amode %d epilogue %d", BN, L.amode,
+                     L.epi);
+  }
   if (L.kb_bytes == 64) {
     // 64-byte K slabs (channel strides of 64 bytes): int8, TMA-fed A only
     if (L.nplane != 1 || L.amode == A_GATHER)

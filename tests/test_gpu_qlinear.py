@@ -102,6 +102,30 @@ def test_stem_auto_r3(cuda_dev):
     assert np.array_equal(y, ref)
 
 
+S2D_SHAPES = [
+    # stride-2 convs over <= 4 channels run as space-to-depth convs (16-byte taps)
+    (2, 3, 64, 64, 64, 7, 7, (2, 2), (3, 3, 3, 3), (1, 1)),      # the ResNet stem
+    (1, 3, 37, 29, 128, 7, 7, (2, 2), (3, 2, 3, 4), (1, 1)),     # odd sizes, asymmetric pads, N tile 128
+    (2, 1, 20, 21, 48, 3, 3, (2, 2), (1, 1, 1, 1), (1, 1)),      # one channel, ragged N
+    (1, 4, 16, 18, 32, 5, 5, (2, 2), (0, 2, 1, 0), (1, 1)),      # four channels, no top pad
+    (3, 2, 15, 15, 64, 2, 2, (2, 2), (0, 0, 0, 0), (1, 1)),      # even kernel, one tap per s2d pixel
+    (1, 3, 9, 9, 16, 3, 4, (2, 2), (2, 1, 0, 2), (1, 1)),        # taps not a multiple of 8
+]
+
+
+@pytest.mark.parametrize("shape", S2D_SHAPES)
+@pytest.mark.parametrize("formula", [O.R1, O.R2, O.R3])
+@pytest.mark.parametrize("layouts", [("NCHW", "NHWC"), ("NHWC", "NCHW")])
+def test_space_to_depth_stride2(cuda_dev, shape, formula, layouts):
+    n, c, h, w, oc, kh, kw, s, p, d = shape
+    rng = np.random.default_rng(hash((shape, formula, "s2d")) & 0xffff)
+    for xz in (0, 131):
+        case = W.random_qconv(rng, n, c, h, w, oc, kh, kw, s, p, d, x_zp=xz)
+        y, _ = run_qconv(cuda_dev, case, formula, layouts[0], layouts[1])
+        ref = oracle_qconv(case, formula, layouts[1])
+        assert np.array_equal(y, ref), f"x_zp {xz}: {(y != ref).sum()} / {y.size} mismatches"
+
+
 def test_no_bias_per_tensor_scale(cuda_dev):
     rng = np.random.default_rng(11)
     case = W.random_qconv(rng, 1, 32, 10, 10, 32, 3, 3, (1, 1), (1, 1, 1, 1), per_channel=False, bias=False)
