@@ -36,9 +36,10 @@ int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
                        int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw,
                        int kslab = 128);
 
-// cuTensorMapEncodeTiled of a 3-d tensor (dims innermost first, unswizzled).
+// cuTensorMapEncodeTiled of a 3-d tensor (dims innermost first).
 int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
-                   const uint64_t strides_bytes[2], const uint32_t box[3]);
+                   const uint64_t strides_bytes[2], const uint32_t box[3],
+                   CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
 enum OpKind : int { OP_QCONV = 1, OP_QMATMUL = 2, OP_CONV_F32 = 3, OP_GEMM_F32 = 4, OP_DWCONV_F32 = 5 };
 
@@ -70,6 +71,7 @@ struct Op {
   // s2d_kh x s2d_kw (taps of 16 bytes, 8 per 128-byte K slab).
   bool s2d = false;
   int s2d_kh = 0, s2d_kw = 0, s2d_pt = 0, s2d_pl = 0, s2d_hp = 0, s2d_wp = 0;
+  int s2d_tpr = 0;              // A_ROWS: taps per s2d kernel row in K (0: hardware im2col instead)
   // device buffers (owned)
   void* wB = nullptr;
   int32_t* colcorr = nullptr;

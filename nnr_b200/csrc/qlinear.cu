@@ -164,7 +164,13 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
     op->pad_in = false;
     op->cs = 16;
     op->kslab = 16;
-    const int taps = op->s2d_kh * op->s2d_kw;
+    // kernel rows of at most 8 taps: one contiguous copy per kernel row
+    // (A_ROWS), taps padded to 2 / 4 / 8 per row; else hardware im2col
+    if (op->s2d_kw <= 8) {
+      op->s2d_tpr = op->s2d_kw <= 2 ? 2 : (op->s2d_kw <= 4 ? 4 : 8);
+      op->amode = A_ROWS;
+    }
+    const int taps = op->s2d_tpr ? op->s2d_kh * op->s2d_tpr : op->s2d_kh * op->s2d_kw;
     op->num_kb = (taps + 7) / 8;
     op->kbytes = taps * 16;
     op->kpad_bytes = op->num_kb * 128;
@@ -174,7 +180,8 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   const size_t wp = d.w + (op->pad_in ? d.pad_left + d.pad_right : 0);
   op->ws_bytes = op->need_in_copy ? (size_t)d.n * hp * wp * op->cs : 0;
   if (op->explicit_im2col) op->ws_bytes = (size_t)op->M * op->kbytes;
-  if (op->s2d) op->ws_bytes = (size_t)d.n * op->s2d_hp * op->s2d_wp * 16;
+  // (A_ROWS copies read up to BM + 8 pixels from a row start: slack at the end)
+  if (op->s2d) op->ws_bytes = (size_t)d.n * op->s2d_hp * op->s2d_wp * 16 + (op->s2d_tpr ? ROWS_BYTES : 0);
 
   // Pack B = W as [npad][kpad] K-major with k = (kh, kw, ic); padded channels,
   // taps and rows are zero. wsum feeds the x_zp compensation.
@@ -191,7 +198,7 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
           if (op->s2d) {
             // [tap][npad][16]: s2d tap (ky, kx), byte (dy * 2 + dx) * C + ic
             const int ry = y + 2 * op->s2d_pt - d.pad_top, rx = x + 2 * op->s2d_pl - d.pad_left;
-            const int tap = (ry >> 1) * op->s2d_kw + (rx >> 1);
+            const int tap = (ry >> 1) * (op->s2d_tpr ? op->s2d_tpr : op->s2d_kw) + (rx >> 1);
             B[((size_t)tap * op->npad + o) * 16 + ((ry & 1) * 2 + (rx & 1)) * d.c + ic] = v;
           } else {
             const int tap_stride = op->explicit_im2col ? d.c : op->cs;  // dense K for explicit im2col
@@ -294,9 +301,12 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   if (op->s2d) {
     g.H = op->s2d_hp; g.W = op->s2d_wp; g.KH = op->s2d_kh; g.KW = op->s2d_kw;
     g.sh = g.sw = 1; g.ph = g.pw = 0; g.dh = g.dw = 1;
-    int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, 16, 0, 0, 0, 0, g.KH, g.KW,
-                                1, 1, 1, 1, 16);
-    if (rc != NNRCU_OK) return rc;
+    g.tpr = op->s2d_tpr;
+    if (!op->s2d_tpr) {
+      int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, 16, 0, 0, 0, 0, g.KH,
+                                  g.KW, 1, 1, 1, 1, 16);
+      if (rc != NNRCU_OK) return rc;
+    }
   } else if (op->amode == A_IM2COL) {
     int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, op->cs, pt, pl, pb, pr,
                                 d.kh, d.kw, d.dil_h, d.dil_w, d.stride_h, d.stride_w, op->kslab);
@@ -334,7 +344,7 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
 
   TcLaunch L{};
   L.bn = op->bn; L.nplane = 1; L.amode = op->amode; L.epi = op->epi;
-  L.m_tiles = (op->M + BM - 1) / BM;
+  L.m_tiles = op->amode == A_ROWS ? d.n * op->oh * ((op->ow + BM - 1) / BM) : (op->M + BM - 1) / BM;
   L.n_tiles = (op->N + op->bn - 1) / op->bn;
   L.tmA0 = &tmA; L.tmA1 = &tmA; L.tmB = &op->tmB;
   L.b_plane_rows = op->npad;

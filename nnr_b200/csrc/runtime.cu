@@ -110,7 +110,7 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
 }
 
 int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
-                   const uint64_t strides_bytes[2], const uint32_t box[3]) {
+                   const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle) {
   int dev = 0;
   int rc = current_device(&dev);
   if (rc != NNRCU_OK) return rc;
@@ -121,7 +121,7 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
   const cuuint32_t b[3] = {box[0], box[1], box[2]};
   const cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = g_encode(map, dtype, 3, const_cast<void*>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(NNRCU_ERR_CUDA, "cuTensorMapEncodeTiled (3-d) failed (%d)", (int)r);
   return NNRCU_OK;
 }

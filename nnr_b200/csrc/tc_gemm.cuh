@@ -32,7 +32,12 @@
 
 namespace nnrcu {
 
-enum : int { A_TMA = 0, A_GATHER = 1, A_IM2COL = 2 };
+// A_ROWS: stride-1 convs over 16-byte pixels of a padded NHWC image (the
+// space-to-depth path). A tile covers up to 128 pixels of ONE output row; for
+// each kernel row one contiguous bulk copy brings BM + 8 input pixels, and the
+// kernel's taps along that row are the same rows shifted by 16 bytes each.
+enum : int { A_TMA = 0, A_GATHER = 1, A_IM2COL = 2, A_ROWS = 3 };
+constexpr int ROWS_BYTES = (128 + 8) * 16;  // one A_ROWS copy: BM + 8 pixels of 16 bytes
 // EPI_R2A: the R2 requant followed by a fused QLinearAdd whose residual
 // tiles are TMA-prefetched one tile ahead (u8 row-major output via TMA store).
 enum : int { EPI_R1 = 1, EPI_R2 = 2, EPI_R3 = 3, EPI_R4 = 4, EPI_R2A = 5, EPI_F32 = 10 };
@@ -89,6 +94,7 @@ struct GatherGeom {
   int OH, OW, KH, KW, sh, sw, ph, pw, dh, dw;
   int kbytes;            // real K in bytes = KH*KW*cbytes
   uint32_t pad_word;     // value written for padding pixels (x_zp replicated, or 0)
+  int tpr;               // A_ROWS: taps per kernel row in K (2, 4 or 8; taps past KW have zero weights)
 };
 
 struct EpiParams {
@@ -325,6 +331,23 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  // Output rows of an M tile: mb = first GEMM row, nvr = valid rows; A_ROWS
+  // tiles also give the output row (image * OH + oh) and first column ow0.
+  auto tile_rows = [&](const int mt, int& mb, int& nvr, int& orow, int& ow0) {
+    if constexpr (AMODE == A_ROWS) {
+      const int owt = (g.OW + BM - 1) / BM;
+      orow = mt / owt;
+      ow0 = (mt - orow * owt) * BM;
+      mb = orow * g.OW + ow0;
+      nvr = min(BM, g.OW - ow0);
+    } else {
+      orow = 0;
+      ow0 = 0;
+      mb = mt * BM;
+      nvr = min(BM, e.M - mb);
+    }
+  };
+
   auto fail = [&](int code) {
     record_status(e.status, code);
     *abort_flag = 1;
@@ -333,7 +356,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   if (warp == R::TMA_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      constexpr uint32_t tx = (AMODE != A_GATHER ? NPLANE * A_BYTES : 0) + NPLANE * B_BYTES;
+      constexpr uint32_t tx = AMODE == A_ROWS ? 0u : (AMODE != A_GATHER ? NPLANE * A_BYTES : 0) + NPLANE * B_BYTES;
+      const uint32_t tx_rows = (uint32_t)(8 / max(g.tpr, 1)) * ROWS_BYTES + B_BYTES;  // A_ROWS stage bytes
       bool aborted = false;
       int it = 0, tlt = 0;
       for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x, ++tlt) {
@@ -349,11 +373,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           i_h = oh * g.sh - g.ph;
           i_w = (p - oh * g.OW) * g.sw - g.pw;
         }
+        int r_mb = 0, r_nvr = 0, r_orow = 0, r_ow0 = 0;
+        if (AMODE == A_ROWS) tile_rows(tile / n_tiles, r_mb, r_nvr, r_orow, r_ow0);
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag)) { fail(ST_TIMEOUT_EMPTY); aborted = true; break; }
-          ptx::mbar_arrive_expect_tx(&full_bar[s], tx);
+          ptx::mbar_arrive_expect_tx(&full_bar[s], AMODE == A_ROWS ? tx_rows : tx);
           uint8_t* a_st = sA + (size_t)s * NPLANE * A_BYTES;
           uint8_t* b_st = sB + (size_t)s * NPLANE * B_BYTES;
           const int kx = kb * KB / (NPLANE == 2 ? 2 : 1);  // element coordinate along K
@@ -362,6 +388,17 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             // hardware im2col copy (128 pixels x 16 B) per tap. Taps past the
             // kernel (zero weights) re-read the last tap to keep the byte count.
             ptx::tma_load_3d(b_st, &tmB, &full_bar[s], 0, n0, kb * 8);
+            if constexpr (AMODE == A_ROWS) {
+              // kernel rows kb * rps .. + rps - 1 (rows past KH re-read the last one: zero weights)
+              const int rps = 8 / g.tpr;
+              const int img = r_orow / g.OH, oh = r_orow - img * g.OH;
+#pragma unroll 1
+              for (int j = 0; j < rps; ++j) {
+                const int kr = min(kb * rps + j, g.KH - 1);
+                const uint8_t* src = g.x + (((size_t)img * g.H + oh + kr) * g.W + r_ow0) * 16;
+                ptx::bulk_load(a_st + j * ROWS_BYTES, src, ROWS_BYTES, &full_bar[s]);
+              }
+            } else {
             const int taps = g.KH * g.KW;
 #pragma unroll 1
             for (int j = 0; j < 8; ++j) {
@@ -369,6 +406,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
               const int kh = tap / g.KW, kw = tap - kh * g.KW;
               ptx::tma_load_im2col_4d(a_st + j * (BM * 16), &tmA0, &full_bar[s], 0, i_w, i_h, i_n,
                                       (uint16_t)(kw * g.dw), (uint16_t)(kh * g.dh));
+            }
             }
           } else {
           for (int p = 0; p < NPLANE; ++p)
@@ -417,7 +455,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
 #pragma unroll
           for (int k = 0; k < Cfg::SLAB / 32; ++k) {
             const uint32_t koff = k * 32;
-            if constexpr (KB == 16) {
+            if constexpr (AMODE == A_ROWS) {
+              // taps 2k, 2k + 1 lie in one kernel row's copy: the same pixel
+              // rows shifted by 16 bytes per tap (K-adjacent columns 16 B apart)
+              const int tap0 = 2 * k, j = tap0 / g.tpr, kw0 = tap0 - j * g.tpr;
+              ptx::mma_i8(d_tmem, ptx::umma_desc_interleaved(a_addr + j * ROWS_BYTES + kw0 * 16, 16, 128),
+                          ptx::umma_desc_interleaved(b_addr + k * 2 * (BN * 16), BN * 16, 128), idesc, (kb | k) != 0);
+            } else if constexpr (KB == 16) {
               // two 16-byte tap columns per K step
               ptx::mma_i8(d_tmem, ptx::umma_desc_interleaved(a_addr + k * 2 * (BM * 16), BM * 16, 128),
                           ptx::umma_desc_interleaved(b_addr + k * 2 * (BN * 16), BN * 16, 128), idesc, (kb | k) != 0);
@@ -554,7 +598,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     if (EPI == EPI_R2A && lane == 0 && (int)blockIdx.x < num_tiles) issue_res(blockIdx.x, 0);
     bool res_failed = false;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
-      const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
+      int m0 = 0, nvr = 0, orow = 0, ow0 = 0;
+      tile_rows(tile / n_tiles, m0, nvr, orow, ow0);
+      const int n0 = (tile % n_tiles) * BN;
       const int acc = lt & 1;
       const uint32_t use_ph = (uint32_t)(lt >> 1) & 1u;
       if (n0 != cached_n0) {
@@ -616,7 +662,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       }
       if (lane == 0) NNRCU_TRACE_AT(warp, lt, 2);
       const int m = m0 + row;
-      const bool mvalid = m < e.M;
+      const bool mvalid = row < nvr;
       int32_t rowc = 0;
       if (EPI == EPI_R4 && e.rowcorr && mvalid) rowc = e.rowcorr[m];
       int img = 0, pix = 0;
@@ -792,7 +838,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       // path: no row / column / tail checks, one inlined copy in the loop.
       bool fast = false;
       if constexpr (EPI != EPI_F32)
-        fast = y_tma && m0 + BM <= e.M && n0 + BN <= e.N &&
+        fast = y_tma && (AMODE == A_ROWS || m0 + BM <= e.M) && n0 + BN <= e.N &&
                (EPI == EPI_R2A ? (long long)(m0 + BM) * e.N <= e.qa_vec_end : e.qres == nullptr);
       auto chunk_fast = [&](const int c0, uint32_t (&v)[CW]) {
         if constexpr (EPI != EPI_F32) {
@@ -905,10 +951,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
         __syncwarp();
         if (lane == 0) {
           constexpr int SEG = Cfg::OUT_SEG;
-          if (m0 + eq * 32 < e.M)
+          if (eq * 32 < nvr)
             for (int h = 0; h < HB / SEG; ++h)
-              if (n0 + col0 + h * SEG < e.N)
-                ptx::tma_store_2d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEG, m0 + eq * 32);
+              if (n0 + col0 + h * SEG < e.N) {
+                // A_ROWS: map [rows][OW][N], pixels past OW are clipped
+                if (AMODE == A_ROWS)
+                  ptx::tma_store_3d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEG, ow0 + eq * 32, orow);
+                else
+                  ptx::tma_store_2d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEG, m0 + eq * 32);
+              }
           ptx::bulk_commit();
         }
       }

@@ -27,7 +27,20 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
   // warp's staged 32 x BN block (coalesced rows instead of per-lane pieces).
   CUtensorMap tmY{};
   int y_tma = 0;
-  if (EPI != EPI_F32 && e.y_layout == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 && (e.ldy & 15) == 0) {
+  if (AMODE == A_ROWS && EPI != EPI_F32 && e.y_layout == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
+      (e.ldy & 15) == 0) {
+    // [output rows][OW][N]: a warp's 32 pixels of one output row, clipped at OW
+    const int seg = Cfg::OUT_SEG;
+    const uint64_t dims[3] = {(uint64_t)e.N, (uint64_t)g.OW, (uint64_t)g.N * g.OH};
+    const uint64_t strides[2] = {(uint64_t)e.ldy, (uint64_t)e.ldy * g.OW};
+    const uint32_t box[3] = {(uint32_t)seg, 32, 1};
+    int rc = encode_tmap_3d(&tmY, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.y, dims, strides, box,
+                            seg == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                       : (seg == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B));
+    if (rc != NNRCU_OK) return rc;
+    y_tma = 1;
+  } else if (AMODE != A_ROWS && EPI != EPI_F32 && e.y_layout == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
+             (e.ldy & 15) == 0) {
     const int seg = Cfg::OUT_SEG;
     int rc = encode_tmap_2d(&tmY, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.y, (uint64_t)e.N, (uint64_t)e.M, (uint64_t)e.ldy,
                             seg, 32,
@@ -58,6 +71,11 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
   if (L.kb_bytes == 16) {
     // eight 16-byte taps per stage (space-to-depth convs): int8 im2col, N tile <= 128
     if constexpr (BN <= 128) {
+      if (L.nplane == 1 && L.amode == A_ROWS) {
+        if (L.epi == EPI_R1) return launch_one<BN, 1, A_ROWS, EPI_R1, 16>(L, g, e, st);
+        if (L.epi == EPI_R2) return launch_one<BN, 1, A_ROWS, EPI_R2, 16>(L, g, e, st);
+        if (L.epi == EPI_R3) return launch_one<BN, 1, A_ROWS, EPI_R3, 16>(L, g, e, st);
+      }
       if (L.nplane == 1 && L.amode == A_IM2COL) {
         if (L.epi == EPI_R1) return launch_one<BN, 1, A_IM2COL, EPI_R1, 16>(L, g, e, st);
         if (L.epi == EPI_R2) return launch_one<BN, 1, A_IM2COL, EPI_R2, 16>(L, g, e, st);
