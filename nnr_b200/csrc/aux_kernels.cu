@@ -106,35 +106,35 @@ __global__ void im2col_u8_kernel(const uint8_t* __restrict x, uint8_t* __restric
 }
 
 // Space-to-depth reorder of a small-channel image into 16-byte s2d pixels
-// inside a fill border (the s2d conv path). One thread per padded pixel.
-__global__ void s2d_u8_kernel(const uint8_t* __restrict x, int nchw, uint8_t* __restrict dst, int n, int c, int h,
-                              int w, int hp, int wp, int pt, int pl, uint8_t fill) {
-  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const long long total = (long long)n * hp * wp;
-  if (idx >= total) return;
-  const int X = (int)(idx % wp);
-  const int Y = (int)((idx / wp) % hp);
-  const int b = (int)(idx / ((long long)wp * hp));
-  uint32_t wv[4];
+// inside a fill border (the s2d conv path). Block (Y, image), threads over X.
+__global__ void s2d_u8_kernel(const uint8_t* __restrict x, int nchw, uint8_t* __restrict dst, int c, int h, int w,
+                              int hp, int wp, int pt, int pl, uint8_t fill) {
+  const int Y = blockIdx.x, b = blockIdx.y;
+  const int ih0 = 2 * (Y - pt);
   const uint32_t f4 = 0x01010101u * fill;
-  wv[0] = wv[1] = wv[2] = wv[3] = f4;
+  uint4* out = reinterpret_cast<uint4*>(dst) + ((size_t)b * hp + Y) * wp;
+  for (int X = threadIdx.x; X < wp; X += blockDim.x) {
+    uint32_t wv[4] = {f4, f4, f4, f4};
+    const int iw0 = 2 * (X - pl);
 #pragma unroll
-  for (int dy = 0; dy < 2; ++dy) {
-    const int ih = 2 * (Y - pt) + dy;
-    if (ih < 0 || ih >= h) continue;
+    for (int dy = 0; dy < 2; ++dy) {
+      const int ih = ih0 + dy;
+      if (ih < 0 || ih >= h) continue;
 #pragma unroll
-    for (int dx = 0; dx < 2; ++dx) {
-      const int iw = 2 * (X - pl) + dx;
-      if (iw < 0 || iw >= w) continue;
-      for (int ci = 0; ci < c; ++ci) {
-        const uint8_t v = nchw ? x[(((size_t)b * c + ci) * h + ih) * w + iw] : x[(((size_t)b * h + ih) * w + iw) * c + ci];
-        const int byte = (dy * 2 + dx) * c + ci;
-        const int sh = 8 * (byte & 3);
-        wv[byte >> 2] = (wv[byte >> 2] & ~(0xFFu << sh)) | ((uint32_t)v << sh);
+      for (int dx = 0; dx < 2; ++dx) {
+        const int iw = iw0 + dx;
+        if (iw < 0 || iw >= w) continue;
+#pragma unroll 4
+        for (int ci = 0; ci < c; ++ci) {
+          const uint8_t v = nchw ? x[(((size_t)b * c + ci) * h + ih) * w + iw] : x[(((size_t)b * h + ih) * w + iw) * c + ci];
+          const int byte = (dy * 2 + dx) * c + ci;
+          const int sh = 8 * (byte & 3);
+          wv[byte >> 2] = (wv[byte >> 2] & ~(0xFFu << sh)) | ((uint32_t)v << sh);
+        }
       }
     }
+    out[X] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
   }
-  reinterpret_cast<uint4*>(dst)[idx] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
 }
 
 __global__ void pad_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, long long pixels, int c,
@@ -466,8 +466,8 @@ int launch_s2d_u8(const uint8_t* x, int nchw, uint8_t* dst, int n, int c, int h,
                   uint8_t fill, cudaStream_t st) {
   if (c * 4 > 16 || (reinterpret_cast<uintptr_t>(dst) & 15))
     return set_error(NNRCU_ERR_INVALID, "space-to-depth needs 4c <= 16 and a 16-byte aligned destination");
-  const long long total = (long long)n * hp * wp;
-  s2d_u8_kernel<<<grid_for(total, 256), 256, 0, st>>>(x, nchw, dst, n, c, h, w, hp, wp, pt, pl, fill);
+  if (n > 65535) return set_error(NNRCU_ERR_INVALID, "space-to-depth: batch above 65535");
+  s2d_u8_kernel<<<dim3(hp, n), 128, 0, st>>>(x, nchw, dst, c, h, w, hp, wp, pt, pl, fill);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

@@ -196,10 +196,12 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
         for (int x = 0; x < d.kw; ++x) {
           const int8_t v = w_host[(((size_t)o * d.c + ic) * d.kh + y) * d.kw + x];
           if (op->s2d) {
-            // [tap][npad][16]: s2d tap (ky, kx), byte (dy * 2 + dx) * C + ic
+            // per (N tile, K slab) the stage's smem image [8 taps][bn rows][16 B]:
+            // s2d tap (ky, kx), byte (dy * 2 + dx) * C + ic
             const int ry = y + 2 * op->s2d_pt - d.pad_top, rx = x + 2 * op->s2d_pl - d.pad_left;
             const int tap = (ry >> 1) * (op->s2d_tpr ? op->s2d_tpr : op->s2d_kw) + (rx >> 1);
-            B[((size_t)tap * op->npad + o) * 16 + ((ry & 1) * 2 + (rx & 1)) * d.c + ic] = v;
+            const int nt = o / op->bn, r = o - nt * op->bn;
+            B[((((size_t)nt * op->num_kb + tap / 8) * 8 + tap % 8) * op->bn + r) * 16 + ((ry & 1) * 2 + (rx & 1)) * d.c + ic] = v;
           } else {
             const int tap_stride = op->explicit_im2col ? d.c : op->cs;  // dense K for explicit im2col
             B[(size_t)o * op->kpad_bytes + (size_t)(y * d.kw + x) * tap_stride + ic] = v;
@@ -235,12 +237,7 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   NNRCU_TRY(upload(&op->cs_arr, csv));
   NNRCU_TRY(upload(&op->bias_f, bias_f));
   NNRCU_TRY(upload(&op->os, osv));
-  if (op->s2d) {
-    const uint64_t dims[3] = {16, (uint64_t)op->npad, (uint64_t)op->num_kb * 8};
-    const uint64_t strides[2] = {16, (uint64_t)op->npad * 16};
-    const uint32_t box[3] = {16, (uint32_t)op->bn, 8};
-    NNRCU_TRY(encode_tmap_3d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, dims, strides, box));
-  } else {
+  if (!op->s2d) {  // (the s2d weights are read by plain bulk copies)
     NNRCU_TRY(encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, op->kpad_bytes, op->npad, op->kpad_bytes,
                              op->kslab, op->bn,
                              op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
@@ -302,6 +299,7 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
     g.H = op->s2d_hp; g.W = op->s2d_wp; g.KH = op->s2d_kh; g.KW = op->s2d_kw;
     g.sh = g.sw = 1; g.ph = g.pw = 0; g.dh = g.dw = 1;
     g.tpr = op->s2d_tpr;
+    g.wb = static_cast<const uint8_t*>(op->wB);
     if (!op->s2d_tpr) {
       int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, 16, 0, 0, 0, 0, g.KH,
                                   g.KW, 1, 1, 1, 1, 16);

@@ -95,6 +95,7 @@ struct GatherGeom {
   int kbytes;            // real K in bytes = KH*KW*cbytes
   uint32_t pad_word;     // value written for padding pixels (x_zp replicated, or 0)
   int tpr;               // A_ROWS: taps per kernel row in K (2, 4 or 8; taps past KW have zero weights)
+  const uint8_t* wb;     // KB = 16: weights as per-(N tile, K slab) shared-memory images of BN x 128 bytes
 };
 
 struct EpiParams {
@@ -387,7 +388,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             // B: [tap][row][16 B] -> eight taps x BN rows x 16 B; A: one
             // hardware im2col copy (128 pixels x 16 B) per tap. Taps past the
             // kernel (zero weights) re-read the last tap to keep the byte count.
-            ptx::tma_load_3d(b_st, &tmB, &full_bar[s], 0, n0, kb * 8);
+            // B: the stage's exact smem image ([8 taps][BN rows][16 B]), one contiguous copy
+            ptx::bulk_load(b_st, g.wb + ((size_t)(n0 / BN) * num_kb + kb) * B_BYTES, B_BYTES, &full_bar[s]);
             if constexpr (AMODE == A_ROWS) {
               // kernel rows kb * rps .. + rps - 1 (rows past KH re-read the last one: zero weights)
               const int rps = 8 / g.tpr;
