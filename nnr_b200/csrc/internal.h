@@ -21,6 +21,10 @@ int cuda_check(cudaError_t e, const char* what);
     if (_rc != NNRCU_OK) return _rc;                      \
   } while (0)
 
+// Whether engine kernels are launched with programmatic dependent launch
+// (on unless the environment sets NNRCU_PDL=0).
+bool pdl_enabled();
+
 // Device address of this device's status word (set up once per device).
 int* status_ptr();
 

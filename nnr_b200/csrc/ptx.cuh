@@ -129,6 +129,12 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
                "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                : "memory");
 }
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait until the kernels this one depends on have completed
+// (both are no-ops without the launch attribute).
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Contiguous global -> shared copy (no tensor map); addresses 16-byte
 // aligned, size a multiple of 16, completion on the mbarrier.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -1,5 +1,6 @@
 // Runtime part of the C ABI: errors, devices, streams, memory, graphs, the
 // device status word and tensor-map encoding.
+#include <cstdlib>
 #include <cudaTypedefs.h>
 #include <cstdio>
 #include <cstring>
@@ -86,6 +87,15 @@ int num_sms() {
   int dev = 0;
   if (current_device(&dev) != NNRCU_OK) return 148;
   return g_num_sms[dev];
+}
+
+bool pdl_enabled() {
+  // programmatic dependent launch of the engine kernels; NNRCU_PDL=0 turns it off
+  static const bool on = [] {
+    const char* v = std::getenv("NNRCU_PDL");
+    return !(v && v[0] == '0');
+  }();
+  return on;
 }
 
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,

@@ -331,6 +331,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // The prologue above touches no tensor data. With programmatic dependent
+  // launch it overlaps the previous kernel's tail; every read of activations
+  // and every write of outputs comes after this wait.
+  ptx::pdl_launch_dependents();
+  ptx::pdl_wait();
 
   // Output rows of an M tile: mb = first GEMM row, nvr = valid rows; A_ROWS
   // tiles also give the output row (image * OH + oh) and first column ow0.

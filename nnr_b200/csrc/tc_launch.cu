@@ -60,8 +60,21 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
                                        : (seg == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B));
     if (rc != NNRCU_OK) return rc;
   }
-  kern<<<grid, Roles<AMODE, BN>::THREADS, Cfg::SMEM_BYTES, stream>>>(*L.tmA0, *L.tmA1, *L.tmB, tmY, tmR, y_tma, L.b_plane_rows, g,
-                                                       e, L.num_kb, L.m_tiles, L.n_tiles);
+  // programmatic dependent launch: the prologue of this grid may overlap the
+  // tail of the previous kernel on the stream (the kernel waits before its
+  // first dependent access)
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Roles<AMODE, BN>::THREADS);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  NNRCU_CUDA(cudaLaunchKernelEx(&cfg, kern, *L.tmA0, *L.tmA1, *L.tmB, tmY, tmR, y_tma, L.b_plane_rows, g, e, L.num_kb,
+                                L.m_tiles, L.n_tiles));
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }
