@@ -8,6 +8,11 @@
     python -m nnr_b200.profile_steps --only b0.out --repeat 3
         launches only the step producing tensor b0.out, 3 times (a target
         for an ncu capture: -k regex:tc_gemm -s 1 -c 1).
+
+    python -m nnr_b200.profile_steps --forward 3
+        replays the captured whole-network graph 3 times and nothing else
+        (a target for an ncu launch list of one forward: skip the first 58
+        launches, capture the next 58).
 """
 from __future__ import annotations
 
@@ -34,6 +39,7 @@ def main(argv=None) -> int:
     ap.add_argument("--only", default=None, help="output tensor of the one step to launch")
     ap.add_argument("--repeat", type=int, default=3)
     ap.add_argument("--json", default=None)
+    ap.add_argument("--forward", type=int, default=0, help="replay the whole forward graph this many times")
     a = ap.parse_args(argv)
 
     import torch
@@ -43,6 +49,13 @@ def main(argv=None) -> int:
     net = graph.DeviceNetwork(m, 0)
     net.view("input").copy_(torch.from_numpy(resnet50.input_batch(0, a.batch)))
     st = net.stream
+    if a.forward:
+        net.capture()
+        for _ in range(a.forward):
+            net.launch()
+        torch.cuda.synchronize()
+        print(f"replayed the forward graph x{a.forward} ({len(net.steps)} steps)")
+        return 0
     if a.only:
         t = [k for k, s in enumerate(net.steps) if s[3] == a.only][0]
         for _ in range(a.repeat):
