@@ -52,6 +52,12 @@ BATCH = 32
 L2_FLUSH_BYTES = 256 << 20
 
 
+# DRAM bytes (read + write) of all tc_gemm_kernel launches of one batch-32
+# forward, from the ncu launch list in profiles/resnet50_b32_forward_launches.md
+# (ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum).
+TC_TRAFFIC_BYTES = 465_100_000
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -362,12 +368,13 @@ def main():
             "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": int(x_np.nbytes),
                     "d2h_bytes_per_step": int(np.prod(model.shapes["logits"]) * 4)},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
-                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "frac": round(achieved / peak, 4), "traffic": TC_TRAFFIC_BYTES,
+                         "traffic_unit": "bytes per forward (DRAM read + write of all tc_gemm launches, one ncu capture)",
                          "kernel": "tc_gemm_kernel: all 53 QLinearConv (16 with the residual QLinearAdd fused) + the QLinearMatMul of one forward",
                          "kernel_ms_per_forward": round(k_ms, 4), "ops_per_forward": int(k_ops),
                          "conv3x3_tops": round(three_tops, 1), "peak_source": peak_note},
             "qlinearconv_config2": c2,
-            "gpu_launches": (len(net.steps) + 1) * args.steps,  # steps + the stem im2col
+            "gpu_launches": (len(net.steps) + 1) * args.steps,  # steps + the stem's space-to-depth reorder
             "clocks": clk.summary(),
         }
         if not args.no_cpu_baseline and world == 1:
