@@ -76,6 +76,13 @@ __device__ __forceinline__ void settle_ns(uint64_t ns) {
   }
 }
 
+// Float -> int32 with round-to-nearest-even as the reference's x86 build
+// converts (cvtps2dq, and (int)nearbyint under GCC): values outside the int32
+// range, and NaN, give INT_MIN ("integer indefinite"), not a saturated value.
+__device__ __forceinline__ int cvt_rne_x86(float f) {
+  return fabsf(f) < 2147483648.0f ? __float2int_rn(f) : (int)0x80000000;
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -165,8 +172,9 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 __device__ __forceinline__ void st_shared_v4(void* dst, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)), "r"(a), "r"(b), "r"(c), "r"(d)
-               : "memory");
+  // no memory clobber: the staging block is only read back by the TMA store,
+  // which is ordered after this by fence.proxy.async (another volatile asm)
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(dst)), "r"(a), "r"(b), "r"(c), "r"(d));
 }
 
 // ---------------------------------------------------------------- tcgen05
@@ -281,8 +289,7 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[16]) {
       "tcgen05.wait::ld.sync.aligned;"
       : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
         "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
-      :
-      : "memory");
+      :);
 }
 // Wait for this thread's outstanding TMEM loads. The destination registers of
 // the load are passed through so no use of them is scheduled before the wait.
@@ -293,8 +300,7 @@ __device__ __forceinline__ void tmem_wait_ld(uint32_t (&r)[32]) {
         "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]),
         "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
         "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
-      :
-      : "memory");
+      :);
 }
 
 }  // namespace ptx

@@ -10,6 +10,7 @@
 #include <cmath>
 
 #include "internal.h"
+#include "ptx.cuh"
 
 namespace nnrcu {
 namespace {
@@ -31,7 +32,7 @@ __global__ void quantize_u8_kernel(const float* __restrict x, uint8_t* __restric
       f = fmaxf(fminf(f, 255.0f), 0.0f);
       q = (uint8_t)__float2int_rn(f);
     } else {
-      q = sat_u8(__float2int_rn(__fdiv_rn(v, scale)) + zp);
+      q = sat_u8(ptx::cvt_rne_x86(__fdiv_rn(v, scale)) + zp);
     }
     if (!out_nhwc) {
       y[i] = q;
@@ -130,7 +131,7 @@ __global__ void qlinearadd_u8_kernel(const uint8_t* __restrict a, const uint8_t*
         const float fb = (float)((bw[k] >> (8 * j)) & 0xffu);
         float v = __fmaf_rn(fb, sb, fixed);
         v = __fmaf_rn(fa, sa, v);
-        int r = __float2int_rn(v);
+        int r = ptx::cvt_rne_x86(v);
         r = r < 0 ? 0 : (r > 255 ? 255 : r);
         o |= (uint32_t)r << (8 * j);
       }
@@ -142,7 +143,7 @@ __global__ void qlinearadd_u8_kernel(const uint8_t* __restrict a, const uint8_t*
        i += (long long)gridDim.x * blockDim.x) {
     const float da = (float)((int)a[i] - a_zp), db = (float)((int)b[i] - b_zp);
     const float val = __fadd_rn(__fmaf_rn(sa, da, __fmul_rn(sb, db)), (float)y_zp);
-    y[i] = sat_u8(__float2int_rn(val));
+    y[i] = sat_u8(ptx::cvt_rne_x86(val));
   }
 }
 
@@ -167,7 +168,7 @@ __global__ void dq_gap_q_kernel(const uint8_t* __restrict x, uint8_t* __restrict
       f = fmaxf(fminf(f, 255.0f), 0.0f);
       q = (uint8_t)__float2int_rn(f);
     } else {
-      q = sat_u8(__float2int_rn(__fdiv_rn(v, ys)) + yzp);
+      q = sat_u8(ptx::cvt_rne_x86(__fdiv_rn(v, ys)) + yzp);
     }
     y[i] = q;
   }

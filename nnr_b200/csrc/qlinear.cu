@@ -338,6 +338,8 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
     e.qa_yzp = out_zp;
     const long long n = (long long)op->M * op->N;
     e.qa_vec_end = n / 16 * 16;
+    e.qa_ovf = 255.0 * (std::fabs((double)e.qa_sa) + std::fabs((double)e.qa_sb)) + std::fabs((double)e.qa_fixed) >=
+               1073741824.0;
   }
 
   TcLaunch L{};

@@ -27,6 +27,7 @@
 //             relative per product.
 #pragma once
 #include <cstdint>
+#include <type_traits>
 #include <cuda.h>
 #include "ptx.cuh"
 
@@ -117,6 +118,7 @@ struct EpiParams {
   float qa_sa, qa_sb, qa_fixed;        // a_s / y_s, b_s / y_s, y_zp - fma(sa, a_zp, sb * b_zp)
   int qa_azp, qa_bzp, qa_yzp;
   long long qa_vec_end;                // elements below use the 16-wide body, the rest the scalar tail
+  int qa_ovf;                          // the add value may reach 2^31 (255 (|sa| + |sb|) + |fixed| >= 2^30)
   // fp32 epilogue
   const float* bias;       // per-n bias or null
   const float* residual;   // same layout as y, or null
@@ -194,11 +196,14 @@ constexpr float BYTE_MAGIC = 8388608.0f;   // 2^23, bits 0x4B000000: 0x4B0000bb 
 
 // R2 requant up to the rounding: returns RND_MAGIC + rne(f) as a float,
 // where f = clamp(float(acc + bias) * os, lo - y_zp, hi - y_zp) (|f| <= 255).
-__device__ __forceinline__ float r2_magic(int32_t raw, int32_t ci, float os, const EpiParams& e) {
+__device__ __forceinline__ float r2_magic(int32_t raw, int32_t ci, float os, float lo, float hi) {
   const int32_t v = (int32_t)((uint32_t)raw + (uint32_t)ci);
   float f = __fmul_rn(__int2float_rn(v), os);
-  f = fminf(fmaxf(f, e.rq_lo), e.rq_hi);
+  f = fminf(fmaxf(f, lo), hi);
   return __fadd_rn(f, RND_MAGIC);
+}
+__device__ __forceinline__ float r2_magic(int32_t raw, int32_t ci, float os, const EpiParams& e) {
+  return r2_magic(raw, ci, os, e.rq_lo, e.rq_hi);
 }
 
 // Requantise one int32 accumulator to u8 with the formula EPI selects; the
@@ -231,10 +236,11 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t 
     return __float_as_uint(__fadd_rn(f, RND_MAGIC));
   } else {  // EPI_R4
     // val = fma(float(acc), a_s*b_s/y_s, y_zp); nearbyint; clamp [0, 255]
-    // == rne(clamp(val, 0, 255)), the clamp bounds being integers
+    // == rne(clamp(val, 0, 255)), the clamp bounds being integers, except that
+    // the x86 conversion turns values >= 2^31 into INT_MIN (clamped to 0)
     int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci + (uint32_t)rowc);
     float f = __fmaf_rn(__int2float_rn(acc), e.combined, e.yzp_f);
-    f = fminf(fmaxf(f, 0.0f), 255.0f);
+    f = f >= 2147483648.0f ? 0.0f : fminf(fmaxf(f, 0.0f), 255.0f);
     return __float_as_uint(__fadd_rn(f, RND_MAGIC));
   }
 }
@@ -593,6 +599,11 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
     const int row = eq * 32 + lane;    // TMEM lane == tile row
     int lt = 0;
     int cached_n0 = -1;
+    // epilogue scalars held in registers for the whole kernel
+    const float kp_lo = e.rq_lo, kp_hi = e.rq_hi, kp_sa = e.qa_sa, kp_sb = e.qa_sb, kp_fx = e.qa_fixed;
+    const float kp_ca = __fsub_rn(e.yzp_f, RND_MAGIC);
+    const uint32_t kp_yzp = (uint32_t)e.yzp;
+    const bool kp_ovf = e.qa_ovf != 0;
     // EPI_R2A: TMA load of this warp's 32 x HB residual block of tile t into buffer buf
     auto issue_res = [&](const int t, const int buf) {
       constexpr int SEG = Cfg::OUT_SEG;
@@ -776,7 +787,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 const float fa = __fadd_rn(t[j], ca);
                 const float fb = byte_to_float(rw[j >> 2], j & 3);
                 float r = __fmaf_rn(fa, sa, __fmaf_rn(fb, sb, fx));
-                r = fminf(fmaxf(r, 0.0f), 255.0f);
+                // x86 conversion: values >= 2^31 become INT_MIN, i.e. 0 after the max
+                r = r >= 2147483648.0f ? 0.0f : fminf(fmaxf(r, 0.0f), 255.0f);
                 q[j] = __float_as_uint(__fadd_rn(r, RND_MAGIC));
               }
               scalar_add = false;
@@ -805,10 +817,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 const int qa = (int)(q[j] & 0xFFu), qb = (int)((rw[j >> 2] >> (8 * (j & 3))) & 0xFFu);
                 int r;
                 if (ebase + j < e.qa_vec_end) {
-                  r = __float2int_rn(__fmaf_rn((float)qa, e.qa_sa, __fmaf_rn((float)qb, e.qa_sb, e.qa_fixed)));
+                  r = ptx::cvt_rne_x86(__fmaf_rn((float)qa, e.qa_sa, __fmaf_rn((float)qb, e.qa_sb, e.qa_fixed)));
                 } else {
                   const float da = (float)(qa - e.qa_azp), db = (float)(qb - e.qa_bzp);
-                  r = __float2int_rn(__fadd_rn(__fmaf_rn(e.qa_sa, da, __fmul_rn(e.qa_sb, db)), (float)e.qa_yzp));
+                  r = ptx::cvt_rne_x86(__fadd_rn(__fmaf_rn(e.qa_sa, da, __fmul_rn(e.qa_sb, db)), (float)e.qa_yzp));
                 }
                 q[j] = (uint32_t)(r < 0 ? 0 : (r > 255 ? 255 : r));
               }
@@ -849,19 +861,35 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                (EPI == EPI_R2A ? (long long)(m0 + BM) * e.N <= e.qa_vec_end : e.qres == nullptr);
       auto chunk_fast = [&](const int c0, uint32_t (&v)[CW]) {
         if constexpr (EPI != EPI_F32) {
+          // Column pairs use the packed fp32 instructions (__fmul2_rn,
+          // __fadd2_rn, __ffma2_rn): two IEEE round-to-nearest operations per
+          // instruction, each lane bit-identical to the scalar operation.
+          const float2 k_magic = make_float2(RND_MAGIC, RND_MAGIC);
           const int pc = c0 - col0;
           uint32_t q[CW];
           if constexpr (EPI == EPI_R2 || EPI == EPI_R2A) {
+            float2 t[CW / 2];  // RND_MAGIC + rne(f), f = clamp(float(acc + bias) * os)
 #pragma unroll
             for (int j = 0; j < CW; j += 4) {
               const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
               const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
-              q[j + 0] = __float_as_uint(r2_magic((int32_t)v[j + 0], ci4.x, a4.x, e));
-              q[j + 1] = __float_as_uint(r2_magic((int32_t)v[j + 1], ci4.y, a4.y, e));
-              q[j + 2] = __float_as_uint(r2_magic((int32_t)v[j + 2], ci4.z, a4.z, e));
-              q[j + 3] = __float_as_uint(r2_magic((int32_t)v[j + 3], ci4.w, a4.w, e));
+              float2 f0 = __fmul2_rn(make_float2(__int2float_rn((int32_t)(v[j + 0] + (uint32_t)ci4.x)),
+                                                 __int2float_rn((int32_t)(v[j + 1] + (uint32_t)ci4.y))),
+                                     make_float2(a4.x, a4.y));
+              float2 f1 = __fmul2_rn(make_float2(__int2float_rn((int32_t)(v[j + 2] + (uint32_t)ci4.z)),
+                                                 __int2float_rn((int32_t)(v[j + 3] + (uint32_t)ci4.w))),
+                                     make_float2(a4.z, a4.w));
+              f0.x = fminf(fmaxf(f0.x, kp_lo), kp_hi);
+              f0.y = fminf(fmaxf(f0.y, kp_lo), kp_hi);
+              f1.x = fminf(fmaxf(f1.x, kp_lo), kp_hi);
+              f1.y = fminf(fmaxf(f1.y, kp_lo), kp_hi);
+              t[j / 2] = __fadd2_rn(f0, k_magic);
+              t[j / 2 + 1] = __fadd2_rn(f1, k_magic);
             }
             if constexpr (EPI == EPI_R2A) {
+              // QLinearAdd body (QLinearAdd.cpp:46-104): fma(a, sa, fma(b, sb, fixed)),
+              // rne, saturate; a = rne(f) + y_zp = t - (RND_MAGIC - y_zp) exactly,
+              // b = (2^23 + byte) - 2^23 exactly
               const int h = pc / SEG, cc = (pc % SEG) >> 4;
               const uint8_t* seg = rstg + h * (32 * SEG) + lane * SEG;
               uint32_t rw[CW / 4];
@@ -870,19 +898,59 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
                 const uint4 r0 = *reinterpret_cast<const uint4*>(seg + (((cc + k) ^ swz) << 4));
                 rw[4 * k] = r0.x; rw[4 * k + 1] = r0.y; rw[4 * k + 2] = r0.z; rw[4 * k + 3] = r0.w;
               }
-              const float sa = e.qa_sa, sb = e.qa_sb, fx = e.qa_fixed;
-              const float ca = __fsub_rn(e.yzp_f, RND_MAGIC);
+              const float2 sa = make_float2(kp_sa, kp_sa), sb = make_float2(kp_sb, kp_sb);
+              const float2 fx = make_float2(kp_fx, kp_fx), ca = make_float2(kp_ca, kp_ca);
+              const float2 nbm = make_float2(-BYTE_MAGIC, -BYTE_MAGIC);
+              auto add_pairs = [&](auto ovf) {
 #pragma unroll
-              for (int j = 0; j < CW; ++j) {
-                const float fa = __fadd_rn(__uint_as_float(q[j]), ca);
-                const float fb = byte_to_float(rw[j >> 2], j & 3);
-                float r = __fmaf_rn(fa, sa, __fmaf_rn(fb, sb, fx));
-                r = fminf(fmaxf(r, 0.0f), 255.0f);
-                q[j] = __float_as_uint(__fadd_rn(r, RND_MAGIC));
-              }
+                for (int j = 0; j < CW; j += 2) {
+                  const float2 fa = __fadd2_rn(t[j / 2], ca);
+                  const uint32_t w = rw[j >> 2];
+                  const float2 fb = __fadd2_rn(make_float2(__uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650 | (j & 3))),
+                                                           __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650 | ((j + 1) & 3)))),
+                                               nbm);
+                  float2 r = __ffma2_rn(fa, sa, __ffma2_rn(fb, sb, fx));
+                  if constexpr (decltype(ovf)::value) {
+                    // x86 conversion: values >= 2^31 become INT_MIN, i.e. 0 after the max
+                    r.x = r.x >= 2147483648.0f ? 0.0f : r.x;
+                    r.y = r.y >= 2147483648.0f ? 0.0f : r.y;
+                  }
+                  r.x = fminf(fmaxf(r.x, 0.0f), 255.0f);
+                  r.y = fminf(fmaxf(r.y, 0.0f), 255.0f);
+                  r = __fadd2_rn(r, k_magic);
+                  q[j] = __float_as_uint(r.x);
+                  q[j + 1] = __float_as_uint(r.y);
+                }
+              };
+              // the 2^31 case is possible only when 255 (|sa| + |sb|) + |fixed| reaches it
+              if (kp_ovf)
+                add_pairs(std::true_type{});
+              else
+                add_pairs(std::false_type{});
             } else {
 #pragma unroll
-              for (int j = 0; j < CW; ++j) q[j] += (uint32_t)e.yzp;
+              for (int j = 0; j < CW; j += 2) {
+                q[j] = __float_as_uint(t[j / 2].x) + kp_yzp;
+                q[j + 1] = __float_as_uint(t[j / 2].y) + kp_yzp;
+              }
+            }
+          } else if constexpr (EPI == EPI_R3) {
+            // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); clamp; rne
+            const float2 iy = make_float2(e.inv_y, e.inv_y), yz = make_float2(e.yzp_f, e.yzp_f);
+#pragma unroll
+            for (int j = 0; j < CW; j += 2) {
+              const int2 ci2 = *reinterpret_cast<const int2*>(s_ci + pc + j);
+              const float2 a2 = *reinterpret_cast<const float2*>(s_f1 + pc + j);
+              const float2 b2 = *reinterpret_cast<const float2*>(s_f2 + pc + j);
+              float2 f = __ffma2_rn(make_float2(__int2float_rn((int32_t)(v[j] + (uint32_t)ci2.x)),
+                                                __int2float_rn((int32_t)(v[j + 1] + (uint32_t)ci2.y))),
+                                    a2, b2);
+              f = __ffma2_rn(f, iy, yz);
+              f.x = fmaxf(fminf(f.x, e.qmax_f), e.qmin_f);
+              f.y = fmaxf(fminf(f.y, e.qmax_f), e.qmin_f);
+              f = __fadd2_rn(f, k_magic);
+              q[j] = __float_as_uint(f.x);
+              q[j + 1] = __float_as_uint(f.y);
             }
           } else {
 #pragma unroll

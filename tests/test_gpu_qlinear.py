@@ -247,3 +247,36 @@ def test_conv_with_fused_residual_add(cuda_dev, shape):
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     assert np.array_equal(y.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("kind", ["1x1", "3x3"])
+def test_saturating_scales(cuda_dev, kind):
+    """Tiny output scales: R2 values far outside [0, 255] (the clamp before the
+    float-adder rounding), and a fused QLinearAdd whose value passes 2^31,
+    where the reference's x86 conversion yields INT_MIN (so 0, not 255).
+    Outputs saturate heavily; both must still match bit for bit."""
+    import ctypes as C
+    from nnr_b200 import ops
+    from nnr_b200._lib import check, lib
+    rng = np.random.default_rng(11 if kind == "1x1" else 12)
+    k, p = (1, 0) if kind == "1x1" else (3, 1)
+    case = W.random_qconv(rng, 2, 64, 16, 16, 128, k, k, (1, 1), (p,) * 4, x_zp=0)
+    case.y_scale = 1e-7
+    y, _ = run_qconv(cuda_dev, case, O.R2, "NHWC", "NHWC")
+    ref = oracle_qconv(case, O.R2, "NHWC")
+    assert np.array_equal(y, ref)
+    op = ops.QLinearConv(case.x.shape, case.w, case.w_scale, case.w_zp, case.bias, case.x_scale, case.x_zp,
+                         case.y_scale, case.y_zp, pads=case.pads, in_layout="NHWC", out_layout="NHWC", requant=O.R2)
+    res = rng.integers(0, 256, size=ref.shape).astype(np.uint8)
+    rs, rz, ys, yz = 0.037, 101, 1e-9, 7
+    want = O.qlinearadd_u8(ref, case.y_scale, case.y_zp, res, rs, rz, ys, yz)
+    x = torch.from_numpy(_to_nhwc(case.x)).to(cuda_dev)
+    r = torch.from_numpy(res).to(cuda_dev)
+    out = torch.empty(ref.shape, dtype=torch.uint8, device=cuda_dev)
+    ws = torch.empty(max(op.workspace_size(), 1), dtype=torch.uint8, device=cuda_dev)
+    check(lib.nnrcu_qlinearconv_run_add(op._op, C.c_void_p(x.data_ptr()), C.c_void_p(r.data_ptr()), rs, rz, ys, yz,
+                                        C.c_void_p(out.data_ptr()), C.c_void_p(ws.data_ptr()),
+                                        C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert np.array_equal(out.cpu().numpy(), want)
