@@ -122,6 +122,17 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
                              int n_w_scale, const int8_t* w_zp, int n_w_zp, const int32_t* bias_host,
                              float x_scale, uint8_t x_zp, float y_scale, uint8_t y_zp, nnrcu_op** op);
 int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream);
+/* QuantizeLinear(x, x_scale, x_zp) followed by QLinearConv in one call: x is
+ * fp32 in the op's input layout, quantised per tensor with QuantizeLinear's
+ * float sequence (backend/cpu/QuantizeLinear.cpp:128-160: the 16-wide body
+ * rne(x * (1/scale)) + zp, the scalar tail nearbyint(x / scale) + zp) inside
+ * the op's input reorder, so the u8 image never reaches HBM. Results equal
+ * nnrcu_quantize_linear_u8 then nnrcu_qlinearconv_run. Space-to-depth ops only
+ * (stride 2 over at most 4 channels: the stem); others return
+ * NNRCU_ERR_UNSUPPORTED. */
+int nnrcu_qlinearconv_run_quantize(nnrcu_op* op, const float* x, float x_scale, uint8_t x_zp, uint8_t* y,
+                                   void* workspace, void* stream);
+
 /* QLinearConv followed by QLinearAdd(conv_out, residual) in one kernel: the
  * conv output is requantised to u8 exactly as above, then combined with the
  * u8 residual (same NHWC shape, scale res_scale, zero point res_zp) into y

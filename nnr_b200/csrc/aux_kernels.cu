@@ -137,6 +137,56 @@ __global__ void s2d_u8_kernel(const uint8_t* __restrict x, int nchw, uint8_t* __
   }
 }
 
+// QuantizeLinear of element i (flat index of the fp32 tensor), as nnr does
+// it (QuantizeLinear.cpp:128-160): the 16-wide body rne(x * inv) + zp clamped
+// in float for i < vec_end, the scalar tail nearbyint(x / scale) + zp
+// saturated as an integer (x86 conversion: out of range -> INT_MIN).
+__device__ __forceinline__ uint32_t quantize_elem(float v, long long i, float scale, float inv, int zp,
+                                                  long long vec_end) {
+  if (i < vec_end) {
+    float f = __fadd_rn(rintf(__fmul_rn(v, inv)), (float)zp);
+    f = fmaxf(fminf(f, 255.0f), 0.0f);
+    return (uint32_t)__float2int_rn(f);
+  }
+  const float d = __fdiv_rn(v, scale);
+  const int r = (fabsf(d) < 2147483648.0f ? __float2int_rn(d) : (int)0x80000000) + zp;
+  return (uint32_t)(r < 0 ? 0 : (r > 255 ? 255 : r));
+}
+
+// QuantizeLinear fused into the space-to-depth reorder: fp32 NCHW / NHWC
+// input straight to the padded 16-byte s2d pixels. Block (Y, image).
+__global__ void quantize_s2d_kernel(const float* __restrict x, int nchw, uint8_t* __restrict dst, int c, int h, int w,
+                                    int hp, int wp, int pt, int pl, uint8_t fill, float scale, float inv, int zp,
+                                    long long vec_end) {
+  const int Y = blockIdx.x, b = blockIdx.y;
+  const int ih0 = 2 * (Y - pt);
+  const uint32_t f4 = 0x01010101u * fill;
+  uint4* out = reinterpret_cast<uint4*>(dst) + ((size_t)b * hp + Y) * wp;
+  for (int X = threadIdx.x; X < wp; X += blockDim.x) {
+    uint32_t wv[4] = {f4, f4, f4, f4};
+    const int iw0 = 2 * (X - pl);
+#pragma unroll
+    for (int dy = 0; dy < 2; ++dy) {
+      const int ih = ih0 + dy;
+      if (ih < 0 || ih >= h) continue;
+#pragma unroll
+      for (int dx = 0; dx < 2; ++dx) {
+        const int iw = iw0 + dx;
+        if (iw < 0 || iw >= w) continue;
+#pragma unroll 4
+        for (int ci = 0; ci < c; ++ci) {
+          const long long i = nchw ? (((long long)b * c + ci) * h + ih) * w + iw : (((long long)b * h + ih) * w + iw) * c + ci;
+          const uint32_t v = quantize_elem(x[i], i, scale, inv, zp, vec_end);
+          const int byte = (dy * 2 + dx) * c + ci;
+          const int sh = 8 * (byte & 3);
+          wv[byte >> 2] = (wv[byte >> 2] & ~(0xFFu << sh)) | (v << sh);
+        }
+      }
+    }
+    out[X] = make_uint4(wv[0], wv[1], wv[2], wv[3]);
+  }
+}
+
 __global__ void pad_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, long long pixels, int c,
                                    int cs, uint8_t fill) {
   const long long total = pixels * cs;
@@ -468,6 +518,18 @@ int launch_s2d_u8(const uint8_t* x, int nchw, uint8_t* dst, int n, int c, int h,
     return set_error(NNRCU_ERR_INVALID, "space-to-depth needs 4c <= 16 and a 16-byte aligned destination");
   if (n > 65535) return set_error(NNRCU_ERR_INVALID, "space-to-depth: batch above 65535");
   s2d_u8_kernel<<<dim3(hp, n), 128, 0, st>>>(x, nchw, dst, c, h, w, hp, wp, pt, pl, fill);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_quantize_s2d(const float* x, int nchw, uint8_t* dst, int n, int c, int h, int w, int hp, int wp, int pt,
+                        int pl, uint8_t fill, float scale, uint8_t zp, cudaStream_t st) {
+  if (c * 4 > 16 || (reinterpret_cast<uintptr_t>(dst) & 15) || n > 65535)
+    return set_error(NNRCU_ERR_INVALID, "quantize + space-to-depth: needs 4c <= 16, an aligned destination, n <= 65535");
+  const long long total = (long long)n * c * h * w;
+  const long long vec_end = total >= 64 ? total / 16 * 16 : 0;  // QuantizeLinear.cpp:132
+  quantize_s2d_kernel<<<dim3(hp, n), 128, 0, st>>>(x, nchw, dst, c, h, w, hp, wp, pt, pl, fill, scale, 1.0f / scale, zp,
+                                                  vec_end);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

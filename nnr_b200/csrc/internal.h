@@ -135,6 +135,9 @@ int launch_im2col_u8(const uint8_t* x, uint8_t* a, int nchw, int n, int c, int h
 // past 4C hold fill.
 int launch_s2d_u8(const uint8_t* x, int nchw, uint8_t* dst, int n, int c, int h, int w, int hp, int wp, int pt, int pl,
                   uint8_t fill, cudaStream_t st);
+// QuantizeLinear (per tensor) fused into launch_s2d_u8's reorder, from fp32.
+int launch_quantize_s2d(const float* x, int nchw, uint8_t* dst, int n, int c, int h, int w, int hp, int wp, int pt,
+                        int pl, uint8_t fill, float scale, uint8_t zp, cudaStream_t st);
 int launch_pad_nhwc_u8(const uint8_t* src, uint8_t* dst, int pixels, int c, int cs, uint8_t fill, cudaStream_t st);
 int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
                            int cs, cudaStream_t st);

@@ -55,33 +55,30 @@ __global__ void fill_u8_kernel(uint8_t* __restrict y, long long pixels, int c, i
 }
 
 // MaxPool over u8 NHWC (MaxPool.cpp:279): padding positions are skipped.
-// One thread per 16 channels of one output pixel.
-__global__ void maxpool_u8_nhwc_kernel(const uint8_t* __restrict x, uint8_t* __restrict y, int n, int h, int w, int c,
+// One block per output row (image, oy); threads over (ox, 16-channel vector).
+__global__ void maxpool_u8_nhwc_kernel(const uint8_t* __restrict x, uint8_t* __restrict y, int h, int w, int c,
                                        int oh, int ow, int kh, int kw, int sh, int sw, int pt, int pl) {
   const int cv = c / 16;
-  const long long total = (long long)n * oh * ow * cv;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int v = (int)(i % cv);
-    long long p = i / cv;
-    const int ox = (int)(p % ow);
-    p /= ow;
-    const int oy = (int)(p % oh);
-    const int img = (int)(p / oh);
+  const int row = blockIdx.x;  // img * oh + oy
+  const int img = row / oh, oy = row - img * oh;
+  const int y0 = oy * sh - pt;
+  const int ya = max(y0, 0), yb = min(y0 + kh, h);
+  const uint4* xin = reinterpret_cast<const uint4*>(x + (size_t)img * h * w * c);
+  uint4* out = reinterpret_cast<uint4*>(y + (size_t)row * ow * c);
+  for (int i = threadIdx.x; i < ow * cv; i += blockDim.x) {
+    const int ox = i / cv, v = i - ox * cv;
+    const int x0 = ox * sw - pl;
+    const int xa = max(x0, 0), xb = min(x0 + kw, w);
     uint4 m = make_uint4(0, 0, 0, 0);
-    for (int a = 0; a < kh; ++a) {
-      const int iy = oy * sh - pt + a;
-      if ((unsigned)iy >= (unsigned)h) continue;
-      for (int b = 0; b < kw; ++b) {
-        const int ix = ox * sw - pl + b;
-        if ((unsigned)ix >= (unsigned)w) continue;
-        const uint4 t = reinterpret_cast<const uint4*>(x + (((size_t)img * h + iy) * w + ix) * c)[v];
+    for (int iy = ya; iy < yb; ++iy)
+      for (int ix = xa; ix < xb; ++ix) {
+        const uint4 t = xin[((size_t)iy * w + ix) * cv + v];
         m.x = __vmaxu4(m.x, t.x);
         m.y = __vmaxu4(m.y, t.y);
         m.z = __vmaxu4(m.z, t.z);
         m.w = __vmaxu4(m.w, t.w);
       }
-    }
-    reinterpret_cast<uint4*>(y + (((size_t)img * oh + oy) * ow + ox) * c)[v] = m;
+    out[i] = m;
   }
 }
 
@@ -227,8 +224,7 @@ int nnrcu_maxpool_u8_nhwc(const uint8_t* x, uint8_t* y, int n, int h, int w, int
   if (oh <= 0 || ow <= 0) return set_error(NNRCU_ERR_INVALID, "MaxPool window larger than the padded input");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (c % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
-    const long long total = (long long)n * oh * ow * (c / 16);
-    maxpool_u8_nhwc_kernel<<<blocks_for(total, 256), 256, 0, st>>>(x, y, n, h, w, c, oh, ow, kh, kw, sh, sw, pt, pl);
+    maxpool_u8_nhwc_kernel<<<n * oh, 256, 0, st>>>(x, y, h, w, c, oh, ow, kh, kw, sh, sw, pt, pl);
   } else {
     const long long total = (long long)n * oh * ow * c;
     maxpool_u8_nhwc_scalar_kernel<<<blocks_for(total, 256), 256, 0, st>>>(x, y, n, h, w, c, oh, ow, kh, kw, sh, sw,

@@ -246,18 +246,27 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   return NNRCU_OK;
 }
 
+// xf != NULL: the input is fp32 and QuantizeLinear(xf, q_scale, q_zp) is
+// fused into the input reorder (space-to-depth ops only); x is then unused.
 static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream, const uint8_t* res,
-                     float res_scale, uint8_t res_zp, float out_scale, uint8_t out_zp) {
+                     float res_scale, uint8_t res_zp, float out_scale, uint8_t out_zp, const float* xf = nullptr,
+                     float q_scale = 0.0f, uint8_t q_zp = 0) {
   if (!op || op->kind != OP_QCONV) return set_error(NNRCU_ERR_INVALID, "not a QLinearConv operator");
-  if (!x || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
+  if ((!x && !xf) || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
+  if (xf && !op->s2d)
+    return set_error(NNRCU_ERR_UNSUPPORTED, "QuantizeLinear fusion needs a space-to-depth QLinearConv (stride 2, <= 4 channels)");
+  if (xf && !(q_scale > 0.0f)) return set_error(NNRCU_ERR_INVALID, "QuantizeLinear scale must be positive");
   if (op->ws_bytes && !workspace)
     return set_error(NNRCU_ERR_INVALID, "workspace of %zu bytes required", op->ws_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const nnrcu_conv_desc& d = op->d;
   const uint8_t* xin = x;
   if (op->s2d) {
-    int rc = launch_s2d_u8(x, d.in_layout == NNRCU_LAYOUT_NCHW, static_cast<uint8_t*>(workspace), d.n, d.c, d.h, d.w,
-                           op->s2d_hp, op->s2d_wp, op->s2d_pt, op->s2d_pl, (uint8_t)op->x_zp, st);
+    int rc = xf ? launch_quantize_s2d(xf, d.in_layout == NNRCU_LAYOUT_NCHW, static_cast<uint8_t*>(workspace), d.n, d.c,
+                                      d.h, d.w, op->s2d_hp, op->s2d_wp, op->s2d_pt, op->s2d_pl, (uint8_t)op->x_zp,
+                                      q_scale, q_zp, st)
+                : launch_s2d_u8(x, d.in_layout == NNRCU_LAYOUT_NCHW, static_cast<uint8_t*>(workspace), d.n, d.c, d.h,
+                                d.w, op->s2d_hp, op->s2d_wp, op->s2d_pt, op->s2d_pl, (uint8_t)op->x_zp, st);
     if (rc != NNRCU_OK) return rc;
     xin = static_cast<const uint8_t*>(workspace);
   } else if (op->explicit_im2col) {
@@ -355,6 +364,11 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
 
 int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream) {
   return qconv_run(op, x, y, workspace, stream, nullptr, 0.0f, 0, 0.0f, 0);
+}
+
+int nnrcu_qlinearconv_run_quantize(nnrcu_op* op, const float* x, float x_scale, uint8_t x_zp, uint8_t* y,
+                                   void* workspace, void* stream) {
+  return qconv_run(op, nullptr, y, workspace, stream, nullptr, 0.0f, 0, 0.0f, 0, x, x_scale, x_zp);
 }
 
 int nnrcu_qlinearconv_run_add(nnrcu_op* op, const uint8_t* x, const uint8_t* residual, float res_scale,

@@ -133,8 +133,20 @@ class DeviceNetwork:
                 i = producer.get(a)
                 if i is not None and nodes[i].op == "QLinearConv" and consumers.get(a, 0) == 1:
                     fused_conv[i] = j
+        # QuantizeLinear whose only consumer is a space-to-depth QLinearConv
+        # (the stem): quantised inside the conv's input reorder
+        # (nnrcu_qlinearconv_run_quantize); the u8 image is never materialised
+        fused_q = {}
+        if fuse_add:
+            for j, nd in enumerate(nodes):
+                if nd.op != "QuantizeLinear" or consumers.get(nd.output, 0) != 1:
+                    continue
+                for i, c in enumerate(nodes):
+                    if c.op == "QLinearConv" and c.inputs[0] == nd.output and self.ops[i] is not None \
+                            and self.ops[i].space_to_depth:
+                        fused_q[i] = j
         self.steps = []  # (kind, node index, inputs, output, conv node index)
-        folded = set(fused_conv)
+        folded = set(fused_conv) | set(fused_q.values())
         add_of = {j: i for i, j in fused_conv.items()}
         for j, nd in enumerate(nodes):
             if j in folded:
@@ -142,9 +154,12 @@ class DeviceNetwork:
             if j in add_of:
                 i = add_of[j]
                 self.steps.append(("QConvAdd", j, [nodes[i].inputs[0], nd.inputs[1]], nd.output, i))
+            elif j in fused_q:
+                q = nodes[fused_q[j]]
+                self.steps.append(("QQConv", fused_q[j], [q.inputs[0]], nd.output, j))
             else:
                 self.steps.append((nd.op, j, list(nd.inputs), nd.output, j))
-        self.fused_away = {nodes[i].output for i in fused_conv}
+        self.fused_away = {nodes[i].output for i in fused_conv} | {nodes[j].output for j in fused_q.values()}
 
     # ------------------------------------------------------------------ memory
     def _nbytes(self, name: str) -> int:
@@ -202,6 +217,11 @@ class DeviceNetwork:
             ws = C.c_void_p(P[f"ws{i}"]) if self.ws[i] else None
             call("nnrcu_qlinearconv_run_add", self.ops[i]._op, C.c_void_p(P[ins[0]]), C.c_void_p(P[ins[1]]),
                  qb.scale, qb.zp, qy.scale, qy.zp, out, ws, st)
+        elif kind == "QQConv":
+            qn = m.nodes[j]
+            q = qp[qn.output]
+            ws = C.c_void_p(P[f"ws{i}"]) if self.ws[i] else None
+            call("nnrcu_qlinearconv_run_quantize", self.ops[i]._op, C.c_void_p(P[ins[0]]), q.scale, q.zp, out, ws, st)
         elif nd.op == "QuantizeLinear":
             n, c, h, w = m.shapes[nd.inputs[0]]
             q = qp[nd.output]

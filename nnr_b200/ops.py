@@ -177,12 +177,27 @@ class QLinearConv(Operator):
         n, c, h, wd = self.x_shape
         oh, ow = conv_out_hw(h, wd, w.shape[2], w.shape[3], self.strides, self.pads, self.dilations)
         self.y_shape = (n, w.shape[0], oh, ow) if out_layout == "NCHW" else (n, oh, ow, w.shape[0])
+        # the library's space-to-depth form (stride 2 over <= 4 channels), which
+        # accepts a fused QuantizeLinear (exec_quantize)
+        self.space_to_depth = (c * 4 <= 16 and self.strides == (2, 2) and self.dilations == (1, 1)
+                               and w.shape[2] * w.shape[3] > 1 and group == 1)
 
     def exec(self, x: torch.Tensor, y: Optional[torch.Tensor] = None, workspace=None, stream=None) -> torch.Tensor:
         if y is None:
             y = torch.empty(self.y_shape, dtype=torch.uint8, device=x.device)
         ws, ws_p = self._workspace(workspace, x.device)
         call("nnrcu_qlinearconv_run", self._op, _ptr(x), _ptr(y), ws_p, C.c_void_p(_stream(stream)))
+        return y
+
+    def exec_quantize(self, x: torch.Tensor, x_scale: float, x_zp: int, y: Optional[torch.Tensor] = None,
+                      workspace=None, stream=None) -> torch.Tensor:
+        """QuantizeLinear(x fp32, x_scale, x_zp) followed by this QLinearConv in
+        one call (nnrcu_qlinearconv_run_quantize)."""
+        if y is None:
+            y = torch.empty(self.y_shape, dtype=torch.uint8, device=x.device)
+        ws, ws_p = self._workspace(workspace, x.device)
+        call("nnrcu_qlinearconv_run_quantize", self._op, _ptr(x), float(x_scale), int(x_zp), _ptr(y), ws_p,
+             C.c_void_p(_stream(stream)))
         return y
 
 

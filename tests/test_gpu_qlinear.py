@@ -280,3 +280,35 @@ def test_saturating_scales(cuda_dev, kind):
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     assert np.array_equal(out.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("shape", S2D_SHAPES[:4])
+@pytest.mark.parametrize("in_layout", ["NCHW", "NHWC"])
+def test_quantize_fused_into_space_to_depth(cuda_dev, shape, in_layout):
+    """nnrcu_qlinearconv_run_quantize == QuantizeLinear then QLinearConv; an
+    element count that is not a multiple of 16 exercises QuantizeLinear's
+    scalar tail, and large inputs its saturation."""
+    from nnr_b200 import ops
+    n, c, h, w, oc, kh, kw, s, p, d = shape
+    rng = np.random.default_rng(hash((shape, in_layout)) & 0xffff)
+    case = W.random_qconv(rng, n, c, h, w, oc, kh, kw, s, p, d, x_zp=117)
+    xf = (rng.standard_normal((n, c, h, w)) * 3.0).astype(np.float32)
+    xf.flat[::97] *= 1e4
+    qs = 0.021
+    # QuantizeLinear's body/tail split follows the flat index of the tensor as laid out
+    if in_layout == "NCHW":
+        xq = O.quantize_u8(xf.ravel(), qs, 117).reshape(xf.shape)
+    else:
+        xq = O.quantize_u8(_to_nhwc(xf).ravel(), qs, 117).reshape(n, h, w, c).transpose(0, 3, 1, 2).copy()
+    ref = O.qlinearconv(xq, case.w, case.w_scale, case.bias, case.x_scale, 117, case.y_scale, case.y_zp,
+                        strides=case.strides, pads=case.pads, dilations=case.dilations, formula=O.R3,
+                        out_layout="NHWC")
+    op = ops.QLinearConv(xf.shape, case.w, case.w_scale, case.w_zp, case.bias, case.x_scale, 117, case.y_scale,
+                         case.y_zp, strides=case.strides, pads=case.pads, dilations=case.dilations,
+                         in_layout=in_layout, out_layout="NHWC", requant=O.R3)
+    assert op.space_to_depth
+    x = torch.from_numpy(xf if in_layout == "NCHW" else _to_nhwc(xf)).to(cuda_dev)
+    y = op.exec_quantize(x, qs, 117)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert np.array_equal(y.cpu().numpy(), ref)
