@@ -132,25 +132,29 @@ struct EpiParams {
   int* status;             // device status word (first error wins)
 };
 
-template <int BN, int NPLANE, int EPI, int KB = BKB, int SPLIT = 1>
+// NKBR > 0: the whole B operand (num_kb <= NKBR slabs of one N tile) stays
+// resident in shared memory, loaded once per CTA; the stage ring holds A only.
+template <int BN, int NPLANE, int EPI, int KB = BKB, int SPLIT = 1, int NKBR = 0>
 struct TileCfg {
+  static constexpr int BUDGET = 212 * 1024;  // stages + staging + resident B
   // K bytes per stage: KB, except KB = 16 (eight 16-byte taps per 128-byte stage)
   static constexpr int SLAB = KB == 16 ? 128 : KB;
   static constexpr int A_BYTES = BM * SLAB;            // 16 KB per plane (8 KB with 64-byte slabs)
   static constexpr int B_BYTES = BN * SLAB;
-  static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + B_BYTES);
+  static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + (NKBR ? 0 : B_BYTES));
+  static constexpr int BRES_BYTES = NKBR * B_BYTES;
   // u8 epilogues stage each warp's 32 x BN output block for a TMA store
   static constexpr int OUT_BLOCK = (EPI == EPI_F32) ? 0 : 4 * 32 * BN;  // one 32 x HB block per epilogue warp
   // EPI_R2A: two residual blocks per epilogue warp (tile i in use, tile i+1 landing)
   static constexpr int RES_BYTES = (EPI == EPI_R2A) ? 2 * OUT_BLOCK : 0;
   // Output staging is double-buffered (the store of tile i drains while tile
   // i+1 is requantised) when that still leaves three pipeline stages.
-  static constexpr int OUT_BUFS = (200 * 1024 - 2 * OUT_BLOCK - RES_BYTES) / STAGE_BYTES >= 3 ? 2 : 1;
+  static constexpr int OUT_BUFS = (BUDGET - 2 * OUT_BLOCK - RES_BYTES - BRES_BYTES) / STAGE_BYTES >= 3 ? 2 : 1;
   static constexpr int OUT_BYTES = OUT_BUFS * OUT_BLOCK;
   // Epilogue warps: 4 x SPLIT, each covering 32 TMEM lanes x BN / SPLIT columns.
   static constexpr int HB = BN / SPLIT;
   static constexpr int OUT_SEG = HB >= 128 ? 128 : HB;  // bytes per staged row segment (= TMA box width)
-  static constexpr int STAGES_RAW = (200 * 1024 - OUT_BYTES - RES_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES_RAW = (BUDGET - OUT_BYTES - RES_BYTES - BRES_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
   // Gather producers publish a stage LAG iterations after issuing it: LAG
   // stages of copies in flight, STAGES - 1 - LAG stages of slack for the MMA.
@@ -159,7 +163,7 @@ struct TileCfg {
   static constexpr int PARAM_BYTES = 4 * SPLIT /*epilogue warps*/ * 3 * HB * 4;
   static constexpr int BAR_BYTES = 1024;  // mbarriers, TMEM slot, abort flag
   static constexpr int SMEM_BYTES =
-      1024 /*align slack*/ + STAGES * STAGE_BYTES + OUT_BYTES + RES_BYTES + BAR_BYTES + PARAM_BYTES;
+      1024 /*align slack*/ + STAGES * STAGE_BYTES + BRES_BYTES + OUT_BYTES + RES_BYTES + BAR_BYTES + PARAM_BYTES;
   static_assert(STAGES >= 2, "need at least two pipeline stages");
   static_assert(BN == 64 || BN == 128 || BN == 256, "BN must be 64, 128 or 256");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
@@ -265,7 +269,7 @@ __device__ __forceinline__ float byte_to_float(uint32_t w, int j) {
 // The smem stage ring runs continuously across tiles, and the accumulator is
 // double-buffered in TMEM (2 x BN columns), so the epilogue of tile i overlaps
 // the loads and MMAs of tile i + 1.
-template <int BN, int NPLANE, int AMODE, int EPI, int KB>
+template <int BN, int NPLANE, int AMODE, int EPI, int KB, int NKBR = 0>
 __global__ void __launch_bounds__(Roles<AMODE, BN>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY,
@@ -277,7 +281,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   constexpr int SPLIT = R::SPLIT;
   constexpr int CW = R::CW;
   constexpr int HB = BN / SPLIT;
-  using Cfg = TileCfg<BN, NPLANE, EPI, KB, SPLIT>;
+  using Cfg = TileCfg<BN, NPLANE, EPI, KB, SPLIT, NKBR>;
+  static_assert(NKBR == 0 || (NPLANE == 1 && KB != 16 && AMODE != A_GATHER), "resident B: int8, TMA-fed A");
   static_assert(KB == BKB || AMODE != A_GATHER, "the gather producers fill 128-byte slabs");
   constexpr int STAGES = Cfg::STAGES;
   constexpr int A_BYTES = Cfg::A_BYTES;
@@ -288,8 +293,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   // so that accesses through it stay shared-memory (not generic) accesses
   uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;                                        // [STAGES][NPLANE][A_BYTES]
-  uint8_t* sB = sA + STAGES * NPLANE * A_BYTES;              // [STAGES][NPLANE][B_BYTES]
-  uint8_t* sOut = sB + STAGES * NPLANE * B_BYTES;            // [4 warps][32 rows][BN] (u8 epilogues)
+  uint8_t* sB = sA + STAGES * NPLANE * A_BYTES;              // [STAGES][NPLANE][B_BYTES], or [NKBR][B_BYTES]
+  uint8_t* sOut = sB + (NKBR ? Cfg::BRES_BYTES : STAGES * NPLANE * B_BYTES);  // u8 epilogue staging
   uint8_t* sRes = sOut + Cfg::OUT_BYTES;                      // [2][8 warps][32 rows][HB] (EPI_R2A)
   // sOut: [OUT_BUFS][8 warps][32 rows][HB]
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sRes + Cfg::RES_BYTES);
@@ -297,7 +302,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   uint64_t* tfull_bar = empty_bar + STAGES;                  // [2] accumulator ready
   uint64_t* tempty_bar = tfull_bar + 2;                      // [2] accumulator drained
   uint64_t* res_bar = tempty_bar + 2;                        // [2][16] residual block landed (buffer, warp)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + 32);
+  uint64_t* bres_bar = res_bar + 32;                         // resident B landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bres_bar + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -317,6 +323,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       ptx::mbar_init(&empty_bar[s], 1);
     }
     for (int a = 0; a < 32; ++a) ptx::mbar_init(&res_bar[a], 1);
+    ptx::mbar_init(bres_bar, 1);
     for (int a = 0; a < 2; ++a) {
       ptx::mbar_init(&tfull_bar[a], 1);
       ptx::mbar_init(&tempty_bar[a], 4 * SPLIT);
@@ -368,7 +375,13 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   if (warp == R::TMA_WARP) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      constexpr uint32_t tx = AMODE == A_ROWS ? 0u : (AMODE != A_GATHER ? NPLANE * A_BYTES : 0) + NPLANE * B_BYTES;
+      constexpr uint32_t tx =
+          AMODE == A_ROWS ? 0u : (AMODE != A_GATHER ? NPLANE * A_BYTES : 0) + (NKBR ? 0 : NPLANE * B_BYTES);
+      if constexpr (NKBR > 0) {
+        // the single N tile's B, all K slabs, once per CTA
+        ptx::mbar_arrive_expect_tx(bres_bar, (uint32_t)(num_kb * B_BYTES));
+        for (int kb = 0; kb < num_kb; ++kb) ptx::tma_load_2d(sB + (size_t)kb * B_BYTES, &tmB, bres_bar, kb * KB, 0);
+      }
       const uint32_t tx_rows = (uint32_t)(8 / max(g.tpr, 1)) * ROWS_BYTES + B_BYTES;  // A_ROWS stage bytes
       bool aborted = false;
       int it = 0, tlt = 0;
@@ -422,8 +435,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
             }
             }
           } else {
-          for (int p = 0; p < NPLANE; ++p)
-            ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
+          if (NKBR == 0)
+            for (int p = 0; p < NPLANE; ++p)
+              ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
           if (AMODE == A_TMA) {
             ptx::tma_load_2d(a_st, &tmA0, &full_bar[s], kx, m0);
             if (NPLANE == 2) ptx::tma_load_2d(a_st + A_BYTES, &tmA1, &full_bar[s], kx, m0);
@@ -449,6 +463,10 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       constexpr uint32_t idesc = (NPLANE == 1) ? ptx::umma_idesc(2, 0, 1, BM, BN) : ptx::umma_idesc(1, 1, 1, BM, BN);
       bool aborted = false;
       int it = 0, lt = 0;
+      if (NKBR > 0 && !ptx::mbar_wait(bres_bar, 0u, abort_flag)) {
+        fail(ST_TIMEOUT_FULL);
+        aborted = true;
+      }
       for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x, ++lt) {
         const int acc = lt & 1;
         const uint32_t use_ph = (uint32_t)(lt >> 1) & 1u;
@@ -464,7 +482,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
           ptx::tc_fence_after();
           ptx::fence_proxy_async_smem();
           const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * NPLANE * A_BYTES);
-          const uint32_t b_addr = ptx::smem_u32(sB + (size_t)s * NPLANE * B_BYTES);
+          const uint32_t b_addr = ptx::smem_u32(NKBR ? sB + (size_t)kb * B_BYTES : sB + (size_t)s * NPLANE * B_BYTES);
 #pragma unroll
           for (int k = 0; k < Cfg::SLAB / 32; ++k) {
             const uint32_t koff = k * 32;

@@ -8,10 +8,10 @@ namespace nnrcu {
 
 namespace {
 
-template <int BN, int NPLANE, int AMODE, int EPI, int KB = BKB>
+template <int BN, int NPLANE, int AMODE, int EPI, int KB = BKB, int NKBR = 0>
 int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
-  using Cfg = TileCfg<BN, NPLANE, EPI, KB, Roles<AMODE, BN>::SPLIT>;
-  auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI, KB>;
+  using Cfg = TileCfg<BN, NPLANE, EPI, KB, Roles<AMODE, BN>::SPLIT, NKBR>;
+  auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI, KB, NKBR>;
   // The attribute is per function; setting it is cheap but not free, so do it
   // once per device.
   static unsigned long long configured = 0;
@@ -177,6 +177,13 @@ int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaSt
   // an R2 requant with a fused add whose output and residual can move by
   // TMA (16-byte aligned NHWC rows) runs the residual-prefetching instance
   TcLaunch L2 = L;
+  // Resident B: a single N tile whose K fits 9 slabs (3x3 convs over 64 or
+  // 128 channels), im2col-fed, R2
+  if (L.n_tiles == 1 && L.num_kb <= 9 && L.amode == A_IM2COL && L.epi == EPI_R2 && L.nplane == 1 &&
+      ((L.bn == 64 && L.kb_bytes == 64) || (L.bn == 128 && L.kb_bytes == 128))) {
+    if (L.bn == 64) return launch_one<64, 1, A_IM2COL, EPI_R2, 64, 9>(L, g, e, stream);
+    return launch_one<128, 1, A_IM2COL, EPI_R2, 128, 9>(L, g, e, stream);
+  }
   if (L.epi == EPI_R2 && L.amode == A_TMA && e.qres && e.y_layout == 0 && (e.ldy & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 && (reinterpret_cast<uintptr_t>(e.qres) & 15) == 0)
     L2.epi = EPI_R2A;
