@@ -40,6 +40,9 @@ int encode_tmap_im2col(CUtensorMap* map, CUtensorMapDataType dtype, int elem_byt
                        int w, int c, int pt, int pl, int pb, int pr, int kh, int kw, int dh, int dw, int sh, int sw,
                        int kslab = 128);
 
+// cuTensorMapEncodeTiled of a rank 1..5 tensor (dims innermost first, rank - 1 strides).
+int encode_tmap_nd(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
 // cuTensorMapEncodeTiled of a 3-d tensor (dims innermost first).
 int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
                    const uint64_t strides_bytes[2], const uint32_t box[3],

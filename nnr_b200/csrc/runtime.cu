@@ -119,6 +119,30 @@ int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
   return NNRCU_OK;
 }
 
+int encode_tmap_nd(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, int rank, const uint64_t* dims,
+                   const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  int dev = 0;
+  int rc = current_device(&dev);
+  if (rc != NNRCU_OK) return rc;
+  if (rank < 1 || rank > 5 || (reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    return set_error(NNRCU_ERR_INVALID, "TMA operand: rank %d, base must be 16-byte aligned", rank);
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    estr[i] = 1;
+    if (i < rank - 1) {
+      if (strides_bytes[i] & 15) return set_error(NNRCU_ERR_INVALID, "TMA stride must be a multiple of 16 bytes");
+      st[i] = strides_bytes[i];
+    }
+  }
+  CUresult r = g_encode(map, dtype, rank, const_cast<void*>(base), d, st, b, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(NNRCU_ERR_CUDA, "cuTensorMapEncodeTiled (%d-d) failed (%d)", rank, (int)r);
+  return NNRCU_OK;
+}
+
 int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, const uint64_t dims[3],
                    const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle swizzle) {
   int dev = 0;

@@ -44,7 +44,7 @@ constexpr int ROWS_BYTES = (128 + 8) * 16;  // one A_ROWS copy: BM + 8 pixels of
 enum : int { EPI_R1 = 1, EPI_R2 = 2, EPI_R3 = 3, EPI_R4 = 4, EPI_R2A = 5, EPI_F32 = 10 };
 enum : int { ACT_NONE = 0, ACT_RELU = 1, ACT_CLIP = 2, ACT_HARDSWISH = 3, ACT_SIGMOID = 4, ACT_LEAKYRELU = 5,
              ACT_TANH = 6 };
-enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_ACCUM = 3 };
+enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_ACCUM = 3, ST_SMEM = 4 };
 
 // Opt-in phase trace for performance analysis (built only with -DNNRCU_TRACE):
 // clock64 stamps of CTAs 0-3, per warp, per local tile (first 16), 4 events.
@@ -169,6 +169,11 @@ struct TileCfg {
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
+// The tile configuration of one engine instance; the kernel's shared-memory
+// carve-up and the launcher's allocation both come from this one alias.
+template <int BN, int NPLANE, int AMODE, int EPI, int KB, int NKBR>
+using KernelCfg = TileCfg<BN, NPLANE, EPI, KB, Roles<AMODE, BN>::SPLIT, NKBR>;
+
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
@@ -281,7 +286,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   constexpr int SPLIT = R::SPLIT;
   constexpr int CW = R::CW;
   constexpr int HB = BN / SPLIT;
-  using Cfg = TileCfg<BN, NPLANE, EPI, KB, SPLIT, NKBR>;
+  using Cfg = KernelCfg<BN, NPLANE, AMODE, EPI, KB, NKBR>;
   static_assert(NKBR == 0 || (NPLANE == 1 && KB != 16 && AMODE != A_GATHER), "resident B: int8, TMA-fed A");
   static_assert(KB == BKB || AMODE != A_GATHER, "the gather producers fill 128-byte slabs");
   constexpr int STAGES = Cfg::STAGES;
@@ -289,6 +294,15 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   constexpr int B_BYTES = Cfg::B_BYTES;
 
   extern __shared__ uint8_t smem_raw[];
+  {
+    // the launch must provide this instance's whole layout (checked before any shared access)
+    uint32_t dsmem;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dsmem));
+    if (dsmem < (uint32_t)Cfg::SMEM_BYTES) {
+      if (threadIdx.x == 0) record_status(e.status, ST_SMEM);
+      return;
+    }
+  }
   // 1024-byte aligned base, derived by pointer arithmetic on the shared array
   // so that accesses through it stay shared-memory (not generic) accesses
   uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -353,7 +367,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   // Output rows of an M tile: mb = first GEMM row, nvr = valid rows; A_ROWS
   // tiles also give the output row (image * OH + oh) and first column ow0.
   auto tile_rows = [&](const int mt, int& mb, int& nvr, int& orow, int& ow0) {
-    if constexpr (AMODE == A_ROWS) {
+if constexpr (AMODE == A_ROWS) {
       const int owt = (g.OW + BM - 1) / BM;
       orow = mt / owt;
       ow0 = (mt - orow * owt) * BM;

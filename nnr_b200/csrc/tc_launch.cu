@@ -10,7 +10,7 @@ namespace {
 
 template <int BN, int NPLANE, int AMODE, int EPI, int KB = BKB, int NKBR = 0>
 int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
-  using Cfg = TileCfg<BN, NPLANE, EPI, KB, Roles<AMODE, BN>::SPLIT, NKBR>;
+  using Cfg = KernelCfg<BN, NPLANE, AMODE, EPI, KB, NKBR>;
   auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI, KB, NKBR>;
   // The attribute is per function; setting it is cheap but not free, so do it
   // once per device.

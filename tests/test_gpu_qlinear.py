@@ -312,3 +312,4 @@ def test_quantize_fused_into_space_to_depth(cuda_dev, shape, in_layout):
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     assert np.array_equal(y.cpu().numpy(), ref)
+
