@@ -241,6 +241,52 @@ def config2_qlinearconv(ops, W, torch, dev, stream, flush, steps=50):
             "kernel_tops": round(case.ops / k_ms / 1e9, 1), "kernel_ms": round(k_ms, 5), "ops": case.ops}
 
 
+def other_rows(ops, W, torch, dev, stream, flush, steps=30):
+    """The other BASELINE configs as operator timings (device-resident inputs,
+    L2 flushed before each step): config 1 fp32 Conv+Relu (NCHW in/out),
+    config 3 fp32 Gemm and int8 QLinearMatMul. fp32 runs as split-bf16 (three
+    bf16 products per multiply-add), so its peak is a third of the measured
+    bf16 one."""
+    def timed(fn):
+        for _ in range(5):
+            fn()
+        tot = 0.0
+        for _ in range(steps):
+            with torch.cuda.stream(stream):
+                flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / steps
+
+    c1 = W.config1_conv_relu()
+    conv = ops.Conv(c1.x.shape, c1.w, c1.bias, pads=c1.pads, post="Relu")
+    x1 = torch.from_numpy(c1.x).to(dev)
+    y1 = torch.empty(conv.y_shape, dtype=torch.float32, device=dev)
+    ws1 = torch.empty(max(conv.workspace_size(), 1), dtype=torch.uint8, device=dev)
+    ms1 = timed(lambda: conv.exec(x1, y1, None, ws1, stream=stream))
+    f1 = 2 * 64 * 56 * 56 * 64 * 9
+    c3 = W.config3_matmul()
+    gemm = ops.Gemm(4096, c3.b_f32, c3.c_f32)
+    a3 = torch.from_numpy(c3.a_f32).to(dev)
+    y3 = torch.empty((4096, 3072), dtype=torch.float32, device=dev)
+    ws3 = torch.empty(max(gemm.workspace_size(), 1), dtype=torch.uint8, device=dev)
+    ms3 = timed(lambda: gemm.exec(a3, y3, ws3, stream=stream))
+    qmm = ops.QLinearMatMul(4096, c3.b_s8, c3.a_scale, c3.a_zp, c3.b_scale, c3.b_zp, c3.y_scale, c3.y_zp)
+    aq = torch.from_numpy(c3.a_u8).to(dev)
+    yq = torch.empty((4096, 3072), dtype=torch.uint8, device=dev)
+    wsq = torch.empty(max(qmm.workspace_size(), 1), dtype=torch.uint8, device=dev)
+    msq = timed(lambda: qmm.exec(aq, yq, wsq, stream=stream))
+    f3 = 2 * 4096 * 768 * 3072
+    return {"config1_conv_relu_fp32": {"ms": round(ms1, 5), "tflops": round(f1 / ms1 / 1e9, 1)},
+            "config3_gemm_fp32": {"ms": round(ms3, 5), "tflops": round(f3 / ms3 / 1e9, 1)},
+            "config3_qlinearmatmul": {"ms": round(msq, 5), "tops": round(f3 / msq / 1e9, 1)},
+            "fp32_peak_note": "split-bf16: 3 bf16 products per fp32 multiply-add; peak = measured bf16 / 3"}
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
@@ -271,7 +317,7 @@ def main():
     stream = net.stream
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     # steps that launch the tcgen05 engine (conv, conv + fused add, matmul): (step, node)
-    tc_steps = [(t, st_[4]) for t, st_ in enumerate(net.steps) if st_[0] in ("QLinearConv", "QLinearMatMul", "QConvAdd")]
+    tc_steps = [(t, st_[4]) for t, st_ in enumerate(net.steps) if st_[0] in ("QLinearConv", "QLinearMatMul", "QConvAdd", "QQConv")]
     tc_nodes = [i for _, i in tc_steps]
 
     net.capture()
@@ -326,6 +372,7 @@ def main():
         barrier()
         ktimes = node_times()
         c2 = config2_qlinearconv(ops, W, torch, dev, stream, flush) if rank == 0 else None
+        rows = other_rows(ops, W, torch, dev, stream, flush) if rank == 0 else None
     assert ops.device_status() == 0
 
     t = torch.tensor([dev_ms, e2e_ms], dtype=torch.float64, device=dev)
@@ -374,6 +421,7 @@ def main():
                          "kernel_ms_per_forward": round(k_ms, 4), "ops_per_forward": int(k_ops),
                          "conv3x3_tops": round(three_tops, 1), "peak_source": peak_note},
             "qlinearconv_config2": c2,
+            "other_configs": rows,
             "gpu_launches": (len(net.steps) + 1) * args.steps,  # steps + the stem's space-to-depth reorder
             "clocks": clk.summary(),
         }

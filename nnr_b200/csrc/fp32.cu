@@ -121,6 +121,10 @@ int nnrcu_conv_f32_create(const nnrcu_conv_desc* desc, const float* w_host, cons
   const bool one_by_one = d.kh == 1 && d.kw == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_top == 0 &&
                           d.pad_left == 0 && d.pad_bottom == 0 && d.pad_right == 0;
   op->amode = (one_by_one && op->kbytes >= BKB) ? A_TMA : A_GATHER;
+  // hardware im2col (TMA) when a pixel is whole 128-byte slabs of bf16 (C a
+  // multiple of 64); its zero fill is the fp32 padding value
+  if (op->amode == A_GATHER && (op->cs * 2) % BKB == 0 && (size_t)d.n * d.h * d.w * op->cs * 2 >= 128 * 1024)
+    op->amode = A_IM2COL;
   const size_t plane = round_up_sz((size_t)d.n * d.h * d.w * op->cs * 2, 256);
   op->ws_bytes = 2 * plane;
   const int cs = op->cs;
@@ -172,6 +176,15 @@ int nnrcu_conv_f32_run(nnrcu_op* op, const float* x, float* y, const float* resi
     rc = encode_tmap_2d(&tmA0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, hi, op->cs, npix, op->cs * 2, BKB / 2, BM);
     if (rc != NNRCU_OK) return rc;
     rc = encode_tmap_2d(&tmA1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lo, op->cs, npix, op->cs * 2, BKB / 2, BM);
+    if (rc != NNRCU_OK) return rc;
+  } else if (op->amode == A_IM2COL) {
+    rc = encode_tmap_im2col(&tmA0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hi, d.n, d.h, d.w, op->cs, d.pad_top,
+                            d.pad_left, d.pad_bottom, d.pad_right, d.kh, d.kw, d.dil_h, d.dil_w, d.stride_h,
+                            d.stride_w, BKB);
+    if (rc != NNRCU_OK) return rc;
+    rc = encode_tmap_im2col(&tmA1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, lo, d.n, d.h, d.w, op->cs, d.pad_top,
+                            d.pad_left, d.pad_bottom, d.pad_right, d.kh, d.kw, d.dil_h, d.dil_w, d.stride_h,
+                            d.stride_w, BKB);
     if (rc != NNRCU_OK) return rc;
   }
   GatherGeom g{};

@@ -724,41 +724,69 @@ if constexpr (AMODE == A_ROWS) {
         if (!mvalid || n0 + c0 >= e.N) return;
         const int nvalid = min(CW, e.N - (n0 + c0));
         if constexpr (EPI == EPI_F32) {
+          // bias, residual and post-op for the whole chunk in registers, then
+          // the stores (rows are lanes: row-major stores are per-lane float4s,
+          // NCHW stores are coalesced across lanes for each column)
           float* y = static_cast<float*>(e.y);
           const bool rowmajor = e.y_layout == 0;
-          float* dst = rowmajor ? y + (size_t)m * e.ldy + n0 + c0 : nullptr;
-          const float* res = (e.residual && rowmajor) ? e.residual + (size_t)m * e.ldy + n0 + c0 : nullptr;
-          if (rowmajor && nvalid == CW && (e.ldy & 3) == 0 && ((reinterpret_cast<uintptr_t>(e.y) & 15) == 0) &&
-              (!e.residual || (reinterpret_cast<uintptr_t>(e.residual) & 15) == 0)) {
+          const bool vec = rowmajor && nvalid == CW && (e.ldy & 3) == 0 && ((reinterpret_cast<uintptr_t>(e.y) & 15) == 0) &&
+                           (!e.residual || (reinterpret_cast<uintptr_t>(e.residual) & 15) == 0);
+          const size_t base = rowmajor ? (size_t)m * e.ldy + n0 + c0 : ((size_t)img * e.N + n0 + c0) * e.ohw + pix;
+          const size_t step = rowmajor ? 1 : (size_t)e.ohw;
+          float o[CW];
 #pragma unroll
-            for (int j = 0; j < CW; j += 4) {
-              float o[4];
-              float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
-              if (res) rr = *reinterpret_cast<const float4*>(res + j);
-              const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
+          for (int j = 0; j < CW; j += 4) {
+            const float4 b4 = *reinterpret_cast<const float4*>(s_f2 + pc + j);
+            o[j + 0] = __uint_as_float(v[j + 0]) + b4.x;
+            o[j + 1] = __uint_as_float(v[j + 1]) + b4.y;
+            o[j + 2] = __uint_as_float(v[j + 2]) + b4.z;
+            o[j + 3] = __uint_as_float(v[j + 3]) + b4.w;
+          }
+          float r[CW];
+          const bool has_res = e.residual != nullptr && e.res_mode != 0;
+          if (has_res) {
+            if (vec) {
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                float a = __uint_as_float(v[j + u]) + s_f2[pc + j + u];
-                if (e.res_mode == 1) a = fmaf(e.res_scale, rv[u], a);
-                a = apply_act(a, e.act, e.act_a, e.act_b);
-                if (e.res_mode == 2) a += rv[u];
-                o[u] = a;
+              for (int j = 0; j < CW; j += 4) {
+                const float4 r4 = *reinterpret_cast<const float4*>(e.residual + base + j);
+                r[j] = r4.x; r[j + 1] = r4.y; r[j + 2] = r4.z; r[j + 3] = r4.w;
               }
-              *reinterpret_cast<float4*>(dst + j) = make_float4(o[0], o[1], o[2], o[3]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < CW; ++j) r[j] = j < nvalid ? e.residual[base + j * step] : 0.0f;
             }
+            if (e.res_mode == 1) {
+#pragma unroll
+              for (int j = 0; j < CW; ++j) o[j] = fmaf(e.res_scale, r[j], o[j]);
+            }
+          }
+          switch (e.act) {
+            case ACT_NONE: break;
+            case ACT_RELU:
+#pragma unroll
+              for (int j = 0; j < CW; ++j) o[j] = fmaxf(o[j], 0.0f);
+              break;
+            case ACT_CLIP:
+#pragma unroll
+              for (int j = 0; j < CW; ++j) o[j] = fminf(fmaxf(o[j], e.act_a), e.act_b);
+              break;
+            default:
+#pragma unroll
+              for (int j = 0; j < CW; ++j) o[j] = apply_act(o[j], e.act, e.act_a, e.act_b);
+              break;
+          }
+          if (has_res && e.res_mode == 2) {
+#pragma unroll
+            for (int j = 0; j < CW; ++j) o[j] += r[j];
+          }
+          if (vec) {
+#pragma unroll
+            for (int j = 0; j < CW; j += 4)
+              *reinterpret_cast<float4*>(y + base + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
           } else {
 #pragma unroll
-            for (int j = 0; j < CW; ++j) {
-              if (j >= nvalid) break;
-              const size_t idx = rowmajor ? (size_t)m * e.ldy + n0 + c0 + j
-                                          : ((size_t)img * e.N + n0 + c0 + j) * e.ohw + pix;
-              const float rr = e.residual ? e.residual[idx] : 0.0f;
-              float a = __uint_as_float(v[j]) + s_f2[pc + j];
-              if (e.res_mode == 1) a = fmaf(e.res_scale, rr, a);
-              a = apply_act(a, e.act, e.act_a, e.act_b);
-              if (e.res_mode == 2) a += rr;
-              y[idx] = a;
-            }
+            for (int j = 0; j < CW; ++j)
+              if (j < nvalid) y[base + j * step] = o[j];
           }
         } else {
           // q[j]: the requantised value in the low byte
