@@ -67,6 +67,7 @@ SIGNATURES = {
     "nnrcu_qlinearconv_run": [P, P, P, P, P],
     "nnrcu_qlinearconv_run_add": [P, P, P, F, U8, F, U8, P, P, P],
     "nnrcu_qlinearconv_run_quantize": [P, P, F, U8, P, P, P],
+    "nnrcu_gap_f32_nhwc": [P, I, I, I, P, P],
     "nnrcu_qlinearmatmul_create": [I, I, I, F, U8, P, F, I8, F, U8, PP],
     "nnrcu_qlinearmatmul_run": [P, P, P, P, P],
     "nnrcu_qlinearmatmul_noalloc": [P, P, P, I, I, I, F, U8, F, I8, F, U8, P],

@@ -1,6 +1,7 @@
 // Memory-bound helper kernels: layout reorders, the fp32 -> split-bf16
 // operand preparation, row sums for QLinearMatMul zero points, and the
 // depthwise fp32 convolution (CUDA cores, NHWC, 128-bit channel vectors).
+#include <algorithm>
 #include <cuda_bf16.h>
 
 #include "internal.h"
@@ -318,28 +319,34 @@ __global__ void transpose_kernel(const T* __restrict src, T* __restrict dst, int
 
 // Depthwise fp32 conv, NHWC in/out. Each thread produces 4 consecutive
 // channels (one float4) of one output pixel; weights are [kh][kw][c].
+// Depthwise fp32 conv on NHWC (Conv_depthwise.h:11). One block per output
+// row (image, oy); threads over (ox, 4-channel vector), so consecutive threads
+// read consecutive channels of one pixel. Bias, post-op and residual fused.
+template <int ACT>
 __global__ void depthwise_f32_kernel(const float* __restrict x, const float* __restrict w, const float* __restrict bias,
-                                     float* __restrict y, const float* __restrict residual, int n, int h, int wd, int c,
+                                     float* __restrict y, const float* __restrict residual, int h, int wd, int c,
                                      int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int dh, int dw,
-                                     int act, float act_a, float act_b, int res_mode, float res_scale) {
+                                     int act, float act_a, float act_b) {
   const int c4 = c >> 2;
-  const long long total = (long long)n * oh * ow * c4;
-  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const int cv = (int)(i % c4);
-    long long p = i / c4;
-    const int ox = (int)(p % ow);
-    p /= ow;
-    const int oy = (int)(p % oh);
-    const int img = (int)(p / oh);
+  const int row = blockIdx.x;  // img * oh + oy
+  const int img = row / oh, oy = row - img * oh;
+  const float4* xin = reinterpret_cast<const float4*>(x) + (size_t)img * h * wd * c4;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4* out = reinterpret_cast<float4*>(y) + (size_t)row * ow * c4;
+  const float4* res = residual ? reinterpret_cast<const float4*>(residual) + (size_t)row * ow * c4 : nullptr;
+  for (int t = threadIdx.x; t < ow * c4; t += blockDim.x) {
+    const int ox = t / c4, cv = t - ox * c4;
     float4 acc = bias ? reinterpret_cast<const float4*>(bias)[cv] : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int ky = 0; ky < kh; ++ky) {
       const int iy = oy * sh - ph + ky * dh;
       if ((unsigned)iy >= (unsigned)h) continue;
+      const float4* xr = xin + (size_t)iy * wd * c4 + cv;
+      const float4* wr = w4 + (size_t)ky * kw * c4 + cv;
       for (int kx = 0; kx < kw; ++kx) {
         const int ix = ox * sw - pw + kx * dw;
         if ((unsigned)ix >= (unsigned)wd) continue;
-        const float4 xv = reinterpret_cast<const float4*>(x + (((size_t)img * h + iy) * wd + ix) * c)[cv];
-        const float4 wv = reinterpret_cast<const float4*>(w + ((size_t)ky * kw + kx) * c)[cv];
+        const float4 xv = xr[(size_t)ix * c4];
+        const float4 wv = wr[(size_t)kx * c4];
         acc.x = fmaf(xv.x, wv.x, acc.x);
         acc.y = fmaf(xv.y, wv.y, acc.y);
         acc.z = fmaf(xv.z, wv.z, acc.z);
@@ -347,18 +354,64 @@ __global__ void depthwise_f32_kernel(const float* __restrict x, const float* __r
       }
     }
     float o[4] = {acc.x, acc.y, acc.z, acc.w};
-    float4 rr = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (residual) rr = reinterpret_cast<const float4*>(residual)[i];
-    const float rv[4] = {rr.x, rr.y, rr.z, rr.w};
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      float a = o[u];
-      if (res_mode == 1) a = fmaf(res_scale, rv[u], a);
-      a = apply_act(a, act, act_a, act_b);
-      if (res_mode == 2) a += rv[u];
-      o[u] = a;
+      if constexpr (ACT == ACT_CLIP) o[u] = fminf(fmaxf(o[u], act_a), act_b);
+      else if constexpr (ACT == ACT_RELU) o[u] = fmaxf(o[u], 0.0f);
+      else if constexpr (ACT != ACT_NONE) o[u] = apply_act(o[u], act, act_a, act_b);
     }
-    reinterpret_cast<float4*>(y)[i] = make_float4(o[0], o[1], o[2], o[3]);
+    if (res) {
+      const float4 rr = res[t];
+      o[0] += rr.x; o[1] += rr.y; o[2] += rr.z; o[3] += rr.w;
+    }
+    out[t] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// Explicit im2col for fp32 small-channel convs, written as split bf16:
+// row m (output pixel) holds k = (kh, kw, ic) for k < KH*KW*C, zeros up to kp;
+// hi = bf16(x), lo = bf16(x - hi). One thread per output pixel, 8 elements
+// (16 bytes) per store.
+__global__ void im2col_split_bf16_kernel(const float* __restrict x, int nchw, uint16_t* __restrict hi,
+                                         uint16_t* __restrict lo, long long m_total, int c, int h, int w, int oh,
+                                         int ow, int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw,
+                                         int kp) {
+  for (long long m = blockIdx.x * (long long)blockDim.x + threadIdx.x; m < m_total;
+       m += (long long)gridDim.x * blockDim.x) {
+    const int ox = (int)(m % ow);
+    const long long r = m / ow;
+    const int oy = (int)(r % oh);
+    const int img = (int)(r / oh);
+    const int kd = kh * kw * c;
+    uint4* hrow = reinterpret_cast<uint4*>(hi + m * kp);
+    uint4* lrow = reinterpret_cast<uint4*>(lo + m * kp);
+    for (int k0 = 0; k0 < kp; k0 += 8) {
+      uint32_t hw_[4], lw_[4];
+#pragma unroll
+      for (int q = 0; q < 8; q += 2) {
+        float v[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int k = k0 + q + u;
+          float val = 0.0f;
+          if (k < kd) {
+            const int tap = k / c, ic = k - tap * c;
+            const int ky = tap / kw, kx = tap - ky * kw;
+            const int iy = oy * sh - pt + ky * dh, ix = ox * sw - pl + kx * dw;
+            if ((unsigned)iy < (unsigned)h && (unsigned)ix < (unsigned)w)
+              val = nchw ? x[(((size_t)img * c + ic) * h + iy) * w + ix] : x[(((size_t)img * h + iy) * w + ix) * c + ic];
+          }
+          v[u] = val;
+        }
+        const __nv_bfloat16 h0 = __float2bfloat16_rn(v[0]), h1 = __float2bfloat16_rn(v[1]);
+        const __nv_bfloat16 l0 = __float2bfloat16_rn(v[0] - __bfloat162float(h0));
+        const __nv_bfloat16 l1 = __float2bfloat16_rn(v[1] - __bfloat162float(h1));
+        hw_[q / 2] = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+        lw_[q / 2] = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+      }
+      hrow[k0 / 8] = make_uint4(hw_[0], hw_[1], hw_[2], hw_[3]);
+      lrow[k0 / 8] = make_uint4(lw_[0], lw_[1], lw_[2], lw_[3]);
+    }
   }
 }
 
@@ -560,6 +613,18 @@ int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_
   return NNRCU_OK;
 }
 
+int launch_im2col_split_bf16(const float* x, int nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
+                             int oh, int ow, int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw, int kp,
+                             cudaStream_t st) {
+  if (kp % 8 != 0 || (reinterpret_cast<uintptr_t>(hi) & 15) || (reinterpret_cast<uintptr_t>(lo) & 15))
+    return set_error(NNRCU_ERR_INVALID, "im2col split: kp %% 8 and 16-byte aligned planes required");
+  const long long m = (long long)n * oh * ow;
+  im2col_split_bf16_kernel<<<grid_for(m, 256), 256, 0, st>>>(x, nchw, hi, lo, m, c, h, w, oh, ow, kh, kw, sh, sw, pt,
+                                                             pl, dh, dw, kp);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
 int launch_split_bf16_rows(const float* src, int trans, uint16_t* hi, uint16_t* lo, int m, int k, int kp,
                            cudaStream_t st) {
   if (!trans && k == kp && (k % 4) == 0) {
@@ -596,10 +661,19 @@ int launch_transpose_generic(const void* src, void* dst, int n, int c, int hw, i
 
 int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const float* residual, cudaStream_t st) {
   const nnrcu_conv_desc& d = op.d;
-  const long long total = (long long)d.n * op.oh * op.ow * (d.c / 4);
-  depthwise_f32_kernel<<<grid_for(total, 256), 256, 0, st>>>(
-      x_nhwc, op.w_dw, op.bias, y, residual, d.n, d.h, d.w, d.c, op.oh, op.ow, d.kh, d.kw, d.stride_h, d.stride_w,
-      d.pad_top, d.pad_left, d.dil_h, d.dil_w, op.act, op.act_a, op.act_b, residual ? 2 : 0, 1.0f);
+  const int rows = d.n * op.oh;
+  const int threads = std::min(256, std::max(32, (op.ow * (d.c / 4) + 31) / 32 * 32));
+#define NNRCU_DW(A)                                                                                                   \
+  depthwise_f32_kernel<A><<<rows, threads, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh,      \
+                                                    op.ow, d.kh, d.kw, d.stride_h, d.stride_w, d.pad_top, d.pad_left,  \
+                                                    d.dil_h, d.dil_w, op.act, op.act_a, op.act_b)
+  switch (op.act) {
+    case ACT_NONE: NNRCU_DW(ACT_NONE); break;
+    case ACT_RELU: NNRCU_DW(ACT_RELU); break;
+    case ACT_CLIP: NNRCU_DW(ACT_CLIP); break;
+    default: NNRCU_DW(ACT_HARDSWISH); break;  // generic post-op switch
+  }
+#undef NNRCU_DW
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

@@ -52,7 +52,8 @@ static int pack_split_planes(Op* op, int rows, int k, F get) {
   NNRCU_CUDA(cudaMalloc(&op->wB, B.size() * 2));
   NNRCU_CUDA(cudaMemcpy(op->wB, B.data(), B.size() * 2, cudaMemcpyHostToDevice));
   return encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, op->wB, kpe, (uint64_t)2 * op->npad,
-                        op->kpad_bytes, BKB / 2, op->bn);
+                        op->kpad_bytes, op->kslab / 2, op->bn,
+                        op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
 }  // namespace nnrcu
@@ -112,22 +113,43 @@ int nnrcu_conv_f32_create(const nnrcu_conv_desc* desc, const float* w_host, cons
   op->kind = OP_CONV_F32;
   op->nplane = 2;
   op->epi = EPI_F32;
+  op->kslab = BKB;
   op->cs = round_up(d.c, 8);  // bf16 elements: 16-byte pixel stride
-  op->kbytes = d.kh * d.kw * op->cs * 2;
-  op->kpad_bytes = round_up(op->kbytes, BKB);
-  op->num_kb = op->kpad_bytes / BKB;
-  op->npad = round_up(d.oc, 256);
-  op->bn = pick_bn(op->M, op->N, 2, num_sms());
   const bool one_by_one = d.kh == 1 && d.kw == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_top == 0 &&
                           d.pad_left == 0 && d.pad_bottom == 0 && d.pad_right == 0;
-  op->amode = (one_by_one && op->kbytes >= BKB) ? A_TMA : A_GATHER;
+  // 1x1 convs over fewer than 64 channels: channel stride padded to 32 or 64
+  // bf16 so that A is one 64- or 128-byte slab per pixel, fed by 2-D TMA
+  if (one_by_one && d.c < 64) {
+    op->cs = d.c <= 32 ? 32 : 64;
+    op->kslab = d.c <= 32 ? 64 : 128;
+  }
+  op->kbytes = d.kh * d.kw * op->cs * 2;
+  op->kpad_bytes = round_up(op->kbytes, op->kslab);
+  op->num_kb = op->kpad_bytes / op->kslab;
+  op->npad = round_up(d.oc, 256);
+  op->bn = pick_bn(op->M, op->N, 2, num_sms());
+  op->amode = (one_by_one && op->kbytes >= op->kslab) ? A_TMA : A_GATHER;
   // hardware im2col (TMA) when a pixel is whole 128-byte slabs of bf16 (C a
   // multiple of 64); its zero fill is the fp32 padding value
   if (op->amode == A_GATHER && (op->cs * 2) % BKB == 0 && (size_t)d.n * d.h * d.w * op->cs * 2 >= 128 * 1024)
     op->amode = A_IM2COL;
-  const size_t plane = round_up_sz((size_t)d.n * d.h * d.w * op->cs * 2, 256);
+  // Small-channel convs with a spatial kernel (the 3-channel stem): A is
+  // materialised as dense split-bf16 rows [M][kp] (k = (kh, kw, ic), kp = K
+  // rounded to 32 or 64 elements) by one im2col pass, then fed by 2-D TMA
+  if (d.c < 16 && d.kh * d.kw > 1) {
+    op->explicit_im2col = true;
+    const int kd = d.kh * d.kw * d.c;
+    op->cs = kd <= 32 ? 32 : round_up(kd, 64);
+    op->kslab = kd <= 32 ? 64 : 128;
+    op->kbytes = op->cs * 2;
+    op->kpad_bytes = op->kbytes;
+    op->num_kb = op->kbytes / op->kslab;
+    op->amode = A_TMA;
+  }
+  const size_t plane = op->explicit_im2col ? round_up_sz((size_t)op->M * op->cs * 2, 256)
+                                           : round_up_sz((size_t)d.n * d.h * d.w * op->cs * 2, 256);
   op->ws_bytes = 2 * plane;
-  const int cs = op->cs;
+  const int cs = op->explicit_im2col ? d.c : op->cs;  // dense (kh, kw, ic) K for explicit im2col
   NNRCU_TRY(pack_split_planes(op, d.oc, op->kpad_bytes / 2, [&](int r, int kk) -> float {
     const int tap = kk / cs, ic = kk - tap * cs;
     if (tap >= d.kh * d.kw || ic >= d.c) return 0.0f;
@@ -165,17 +187,24 @@ int nnrcu_conv_f32_run(nnrcu_op* op, const float* x, float* y, const float* resi
     return launch_transpose_generic(tmp, y, d.n, d.oc, op->oh * op->ow, 4, 0, st);
   }
 
-  const size_t plane = round_up_sz((size_t)d.n * d.h * d.w * op->cs * 2, 256);
+  const size_t plane = op->explicit_im2col ? round_up_sz((size_t)op->M * op->cs * 2, 256)
+                                           : round_up_sz((size_t)d.n * d.h * d.w * op->cs * 2, 256);
   uint16_t* hi = reinterpret_cast<uint16_t*>(ws);
   uint16_t* lo = reinterpret_cast<uint16_t*>(ws + plane);
-  int rc = launch_split_bf16_nhwc(x, d.in_layout == NNRCU_LAYOUT_NCHW, hi, lo, d.n, d.c, d.h, d.w, op->cs, st);
+  int rc = op->explicit_im2col
+               ? launch_im2col_split_bf16(x, d.in_layout == NNRCU_LAYOUT_NCHW, hi, lo, d.n, d.c, d.h, d.w, op->oh,
+                                          op->ow, d.kh, d.kw, d.stride_h, d.stride_w, d.pad_top, d.pad_left, d.dil_h,
+                                          d.dil_w, op->cs, st)
+               : launch_split_bf16_nhwc(x, d.in_layout == NNRCU_LAYOUT_NCHW, hi, lo, d.n, d.c, d.h, d.w, op->cs, st);
   if (rc != NNRCU_OK) return rc;
   CUtensorMap tmA0{}, tmA1{};
   if (op->amode == A_TMA) {
-    const uint64_t npix = (uint64_t)d.n * d.h * d.w;
-    rc = encode_tmap_2d(&tmA0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, hi, op->cs, npix, op->cs * 2, BKB / 2, BM);
+    // rows: input pixels (1x1) or output pixels (explicit im2col)
+    const uint64_t rows = op->explicit_im2col ? (uint64_t)op->M : (uint64_t)d.n * d.h * d.w;
+    const CUtensorMapSwizzle sw = op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+    rc = encode_tmap_2d(&tmA0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, hi, op->cs, rows, op->cs * 2, op->kslab / 2, BM, sw);
     if (rc != NNRCU_OK) return rc;
-    rc = encode_tmap_2d(&tmA1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lo, op->cs, npix, op->cs * 2, BKB / 2, BM);
+    rc = encode_tmap_2d(&tmA1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, lo, op->cs, rows, op->cs * 2, op->kslab / 2, BM, sw);
     if (rc != NNRCU_OK) return rc;
   } else if (op->amode == A_IM2COL) {
     rc = encode_tmap_im2col(&tmA0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, hi, d.n, d.h, d.w, op->cs, d.pad_top,
@@ -215,6 +244,7 @@ int nnrcu_conv_f32_run(nnrcu_op* op, const float* x, float* y, const float* resi
   L.tmA0 = &tmA0; L.tmA1 = &tmA1; L.tmB = &op->tmB;
   L.b_plane_rows = op->npad;
   L.num_kb = op->num_kb;
+  L.kb_bytes = op->kslab;
   return tc_launch(L, g, e, st);
 }
 

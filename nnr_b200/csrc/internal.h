@@ -144,6 +144,10 @@ int launch_quantize_s2d(const float* x, int nchw, uint8_t* dst, int n, int c, in
 int launch_pad_nhwc_u8(const uint8_t* src, uint8_t* dst, int pixels, int c, int cs, uint8_t fill, cudaStream_t st);
 int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
                            int cs, cudaStream_t st);
+// Explicit im2col of an fp32 conv input into split-bf16 rows [M][kp].
+int launch_im2col_split_bf16(const float* x, int nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
+                             int oh, int ow, int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw, int kp,
+                             cudaStream_t st);
 int launch_split_bf16_rows(const float* src, int trans, uint16_t* hi, uint16_t* lo, int m, int k, int kp,
                            cudaStream_t st);
 int launch_rowcorr_u8(const uint8_t* a, int m, int k, int lda, int b_zp, int32_t* out, cudaStream_t st);

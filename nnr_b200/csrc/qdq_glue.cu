@@ -181,6 +181,20 @@ __global__ void dequant_bias_kernel(const uint8_t* __restrict x, float scale, fl
   }
 }
 
+// GlobalAveragePool on fp32 NHWC [n, hw, c] (kernel/pool.h:109-125): per
+// channel a sequential sum over the positions, times 1/spatial. One thread per
+// (image, channel): consecutive threads read consecutive channels.
+__global__ void gap_f32_kernel(const float* __restrict x, float* __restrict y, int n, int hw, int c, float inv_hw) {
+  const long long total = (long long)n * c;
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int img = (int)(i / c), ch = (int)(i - (long long)img * c);
+    const float* px = x + (size_t)img * hw * c + ch;
+    float sum = 0.0f;
+    for (int s = 0; s < hw; ++s) sum = __fadd_rn(sum, px[(size_t)s * c]);
+    y[i] = __fmul_rn(sum, inv_hw);
+  }
+}
+
 int blocks_for(long long total, int threads) {
   long long b = (total + threads - 1) / threads;
   const long long cap = (long long)num_sms() * 32;
@@ -262,6 +276,15 @@ int nnrcu_dq_gap_q_u8_nhwc(const uint8_t* x, int n, int hw, int c, float x_scale
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   dq_gap_q_kernel<<<blocks_for(total, 256), 256, 0, st>>>(x, y, n, hw, c, x_scale, (float)x_zp, inv_hw, y_scale, inv_ys,
                                                           y_zp, vec_end);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int nnrcu_gap_f32_nhwc(const float* x, int n, int hw, int c, float* y, void* stream) {
+  if (!x || !y || n <= 0 || hw <= 0 || c <= 0) return set_error(NNRCU_ERR_INVALID, "nnrcu_gap_f32_nhwc: bad arguments");
+  const long long total = (long long)n * c;
+  gap_f32_kernel<<<blocks_for(total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n, hw, c,
+                                                                                     1.0f / (float)hw);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

@@ -99,9 +99,13 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
                      L.epi);
   }
   if (L.kb_bytes == 64) {
-    // 64-byte K slabs (channel strides of 64 bytes): int8, TMA-fed A only
+    // 64-byte K slabs (channel strides of 64 bytes): TMA-fed A only; split-bf16
+    // fp32 (32 bf16 per slab) with 2-D TMA tiles
+    if (L.nplane == 2 && L.amode == A_TMA && L.epi == EPI_F32) {
+      if constexpr (BN <= 128) return launch_one<BN, 2, A_TMA, EPI_F32, 64>(L, g, e, st);
+    }
     if (L.nplane != 1 || L.amode == A_GATHER)
-      return set_error(NNRCU_ERR_INVALID, "64-byte K slabs need int8 with a TMA-fed A operand");
+      return set_error(NNRCU_ERR_INVALID, "64-byte K slabs need int8 or split-bf16 with a TMA-fed A operand");
     if (L.epi == EPI_R2A && L.amode == A_TMA) return launch_one<BN, 1, A_TMA, EPI_R2A, 64>(L, g, e, st);
     if (L.amode == A_IM2COL) {
       if (L.epi == EPI_R1) return launch_one<BN, 1, A_IM2COL, EPI_R1, 64>(L, g, e, st);

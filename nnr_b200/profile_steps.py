@@ -23,6 +23,13 @@ import sys
 
 def step_ops(model, node_index: int) -> int:
     nd = model.nodes[node_index]
+    if nd.op == "Conv":
+        w = nd.attrs["w"]
+        n, oh, ow, oc = model.shapes[nd.output]
+        return 2 * n * oh * ow * oc * w.shape[1] * w.shape[2] * w.shape[3]
+    if nd.op == "Gemm":
+        b = nd.attrs["b"]
+        return 2 * model.shapes[nd.output][0] * b.shape[0] * b.shape[1]
     if nd.op == "QLinearConv":
         n, oh, ow, oc = model.shapes[nd.output]
         w = nd.attrs["w"]
@@ -35,7 +42,8 @@ def step_ops(model, node_index: int) -> int:
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--batch", type=int, default=32)
+    ap.add_argument("--model", default="resnet50", choices=["resnet50", "mobilenetv2"])
+    ap.add_argument("--batch", type=int, default=None, help="default: 32 (resnet50), 128 (mobilenetv2)")
     ap.add_argument("--only", default=None, help="output tensor of the one step to launch")
     ap.add_argument("--repeat", type=int, default=3)
     ap.add_argument("--json", default=None)
@@ -45,9 +53,17 @@ def main(argv=None) -> int:
     import torch
     from . import graph, resnet50
 
-    m = resnet50.build(batch=a.batch)
-    net = graph.DeviceNetwork(m, 0)
-    net.view("input").copy_(torch.from_numpy(resnet50.input_batch(0, a.batch)))
+    if a.model == "resnet50":
+        a.batch = a.batch or 32
+        m = resnet50.build(batch=a.batch)
+        net = graph.DeviceNetwork(m, 0)
+        net.view("input").copy_(torch.from_numpy(resnet50.input_batch(0, a.batch)))
+    else:
+        from . import fgraph, mobilenetv2
+        a.batch = a.batch or 128
+        m = mobilenetv2.build(batch=a.batch)
+        net = fgraph.FloatNetwork(m, 0)
+        net.view("input").copy_(torch.from_numpy(mobilenetv2.input_batch(0, a.batch)))
     st = net.stream
     if a.forward:
         net.capture()
@@ -87,8 +103,9 @@ def main(argv=None) -> int:
         us = e0.elapsed_time(e1) * 1e3 / 50
         nd = m.nodes[i]
         ops = step_ops(m, i)
-        k = nd.attrs["w"].shape[2] if nd.op == "QLinearConv" else None
-        label = kind + (f" {k}x{k}" if k else "")
+        k = nd.attrs["w"].shape[2] if nd.op in ("QLinearConv", "Conv") else None
+        dw = nd.op == "Conv" and nd.attrs["group"] > 1
+        label = kind + (f" {k}x{k}" if k else "") + (" dw" if dw else "")
         rows.append(dict(step=t, kind=label, output=out, us=round(us, 2),
                          tops=round(ops / us / 1e6, 1) if ops else None))
     total = sum(r["us"] for r in rows)

@@ -415,6 +415,20 @@ int oracle_dq_gap_q_u8_nhwc(const uint8_t* x, int n, int hw, int c, float xs, ui
   return rc;
 }
 
+/* GlobalAveragePool on fp32 NHWC [n, hw, c] -> [n, c]: per channel a sum
+ * from 0 over the spatial positions in order, times 1/spatial
+ * (kernel/pool.h:109-125). */
+int oracle_gap_f32_nhwc(const float* x, int n, int hw, int c, float* y) {
+  const float inv_hw = 1.0f / (float)hw;
+  for (int img = 0; img < n; ++img)
+    for (int ch = 0; ch < c; ++ch) {
+      float sum = 0.0f;
+      for (int s = 0; s < hw; ++s) sum += x[((size_t)img * hw + s) * c + ch];
+      y[(size_t)img * c + ch] = sum * inv_hw;
+    }
+  return 0;
+}
+
 /* DequantizeLinear of u8 [rows, cols] then + bias[cols] (fp32 Add). */
 int oracle_dequantize_u8(const uint8_t* x, float scale, uint8_t zp, const float* bias, int rows, int cols, float* y) {
   for (long long i = 0; i < (long long)rows * cols; ++i) {

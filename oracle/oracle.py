@@ -219,6 +219,15 @@ def dq_gap_q_u8_nhwc(x, x_scale, x_zp, y_scale, y_zp):
     return y
 
 
+def gap_f32_nhwc(x):
+    """GlobalAveragePool of fp32 NHWC [n, h, w, c] -> [n, c]."""
+    x = np.ascontiguousarray(x, np.float32)
+    n, h, w, c = x.shape
+    y = np.empty((n, c), np.float32)
+    lib().oracle_gap_f32_nhwc(_p(x), n, h * w, c, _p(y))
+    return y
+
+
 def dequantize_u8(x, scale, zp, bias=None):
     x = np.ascontiguousarray(x, np.uint8)
     rows, cols = x.shape
@@ -268,3 +277,29 @@ def run_qmodel(model, x, keep=False):
                 if name != "input" and all(name not in n2.inputs for n2 in model.nodes[model.nodes.index(nd) + 1:]):
                     t.pop(name, None)
     return (t["logits"], t) if keep else t["logits"]
+
+
+# ------------------------------------------------------------------ whole fp32 network
+def run_fmodel(model, x, keep=False):
+    """Runs an fp32 network (nnr_b200.mobilenetv2.FModel) node by node on the
+    CPU with the restated operators (fp64 accumulation). x: fp32 NCHW input.
+    Returns the logits, plus every intermediate tensor when keep is set."""
+    t = {"input": np.ascontiguousarray(x, np.float32)}
+    for nd in model.nodes:
+        a = nd.attrs
+        if nd.op == "Conv":
+            lay = "NCHW" if nd.inputs[0] == "input" else "NHWC"
+            post = 2 if a["post"] == "Clip" else 0
+            t[nd.output] = conv_f32(t[nd.inputs[0]], a["w"], a["b"], strides=(a["stride"],) * 2, pads=(a["pad"],) * 4,
+                                    group=a["group"], post=post, post_a=0.0, post_b=6.0, in_layout=lay,
+                                    out_layout="NHWC")
+        elif nd.op == "Add":
+            t[nd.output] = t[nd.inputs[0]] + t[nd.inputs[1]]
+        elif nd.op == "GlobalAveragePool":
+            t[nd.output] = gap_f32_nhwc(t[nd.inputs[0]])
+        elif nd.op == "Gemm":
+            t[nd.output] = gemm_f32(t[nd.inputs[0]], a["b"], a["c"])
+        else:
+            raise ValueError(nd.op)
+    return (t["logits"], t) if keep else t["logits"]
+

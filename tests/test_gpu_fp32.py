@@ -42,6 +42,9 @@ def test_config1_conv_relu(cuda_dev):
 @pytest.mark.parametrize("case", [
     dict(n=2, c=64, h=28, w=28, oc=128, k=3, s=2, p=1, post="Clip"),
     dict(n=2, c=128, h=20, w=18, oc=64, k=3, s=1, p=1, post="Relu"),   # hardware im2col, 2 slabs per tap
+    dict(n=2, c=16, h=20, w=20, oc=96, k=1, s=1, p=0, post="Clip"),    # 1x1, 64-byte K slabs (MobileNet expand)
+    dict(n=1, c=40, h=14, w=14, oc=24, k=1, s=1, p=0, post=None),      # 1x1, channels padded to 64
+    dict(n=2, c=3, h=33, w=31, oc=32, k=3, s=2, p=1, post="Clip"),     # explicit im2col, K 27 -> 32
     dict(n=1, c=96, h=14, w=14, oc=160, k=1, s=1, p=0, post=None),      # 1x1 -> TMA A path (NHWC)
     dict(n=2, c=3, h=32, w=32, oc=32, k=3, s=2, p=1, post="HardSwish"),  # stem
     dict(n=1, c=24, h=9, w=9, oc=40, k=5, s=1, p=2, post="Sigmoid"),
