@@ -368,6 +368,74 @@ __global__ void depthwise_f32_kernel(const float* __restrict x, const float* __r
   }
 }
 
+// 3x3 depthwise fp32 conv (stride SW, dilation 1) on NHWC: each thread makes
+// four consecutive outputs along x for one 4-channel vector, with the
+// 3 x (3 * SW + 3) input vectors they share loaded once, up front (all loads
+// in flight together). One block per output row.
+template <int ACT, int SW>
+__global__ void dw3x3_f32_kernel(const float* __restrict x, const float* __restrict w, const float* __restrict bias,
+                                 float* __restrict y, const float* __restrict residual, int h, int wd, int c, int oh,
+                                 int ow, int ph, int pw, int act, float act_a, float act_b) {
+  constexpr int OXT = 4, NC = (OXT - 1) * SW + 3;
+  const int c4 = c >> 2;
+  const int row = blockIdx.x;
+  const int img = row / oh, oy = row - img * oh;
+  const float4* xin = reinterpret_cast<const float4*>(x) + (size_t)img * h * wd * c4;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4* out = reinterpret_cast<float4*>(y) + (size_t)row * ow * c4;
+  const float4* res = residual ? reinterpret_cast<const float4*>(residual) + (size_t)row * ow * c4 : nullptr;
+  const int groups = (ow + OXT - 1) / OXT;
+  const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int t = threadIdx.x; t < groups * c4; t += blockDim.x) {
+    const int g = t / c4, cv = t - g * c4;
+    const int ox0 = g * OXT;
+    float4 xv[3][NC];
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky) {
+      const int iy = oy * SW - ph + ky;
+      const bool vy = (unsigned)iy < (unsigned)h;
+      const float4* xr = xin + (size_t)(vy ? iy : 0) * wd * c4 + cv;
+#pragma unroll
+      for (int j = 0; j < NC; ++j) {
+        const int ix = ox0 * SW - pw + j;
+        xv[ky][j] = (vy && (unsigned)ix < (unsigned)wd) ? xr[(size_t)ix * c4] : z;
+      }
+    }
+    float4 wv[9];
+#pragma unroll
+    for (int k = 0; k < 9; ++k) wv[k] = w4[(size_t)k * c4 + cv];
+    const float4 b4 = bias ? reinterpret_cast<const float4*>(bias)[cv] : z;
+#pragma unroll
+    for (int o = 0; o < OXT; ++o) {
+      if (ox0 + o >= ow) break;
+      float4 acc = b4;
+#pragma unroll
+      for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+          const float4 xx = xv[ky][o * SW + kx], ww = wv[ky * 3 + kx];
+          acc.x = fmaf(xx.x, ww.x, acc.x);
+          acc.y = fmaf(xx.y, ww.y, acc.y);
+          acc.z = fmaf(xx.z, ww.z, acc.z);
+          acc.w = fmaf(xx.w, ww.w, acc.w);
+        }
+      float r[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if constexpr (ACT == ACT_CLIP) r[u] = fminf(fmaxf(r[u], act_a), act_b);
+        else if constexpr (ACT == ACT_RELU) r[u] = fmaxf(r[u], 0.0f);
+        else if constexpr (ACT != ACT_NONE) r[u] = apply_act(r[u], act, act_a, act_b);
+      }
+      const size_t oi = (size_t)(ox0 + o) * c4 + cv;
+      if (res) {
+        const float4 rr = res[oi];
+        r[0] += rr.x; r[1] += rr.y; r[2] += rr.z; r[3] += rr.w;
+      }
+      out[oi] = make_float4(r[0], r[1], r[2], r[3]);
+    }
+  }
+}
+
 // Explicit im2col for fp32 small-channel convs, written as split bf16:
 // row m (output pixel) holds k = (kh, kw, ic) for k < KH*KW*C, zeros up to kp;
 // hi = bf16(x), lo = bf16(x - hi). One thread per output pixel, 8 elements
@@ -667,6 +735,26 @@ int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const floa
   depthwise_f32_kernel<A><<<rows, threads, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh,      \
                                                     op.ow, d.kh, d.kw, d.stride_h, d.stride_w, d.pad_top, d.pad_left,  \
                                                     d.dil_h, d.dil_w, op.act, op.act_a, op.act_b)
+  if (d.kh == 3 && d.kw == 3 && d.dil_h == 1 && d.dil_w == 1 && d.stride_h == d.stride_w &&
+      (d.stride_h == 1 || d.stride_h == 2)) {
+    const int groups = (op.ow + 3) / 4;
+    const int th = std::min(256, std::max(32, (groups * (d.c / 4) + 31) / 32 * 32));
+#define NNRCU_DW3(A, S)                                                                                                 \
+  dw3x3_f32_kernel<A, S><<<rows, th, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh, op.ow,     \
+                                              d.pad_top, d.pad_left, op.act, op.act_a, op.act_b)
+#define NNRCU_DW3S(A) \
+  if (d.stride_h == 1) NNRCU_DW3(A, 1); else NNRCU_DW3(A, 2)
+    switch (op.act) {
+      case ACT_NONE: NNRCU_DW3S(ACT_NONE); break;
+      case ACT_RELU: NNRCU_DW3S(ACT_RELU); break;
+      case ACT_CLIP: NNRCU_DW3S(ACT_CLIP); break;
+      default: NNRCU_DW3S(ACT_HARDSWISH); break;
+    }
+#undef NNRCU_DW3S
+#undef NNRCU_DW3
+    NNRCU_CUDA(cudaGetLastError());
+    return NNRCU_OK;
+  }
   switch (op.act) {
     case ACT_NONE: NNRCU_DW(ACT_NONE); break;
     case ACT_RELU: NNRCU_DW(ACT_RELU); break;

@@ -143,8 +143,12 @@ struct TileCfg {
   static constexpr int B_BYTES = BN * SLAB;
   static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + (NKBR ? 0 : B_BYTES));
   static constexpr int BRES_BYTES = NKBR * B_BYTES;
-  // u8 epilogues stage each warp's 32 x BN output block for a TMA store
-  static constexpr int OUT_BLOCK = (EPI == EPI_F32) ? 0 : 4 * 32 * BN;  // one 32 x HB block per epilogue warp
+  // Epilogues stage each warp's 32-row output block for a TMA store: u8
+  // always; fp32 (4 bytes per element) when that still leaves three stages.
+  static constexpr int ESZ = EPI == EPI_F32 ? 4 : 1;
+  static constexpr int OUT_BLOCK_RAW = 4 * 32 * BN * ESZ;  // one 32 x HB block per epilogue warp
+  static constexpr int OUT_BLOCK =
+      (EPI == EPI_F32 && (BUDGET - OUT_BLOCK_RAW - BRES_BYTES) / STAGE_BYTES < 3) ? 0 : OUT_BLOCK_RAW;
   // EPI_R2A: two residual blocks per epilogue warp (tile i in use, tile i+1 landing)
   static constexpr int RES_BYTES = (EPI == EPI_R2A) ? 2 * OUT_BLOCK : 0;
   // Output staging is double-buffered (the store of tile i drains while tile
@@ -153,7 +157,8 @@ struct TileCfg {
   static constexpr int OUT_BYTES = OUT_BUFS * OUT_BLOCK;
   // Epilogue warps: 4 x SPLIT, each covering 32 TMEM lanes x BN / SPLIT columns.
   static constexpr int HB = BN / SPLIT;
-  static constexpr int OUT_SEG = HB >= 128 ? 128 : HB;  // bytes per staged row segment (= TMA box width)
+  static constexpr int ROW_BYTES = HB * ESZ;                       // bytes of one staged row
+  static constexpr int OUT_SEG = ROW_BYTES >= 128 ? 128 : ROW_BYTES;  // bytes per staged row segment (= TMA box width)
   static constexpr int STAGES_RAW = (BUDGET - OUT_BYTES - RES_BYTES - BRES_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
   // Gather producers publish a stage LAG iterations after issuing it: LAG
@@ -679,12 +684,12 @@ if constexpr (AMODE == A_ROWS) {
       }
       // the staging block may be rewritten once the previous tile's stores have read it
       if (lane == 0) NNRCU_TRACE_AT(warp, lt, 0);
-      uint8_t* const stg = sOut + (Cfg::OUT_BUFS == 2 ? (lt & 1) * Cfg::OUT_BLOCK : 0) + warp * (32 * HB);
+      uint8_t* const stg = sOut + (Cfg::OUT_BUFS == 2 ? (lt & 1) * Cfg::OUT_BLOCK : 0) + warp * (32 * Cfg::ROW_BYTES);
       constexpr int SEG = Cfg::OUT_SEG;
       // swizzle of a staged row (the store / residual maps' 128B, 64B or 32B
       // swizzle): row r, 16-byte chunk c of a segment lives at r*SEG + ((c ^ f(r)) << 4)
       const int swz = SEG == 128 ? (lane & 7) : (SEG == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
-      if (EPI != EPI_F32 && y_tma) {
+      if (Cfg::OUT_BLOCK > 0 && y_tma) {
         if (lane == 0) {
           ptx::bulk_wait_read<Cfg::OUT_BUFS - 1>();  // the store that last used this buffer has read it
           if constexpr (EPI == EPI_R2A) {
@@ -779,7 +784,17 @@ if constexpr (AMODE == A_ROWS) {
 #pragma unroll
             for (int j = 0; j < CW; ++j) o[j] += r[j];
           }
-          if (vec) {
+          if (Cfg::OUT_BLOCK > 0 && y_tma) {
+            // swizzled staging, as the u8 epilogue (16-byte chunk c of row r at
+            // r * SEG + ((c ^ f(r)) << 4)); the TMA store writes whole rows
+            constexpr int SEG = Cfg::OUT_SEG;
+            const int pb = pc * 4, h = pb / SEG, cc = (pb % SEG) >> 4;
+            uint8_t* seg = stg + h * (32 * SEG) + lane * SEG;
+#pragma unroll
+            for (int k = 0; k < CW / 4; ++k)
+              ptx::st_shared_v4(seg + (((cc + k) ^ swz) << 4), __float_as_uint(o[4 * k]), __float_as_uint(o[4 * k + 1]),
+                                __float_as_uint(o[4 * k + 2]), __float_as_uint(o[4 * k + 3]));
+          } else if (vec) {
 #pragma unroll
             for (int j = 0; j < CW; j += 4)
               *reinterpret_cast<float4*>(y + base + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
@@ -1080,26 +1095,27 @@ if constexpr (AMODE == A_ROWS) {
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
-      if (EPI != EPI_F32 && y_tma) {
+      if (Cfg::OUT_BLOCK > 0 && y_tma) {
         // publish the staged block: rows >= M and columns >= N are clipped by the map
         ptx::fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
           constexpr int SEG = Cfg::OUT_SEG;
+          constexpr int SEGE = SEG / Cfg::ESZ;  // elements per segment
           if (eq * 32 < nvr)
-            for (int h = 0; h < HB / SEG; ++h)
-              if (n0 + col0 + h * SEG < e.N) {
+            for (int h = 0; h < Cfg::ROW_BYTES / SEG; ++h)
+              if (n0 + col0 + h * SEGE < e.N) {
                 // A_ROWS: map [rows][OW][N], pixels past OW are clipped
                 if (AMODE == A_ROWS)
-                  ptx::tma_store_3d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEG, ow0 + eq * 32, orow);
+                  ptx::tma_store_3d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEGE, ow0 + eq * 32, orow);
                 else
-                  ptx::tma_store_2d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEG, m0 + eq * 32);
+                  ptx::tma_store_2d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEGE, m0 + eq * 32);
               }
           ptx::bulk_commit();
         }
       }
     }
-    if (EPI != EPI_F32 && y_tma && lane == 0) ptx::bulk_wait0();  // stores complete before smem is released
+    if (Cfg::OUT_BLOCK > 0 && y_tma && lane == 0) ptx::bulk_wait0();  // stores complete before smem is released
     if (EPI == EPI_R2A && res_failed) ptx::settle_ns(200000);      // residual loads still in flight land first
   }
 

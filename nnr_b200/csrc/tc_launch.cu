@@ -49,6 +49,17 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
     if (rc != NNRCU_OK) return rc;
     y_tma = 1;
   }
+  if (EPI == EPI_F32 && Cfg::OUT_BLOCK > 0 && AMODE != A_ROWS && e.y_layout == 0 &&
+      (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 && (e.ldy & 3) == 0) {
+    // fp32 rows leave through the staged TMA store too (32-float segments)
+    const int seg = Cfg::OUT_SEG;
+    int rc = encode_tmap_2d(&tmY, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, e.y, (uint64_t)e.N, (uint64_t)e.M,
+                            (uint64_t)e.ldy * 4, seg / 4, 32,
+                            seg == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                       : (seg == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B));
+    if (rc != NNRCU_OK) return rc;
+    y_tma = 1;
+  }
   CUtensorMap tmR{};
   if (EPI == EPI_R2A) {
     if (!y_tma) return set_error(NNRCU_ERR_INVALID, "the prefetched residual add needs a TMA-stored output");

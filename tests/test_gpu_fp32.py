@@ -71,11 +71,13 @@ def test_conv_shapes(cuda_dev, case, layout):
 
 @pytest.mark.parametrize("s", [1, 2])
 @pytest.mark.parametrize("layout", ["NCHW", "NHWC"])
-def test_depthwise_clip(cuda_dev, s, layout):
-    """MobileNetV2 depthwise 3x3 + ReLU6 (Clip(0,6))."""
+@pytest.mark.parametrize("hw", [(28, 28), (13, 15)])
+def test_depthwise_clip(cuda_dev, s, layout, hw):
+    """MobileNetV2 depthwise 3x3 + ReLU6 (Clip(0,6)); 13x15 leaves partial
+    four-output strips at the row ends."""
     rng = np.random.default_rng(s)
     c = 96
-    x = rng.normal(0, 1, size=(2, c, 28, 28)).astype(np.float32)
+    x = rng.normal(0, 1, size=(2, c) + hw).astype(np.float32)
     w = rng.normal(0, 0.3, size=(c, 1, 3, 3)).astype(np.float32)
     b = rng.normal(0, 0.1, size=c).astype(np.float32)
     xin = x if layout == "NCHW" else np.ascontiguousarray(x.transpose(0, 2, 3, 1))
