@@ -369,14 +369,14 @@ __global__ void depthwise_f32_kernel(const float* __restrict x, const float* __r
 }
 
 // 3x3 depthwise fp32 conv (stride SW, dilation 1) on NHWC: each thread makes
-// four consecutive outputs along x for one 4-channel vector, with the
-// 3 x (3 * SW + 3) input vectors they share loaded once, up front (all loads
-// in flight together). One block per output row.
+// OXT consecutive outputs along x (4 at stride 1, 2 at stride 2) for one
+// 4-channel vector, with the input vectors they share loaded once, up front
+// (all loads in flight together). One block per output row.
 template <int ACT, int SW>
-__global__ void dw3x3_f32_kernel(const float* __restrict x, const float* __restrict w, const float* __restrict bias,
+__global__ void __launch_bounds__(256, 2) dw3x3_f32_kernel(const float* __restrict x, const float* __restrict w, const float* __restrict bias,
                                  float* __restrict y, const float* __restrict residual, int h, int wd, int c, int oh,
                                  int ow, int ph, int pw, int act, float act_a, float act_b) {
-  constexpr int OXT = 4, NC = (OXT - 1) * SW + 3;
+  constexpr int OXT = SW == 1 ? 4 : 2, NC = (OXT - 1) * SW + 3;
   const int c4 = c >> 2;
   const int row = blockIdx.x;
   const int img = row / oh, oy = row - img * oh;
@@ -401,24 +401,29 @@ __global__ void dw3x3_f32_kernel(const float* __restrict x, const float* __restr
         xv[ky][j] = (vy && (unsigned)ix < (unsigned)wd) ? xr[(size_t)ix * c4] : z;
       }
     }
-    float4 wv[9];
-#pragma unroll
-    for (int k = 0; k < 9; ++k) wv[k] = w4[(size_t)k * c4 + cv];
     const float4 b4 = bias ? reinterpret_cast<const float4*>(bias)[cv] : z;
+    float4 accs[OXT];
+#pragma unroll
+    for (int o = 0; o < OXT; ++o) accs[o] = b4;
+    // taps outer, outputs inner: a weight vector is live for one tap only
+#pragma unroll
+    for (int ky = 0; ky < 3; ++ky)
+#pragma unroll
+      for (int kx = 0; kx < 3; ++kx) {
+        const float4 ww = w4[(size_t)(ky * 3 + kx) * c4 + cv];
+#pragma unroll
+        for (int o = 0; o < OXT; ++o) {
+          const float4 xx = xv[ky][o * SW + kx];
+          accs[o].x = fmaf(xx.x, ww.x, accs[o].x);
+          accs[o].y = fmaf(xx.y, ww.y, accs[o].y);
+          accs[o].z = fmaf(xx.z, ww.z, accs[o].z);
+          accs[o].w = fmaf(xx.w, ww.w, accs[o].w);
+        }
+      }
 #pragma unroll
     for (int o = 0; o < OXT; ++o) {
       if (ox0 + o >= ow) break;
-      float4 acc = b4;
-#pragma unroll
-      for (int ky = 0; ky < 3; ++ky)
-#pragma unroll
-        for (int kx = 0; kx < 3; ++kx) {
-          const float4 xx = xv[ky][o * SW + kx], ww = wv[ky * 3 + kx];
-          acc.x = fmaf(xx.x, ww.x, acc.x);
-          acc.y = fmaf(xx.y, ww.y, acc.y);
-          acc.z = fmaf(xx.z, ww.z, acc.z);
-          acc.w = fmaf(xx.w, ww.w, acc.w);
-        }
+      const float4 acc = accs[o];
       float r[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
@@ -737,7 +742,8 @@ int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const floa
                                                     d.dil_h, d.dil_w, op.act, op.act_a, op.act_b)
   if (d.kh == 3 && d.kw == 3 && d.dil_h == 1 && d.dil_w == 1 && d.stride_h == d.stride_w &&
       (d.stride_h == 1 || d.stride_h == 2)) {
-    const int groups = (op.ow + 3) / 4;
+    const int oxt = d.stride_h == 1 ? 4 : 2;  // outputs per thread (the kernel's OXT)
+    const int groups = (op.ow + oxt - 1) / oxt;
     const int th = std::min(256, std::max(32, (groups * (d.c / 4) + 31) / 32 * 32));
 #define NNRCU_DW3(A, S)                                                                                                 \
   dw3x3_f32_kernel<A, S><<<rows, th, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh, op.ow,     \
