@@ -281,7 +281,19 @@ def other_rows(ops, W, torch, dev, stream, flush, steps=30):
     wsq = torch.empty(max(qmm.workspace_size(), 1), dtype=torch.uint8, device=dev)
     msq = timed(lambda: qmm.exec(aq, yq, wsq, stream=stream))
     f3 = 2 * 4096 * 768 * 3072
-    return {"config1_conv_relu_fp32": {"ms": round(ms1, 5), "tflops": round(f1 / ms1 / 1e9, 1)},
+    # config 5: MobileNetV2 fp32, batch 128 per GPU, one captured graph per forward
+    from nnr_b200 import fgraph, mobilenetv2
+    mb = mobilenetv2.build(batch=128)
+    mnet = fgraph.FloatNetwork(mb, dev.index or 0)
+    mnet.stream = stream  # launched (and timed) on the bench's stream
+    mnet.view("input").copy_(torch.from_numpy(mobilenetv2.input_batch(0, 128)))
+    mnet.capture()
+    ms5 = timed(lambda: mnet.launch())
+    mnet.close()
+    del mnet
+    return {"config5_mobilenetv2_fp32": {"images_per_s": round(128 / ms5 * 1e3, 1), "ms_per_128": round(ms5, 4),
+                                         "tflops": round(2 * mb.macs_per_image() * 128 / ms5 / 1e9, 1)},
+            "config1_conv_relu_fp32": {"ms": round(ms1, 5), "tflops": round(f1 / ms1 / 1e9, 1)},
             "config3_gemm_fp32": {"ms": round(ms3, 5), "tflops": round(f3 / ms3 / 1e9, 1)},
             "config3_qlinearmatmul": {"ms": round(msq, 5), "tops": round(f3 / msq / 1e9, 1)},
             "fp32_peak_note": "split-bf16: 3 bf16 products per fp32 multiply-add; peak = measured bf16 / 3"}
