@@ -49,16 +49,16 @@ enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_AC
 // Opt-in phase trace for performance analysis (built only with -DNNRCU_TRACE):
 // clock64 stamps of CTAs 0-3, per warp, per local tile (first 16), 4 events.
 #ifdef NNRCU_TRACE
-__device__ unsigned long long g_trace[4 * 18 * 16 * 4];
+__device__ unsigned long long g_trace[4 * 24 * 16 * 4];
 #define NNRCU_TRACE_AT(w, t, ev)                                                       \
   do {                                                                                 \
-    if (blockIdx.x < 4 && (t) < 16) g_trace[((blockIdx.x * 18 + (w)) * 16 + (t)) * 4 + (ev)] = clock64(); \
+    if (blockIdx.x < 4 && (t) < 16) g_trace[((blockIdx.x * 24 + (w)) * 16 + (t)) * 4 + (ev)] = clock64(); \
   } while (0)
 // finer stamps inside a tile's epilogue: CTAs 0-1, first 4 tiles, 16 events
-__device__ unsigned long long g_trace2[2 * 18 * 4 * 16];
+__device__ unsigned long long g_trace2[2 * 24 * 4 * 16];
 #define NNRCU_TRACE2_AT(w, t, ev)                                                       \
   do {                                                                                  \
-    if (blockIdx.x < 2 && (t) < 4 && (ev) < 16) g_trace2[((blockIdx.x * 18 + (w)) * 4 + (t)) * 16 + (ev)] = clock64(); \
+    if (blockIdx.x < 2 && (t) < 4 && (ev) < 16) g_trace2[((blockIdx.x * 24 + (w)) * 4 + (t)) * 16 + (ev)] = clock64(); \
   } while (0)
 #else
 #define NNRCU_TRACE2_AT(w, t, ev) \
@@ -73,7 +73,7 @@ constexpr int BM = 128;       // rows per tile (TMEM lanes)
 constexpr int BKB = 128;      // K bytes per stage per plane (one swizzle row); 64 for the 64-byte-slab variant
 // Warp roles per A-operand mode and N tile:
 //   gather mode:    warps 0-3 epilogue, 4-7 gather producers, 8 TMA, 9 MMA
-//   TMA / im2col:   warps 0 .. 4*SPLIT-1 epilogue, then TMA, then MMA, with
+//   TMA / im2col:   warps 0 .. 4*SPLIT-1 epilogue, then 3 TMA producers, then MMA, with
 //                   SPLIT epilogue warps per TMEM lane quarter, each draining
 //                   BN / SPLIT columns (16 warps for BN >= 128: the epilogue,
 //                   not the tensor core, bounds the small-K layers)
@@ -81,7 +81,14 @@ template <int AMODE, int BN>
 struct Roles {
   static constexpr int SPLIT = AMODE == A_GATHER ? 1 : (BN >= 128 ? 4 : 2);
   static constexpr int TMA_WARP = AMODE == A_GATHER ? 8 : 4 * SPLIT;
-  static constexpr int MMA_WARP = TMA_WARP + 1;
+  // TMA-fed modes issue their copies from three producer warps (stage it
+  // goes to warp it % NPROD): one warp's copies complete at about one per
+  // several hundred cycles, so more issuing warps raise the load rate (1.4x
+  // with two, 1.8x with four). Three keeps the warp count a multiple of four,
+  // so each SM sub-partition holds the same number of warps and the
+  // register budget per thread stays at 96 with sixteen epilogue warps.
+  static constexpr int NPROD = AMODE == A_GATHER ? 1 : 3;
+  static constexpr int MMA_WARP = TMA_WARP + NPROD;
   static constexpr int THREADS = (MMA_WARP + 1) * 32;
   static constexpr int CW = 32;  // accumulator columns per TMEM load
 };
@@ -328,7 +335,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_tiles = m_tiles * n_tiles;
-  if (threadIdx.x == 0) NNRCU_TRACE_AT(17, 15, 3);  // CTA start
+  if (threadIdx.x == 0) NNRCU_TRACE_AT(23, 15, 3);  // CTA start
   // per-column constants, one private copy per epilogue warp (no cross-warp sync)
   int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + Cfg::BAR_BYTES +
                                              (warp & (4 * SPLIT - 1)) * (3 * HB * 4));
@@ -391,12 +398,13 @@ if constexpr (AMODE == A_ROWS) {
     *abort_flag = 1;
   };
 
-  if (warp == R::TMA_WARP) {
-    // ------------------------------------------------------------ TMA producer
+  if (warp >= R::TMA_WARP && warp < R::TMA_WARP + R::NPROD) {
+    // ------------------------------------------------------------ TMA producers
+    const int pw = warp - R::TMA_WARP;  // this producer issues stages it with it % NPROD == pw
     if (lane == 0) {
       constexpr uint32_t tx =
           AMODE == A_ROWS ? 0u : (AMODE != A_GATHER ? NPLANE * A_BYTES : 0) + (NKBR ? 0 : NPLANE * B_BYTES);
-      if constexpr (NKBR > 0) {
+      if (NKBR > 0 && pw == 0) {
         // the single N tile's B, all K slabs, once per CTA
         ptx::mbar_arrive_expect_tx(bres_bar, (uint32_t)(num_kb * B_BYTES));
         for (int kb = 0; kb < num_kb; ++kb) ptx::tma_load_2d(sB + (size_t)kb * B_BYTES, &tmB, bres_bar, kb * KB, 0);
@@ -420,6 +428,7 @@ if constexpr (AMODE == A_ROWS) {
         int r_mb = 0, r_nvr = 0, r_orow = 0, r_ow0 = 0;
         if (AMODE == A_ROWS) tile_rows(tile / n_tiles, r_mb, r_nvr, r_orow, r_ow0);
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          if (R::NPROD > 1 && it % R::NPROD != pw) continue;
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag)) { fail(ST_TIMEOUT_EMPTY); aborted = true; break; }
