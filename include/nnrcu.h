@@ -218,6 +218,9 @@ int nnrcu_dq_gap_q_u8_nhwc(const uint8_t* x, int n, int hw, int c, float x_scale
 int nnrcu_dequantize_linear_u8(const uint8_t* x, float scale, uint8_t zp, const float* bias, int rows, int cols,
                                float* y, void* stream);
 
+/* GlobalAveragePool on fp32 NHWC [n, hw, c] -> [n, c] (kernel/pool.h:109-125). */
+int nnrcu_gap_f32_nhwc(const float* x, int n, int hw, int c, float* y, void* stream);
+
 /* ---------------------------------------------------------------- layout helpers
  * Device versions of nnr's boundary reorders (src/nnr.cpp:953-1031, kernel/layout.h). */
 int nnrcu_nchw_to_nhwc(const void* src, void* dst, int n, int c, int h, int w, int elem_size, void* stream);
