@@ -156,9 +156,14 @@ __device__ __forceinline__ uint32_t quantize_elem(float v, long long i, float sc
 
 // QuantizeLinear fused into the space-to-depth reorder: fp32 NCHW / NHWC
 // input straight to the padded 16-byte s2d pixels. Block (Y, image).
-__global__ void quantize_s2d_kernel(const float* __restrict x, int nchw, uint8_t* __restrict dst, int c, int h, int w,
-                                    int hp, int wp, int pt, int pl, uint8_t fill, float scale, float inv, int zp,
-                                    long long vec_end) {
+// pairs: NCHW input with an even width, so the two columns (dx = 0, 1) of a
+// pixel are one aligned float2 (coalesced across the warp). CC > 0 fixes the
+// channel count at compile time so that all loads of a pixel issue at once.
+template <int CC>
+__global__ void quantize_s2d_kernel(const float* __restrict x, int nchw, uint8_t* __restrict dst, int c_rt, int h,
+                                    int w, int hp, int wp, int pt, int pl, uint8_t fill, float scale, float inv, int zp,
+                                    long long vec_end, int pairs) {
+  const int c = CC > 0 ? CC : c_rt;
   const int Y = blockIdx.x, b = blockIdx.y;
   const int ih0 = 2 * (Y - pt);
   const uint32_t f4 = 0x01010101u * fill;
@@ -170,6 +175,20 @@ __global__ void quantize_s2d_kernel(const float* __restrict x, int nchw, uint8_t
     for (int dy = 0; dy < 2; ++dy) {
       const int ih = ih0 + dy;
       if (ih < 0 || ih >= h) continue;
+      if (pairs && iw0 >= 0 && iw0 + 1 < w) {
+        const long long i00 = (((long long)b * c) * h + ih) * w + iw0;
+#pragma unroll 4
+        for (int ci = 0; ci < c; ++ci) {
+          const long long i = i00 + (long long)ci * h * w;
+          const float2 v = __ldg(reinterpret_cast<const float2*>(x + i));
+          const uint32_t q0 = quantize_elem(v.x, i, scale, inv, zp, vec_end);
+          const uint32_t q1 = quantize_elem(v.y, i + 1, scale, inv, zp, vec_end);
+          const int b0 = (dy * 2) * c + ci, b1 = (dy * 2 + 1) * c + ci;
+          wv[b0 >> 2] = (wv[b0 >> 2] & ~(0xFFu << (8 * (b0 & 3)))) | (q0 << (8 * (b0 & 3)));
+          wv[b1 >> 2] = (wv[b1 >> 2] & ~(0xFFu << (8 * (b1 & 3)))) | (q1 << (8 * (b1 & 3)));
+        }
+        continue;
+      }
 #pragma unroll
       for (int dx = 0; dx < 2; ++dx) {
         const int iw = iw0 + dx;
@@ -654,8 +673,9 @@ int launch_quantize_s2d(const float* x, int nchw, uint8_t* dst, int n, int c, in
     return set_error(NNRCU_ERR_INVALID, "quantize + space-to-depth: needs 4c <= 16, an aligned destination, n <= 65535");
   const long long total = (long long)n * c * h * w;
   const long long vec_end = total >= 64 ? total / 16 * 16 : 0;  // QuantizeLinear.cpp:132
-  quantize_s2d_kernel<<<dim3(hp, n), 128, 0, st>>>(x, nchw, dst, c, h, w, hp, wp, pt, pl, fill, scale, 1.0f / scale, zp,
-                                                  vec_end);
+  const int pairs = nchw && (w % 2) == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0;
+  auto kern = c == 3 ? quantize_s2d_kernel<3> : quantize_s2d_kernel<0>;
+  kern<<<dim3(hp, n), 128, 0, st>>>(x, nchw, dst, c, h, w, hp, wp, pt, pl, fill, scale, 1.0f / scale, zp, vec_end, pairs);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

@@ -82,6 +82,50 @@ __global__ void maxpool_u8_nhwc_kernel(const uint8_t* __restrict x, uint8_t* __r
   }
 }
 
+// Separable form of the same max (max is associative, so the result is
+// identical): the block first takes the column max over the window's input
+// rows for every input column into shared memory (each input row read once
+// per output row, coalesced), then the row max over kw columns from there.
+__global__ void maxpool_u8_nhwc_sep_kernel(const uint8_t* __restrict x, uint8_t* __restrict y, int h, int w, int c,
+                                           int oh, int ow, int kh, int kw, int sh, int sw, int pt, int pl) {
+  extern __shared__ uint4 colmax[];
+  const int cv = c / 16;
+  const int row = blockIdx.x;
+  const int img = row / oh, oy = row - img * oh;
+  const int y0 = oy * sh - pt;
+  const int ya = max(y0, 0), yb = min(y0 + kh, h);
+  const uint4* xin = reinterpret_cast<const uint4*>(x + (size_t)img * h * w * c) + (size_t)ya * w * cv;
+  const int rowv = w * cv;
+  for (int i = threadIdx.x; i < rowv; i += blockDim.x) {
+    uint4 m = make_uint4(0, 0, 0, 0);
+    const uint4* p = xin + i;
+    for (int iy = ya; iy < yb; ++iy, p += rowv) {
+      const uint4 t = __ldg(p);
+      m.x = __vmaxu4(m.x, t.x);
+      m.y = __vmaxu4(m.y, t.y);
+      m.z = __vmaxu4(m.z, t.z);
+      m.w = __vmaxu4(m.w, t.w);
+    }
+    colmax[i] = m;
+  }
+  __syncthreads();
+  uint4* out = reinterpret_cast<uint4*>(y + (size_t)row * ow * c);
+  for (int i = threadIdx.x; i < ow * cv; i += blockDim.x) {
+    const int ox = i / cv, v = i - ox * cv;
+    const int x0 = ox * sw - pl;
+    const int xa = max(x0, 0), xb = min(x0 + kw, w);
+    uint4 m = make_uint4(0, 0, 0, 0);
+    for (int ix = xa; ix < xb; ++ix) {
+      const uint4 t = colmax[ix * cv + v];
+      m.x = __vmaxu4(m.x, t.x);
+      m.y = __vmaxu4(m.y, t.y);
+      m.z = __vmaxu4(m.z, t.z);
+      m.w = __vmaxu4(m.w, t.w);
+    }
+    out[i] = m;
+  }
+}
+
 __global__ void maxpool_u8_nhwc_scalar_kernel(const uint8_t* __restrict x, uint8_t* __restrict y, int n, int h, int w,
                                               int c, int oh, int ow, int kh, int kw, int sh, int sw, int pt, int pl) {
   const long long total = (long long)n * oh * ow * c;
@@ -238,7 +282,11 @@ int nnrcu_maxpool_u8_nhwc(const uint8_t* x, uint8_t* y, int n, int h, int w, int
   if (oh <= 0 || ow <= 0) return set_error(NNRCU_ERR_INVALID, "MaxPool window larger than the padded input");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (c % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
-    maxpool_u8_nhwc_kernel<<<n * oh, 256, 0, st>>>(x, y, h, w, c, oh, ow, kh, kw, sh, sw, pt, pl);
+    const size_t row_bytes = (size_t)w * c;
+    if (row_bytes <= 48 * 1024)
+      maxpool_u8_nhwc_sep_kernel<<<n * oh, 256, row_bytes, st>>>(x, y, h, w, c, oh, ow, kh, kw, sh, sw, pt, pl);
+    else
+      maxpool_u8_nhwc_kernel<<<n * oh, 256, 0, st>>>(x, y, h, w, c, oh, ow, kh, kw, sh, sw, pt, pl);
   } else {
     const long long total = (long long)n * oh * ow * c;
     maxpool_u8_nhwc_scalar_kernel<<<blocks_for(total, 256), 256, 0, st>>>(x, y, n, h, w, c, oh, ow, kh, kw, sh, sw,
