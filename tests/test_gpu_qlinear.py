@@ -174,7 +174,9 @@ def test_config3_qlinearmatmul_bit_exact(cuda_dev):
 
 
 @pytest.mark.parametrize("m,k,n,b_zp", [(32, 2048, 1000, 0), (200, 100, 70, 0), (129, 256, 300, -3),
-                                        (1, 768, 64, 5), (257, 48, 33, 0)])
+                                        (1, 768, 64, 5), (257, 48, 33, 0),
+                                        # M <= 64: the CUDA-core dp4a path
+                                        (64, 100, 70, -3), (7, 4096, 129, 2), (33, 16, 1000, 0)])
 def test_qlinearmatmul_shapes(cuda_dev, m, k, n, b_zp):
     rng = np.random.default_rng(m * 7 + k)
     a = rng.integers(0, 256, size=(m, k)).astype(np.uint8)
