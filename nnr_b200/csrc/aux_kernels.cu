@@ -207,6 +207,25 @@ __global__ void quantize_s2d_kernel(const float* __restrict x, int nchw, uint8_t
   }
 }
 
+// NHWC u8 [n][h][w][cs] -> spatially padded [n][hp][wp][cs] whose border
+// pixels hold the fill byte (the input zero point). Block (padded row, image):
+// threads over the row's wp * cv 16-byte vectors.
+__global__ void pad_spatial_nhwc_u8_kernel(const uint4* __restrict src, uint4* __restrict dst, int h, int w, int hp,
+                                           int wp, int pt, int pl, int cv, uint32_t fill4) {
+  const int py = blockIdx.x, img = blockIdx.y;
+  const int y = py - pt;
+  const int rowv = wp * cv;
+  uint4* out = dst + ((size_t)img * hp + py) * rowv;
+  const bool yin = (unsigned)y < (unsigned)h;
+  const uint4* in = src + ((size_t)img * h + (yin ? y : 0)) * w * cv;
+  const uint4 fill = make_uint4(fill4, fill4, fill4, fill4);
+  for (int i = threadIdx.x; i < rowv; i += blockDim.x) {
+    const int px = i / cv, v = i - px * cv;
+    const int x = px - pl;
+    out[i] = (yin && (unsigned)x < (unsigned)w) ? __ldg(in + x * cv + v) : fill;
+  }
+}
+
 __global__ void pad_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, long long pixels, int c,
                                    int cs, uint8_t fill) {
   const long long total = pixels * cs;
@@ -676,6 +695,19 @@ int launch_quantize_s2d(const float* x, int nchw, uint8_t* dst, int n, int c, in
   const int pairs = nchw && (w % 2) == 0 && (reinterpret_cast<uintptr_t>(x) & 7) == 0;
   auto kern = c == 3 ? quantize_s2d_kernel<3> : quantize_s2d_kernel<0>;
   kern<<<dim3(hp, n), 128, 0, st>>>(x, nchw, dst, c, h, w, hp, wp, pt, pl, fill, scale, 1.0f / scale, zp, vec_end, pairs);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int launch_pad_spatial_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int h, int w, int cs, int pt, int pl, int pb,
+                               int pr, uint8_t fill, cudaStream_t st) {
+  if ((cs & 15) || ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15))
+    return set_error(NNRCU_ERR_INVALID, "spatial pad: needs 16-byte aligned tensors and channel stride");
+  if (n > 65535) return set_error(NNRCU_ERR_INVALID, "spatial pad: batch over 65535");
+  const int hp = h + pt + pb, wp = w + pl + pr, cv = cs / 16;
+  pad_spatial_nhwc_u8_kernel<<<dim3(hp, n), 256, 0, st>>>(reinterpret_cast<const uint4*>(src),
+                                                           reinterpret_cast<uint4*>(dst), h, w, hp, wp, pt, pl, cv,
+                                                           0x01010101u * fill);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

@@ -24,6 +24,7 @@ int cuda_check(cudaError_t e, const char* what);
 // Whether engine kernels are launched with programmatic dependent launch
 // (on unless the environment sets NNRCU_PDL=0).
 bool pdl_enabled();
+bool shift_enabled();
 
 // Device address of this device's status word (set up once per device).
 int* status_ptr();
@@ -71,6 +72,7 @@ struct Op {
   int cs = 0;                   // device channel stride (elements) of the NHWC operand
   bool need_in_copy = false;    // input must be re-laid-out into the workspace first
   bool pad_in = false;
+  int shift_prows = 0;  // A_SHIFT: patch rows per K slab
   bool explicit_im2col = false; // small-C conv: A materialised densely as [M][kpad] in the workspace
   // Space-to-depth form of a stride-2 small-channel conv (the stem): the
   // input is reordered into s2d pixels of 16 bytes ((dy, dx, c) for 4c <= 16)
@@ -142,6 +144,9 @@ int launch_s2d_u8(const uint8_t* x, int nchw, uint8_t* dst, int n, int c, int h,
 int launch_quantize_s2d(const float* x, int nchw, uint8_t* dst, int n, int c, int h, int w, int hp, int wp, int pt,
                         int pl, uint8_t fill, float scale, uint8_t zp, cudaStream_t st);
 int launch_pad_nhwc_u8(const uint8_t* src, uint8_t* dst, int pixels, int c, int cs, uint8_t fill, cudaStream_t st);
+// NHWC [n][h][w][cs] -> [n][h+pt+pb][w+pl+pr][cs] with a border of fill bytes.
+int launch_pad_spatial_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int h, int w, int cs, int pt, int pl, int pb,
+                               int pr, uint8_t fill, cudaStream_t st);
 int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_t* lo, int n, int c, int h, int w,
                            int cs, cudaStream_t st);
 // Explicit im2col of an fp32 conv input into split-bf16 rows [M][kp].

@@ -176,6 +176,36 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
     op->kpad_bytes = op->num_kb * 128;
     op->bn = std::min(op->bn, 128);
   }
+  // Shifted-patch mode (A_SHIFT in tc_gemm.cuh): stride-1 spatial convs over
+  // whole 64/128-byte channel slabs whose K slabs (at most 9) fit a resident
+  // B, the input copied once into a spatially padded NHWC buffer with an
+  // x_zp border.
+  if (shift_enabled() && !op->s2d && !op->explicit_im2col && d.stride_h == 1 && d.stride_w == 1 &&
+      d.kh * d.kw > 1 && kslab != 0 && op->epi != EPI_R3 &&
+      ((d.in_layout == NNRCU_LAYOUT_NCHW && (d.h * d.w) % 4 == 0) || (d.in_layout == NNRCU_LAYOUT_NHWC && d.c == op->cs))) {
+    const int hp = d.h + d.pad_top + d.pad_bottom, wp = d.w + d.pad_left + d.pad_right;
+    // (slabs start on 1024-byte boundaries: the swizzle pattern repeats there)
+    const int prows = round_up(BM + (d.kh - 1) * d.dil_h * wp + (d.kw - 1) * d.dil_w, 1024 / kslab);
+    const int nslab = op->cs / kslab;
+    const int nkb = d.kh * d.kw * nslab;
+    // N tile 128 (16 epilogue warps) when the output channels are whole
+    // 128-column tiles and the patch still fits beside the larger B
+    const int patch_bytes = nslab * prows * kslab;
+    const bool bn128 = kslab == 128 && d.oc % 128 == 0 && (d.oc / 128 == 1 || d.oc / 128 == 2 || d.oc / 128 == 4) &&
+                       patch_bytes <= KernelCfg<128, 1, A_SHIFT, EPI_R2, 128, 9>::PATCH_BYTES;
+    const int nt = (d.oc + 63) / 64;
+    const int patch_cap = kslab == 128 ? KernelCfg<64, 1, A_SHIFT, EPI_R2, 128, 9>::PATCH_BYTES
+                                       : KernelCfg<64, 1, A_SHIFT, EPI_R2, 64, 9>::PATCH_BYTES;
+    if (prows <= 256 && nkb <= 9 && (bn128 || ((nt == 1 || nt == 2 || nt == 4) && patch_bytes <= patch_cap))) {
+      op->amode = A_SHIFT;
+      op->bn = bn128 ? 128 : 64;
+      op->kslab = kslab;
+      op->num_kb = nkb;
+      op->pad_in = true;
+      op->need_in_copy = true;
+      op->shift_prows = prows;
+    }
+  }
   const size_t hp = d.h + (op->pad_in ? d.pad_top + d.pad_bottom : 0);
   const size_t wp = d.w + (op->pad_in ? d.pad_left + d.pad_right : 0);
   op->ws_bytes = op->need_in_copy ? (size_t)d.n * hp * wp * op->cs : 0;
@@ -277,7 +307,10 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
     xin = static_cast<const uint8_t*>(workspace);
   } else if (op->need_in_copy) {
     uint8_t* ws = static_cast<uint8_t*>(workspace);
-    int rc = op->pad_in ? launch_nchw_to_nhwc_u8_padded(x, ws, d.n, d.c, d.h, d.w, d.pad_top, d.pad_left,
+    int rc = op->pad_in && d.in_layout == NNRCU_LAYOUT_NHWC
+                 ? launch_pad_spatial_nhwc_u8(x, ws, d.n, d.h, d.w, op->cs, d.pad_top, d.pad_left, d.pad_bottom,
+                                              d.pad_right, (uint8_t)op->x_zp, st)
+             : op->pad_in ? launch_nchw_to_nhwc_u8_padded(x, ws, d.n, d.c, d.h, d.w, d.pad_top, d.pad_left,
                                                          d.pad_bottom, d.pad_right, op->cs, (uint8_t)op->x_zp, st)
              : d.in_layout == NNRCU_LAYOUT_NCHW
                  ? launch_nchw_to_nhwc_u8(x, ws, d.n, d.c, d.h, d.w, op->cs, (uint8_t)op->x_zp, st)
@@ -314,6 +347,12 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
                                   g.KW, 1, 1, 1, 1, 16);
       if (rc != NNRCU_OK) return rc;
     }
+  } else if (op->amode == A_SHIFT) {
+    g.prows = op->shift_prows;
+    int rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, xin, op->cs, (uint64_t)g.N * g.H * g.W, op->cs,
+                            op->kslab, op->shift_prows,
+                            op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+    if (rc != NNRCU_OK) return rc;
   } else if (op->amode == A_IM2COL) {
     int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, op->cs, pt, pl, pb, pr,
                                 d.kh, d.kw, d.dil_h, d.dil_w, d.stride_h, d.stride_w, op->kslab);
@@ -354,6 +393,11 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   TcLaunch L{};
   L.bn = op->bn; L.nplane = 1; L.amode = op->amode; L.epi = op->epi;
   L.m_tiles = op->amode == A_ROWS ? d.n * op->oh * ((op->ow + BM - 1) / BM) : (op->M + BM - 1) / BM;
+  if (op->amode == A_SHIFT) {
+    // GEMM rows = padded-grid positions up to the last output pixel
+    e.M = ((d.n - 1) * g.H + op->oh - 1) * g.W + op->ow;
+    L.m_tiles = (e.M + BM - 1) / BM;
+  }
   L.n_tiles = (op->N + op->bn - 1) / op->bn;
   L.tmA0 = &tmA; L.tmA1 = &tmA; L.tmB = &op->tmB;
   L.b_plane_rows = op->npad;

@@ -98,6 +98,13 @@ bool pdl_enabled() {
   return on;
 }
 
+bool shift_enabled() {
+  // shifted-patch mode for stride-1 spatial QLinearConvs; NNRCU_SHIFT=0 turns it off
+  // (read when an operator is created)
+  const char* v = std::getenv("NNRCU_SHIFT");
+  return !(v && v[0] == '0');
+}
+
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   int dev = 0;

@@ -37,7 +37,16 @@ namespace nnrcu {
 // space-to-depth path). A tile covers up to 128 pixels of ONE output row; for
 // each kernel row one contiguous bulk copy brings BM + 8 input pixels, and the
 // kernel's taps along that row are the same rows shifted by 16 bytes each.
-enum : int { A_TMA = 0, A_GATHER = 1, A_IM2COL = 2, A_ROWS = 3 };
+// A_SHIFT: stride-1 convs over an NHWC input whose spatial border (the
+// padding, x_zp bytes) is materialised. Output positions are enumerated on
+// the padded grid [N][Hp][Wp] (positions with oh >= OH or ow >= OW are
+// computed and discarded), so the input rows that tap (kh, kw) needs for a
+// tile's 128 positions are the tile's own rows shifted by kh * Wp + kw: one
+// TMA copy per K slab brings the tile's patch (BM + (KH-1) * Wp + KW - 1 rows)
+// once, and every tap is a view of it starting at a shifted row. The 64/128-
+// byte swizzle is a function of the shared-memory address, so a view may
+// start at any row of the swizzled patch. B is resident.
+enum : int { A_TMA = 0, A_GATHER = 1, A_IM2COL = 2, A_ROWS = 3, A_SHIFT = 4 };
 constexpr int ROWS_BYTES = (128 + 8) * 16;  // one A_ROWS copy: BM + 8 pixels of 16 bytes
 // EPI_R2A: the R2 requant followed by a fused QLinearAdd whose residual
 // tiles are TMA-prefetched one tile ahead (u8 row-major output via TMA store).
@@ -87,7 +96,8 @@ struct Roles {
   // with two, 1.8x with four). Three keeps the warp count a multiple of four,
   // so each SM sub-partition holds the same number of warps and the
   // register budget per thread stays at 96 with sixteen epilogue warps.
-  static constexpr int NPROD = AMODE == A_GATHER ? 1 : 3;
+  // (A_SHIFT issues one patch copy per K slab per tile: one producer.)
+  static constexpr int NPROD = (AMODE == A_GATHER || AMODE == A_SHIFT) ? 1 : 3;
   static constexpr int MMA_WARP = TMA_WARP + NPROD;
   static constexpr int THREADS = (MMA_WARP + 1) * 32;
   static constexpr int CW = 32;  // accumulator columns per TMEM load
@@ -103,6 +113,7 @@ struct GatherGeom {
   int kbytes;            // real K in bytes = KH*KW*cbytes
   uint32_t pad_word;     // value written for padding pixels (x_zp replicated, or 0)
   int tpr;               // A_ROWS: taps per kernel row in K (2, 4 or 8; taps past KW have zero weights)
+  int prows;             // A_SHIFT: patch rows per K slab (BM + (KH-1)*W + KW-1, rounded up to a 1 KB multiple)
   const uint8_t* wb;     // KB = 16: weights as per-(N tile, K slab) shared-memory images of BN x 128 bytes
 };
 
@@ -141,21 +152,24 @@ struct EpiParams {
 
 // NKBR > 0: the whole B operand (num_kb <= NKBR slabs of one N tile) stays
 // resident in shared memory, loaded once per CTA; the stage ring holds A only.
-template <int BN, int NPLANE, int EPI, int KB = BKB, int SPLIT = 1, int NKBR = 0>
+// PATCH (A_SHIFT): the stage ring is two patch buffers that share what the
+// resident B leaves; outputs are stored directly (no staging).
+template <int BN, int NPLANE, int EPI, int KB = BKB, int SPLIT = 1, int NKBR = 0, int PATCH = 0>
 struct TileCfg {
   static constexpr int BUDGET = 212 * 1024;  // stages + staging + resident B
   // K bytes per stage: KB, except KB = 16 (eight 16-byte taps per 128-byte stage)
   static constexpr int SLAB = KB == 16 ? 128 : KB;
-  static constexpr int A_BYTES = BM * SLAB;            // 16 KB per plane (8 KB with 64-byte slabs)
   static constexpr int B_BYTES = BN * SLAB;
-  static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + (NKBR ? 0 : B_BYTES));
   static constexpr int BRES_BYTES = NKBR * B_BYTES;
+  static constexpr int PATCH_BYTES = PATCH ? ((BUDGET - BRES_BYTES) / 2) & ~1023 : 0;  // per patch buffer
+  static constexpr int A_BYTES = PATCH ? PATCH_BYTES : BM * SLAB;  // 16 KB per plane (8 KB with 64-byte slabs)
+  static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + (NKBR ? 0 : B_BYTES));
   // Epilogues stage each warp's 32-row output block for a TMA store: u8
   // always; fp32 (4 bytes per element) when that still leaves three stages.
   static constexpr int ESZ = EPI == EPI_F32 ? 4 : 1;
   static constexpr int OUT_BLOCK_RAW = 4 * 32 * BN * ESZ;  // one 32 x HB block per epilogue warp
   static constexpr int OUT_BLOCK =
-      (EPI == EPI_F32 && (BUDGET - OUT_BLOCK_RAW - BRES_BYTES) / STAGE_BYTES < 3) ? 0 : OUT_BLOCK_RAW;
+      PATCH ? 0 : ((EPI == EPI_F32 && (BUDGET - OUT_BLOCK_RAW - BRES_BYTES) / STAGE_BYTES < 3) ? 0 : OUT_BLOCK_RAW);
   // EPI_R2A: two residual blocks per epilogue warp (tile i in use, tile i+1 landing)
   static constexpr int RES_BYTES = (EPI == EPI_R2A) ? 2 * OUT_BLOCK : 0;
   // Output staging is double-buffered (the store of tile i drains while tile
@@ -167,7 +181,7 @@ struct TileCfg {
   static constexpr int ROW_BYTES = HB * ESZ;                       // bytes of one staged row
   static constexpr int OUT_SEG = ROW_BYTES >= 128 ? 128 : ROW_BYTES;  // bytes per staged row segment (= TMA box width)
   static constexpr int STAGES_RAW = (BUDGET - OUT_BYTES - RES_BYTES - BRES_BYTES) / STAGE_BYTES;
-  static constexpr int STAGES = STAGES_RAW > 12 ? 12 : STAGES_RAW;
+  static constexpr int STAGES = PATCH ? 2 : (STAGES_RAW > 12 ? 12 : STAGES_RAW);
   // Gather producers publish a stage LAG iterations after issuing it: LAG
   // stages of copies in flight, STAGES - 1 - LAG stages of slack for the MMA.
   static constexpr int LAG = (STAGES - 1) / 2 > 1 ? (STAGES - 1) / 2 : 1;
@@ -184,7 +198,7 @@ struct TileCfg {
 // The tile configuration of one engine instance; the kernel's shared-memory
 // carve-up and the launcher's allocation both come from this one alias.
 template <int BN, int NPLANE, int AMODE, int EPI, int KB, int NKBR>
-using KernelCfg = TileCfg<BN, NPLANE, EPI, KB, Roles<AMODE, BN>::SPLIT, NKBR>;
+using KernelCfg = TileCfg<BN, NPLANE, EPI, KB, Roles<AMODE, BN>::SPLIT, NKBR, AMODE == A_SHIFT ? 1 : 0>;
 
 __device__ __forceinline__ void record_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
@@ -301,6 +315,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   using Cfg = KernelCfg<BN, NPLANE, AMODE, EPI, KB, NKBR>;
   static_assert(NKBR == 0 || (NPLANE == 1 && KB != 16 && AMODE != A_GATHER), "resident B: int8, TMA-fed A");
   static_assert(KB == BKB || AMODE != A_GATHER, "the gather producers fill 128-byte slabs");
+  static_assert(AMODE != A_SHIFT || (NKBR > 0 && NPLANE == 1 && (KB == 64 || KB == 128)),
+                "shifted-patch mode: int8, resident B, 64/128-byte slabs");
   constexpr int STAGES = Cfg::STAGES;
   constexpr int A_BYTES = Cfg::A_BYTES;
   constexpr int B_BYTES = Cfg::B_BYTES;
@@ -405,10 +421,28 @@ if constexpr (AMODE == A_ROWS) {
       constexpr uint32_t tx =
           AMODE == A_ROWS ? 0u : (AMODE != A_GATHER ? NPLANE * A_BYTES : 0) + (NKBR ? 0 : NPLANE * B_BYTES);
       if (NKBR > 0 && pw == 0) {
-        // the single N tile's B, all K slabs, once per CTA
+        // this CTA's N tile's B, all K slabs, once per CTA (the grid is a
+        // multiple of n_tiles, so a CTA's tiles all have N tile blockIdx.x % n_tiles)
+        const int bn0 = (int)(blockIdx.x % n_tiles) * BN;
         ptx::mbar_arrive_expect_tx(bres_bar, (uint32_t)(num_kb * B_BYTES));
-        for (int kb = 0; kb < num_kb; ++kb) ptx::tma_load_2d(sB + (size_t)kb * B_BYTES, &tmB, bres_bar, kb * KB, 0);
+        for (int kb = 0; kb < num_kb; ++kb) ptx::tma_load_2d(sB + (size_t)kb * B_BYTES, &tmB, bres_bar, kb * KB, bn0);
       }
+      if constexpr (AMODE == A_SHIFT) {
+        // one patch per tile: each K slab's rows [m0, m0 + prows) of the padded input
+        const int nslab = g.cbytes / KB;
+        const uint32_t ptx_bytes = (uint32_t)(nslab * g.prows * KB);
+        int tlt = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tlt) {
+          const int s = tlt & 1;
+          const uint32_t ph = (uint32_t)(tlt >> 1) & 1u;
+          if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag)) { fail(ST_TIMEOUT_EMPTY); ptx::settle_ns(200000); break; }
+          NNRCU_TRACE_AT(warp, tlt, 0);
+          ptx::mbar_arrive_expect_tx(&full_bar[s], ptx_bytes);
+          const int m0 = (tile / n_tiles) * BM;
+          for (int sl = 0; sl < nslab; ++sl)
+            ptx::tma_load_2d(sA + (size_t)s * A_BYTES + (size_t)sl * g.prows * KB, &tmA0, &full_bar[s], sl * KB, m0);
+        }
+      } else {
       const uint32_t tx_rows = (uint32_t)(8 / max(g.tpr, 1)) * ROWS_BYTES + B_BYTES;  // A_ROWS stage bytes
       bool aborted = false;
       int it = 0, tlt = 0;
@@ -484,6 +518,7 @@ if constexpr (AMODE == A_ROWS) {
         NNRCU_TRACE_AT(warp, tlt, 1);
       }
       if (aborted) ptx::settle_ns(200000);  // let copies already in flight land before the CTA exits
+      }
     }
   } else if (warp == R::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
@@ -491,6 +526,19 @@ if constexpr (AMODE == A_ROWS) {
       constexpr uint32_t idesc = (NPLANE == 1) ? ptx::umma_idesc(2, 0, 1, BM, BN) : ptx::umma_idesc(1, 1, 1, BM, BN);
       bool aborted = false;
       int it = 0, lt = 0;
+      // A_SHIFT: per K step, the A view's start offset within a patch buffer (16-byte units)
+      uint32_t shift_off[AMODE == A_SHIFT ? NKBR : 1];
+      uint64_t bdesc0 = 0;
+      if constexpr (AMODE == A_SHIFT) {
+        const int nslab = g.cbytes / KB;
+#pragma unroll
+        for (int kb = 0; kb < NKBR; ++kb) {
+          const int tap = kb / nslab, sl = kb - tap * nslab;
+          const int kh = tap / g.KW, kw = tap - kh * g.KW;
+          shift_off[kb] = (uint32_t)(((sl * g.prows + kh * g.dh * g.W + kw * g.dw) * KB) >> 4);
+        }
+        bdesc0 = ptx::umma_desc_sw<KB>(ptx::smem_u32(sB));
+      }
       if (NKBR > 0 && !ptx::mbar_wait(bres_bar, 0u, abort_flag)) {
         fail(ST_TIMEOUT_FULL);
         aborted = true;
@@ -502,13 +550,38 @@ if constexpr (AMODE == A_ROWS) {
         NNRCU_TRACE_AT(warp, lt, 0);
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        if constexpr (AMODE == A_SHIFT) {
+          // K step kb = (tap, slab): the slab's patch viewed from row kh * W + kw.
+          // Descriptors are the buffer's base descriptor plus precomputed
+          // start-address offsets (16-byte units; addresses stay below 2^18,
+          // so the 14-bit field never carries): a few instructions per MMA.
+          const int s = lt & 1;
+          if (!ptx::mbar_wait(&full_bar[s], (uint32_t)(lt >> 1) & 1u, abort_flag)) { fail(ST_TIMEOUT_FULL); aborted = true; break; }
+          NNRCU_TRACE_AT(warp, lt, 1);
+          ptx::tc_fence_after();
+          const uint64_t adesc = ptx::umma_desc_sw<KB>(ptx::smem_u32(sA + (size_t)s * A_BYTES));
+#pragma unroll
+          for (int kb = 0; kb < NKBR; ++kb) {
+            if (kb < num_kb) {
+#pragma unroll
+              for (int k = 0; k < KB / 32; ++k)
+                ptx::mma_i8(d_tmem, adesc + (uint64_t)(shift_off[kb] + k * 2),
+                            bdesc0 + (uint64_t)((kb * B_BYTES + k * 32) >> 4), idesc, (kb | k) != 0);
+            }
+          }
+          ptx::mma_commit(&empty_bar[s]);
+          ptx::mma_commit(&tfull_bar[acc]);
+          NNRCU_TRACE_AT(warp, lt, 2);
+          continue;
+        }
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!ptx::mbar_wait(&full_bar[s], ph, abort_flag)) { fail(ST_TIMEOUT_FULL); aborted = true; break; }
           if (kb == 0) NNRCU_TRACE_AT(warp, lt, 1);
           ptx::tc_fence_after();
-          ptx::fence_proxy_async_smem();
+          // (stages filled by TMA are async-proxy writes already; the gather
+          // producers fence their cp.async writes before arriving)
           const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * NPLANE * A_BYTES);
           const uint32_t b_addr = ptx::smem_u32(NKBR ? sB + (size_t)kb * B_BYTES : sB + (size_t)s * NPLANE * B_BYTES);
 #pragma unroll
@@ -525,8 +598,9 @@ if constexpr (AMODE == A_ROWS) {
               ptx::mma_i8(d_tmem, ptx::umma_desc_interleaved(a_addr + k * 2 * (BM * 16), BM * 16, 128),
                           ptx::umma_desc_interleaved(b_addr + k * 2 * (BN * 16), BN * 16, 128), idesc, (kb | k) != 0);
             } else if constexpr (NPLANE == 1) {
-              ptx::mma_i8(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff), ptx::umma_desc_sw<KB>(b_addr + koff), idesc,
-                          (kb | k) != 0);
+              // stage descriptors plus the K offset (16-byte units)
+              ptx::mma_i8(d_tmem, ptx::umma_desc_sw<KB>(a_addr) + (uint64_t)(koff >> 4),
+                          ptx::umma_desc_sw<KB>(b_addr) + (uint64_t)(koff >> 4), idesc, (kb | k) != 0);
             } else {
               // hi*hi, hi*lo, lo*hi
               ptx::mma_f16(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff), ptx::umma_desc_sw<KB>(b_addr + koff), idesc,
@@ -650,6 +724,7 @@ if constexpr (AMODE == A_ROWS) {
     const float kp_ca = __fsub_rn(e.yzp_f, RND_MAGIC);
     const uint32_t kp_yzp = (uint32_t)e.yzp;
     const bool kp_ovf = e.qa_ovf != 0;
+    const bool shift_direct = e.y_layout == 0 && (e.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0;
     // EPI_R2A: TMA load of this warp's 32 x HB residual block of tile t into buffer buf
     auto issue_res = [&](const int t, const int buf) {
       constexpr int SEG = Cfg::OUT_SEG;
@@ -725,8 +800,14 @@ if constexpr (AMODE == A_ROWS) {
         break;
       }
       if (lane == 0) NNRCU_TRACE_AT(warp, lt, 2);
-      const int m = m0 + row;
-      const bool mvalid = row < nvr;
+      int m = m0 + row;  // output row (A_SHIFT: GEMM rows are padded-grid positions, mapped below)
+      bool mvalid = row < nvr;
+      if constexpr (AMODE == A_SHIFT) {
+        const int pr = m / g.W, px = m - pr * g.W;
+        const int im = pr / g.H, py = pr - im * g.H;
+        mvalid = mvalid && px < g.OW && py < g.OH;
+        m = (im * g.OH + py) * g.OW + px;
+      }
       int32_t rowc = 0;
       if (EPI == EPI_R4 && e.rowcorr && mvalid) rowc = e.rowcorr[m];
       int img = 0, pix = 0;
@@ -939,8 +1020,12 @@ if constexpr (AMODE == A_ROWS) {
       };
       // Interior tiles of u8 epilogues with a TMA-stored output take a lean
       // path: no row / column / tail checks, one inlined copy in the loop.
+      // (A_SHIFT: the lean path stores each row's bytes straight to HBM; rows
+      // that are not output pixels are skipped)
       bool fast = false;
-      if constexpr (EPI != EPI_F32)
+      if constexpr (EPI != EPI_F32 && AMODE == A_SHIFT)
+        fast = shift_direct && n0 + BN <= e.N && e.qres == nullptr;
+      else if constexpr (EPI != EPI_F32)
         fast = y_tma && (AMODE == A_ROWS || m0 + BM <= e.M) && n0 + BN <= e.N &&
                (EPI == EPI_R2A ? (long long)(m0 + BM) * e.N <= e.qa_vec_end : e.qres == nullptr);
       auto chunk_fast = [&](const int c0, uint32_t (&v)[CW]) {
@@ -1047,6 +1132,18 @@ if constexpr (AMODE == A_ROWS) {
               q[j + 2] = requant_u8<EPI>((int32_t)v[j + 2], ci4.z, rowc, a4.z, b4.z, e);
               q[j + 3] = requant_u8<EPI>((int32_t)v[j + 3], ci4.w, rowc, a4.w, b4.w, e);
             }
+          }
+          if constexpr (AMODE == A_SHIFT) {
+            if (mvalid) {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(e.y) + (size_t)m * e.ldy + n0 + c0);
+#pragma unroll
+              for (int k = 0; k < CW / 16; ++k)
+                dst[k] = make_uint4(pack_low_bytes(q[16 * k], q[16 * k + 1], q[16 * k + 2], q[16 * k + 3]),
+                                    pack_low_bytes(q[16 * k + 4], q[16 * k + 5], q[16 * k + 6], q[16 * k + 7]),
+                                    pack_low_bytes(q[16 * k + 8], q[16 * k + 9], q[16 * k + 10], q[16 * k + 11]),
+                                    pack_low_bytes(q[16 * k + 12], q[16 * k + 13], q[16 * k + 14], q[16 * k + 15]));
+            }
+            return;
           }
           const int h = pc / SEG, cc = (pc % SEG) >> 4;
           uint8_t* seg = stg + h * (32 * SEG) + lane * SEG;

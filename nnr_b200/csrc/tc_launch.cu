@@ -22,7 +22,10 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
     configured |= 1ull << dev;
   }
   const long long tiles = (long long)L.m_tiles * L.n_tiles;
-  const int grid = (int)std::min<long long>(tiles, (long long)num_sms());
+  int grid = (int)std::min<long long>(tiles, (long long)num_sms());
+  // resident B: each CTA keeps one N tile's weights, so its tiles must all
+  // share that N tile (tile % n_tiles == blockIdx.x % n_tiles)
+  if (NKBR > 0) grid = std::max(L.n_tiles, grid / L.n_tiles * L.n_tiles);
   // u8 outputs in row-major [M, ldy] leave through a TMA store of each
   // warp's staged 32 x BN block (coalesced rows instead of per-lane pieces).
   CUtensorMap tmY{};
@@ -39,7 +42,7 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
                                        : (seg == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B));
     if (rc != NNRCU_OK) return rc;
     y_tma = 1;
-  } else if (AMODE != A_ROWS && EPI != EPI_F32 && e.y_layout == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
+  } else if (AMODE != A_ROWS && AMODE != A_SHIFT && EPI != EPI_F32 && e.y_layout == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
              (e.ldy & 15) == 0) {
     const int seg = Cfg::OUT_SEG;
     int rc = encode_tmap_2d(&tmY, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.y, (uint64_t)e.N, (uint64_t)e.M, (uint64_t)e.ldy,
@@ -198,6 +201,24 @@ int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaSt
       ((L.bn == 64 && L.kb_bytes == 64) || (L.bn == 128 && L.kb_bytes == 128))) {
     if (L.bn == 64) return launch_one<64, 1, A_IM2COL, EPI_R2, 64, 9>(L, g, e, stream);
     return launch_one<128, 1, A_IM2COL, EPI_R2, 128, 9>(L, g, e, stream);
+  }
+  if (L.amode == A_SHIFT) {
+    // shifted-patch convs: N tile 64 (or 128 over 128-byte slabs), resident B of at most 9 K slabs
+    if (!(L.bn == 64 || (L.bn == 128 && L.kb_bytes == 128)) || L.nplane != 1 || L.num_kb > 9 ||
+        !(L.n_tiles == 1 || L.n_tiles == 2 || L.n_tiles == 4))
+      return set_error(NNRCU_ERR_INVALID, "shifted-patch conv: unsupported tiling (bn %d, %d K slabs, %d N tiles)", L.bn,
+                       L.num_kb, L.n_tiles);
+    if (L.bn == 128) {
+      if (L.epi == EPI_R1) return launch_one<128, 1, A_SHIFT, EPI_R1, 128, 9>(L, g, e, stream);
+      if (L.epi == EPI_R2) return launch_one<128, 1, A_SHIFT, EPI_R2, 128, 9>(L, g, e, stream);
+    } else if (L.kb_bytes == 64) {
+      if (L.epi == EPI_R1) return launch_one<64, 1, A_SHIFT, EPI_R1, 64, 9>(L, g, e, stream);
+      if (L.epi == EPI_R2) return launch_one<64, 1, A_SHIFT, EPI_R2, 64, 9>(L, g, e, stream);
+    } else if (L.kb_bytes == 128) {
+      if (L.epi == EPI_R1) return launch_one<64, 1, A_SHIFT, EPI_R1, 128, 9>(L, g, e, stream);
+      if (L.epi == EPI_R2) return launch_one<64, 1, A_SHIFT, EPI_R2, 128, 9>(L, g, e, stream);
+    }
+    return set_error(NNRCU_ERR_INVALID, "no shifted-patch instance for %d-byte slabs, epilogue %d", L.kb_bytes, L.epi);
   }
   if (L.epi == EPI_R2 && L.amode == A_TMA && e.qres && e.y_layout == 0 && (e.ldy & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 && (reinterpret_cast<uintptr_t>(e.qres) & 15) == 0)

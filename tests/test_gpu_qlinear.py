@@ -315,3 +315,73 @@ def test_quantize_fused_into_space_to_depth(cuda_dev, shape, in_layout):
     assert ops.device_status() == 0
     assert np.array_equal(y.cpu().numpy(), ref)
 
+
+
+# Shifted-patch path (A_SHIFT): stride-1 spatial convs over whole 64/128-byte
+# channel slabs, computed on the x_zp-bordered padded grid; a CTA keeps one
+# N tile's weights resident (1, 2 or 4 N tiles of 64, or of 128 columns).
+# n, c, h, w, oc, kh, kw, pads, dilations
+SHIFT_SHAPES = [
+    (4, 64, 56, 56, 64, 3, 3, (1, 1, 1, 1), (1, 1)),     # ResNet-50 stage 1 (largest patch: 256 rows)
+    (2, 128, 28, 28, 128, 3, 3, (1, 1, 1, 1), (1, 1)),   # stage 2: one 128-wide N tile
+    (2, 128, 10, 10, 256, 3, 3, (1, 1, 1, 1), (1, 1)),   # two 128-wide N tiles
+    (3, 64, 17, 23, 100, 3, 3, (1, 1, 1, 1), (1, 1)),    # ragged N (2 tiles of 64), odd extents
+    (2, 64, 9, 11, 256, 3, 3, (0, 2, 1, 0), (1, 1)),     # asymmetric pads, 4 N tiles
+    (2, 128, 12, 12, 64, 3, 3, (2, 2, 2, 2), (2, 2)),    # dilation 2
+    (1, 64, 8, 8, 64, 5, 5, (2, 2, 2, 2), (1, 1)),       # 25 K slabs: not resident, falls back
+    (2, 64, 3, 5, 64, 3, 3, (1, 1, 1, 1), (1, 1)),       # whole images smaller than a tile
+    (1, 64, 6, 120, 64, 3, 3, (1, 1, 1, 1), (1, 1)),     # patch over 256 rows: falls back
+]
+
+
+def _shift_case(shape, x_zp, seed):
+    n, c, h, w, oc, kh, kw, p, d = shape
+    rng = np.random.default_rng(seed)
+    return W.random_qconv(rng, n, c, h, w, oc, kh, kw, (1, 1), p, d, x_zp=x_zp)
+
+
+@pytest.mark.parametrize("shape", SHIFT_SHAPES)
+@pytest.mark.parametrize("formula", [O.R1, O.R2])
+@pytest.mark.parametrize("x_zp", [0, 93])
+def test_shifted_patch_convs(cuda_dev, shape, formula, x_zp):
+    case = _shift_case(shape, x_zp, sum(shape[:7]) + formula + x_zp)
+    for lay in (("NHWC", "NHWC"), ("NCHW", "NHWC"), ("NHWC", "NCHW")):
+        y, _ = run_qconv(cuda_dev, case, formula, lay[0], lay[1])
+        ref = oracle_qconv(case, formula, lay[1])
+        assert np.array_equal(y, ref), f"{lay}: {(y != ref).sum()} / {y.size} mismatches"
+
+
+def test_shifted_patch_is_selected(cuda_dev):
+    """NHWC input with x_zp = 0 needs no workspace on the im2col path; the
+    shifted-patch path copies it into a padded buffer ([n][h+2][w+2][c])."""
+    case = _shift_case(SHIFT_SHAPES[0], 0, 5)
+    _, op = run_qconv(cuda_dev, case, O.R2, "NHWC", "NHWC")
+    n, c, h, w = case.x.shape
+    assert op.workspace_size() == n * (h + 2) * (w + 2) * c
+
+
+@pytest.mark.parametrize("relu", [False, True])
+def test_shifted_patch_fused_relu_and_add(cuda_dev, relu):
+    import ctypes as C
+    from nnr_b200 import ops
+    from nnr_b200._lib import check, lib
+    case = _shift_case(SHIFT_SHAPES[3], 0, 11)
+    case.y_zp = 40
+    op = ops.QLinearConv(case.x.shape, case.w, case.w_scale, case.w_zp, case.bias, case.x_scale, case.x_zp,
+                         case.y_scale, case.y_zp, pads=case.pads, in_layout="NHWC", out_layout="NHWC", requant=O.R2,
+                         fused_relu=relu)
+    conv = oracle_qconv(case, O.R2, out_layout="NHWC", fused_relu=relu)
+    rng = np.random.default_rng(3)
+    res = rng.integers(0, 256, size=conv.shape).astype(np.uint8)
+    rs, rz, ys, yz = 0.037, 101, 0.05, 7
+    ref = O.qlinearadd_u8(conv, case.y_scale, case.y_zp, res, rs, rz, ys, yz)
+    x = torch.from_numpy(_to_nhwc(case.x)).to(cuda_dev)
+    r = torch.from_numpy(res).to(cuda_dev)
+    y = torch.empty(conv.shape, dtype=torch.uint8, device=cuda_dev)
+    ws = torch.empty(max(op.workspace_size(), 1), dtype=torch.uint8, device=cuda_dev)
+    check(lib.nnrcu_qlinearconv_run_add(op._op, C.c_void_p(x.data_ptr()), C.c_void_p(r.data_ptr()), rs, rz, ys, yz,
+                                        C.c_void_p(y.data_ptr()), C.c_void_p(ws.data_ptr()),
+                                        C.c_void_p(torch.cuda.current_stream().cuda_stream)))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert np.array_equal(y.cpu().numpy(), ref)
