@@ -144,6 +144,24 @@ int nnrcu_qlinearconv_run_quantize(nnrcu_op* op, const float* x, float x_scale, 
 int nnrcu_qlinearconv_run_add(nnrcu_op* op, const uint8_t* x, const uint8_t* residual, float res_scale,
                               uint8_t res_zp, float out_scale, uint8_t out_zp, uint8_t* y, void* workspace,
                               void* stream);
+/* Padded activations between two QLinearConvs (a device-executor layout
+ * choice with no counterpart in nnr, whose convs pad inside their own
+ * kernels). Some convs (stride-1 spatial kernels over 64/128-byte channel
+ * strides) read an x_zp-bordered copy of their NHWC input, made in their
+ * workspace on every run; _input_padding reports that border (top, left,
+ * bottom, right; zeros when the op reads its input as is). _set_padded_io
+ * then lets a producer write straight into such a buffer and the consumer
+ * skip the copy:
+ *   in_padded = 1: x passed to nnrcu_qlinearconv_run is already
+ *     [n][h+top+bottom][w+left+right][c] with every border byte = x_zp
+ *     (no workspace is used);
+ *   out_* > 0: nnrcu_qlinearconv_run writes y into the interior of
+ *     [n][oh+top+bottom][ow+left+right][oc] (NHWC, oc % 16 == 0) and leaves
+ *     the border alone (the caller fills it once with the consumer's x_zp).
+ * Results are unchanged. */
+int nnrcu_qlinearconv_input_padding(const nnrcu_op* op, int* pads);
+int nnrcu_qlinearconv_set_padded_io(nnrcu_op* op, int in_padded, int out_top, int out_left, int out_bottom,
+                                    int out_right);
 
 /* ---------------------------------------------------------------- QLinearMatMul (u8 a, s8 b, u8 y)
  * Replaces QLinearMatMul_operator (backend/cpu/QLinearMatMul.cpp:33-232) for a 2-D B

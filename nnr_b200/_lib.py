@@ -66,6 +66,8 @@ SIGNATURES = {
     "nnrcu_qlinearconv_create": [C.POINTER(ConvDesc), P, P, I, P, I, P, F, U8, F, U8, PP],
     "nnrcu_qlinearconv_run": [P, P, P, P, P],
     "nnrcu_qlinearconv_run_add": [P, P, P, F, U8, F, U8, P, P, P],
+    "nnrcu_qlinearconv_input_padding": [P, P],
+    "nnrcu_qlinearconv_set_padded_io": [P, I, I, I, I, I],
     "nnrcu_qlinearconv_run_quantize": [P, P, F, U8, P, P, P],
     "nnrcu_gap_f32_nhwc": [P, I, I, I, P, P],
     "nnrcu_qlinearmatmul_create": [I, I, I, F, U8, P, F, I8, F, U8, PP],

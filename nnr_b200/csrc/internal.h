@@ -73,6 +73,8 @@ struct Op {
   bool need_in_copy = false;    // input must be re-laid-out into the workspace first
   bool pad_in = false;
   int shift_prows = 0;  // A_SHIFT: patch rows per K slab
+  bool in_padded = false;        // x is already the x_zp-bordered padded copy (A_SHIFT, NHWC input)
+  int out_pad[4] = {0, 0, 0, 0};  // output written into a padded NHWC buffer (top, left, bottom, right)
   bool explicit_im2col = false; // small-C conv: A materialised densely as [M][kpad] in the workspace
   // Space-to-depth form of a stride-2 small-channel conv (the stem): the
   // input is reordered into s2d pixels of 16 bytes ((dy, dx, c) for 4c <= 16)

@@ -286,7 +286,7 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   if (xf && !op->s2d)
     return set_error(NNRCU_ERR_UNSUPPORTED, "QuantizeLinear fusion needs a space-to-depth QLinearConv (stride 2, <= 4 channels)");
   if (xf && !(q_scale > 0.0f)) return set_error(NNRCU_ERR_INVALID, "QuantizeLinear scale must be positive");
-  if (op->ws_bytes && !workspace)
+  if (op->ws_bytes && !workspace && !op->in_padded)
     return set_error(NNRCU_ERR_INVALID, "workspace of %zu bytes required", op->ws_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const nnrcu_conv_desc& d = op->d;
@@ -305,6 +305,8 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
                               d.dil_w, op->kbytes, (uint8_t)op->x_zp, st);
     if (rc != NNRCU_OK) return rc;
     xin = static_cast<const uint8_t*>(workspace);
+  } else if (op->in_padded) {
+    xin = x;  // the caller's buffer already is the padded copy
   } else if (op->need_in_copy) {
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     int rc = op->pad_in && d.in_layout == NNRCU_LAYOUT_NHWC
@@ -371,6 +373,15 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   e.ldy = d.oc;
   e.ohw = op->oh * op->ow;
   e.status = status_ptr();
+  if (op->out_pad[0] | op->out_pad[1] | op->out_pad[2] | op->out_pad[3]) {
+    if (res || xf) return set_error(NNRCU_ERR_UNSUPPORTED, "a padded output is available through nnrcu_qlinearconv_run only");
+    e.opad = 1;
+    e.o_w = op->ow;
+    e.o_hw = op->oh * op->ow;
+    e.o_wp = op->ow + op->out_pad[1] + op->out_pad[3];
+    e.o_hwp = (op->oh + op->out_pad[0] + op->out_pad[2]) * e.o_wp;
+    e.o_off = op->out_pad[0] * e.o_wp + op->out_pad[1];
+  }
   if (res) {
     if (d.out_layout != NNRCU_LAYOUT_NHWC)
       return set_error(NNRCU_ERR_UNSUPPORTED, "a fused residual add needs an NHWC output");
@@ -404,6 +415,31 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   L.num_kb = op->num_kb;
   L.kb_bytes = op->kslab;
   return tc_launch(L, g, e, st);
+}
+
+int nnrcu_qlinearconv_input_padding(const nnrcu_op* op, int* pads) {
+  if (!op || op->kind != OP_QCONV || !pads) return set_error(NNRCU_ERR_INVALID, "not a QLinearConv operator");
+  const bool padded = op->amode == A_SHIFT && op->d.in_layout == NNRCU_LAYOUT_NHWC;
+  pads[0] = padded ? op->d.pad_top : 0;
+  pads[1] = padded ? op->d.pad_left : 0;
+  pads[2] = padded ? op->d.pad_bottom : 0;
+  pads[3] = padded ? op->d.pad_right : 0;
+  return NNRCU_OK;
+}
+
+int nnrcu_qlinearconv_set_padded_io(nnrcu_op* op, int in_padded, int out_top, int out_left, int out_bottom,
+                                    int out_right) {
+  if (!op || op->kind != OP_QCONV) return set_error(NNRCU_ERR_INVALID, "not a QLinearConv operator");
+  if (in_padded && !(op->amode == A_SHIFT && op->d.in_layout == NNRCU_LAYOUT_NHWC))
+    return set_error(NNRCU_ERR_INVALID, "this QLinearConv does not read a padded input copy");
+  if (out_top < 0 || out_left < 0 || out_bottom < 0 || out_right < 0)
+    return set_error(NNRCU_ERR_INVALID, "negative output padding");
+  if ((out_top | out_left | out_bottom | out_right) &&
+      (op->d.out_layout != NNRCU_LAYOUT_NHWC || op->s2d || op->d.oc % 16 != 0))
+    return set_error(NNRCU_ERR_UNSUPPORTED, "a padded output needs an NHWC output with a multiple of 16 channels");
+  op->in_padded = in_padded != 0;
+  op->out_pad[0] = out_top; op->out_pad[1] = out_left; op->out_pad[2] = out_bottom; op->out_pad[3] = out_right;
+  return NNRCU_OK;
 }
 
 int nnrcu_qlinearconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream) {

@@ -147,6 +147,10 @@ struct EpiParams {
   void* y;
   int y_layout;            // 0: row-major [M, ldy]; 1: NCHW with M = img*ohw + p
   int ldy, ohw;
+  // opad: u8 row-major output written into the interior of a spatially padded
+  // NHWC buffer: output pixel m = (img, oy, ox) of an o_h x o_w image goes to
+  // row img * o_hwp + oy * o_wp + ox + o_off (o_off = top * o_wp + left)
+  int opad, o_w, o_hw, o_wp, o_hwp, o_off;
   int* status;             // device status word (first error wins)
 };
 
@@ -725,6 +729,7 @@ if constexpr (AMODE == A_ROWS) {
     const uint32_t kp_yzp = (uint32_t)e.yzp;
     const bool kp_ovf = e.qa_ovf != 0;
     const bool shift_direct = e.y_layout == 0 && (e.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0;
+    const bool direct = AMODE == A_SHIFT || e.opad != 0;  // lean path stores rows straight to HBM
     // EPI_R2A: TMA load of this warp's 32 x HB residual block of tile t into buffer buf
     auto issue_res = [&](const int t, const int buf) {
       constexpr int SEG = Cfg::OUT_SEG;
@@ -812,6 +817,11 @@ if constexpr (AMODE == A_ROWS) {
       if (EPI == EPI_R4 && e.rowcorr && mvalid) rowc = e.rowcorr[m];
       int img = 0, pix = 0;
       if (e.y_layout == 1 && mvalid) { img = m / e.ohw; pix = m - img * e.ohw; }
+      int mst = m;  // row of the output buffer
+      if (e.opad) {
+        const int im = m / e.o_hw, r = m - im * e.o_hw, oy = r / e.o_w;
+        mst = im * e.o_hwp + oy * e.o_wp + (r - oy * e.o_w) + e.o_off;
+      }
       const uint32_t t_addr = tmem_base + ((uint32_t)(eq * 32) << 16) + (uint32_t)(acc * BN);
       // one CW-column chunk: requant / bias / post-op / stores
       auto chunk = [&](const int c0, uint32_t (&v)[CW]) {
@@ -1001,7 +1011,7 @@ if constexpr (AMODE == A_ROWS) {
             for (int k = 0; k < CW / 16; ++k)
               ptx::st_shared_v4(seg + (((cc + k) ^ swz) << 4), w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
           } else if (e.y_layout == 0) {
-            uint8_t* dst = y + (size_t)m * e.ldy + n0 + c0;
+            uint8_t* dst = y + (size_t)mst * e.ldy + n0 + c0;
             if (nvalid == CW && (e.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0) {
 #pragma unroll
               for (int k = 0; k < CW / 16; ++k)
@@ -1023,11 +1033,13 @@ if constexpr (AMODE == A_ROWS) {
       // (A_SHIFT: the lean path stores each row's bytes straight to HBM; rows
       // that are not output pixels are skipped)
       bool fast = false;
-      if constexpr (EPI != EPI_F32 && AMODE == A_SHIFT)
-        fast = shift_direct && n0 + BN <= e.N && e.qres == nullptr;
-      else if constexpr (EPI != EPI_F32)
-        fast = y_tma && (AMODE == A_ROWS || m0 + BM <= e.M) && n0 + BN <= e.N &&
+      if constexpr (EPI != EPI_F32) {
+        if (direct)
+          fast = shift_direct && n0 + BN <= e.N && e.qres == nullptr;
+        else
+          fast = y_tma && (AMODE == A_ROWS || m0 + BM <= e.M) && n0 + BN <= e.N &&
                (EPI == EPI_R2A ? (long long)(m0 + BM) * e.N <= e.qa_vec_end : e.qres == nullptr);
+      }
       auto chunk_fast = [&](const int c0, uint32_t (&v)[CW]) {
         if constexpr (EPI != EPI_F32) {
           // Column pairs use the packed fp32 instructions (__fmul2_rn,
@@ -1133,9 +1145,9 @@ if constexpr (AMODE == A_ROWS) {
               q[j + 3] = requant_u8<EPI>((int32_t)v[j + 3], ci4.w, rowc, a4.w, b4.w, e);
             }
           }
-          if constexpr (AMODE == A_SHIFT) {
+          if (direct) {
             if (mvalid) {
-              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(e.y) + (size_t)m * e.ldy + n0 + c0);
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(e.y) + (size_t)mst * e.ldy + n0 + c0);
 #pragma unroll
               for (int k = 0; k < CW / 16; ++k)
                 dst[k] = make_uint4(pack_low_bytes(q[16 * k], q[16 * k + 1], q[16 * k + 2], q[16 * k + 3]),

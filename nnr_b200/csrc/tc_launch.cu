@@ -30,7 +30,7 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
   // warp's staged 32 x BN block (coalesced rows instead of per-lane pieces).
   CUtensorMap tmY{};
   int y_tma = 0;
-  if (AMODE == A_ROWS && EPI != EPI_F32 && e.y_layout == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
+  if (AMODE == A_ROWS && EPI != EPI_F32 && e.y_layout == 0 && !e.opad && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
       (e.ldy & 15) == 0) {
     // [output rows][OW][N]: a warp's 32 pixels of one output row, clipped at OW
     const int seg = Cfg::OUT_SEG;
@@ -42,7 +42,7 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
                                        : (seg == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B));
     if (rc != NNRCU_OK) return rc;
     y_tma = 1;
-  } else if (AMODE != A_ROWS && AMODE != A_SHIFT && EPI != EPI_F32 && e.y_layout == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
+  } else if (AMODE != A_ROWS && AMODE != A_SHIFT && EPI != EPI_F32 && e.y_layout == 0 && !e.opad && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
              (e.ldy & 15) == 0) {
     const int seg = Cfg::OUT_SEG;
     int rc = encode_tmap_2d(&tmY, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.y, (uint64_t)e.N, (uint64_t)e.M, (uint64_t)e.ldy,

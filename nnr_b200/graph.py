@@ -108,6 +108,7 @@ class DeviceNetwork:
             if nd.op == "DequantizeLinear" and nd.attrs.get("bias") is not None:
                 self.bias[i] = torch.from_numpy(np.ascontiguousarray(nd.attrs["bias"], np.float32)).to(self.dev)
         self._schedule(fuse_add)
+        self._link_padded()
         self._plan(reuse)
         self.stream = torch.cuda.Stream(device=self.dev)
         self.graph_exec = None
@@ -161,6 +162,36 @@ class DeviceNetwork:
                 self.steps.append((nd.op, j, list(nd.inputs), nd.output, j))
         self.fused_away = {nodes[i].output for i in fused_conv} | {nodes[j].output for j in fused_q.values()}
 
+    def _link_padded(self):
+        """A conv that reads an x_zp-bordered copy of its input (reported by
+        input_padding) gets that layout straight from its producer conv when
+        it is the tensor's only consumer: the producer writes the interior of
+        a dedicated padded buffer whose border is filled once here with the
+        tensor's zero point, and the consumer skips its copy."""
+        t = self.torch
+        nodes, qp = self.model.nodes, self.model.qparams
+        consumers: Dict[str, int] = {}
+        for nd in nodes:
+            for x in nd.inputs:
+                consumers[x] = consumers.get(x, 0) + 1
+        plain_conv = {out: i for kind, _, _, out, i in self.steps if kind == "QLinearConv"}
+        self.padded = {}  # tensor name -> (pads, padded device buffer)
+        for kind, _, ins, _, j in self.steps:
+            if kind != "QLinearConv" or self.ops[j] is None:
+                continue
+            x = ins[0]
+            pads = self.ops[j].input_padding()
+            i = plain_conv.get(x)
+            if not any(pads) or i is None or consumers.get(x, 0) != 1:
+                continue
+            n, h, w, c = self.model.shapes[x]
+            buf = t.full((n, h + pads[0] + pads[2], w + pads[1] + pads[3], c), qp[x].zp, dtype=t.uint8,
+                         device=self.dev)
+            self.ops[i].set_padded_io(out_pads=pads)
+            self.ops[j].set_padded_io(in_padded=True)
+            self.ws[j] = 0
+            self.padded[x] = (pads, buf)
+
     # ------------------------------------------------------------------ memory
     def _nbytes(self, name: str) -> int:
         elem = 4 if name in ("input", "logits") else 1
@@ -175,7 +206,8 @@ class DeviceNetwork:
             for x in ins:
                 last[x] = t
         last["logits"] = len(steps)  # graph output lives to the end
-        items = [Interval(name, self._nbytes(name), first[name], last.get(name, first[name])) for name in first]
+        items = [Interval(name, self._nbytes(name), first[name], last.get(name, first[name])) for name in first
+                 if name not in self.padded]
         for t, (_, _, _, _, ci) in enumerate(steps):
             if self.ws[ci]:
                 items.append(Interval(f"ws{ci}", self.ws[ci], t, t))
@@ -187,12 +219,17 @@ class DeviceNetwork:
         self.arena = self.torch.empty(max(self.arena_bytes, ALIGN), dtype=self.torch.uint8, device=self.dev)
         base = self.arena.data_ptr()
         self.ptr = {k: base + v for k, v in self.offsets.items()}
+        for name, (_, buf) in self.padded.items():
+            self.ptr[name] = buf.data_ptr()
 
     def view(self, name: str):
         """A torch view of a tensor's arena slot (for inputs and inspection)."""
         t = self.torch
         shape = self.model.shapes[name]
         dtype = t.float32 if name in ("input", "logits") else t.uint8
+        if name in self.padded:
+            (pt, pl, _, _), buf = self.padded[name]
+            return buf[:, pt:pt + shape[1], pl:pl + shape[2], :]
         off = self.offsets[name]
         return self.arena[off:off + self._nbytes(name)].view(dtype).view(shape)
 

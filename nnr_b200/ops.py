@@ -189,6 +189,18 @@ class QLinearConv(Operator):
         call("nnrcu_qlinearconv_run", self._op, _ptr(x), _ptr(y), ws_p, C.c_void_p(_stream(stream)))
         return y
 
+    def input_padding(self):
+        """(top, left, bottom, right) border of the x_zp-padded input copy this
+        op makes in its workspace, or zeros (nnrcu_qlinearconv_input_padding)."""
+        pads = (C.c_int * 4)()
+        call("nnrcu_qlinearconv_input_padding", self._op, pads)
+        return tuple(int(v) for v in pads)
+
+    def set_padded_io(self, in_padded: bool = False, out_pads=(0, 0, 0, 0)) -> None:
+        """Read an already padded input / write into a padded output buffer
+        (nnrcu_qlinearconv_set_padded_io)."""
+        call("nnrcu_qlinearconv_set_padded_io", self._op, 1 if in_padded else 0, *[int(v) for v in out_pads])
+
     def exec_quantize(self, x: torch.Tensor, x_scale: float, x_zp: int, y: Optional[torch.Tensor] = None,
                       workspace=None, stream=None) -> torch.Tensor:
         """QuantizeLinear(x fp32, x_scale, x_zp) followed by this QLinearConv in

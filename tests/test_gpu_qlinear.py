@@ -385,3 +385,40 @@ def test_shifted_patch_fused_relu_and_add(cuda_dev, relu):
     torch.cuda.synchronize()
     assert ops.device_status() == 0
     assert np.array_equal(y.cpu().numpy(), ref)
+
+
+def test_padded_output_feeds_padded_input(cuda_dev):
+    """1x1 conv writing into the interior of an x_zp-bordered buffer, read as is
+    by a shifted-patch 3x3 conv (nnrcu_qlinearconv_set_padded_io): both outputs
+    equal the unpadded chain's, and the border keeps its fill."""
+    from nnr_b200 import ops
+    rng = np.random.default_rng(21)
+    n, c, h, w = 2, 64, 20, 17
+    c1 = W.random_qconv(rng, n, c, h, w, 64, 1, 1, (1, 1), (0, 0, 0, 0), x_zp=0)
+    c1.y_zp = 57
+    y1 = oracle_qconv(c1, O.R2, out_layout="NHWC")
+    c2 = W.random_qconv(rng, n, 64, h, w, 128, 3, 3, (1, 1), (1, 1, 1, 1))
+    c2.x = np.ascontiguousarray(y1.transpose(0, 3, 1, 2))
+    c2.x_scale, c2.x_zp = c1.y_scale, c1.y_zp
+    y2 = oracle_qconv(c2, O.R2, out_layout="NHWC")
+
+    def mk(cs):
+        return ops.QLinearConv(cs.x.shape, cs.w, cs.w_scale, cs.w_zp, cs.bias, cs.x_scale, cs.x_zp, cs.y_scale,
+                               cs.y_zp, pads=cs.pads, in_layout="NHWC", out_layout="NHWC", requant=O.R2)
+    op1, op2 = mk(c1), mk(c2)
+    pads = op2.input_padding()
+    assert pads == (1, 1, 1, 1)
+    assert mk(c1).input_padding() == (0, 0, 0, 0)
+    op1.set_padded_io(out_pads=pads)
+    op2.set_padded_io(in_padded=True)
+    buf = torch.full((n, h + 2, w + 2, 64), c1.y_zp, dtype=torch.uint8, device=cuda_dev)
+    op1.exec(torch.from_numpy(_to_nhwc(c1.x)).to(cuda_dev), y=buf)
+    out = op2.exec(buf)
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    b = buf.cpu().numpy()
+    assert np.array_equal(b[:, 1:h + 1, 1:w + 1, :], y1)
+    border = np.ones(b.shape[:3], bool)
+    border[:, 1:h + 1, 1:w + 1] = False
+    assert (b[border] == c1.y_zp).all()
+    assert np.array_equal(out.cpu().numpy(), y2)
