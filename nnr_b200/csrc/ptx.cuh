@@ -83,6 +83,16 @@ __device__ __forceinline__ int cvt_rne_x86(float f) {
   return fabsf(f) < 2147483648.0f ? __float2int_rn(f) : (int)0x80000000;
 }
 
+// rne(f) clamped to [0, 255] in one conversion (the conversion unit, not the
+// ALU/FMA pipes): equals clamp-then-round for any finite f, since the clamp
+// bounds are integers. (Not the x86 semantics for f >= 2^31: callers that can
+// reach that keep the explicit sequence.)
+__device__ __forceinline__ uint32_t cvt_rni_sat_u8(float f) {
+  uint32_t r;
+  asm("cvt.rni.sat.u8.f32 %0, %1;" : "=r"(r) : "f"(f));
+  return r;
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -1091,6 +1091,11 @@ if constexpr (AMODE == A_ROWS) {
                                                            __uint_as_float(__byte_perm(w, 0x4B000000u, 0x7650 | ((j + 1) & 3)))),
                                                nbm);
                   float2 r = __ffma2_rn(fa, sa, __ffma2_rn(fb, sb, fx));
+                  if constexpr (!decltype(ovf)::value) {
+                    q[j] = ptx::cvt_rni_sat_u8(r.x);
+                    q[j + 1] = ptx::cvt_rni_sat_u8(r.y);
+                    continue;
+                  }
                   if constexpr (decltype(ovf)::value) {
                     // x86 conversion: values >= 2^31 become INT_MIN, i.e. 0 after the max
                     r.x = r.x >= 2147483648.0f ? 0.0f : r.x;
