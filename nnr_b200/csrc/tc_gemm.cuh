@@ -1174,7 +1174,19 @@ if constexpr (AMODE == A_ROWS) {
       };
       uint32_t va[CW], vb[CW];
       int tev = 0;
-      if (fast) {
+      bool released = false;
+      if (fast && HB == CW) {
+        // one chunk per warp: the accumulator goes back to the MMA warp as
+        // soon as it is in registers, so the next tiles' MMAs overlap this
+        // requantisation
+        ptx::tmem_ld_async(t_addr + (uint32_t)col0, va);
+        ptx::tmem_wait_ld(va);
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+        released = true;
+        chunk_fast(col0, va);
+      } else if (fast) {
         // many epilogue warps per SM hide the TMEM load latency: one buffer
 #pragma unroll 1
         for (int c0 = col0; c0 < col0 + HB; c0 += CW) {
@@ -1215,9 +1227,11 @@ if constexpr (AMODE == A_ROWS) {
       }
       if (lane == 0) NNRCU_TRACE_AT(warp, lt, 3);
       // hand the accumulator back to the MMA warp
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+      if (!released) {
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
+      }
       if (Cfg::OUT_BLOCK > 0 && y_tma) {
         // publish the staged block: rows >= M and columns >= N are clipped by the map
         ptx::fence_proxy_async_smem();
