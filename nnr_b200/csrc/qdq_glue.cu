@@ -86,6 +86,9 @@ __global__ void maxpool_u8_nhwc_kernel(const uint8_t* __restrict x, uint8_t* __r
 // identical): the block first takes the column max over the window's input
 // rows for every input column into shared memory (each input row read once
 // per output row, coalesced), then the row max over kw columns from there.
+// KMAX > 0: windows of at most KMAX x KMAX; the window's loads of a column
+// are unrolled so that they are all in flight together.
+template <int KMAX>
 __global__ void maxpool_u8_nhwc_sep_kernel(const uint8_t* __restrict x, uint8_t* __restrict y, int h, int w, int c,
                                            int oh, int ow, int kh, int kw, int sh, int sw, int pt, int pl) {
   extern __shared__ uint4 colmax[];
@@ -96,15 +99,29 @@ __global__ void maxpool_u8_nhwc_sep_kernel(const uint8_t* __restrict x, uint8_t*
   const int ya = max(y0, 0), yb = min(y0 + kh, h);
   const uint4* xin = reinterpret_cast<const uint4*>(x + (size_t)img * h * w * c) + (size_t)ya * w * cv;
   const int rowv = w * cv;
+  const int nr = yb - ya;
   for (int i = threadIdx.x; i < rowv; i += blockDim.x) {
     uint4 m = make_uint4(0, 0, 0, 0);
     const uint4* p = xin + i;
-    for (int iy = ya; iy < yb; ++iy, p += rowv) {
-      const uint4 t = __ldg(p);
-      m.x = __vmaxu4(m.x, t.x);
-      m.y = __vmaxu4(m.y, t.y);
-      m.z = __vmaxu4(m.z, t.z);
-      m.w = __vmaxu4(m.w, t.w);
+    if constexpr (KMAX > 0) {
+      uint4 t[KMAX];
+#pragma unroll
+      for (int r = 0; r < KMAX; ++r) t[r] = r < nr ? __ldg(p + (size_t)r * rowv) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int r = 0; r < KMAX; ++r) {
+        m.x = __vmaxu4(m.x, t[r].x);
+        m.y = __vmaxu4(m.y, t[r].y);
+        m.z = __vmaxu4(m.z, t[r].z);
+        m.w = __vmaxu4(m.w, t[r].w);
+      }
+    } else {
+      for (int iy = ya; iy < yb; ++iy, p += rowv) {
+        const uint4 t = __ldg(p);
+        m.x = __vmaxu4(m.x, t.x);
+        m.y = __vmaxu4(m.y, t.y);
+        m.z = __vmaxu4(m.z, t.z);
+        m.w = __vmaxu4(m.w, t.w);
+      }
     }
     colmax[i] = m;
   }
@@ -283,10 +300,12 @@ int nnrcu_maxpool_u8_nhwc(const uint8_t* x, uint8_t* y, int n, int h, int w, int
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (c % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
     const size_t row_bytes = (size_t)w * c;
-    if (row_bytes <= 48 * 1024)
-      maxpool_u8_nhwc_sep_kernel<<<n * oh, 256, row_bytes, st>>>(x, y, h, w, c, oh, ow, kh, kw, sh, sw, pt, pl);
-    else
+    if (row_bytes <= 48 * 1024) {
+      auto kern = kh <= 3 ? maxpool_u8_nhwc_sep_kernel<3> : maxpool_u8_nhwc_sep_kernel<0>;
+      kern<<<n * oh, 256, row_bytes, st>>>(x, y, h, w, c, oh, ow, kh, kw, sh, sw, pt, pl);
+    } else {
       maxpool_u8_nhwc_kernel<<<n * oh, 256, 0, st>>>(x, y, h, w, c, oh, ow, kh, kw, sh, sw, pt, pl);
+    }
   } else {
     const long long total = (long long)n * oh * ow * c;
     maxpool_u8_nhwc_scalar_kernel<<<blocks_for(total, 256), 256, 0, st>>>(x, y, n, h, w, c, oh, ow, kh, kw, sh, sw,
