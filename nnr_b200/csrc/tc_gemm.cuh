@@ -175,7 +175,13 @@ struct TileCfg {
   static constexpr int OUT_BLOCK =
       PATCH ? 0 : ((EPI == EPI_F32 && (BUDGET - OUT_BLOCK_RAW - BRES_BYTES) / STAGE_BYTES < 3) ? 0 : OUT_BLOCK_RAW);
   // EPI_R2A: two residual blocks per epilogue warp (tile i in use, tile i+1 landing)
-  static constexpr int RES_BYTES = (EPI == EPI_R2A) ? 2 * OUT_BLOCK : 0;
+  // The residual block of EPI_R2A: TMA-prefetched one tile ahead into
+  // shared memory, or (64-byte K slabs, i.e. the K = 64 layers whose
+  // epilogue is the bottleneck) read by each lane with plain loads issued
+  // before its requantisation: there the TMA issue of the prefetch stalled
+  // the epilogue warps for ~500 cycles per tile behind the producers' copies.
+  static constexpr bool RES_TMA = KB != 64;
+  static constexpr int RES_BYTES = (EPI == EPI_R2A && RES_TMA) ? 2 * OUT_BLOCK : 0;
   // Output staging is double-buffered (the store of tile i drains while tile
   // i+1 is requantised) when that still leaves three pipeline stages.
   static constexpr int OUT_BUFS = (BUDGET - 2 * OUT_BLOCK - RES_BYTES - BRES_BYTES) / STAGE_BYTES >= 3 ? 2 : 1;
@@ -384,6 +390,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
       ptx::tma_prefetch_desc(&tmA0);
       if (NPLANE == 2) ptx::tma_prefetch_desc(&tmA1);
     }
+    if (y_tma) ptx::tma_prefetch_desc(&tmY);
+    if (EPI == EPI_R2A) ptx::tma_prefetch_desc(&tmR);
   }
   if (warp == R::MMA_WARP) ptx::tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
   ptx::tc_fence_before();
@@ -739,7 +747,7 @@ if constexpr (AMODE == A_ROWS) {
       ptx::mbar_arrive_expect_tx(bar, 32 * HB);
       for (int h = 0; h < HB / SEG; ++h) ptx::tma_load_2d(dst + h * (32 * SEG), &tmR, bar, rn0 + col0 + h * SEG, rm0 + eq * 32);
     };
-    if (EPI == EPI_R2A && lane == 0 && (int)blockIdx.x < num_tiles) issue_res(blockIdx.x, 0);
+    if (EPI == EPI_R2A && Cfg::RES_TMA && lane == 0 && (int)blockIdx.x < num_tiles) issue_res(blockIdx.x, 0);
     bool res_failed = false;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
       int m0 = 0, nvr = 0, orow = 0, ow0 = 0;
@@ -781,7 +789,8 @@ if constexpr (AMODE == A_ROWS) {
       if (Cfg::OUT_BLOCK > 0 && y_tma) {
         if (lane == 0) {
           ptx::bulk_wait_read<Cfg::OUT_BUFS - 1>();  // the store that last used this buffer has read it
-          if constexpr (EPI == EPI_R2A) {
+          NNRCU_TRACE2_AT(warp, lt, 12);
+          if constexpr (EPI == EPI_R2A && Cfg::RES_TMA) {
             // prefetch the residual block of this warp's next tile into the
             // other buffer (its previous contents were consumed by tile lt - 1)
             const int nxt = tile + gridDim.x;
@@ -790,6 +799,7 @@ if constexpr (AMODE == A_ROWS) {
         }
         __syncwarp();
       }
+      if (lane == 0) NNRCU_TRACE2_AT(warp, lt, 13);
       if (!__all_sync(0xffffffffu, ptx::mbar_wait(&tfull_bar[acc], use_ph, abort_flag))) {
         fail(ST_TIMEOUT_ACCUM);
         res_failed = true;
@@ -798,7 +808,7 @@ if constexpr (AMODE == A_ROWS) {
       ptx::tc_fence_after();
       if (lane == 0) NNRCU_TRACE_AT(warp, lt, 1);
       const uint8_t* rstg = sRes + (lt & 1) * Cfg::OUT_BLOCK + warp * (32 * HB);
-      if (EPI == EPI_R2A &&
+      if (EPI == EPI_R2A && Cfg::RES_TMA &&
           !__all_sync(0xffffffffu, ptx::mbar_wait(&res_bar[(lt & 1) * 16 + warp], (uint32_t)(lt >> 1) & 1u, abort_flag))) {
         fail(ST_TIMEOUT_ACCUM);
         res_failed = true;
@@ -910,7 +920,7 @@ if constexpr (AMODE == A_ROWS) {
           // residual words (4 bytes each) of this row's CW columns
           uint32_t rw[CW / 4];
           if (fused) {
-            if constexpr (EPI == EPI_R2A) {
+            if constexpr (EPI == EPI_R2A && Cfg::RES_TMA) {
               const int h = pc / SEG, cc = (pc % SEG) >> 4;
               const uint8_t* seg = rstg + h * (32 * SEG) + lane * SEG;
 #pragma unroll
@@ -1048,6 +1058,14 @@ if constexpr (AMODE == A_ROWS) {
           const float2 k_magic = make_float2(RND_MAGIC, RND_MAGIC);
           const int pc = c0 - col0;
           uint32_t q[CW];
+          // R2A: this row's residual bytes, loaded first so that their
+          // latency overlaps the requantisation below
+          uint4 rq[CW / 16];
+          if constexpr (EPI == EPI_R2A && !Cfg::RES_TMA) {
+            const uint4* rp = reinterpret_cast<const uint4*>(e.qres + (size_t)m * e.ldy + n0 + c0);
+#pragma unroll
+            for (int k = 0; k < CW / 16; ++k) rq[k] = __ldg(rp + k);
+          }
           if constexpr (EPI == EPI_R2 || EPI == EPI_R2A) {
             float2 t[CW / 2];  // RND_MAGIC + rne(f), f = clamp(float(acc + bias) * os)
 #pragma unroll
@@ -1071,13 +1089,16 @@ if constexpr (AMODE == A_ROWS) {
               // QLinearAdd body (QLinearAdd.cpp:46-104): fma(a, sa, fma(b, sb, fixed)),
               // rne, saturate; a = rne(f) + y_zp = t - (RND_MAGIC - y_zp) exactly,
               // b = (2^23 + byte) - 2^23 exactly
-              const int h = pc / SEG, cc = (pc % SEG) >> 4;
-              const uint8_t* seg = rstg + h * (32 * SEG) + lane * SEG;
               uint32_t rw[CW / 4];
+              if constexpr (Cfg::RES_TMA) {
+                const int h = pc / SEG, cc = (pc % SEG) >> 4;
+                const uint8_t* seg = rstg + h * (32 * SEG) + lane * SEG;
+#pragma unroll
+                for (int k = 0; k < CW / 16; ++k) rq[k] = *reinterpret_cast<const uint4*>(seg + (((cc + k) ^ swz) << 4));
+              }
 #pragma unroll
               for (int k = 0; k < CW / 16; ++k) {
-                const uint4 r0 = *reinterpret_cast<const uint4*>(seg + (((cc + k) ^ swz) << 4));
-                rw[4 * k] = r0.x; rw[4 * k + 1] = r0.y; rw[4 * k + 2] = r0.z; rw[4 * k + 3] = r0.w;
+                rw[4 * k] = rq[k].x; rw[4 * k + 1] = rq[k].y; rw[4 * k + 2] = rq[k].z; rw[4 * k + 3] = rq[k].w;
               }
               const float2 sa = make_float2(kp_sa, kp_sa), sb = make_float2(kp_sb, kp_sb);
               const float2 fx = make_float2(kp_fx, kp_fx), ca = make_float2(kp_ca, kp_ca);
@@ -1236,6 +1257,7 @@ if constexpr (AMODE == A_ROWS) {
         // publish the staged block: rows >= M and columns >= N are clipped by the map
         ptx::fence_proxy_async_smem();
         __syncwarp();
+        if (lane == 0) NNRCU_TRACE2_AT(warp, lt, 14);
         if (lane == 0) {
           constexpr int SEG = Cfg::OUT_SEG;
           constexpr int SEGE = SEG / Cfg::ESZ;  // elements per segment
@@ -1249,6 +1271,7 @@ if constexpr (AMODE == A_ROWS) {
                   ptx::tma_store_2d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEGE, m0 + eq * 32);
               }
           ptx::bulk_commit();
+          NNRCU_TRACE2_AT(warp, lt, 15);
         }
       }
     }
