@@ -323,6 +323,41 @@ class DeviceNetwork:
             out_host.copy_(self.view("logits"), non_blocking=True)
         return out_host
 
+    def forward_many(self, x_hosts, out_hosts, between=None):
+        """Pipelined forwards over a sequence of host batches: batch i+1's
+        host-to-device copy runs on a second stream (into one of two device
+        staging buffers) while batch i is computed; each forward then copies
+        its staged input into the network's input slot, runs, and copies its
+        logits to out_hosts[i]. `between` (optional) is enqueued on the
+        network's stream before each forward. Returns after enqueueing; the
+        caller synchronises self.stream."""
+        t = self.torch
+        if not hasattr(self, "_stage"):
+            xin = self.view("input")
+            self._stage = [t.empty_like(xin), t.empty_like(xin)]
+            self._copy_stream = t.cuda.Stream(device=self.dev)
+            self._staged = [t.cuda.Event(), t.cuda.Event()]
+            self._consumed = [t.cuda.Event(), t.cuda.Event()]
+        xin, logits = self.view("input"), self.view("logits")
+        cs = self._copy_stream
+        cs.wait_stream(self.stream)  # (work already enqueued on the network's stream comes first)
+        for i, (xh, oh) in enumerate(zip(x_hosts, out_hosts)):
+            k = i & 1
+            with t.cuda.stream(cs):
+                if i >= 2:
+                    cs.wait_event(self._consumed[k])   # forward i - 2 has read this buffer
+                self._stage[k].copy_(xh, non_blocking=True)
+                self._staged[k].record(cs)
+            with t.cuda.stream(self.stream):
+                self.stream.wait_event(self._staged[k])
+                xin.copy_(self._stage[k], non_blocking=True)
+                self._consumed[k].record(self.stream)
+                if between is not None:
+                    between()
+                self.launch()
+                oh.copy_(logits, non_blocking=True)
+        return out_hosts
+
     def close(self):
         from ._lib import lib
         if self.graph_exec is not None:

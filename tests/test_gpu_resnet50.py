@@ -62,3 +62,22 @@ def test_resnet50_graph_replay_and_host_path(cuda_dev, model4):
         net.stream.synchronize()
         assert np.array_equal(out.numpy(), ref)
     net.close()
+
+
+def test_resnet50_pipelined_forwards(cuda_dev, model4):
+    """DeviceNetwork.forward_many (input copies overlapped with the previous
+    forward) gives each batch the same logits as a lone forward."""
+    from nnr_b200 import graph, resnet50
+    net = graph.DeviceNetwork(model4, 0)
+    try:
+        net.capture()
+        xs = [torch.from_numpy(resnet50.input_batch(4 * i, 4)).pin_memory() for i in range(3)]
+        outs = [torch.empty(model4.shapes["logits"], dtype=torch.float32).pin_memory() for _ in range(3)]
+        net.forward_many(xs, outs)
+        net.stream.synchronize()
+        for x, o in zip(xs, outs):
+            ref = net.forward(x)
+            net.stream.synchronize()
+            assert torch.equal(o, ref)
+    finally:
+        net.close()
