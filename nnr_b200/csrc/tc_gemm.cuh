@@ -1144,6 +1144,7 @@ if constexpr (AMODE == A_ROWS) {
           } else if constexpr (EPI == EPI_R3) {
             // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); clamp; rne
             const float2 iy = make_float2(e.inv_y, e.inv_y), yz = make_float2(e.yzp_f, e.yzp_f);
+            const uint32_t qmin_u = (uint32_t)e.qmin_f;
 #pragma unroll
             for (int j = 0; j < CW; j += 2) {
               const int2 ci2 = *reinterpret_cast<const int2*>(s_ci + pc + j);
@@ -1153,11 +1154,10 @@ if constexpr (AMODE == A_ROWS) {
                                                 __int2float_rn((int32_t)(v[j + 1] + (uint32_t)ci2.y))),
                                     a2, b2);
               f = __ffma2_rn(f, iy, yz);
-              f.x = fmaxf(fminf(f.x, e.qmax_f), e.qmin_f);
-              f.y = fmaxf(fminf(f.y, e.qmax_f), e.qmin_f);
-              f = __fadd2_rn(f, k_magic);
-              q[j] = __float_as_uint(f.x);
-              q[j + 1] = __float_as_uint(f.y);
+              // the upper bound is 255: rne + clamp to [0, 255] in one
+              // conversion, then the lower bound (y_zp under a fused Relu)
+              q[j] = max(ptx::cvt_rni_sat_u8(f.x), qmin_u);
+              q[j + 1] = max(ptx::cvt_rni_sat_u8(f.y), qmin_u);
             }
           } else {
 #pragma unroll
