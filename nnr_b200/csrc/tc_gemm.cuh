@@ -86,10 +86,15 @@ constexpr int BKB = 128;      // K bytes per stage per plane (one swizzle row); 
 //                   SPLIT epilogue warps per TMEM lane quarter, each draining
 //                   BN / SPLIT columns (16 warps for BN >= 128: the epilogue,
 //                   not the tensor core, bounds the small-K layers)
-template <int AMODE, int BN>
+template <int AMODE, int BN, int EPI = 0>
 struct Roles {
   static constexpr int SPLIT = AMODE == A_GATHER ? 1 : (BN >= 128 ? 4 : 2);
-  static constexpr int TMA_WARP = AMODE == A_GATHER ? 8 : 4 * SPLIT;
+  // 64-wide N tiles of u8 epilogues (other than the residual-prefetching
+  // EPI_R2A): two groups of 4 x SPLIT epilogue warps take alternate tiles,
+  // one per TMEM accumulator, so that two tiles' requantisation is in flight
+  static constexpr int EGROUPS =
+      (BN == 64 && AMODE != A_GATHER && EPI != 0 && EPI != EPI_R2A && EPI != EPI_F32) ? 2 : 1;
+  static constexpr int TMA_WARP = AMODE == A_GATHER ? 8 : 4 * SPLIT * EGROUPS;
   // TMA-fed modes issue their copies from three producer warps (stage it
   // goes to warp it % NPROD): one warp's copies complete at about one per
   // several hundred cycles, so more issuing warps raise the load rate (1.4x
@@ -196,7 +201,7 @@ struct TileCfg {
   // stages of copies in flight, STAGES - 1 - LAG stages of slack for the MMA.
   static constexpr int LAG = (STAGES - 1) / 2 > 1 ? (STAGES - 1) / 2 : 1;
   static constexpr int TMEM_COLS = 2 * BN;  // two accumulators (power of two)
-  static constexpr int PARAM_BYTES = 4 * SPLIT /*epilogue warps*/ * 3 * HB * 4;
+  static constexpr int PARAM_BYTES = (BN == 64 ? 2 : 1) * 4 * SPLIT /*epilogue warps*/ * 3 * HB * 4;
   static constexpr int BAR_BYTES = 1024;  // mbarriers, TMEM slot, abort flag
   static constexpr int SMEM_BYTES =
       1024 /*align slack*/ + STAGES * STAGE_BYTES + BRES_BYTES + OUT_BYTES + RES_BYTES + BAR_BYTES + PARAM_BYTES;
@@ -311,14 +316,15 @@ __device__ __forceinline__ float byte_to_float(uint32_t w, int j) {
 // double-buffered in TMEM (2 x BN columns), so the epilogue of tile i overlaps
 // the loads and MMAs of tile i + 1.
 template <int BN, int NPLANE, int AMODE, int EPI, int KB, int NKBR = 0>
-__global__ void __launch_bounds__(Roles<AMODE, BN>::THREADS, 1)
+__global__ void __launch_bounds__(Roles<AMODE, BN, EPI>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY,
                const __grid_constant__ CUtensorMap tmR, int y_tma,
                int b_plane_rows, GatherGeom g, EpiParams e, int num_kb, int m_tiles, int n_tiles) {
   // In TMA / im2col modes the gather warps 4-7 are free and join the epilogue:
   // warps w and w + 4 drain the same 32 TMEM lanes, each half of the columns.
-  using R = Roles<AMODE, BN>;
+  using R = Roles<AMODE, BN, EPI>;
+  constexpr int EG = R::EGROUPS;
   constexpr int SPLIT = R::SPLIT;
   constexpr int CW = R::CW;
   constexpr int HB = BN / SPLIT;
@@ -364,7 +370,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   if (threadIdx.x == 0) NNRCU_TRACE_AT(23, 15, 3);  // CTA start
   // per-column constants, one private copy per epilogue warp (no cross-warp sync)
   int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + Cfg::BAR_BYTES +
-                                             (warp & (4 * SPLIT - 1)) * (3 * HB * 4));
+                                             (warp % (4 * SPLIT * EG)) * (3 * HB * 4));
   float* s_f1 = reinterpret_cast<float*>(s_ci + HB);
   float* s_f2 = s_f1 + HB;
 
@@ -724,12 +730,15 @@ if constexpr (AMODE == A_ROWS) {
         for (int q = first; q < it; ++q) ptx::mbar_arrive(&full_bar[q % STAGES]);
       }
     }
-  } else if (warp < 4 * SPLIT) {
+  } else if (warp < 4 * SPLIT * EG) {
     // ------------------------------------------------------------ epilogue (warps 0-3, and 4-7 when SPLIT = 2)
-    const int eq = warp & 3;           // TMEM lane quarter
-    const int col0 = (warp >> 2) * HB; // this warp's columns [col0, col0 + HB) of the tile
+    static_assert(EG == 1 || Cfg::OUT_BLOCK == 0 || Cfg::OUT_BUFS == 2, "epilogue groups need a staging buffer each");
+    const int group = warp / (4 * SPLIT);  // EG = 2: tiles lt with lt % 2 == group
+    const int wig = warp % (4 * SPLIT);    // warp within its group
+    const int eq = wig & 3;            // TMEM lane quarter
+    const int col0 = (wig >> 2) * HB;  // this warp's columns [col0, col0 + HB) of the tile
     const int row = eq * 32 + lane;    // TMEM lane == tile row
-    int lt = 0;
+    int lt = group;
     int cached_n0 = -1;
     // epilogue scalars held in registers for the whole kernel
     const float kp_lo = e.rq_lo, kp_hi = e.rq_hi, kp_sa = e.qa_sa, kp_sb = e.qa_sb, kp_fx = e.qa_fixed;
@@ -749,7 +758,7 @@ if constexpr (AMODE == A_ROWS) {
     };
     if (EPI == EPI_R2A && Cfg::RES_TMA && lane == 0 && (int)blockIdx.x < num_tiles) issue_res(blockIdx.x, 0);
     bool res_failed = false;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
+    for (int tile = blockIdx.x + group * gridDim.x; tile < num_tiles; tile += EG * gridDim.x, lt += EG) {
       int m0 = 0, nvr = 0, orow = 0, ow0 = 0;
       tile_rows(tile / n_tiles, m0, nvr, orow, ow0);
       const int n0 = (tile % n_tiles) * BN;
@@ -781,14 +790,17 @@ if constexpr (AMODE == A_ROWS) {
       }
       // the staging block may be rewritten once the previous tile's stores have read it
       if (lane == 0) NNRCU_TRACE_AT(warp, lt, 0);
-      uint8_t* const stg = sOut + (Cfg::OUT_BUFS == 2 ? (lt & 1) * Cfg::OUT_BLOCK : 0) + warp * (32 * Cfg::ROW_BYTES);
+      // (EG = 2: each group has its own staging buffer)
+      uint8_t* const stg = sOut + (Cfg::OUT_BUFS == 2 ? (EG == 2 ? group : (lt & 1)) * Cfg::OUT_BLOCK : 0) +
+                           wig * (32 * Cfg::ROW_BYTES);
       constexpr int SEG = Cfg::OUT_SEG;
       // swizzle of a staged row (the store / residual maps' 128B, 64B or 32B
       // swizzle): row r, 16-byte chunk c of a segment lives at r*SEG + ((c ^ f(r)) << 4)
       const int swz = SEG == 128 ? (lane & 7) : (SEG == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
       if (Cfg::OUT_BLOCK > 0 && y_tma) {
         if (lane == 0) {
-          ptx::bulk_wait_read<Cfg::OUT_BUFS - 1>();  // the store that last used this buffer has read it
+          // the store that last used this buffer has read it
+          ptx::bulk_wait_read<EG == 2 ? 0 : Cfg::OUT_BUFS - 1>();
           NNRCU_TRACE2_AT(warp, lt, 12);
           if constexpr (EPI == EPI_R2A && Cfg::RES_TMA) {
             // prefetch the residual block of this warp's next tile into the

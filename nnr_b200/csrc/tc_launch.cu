@@ -79,7 +79,7 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
   // first dependent access)
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(Roles<AMODE, BN>::THREADS);
+  cfg.blockDim = dim3(Roles<AMODE, BN, EPI>::THREADS);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
