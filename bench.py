@@ -17,14 +17,20 @@ one captured CUDA graph.
   e2e       the same forward through the public API with host buffers:
             every step a pinned H2D of its fp32 input batch, the forward and
             a D2H of the fp32 logits, pipelined (DeviceNetwork.forward_many:
-            a step's H2D runs on a copy stream while the previous step
-            computes), L2 flushed before each forward, one CUDA-event window
-            over all steps; the serial form (copy, forward, copy per step)
-            is reported beside it as serial_value.
-  roofline  the tcgen05 conv/matmul kernels of the forward: each engine step
-            timed as 10 launches replayed from a CUDA graph (CUDA events on
-            the launching stream); algorithmic int8 ops / summed kernel time
-            vs the int8 tensor peak.
+            a step's H2D runs on a copy stream into one of two staging
+            buffers while the previous step computes; each forward is the
+            graph captured on its staging buffer), L2 flushed before each
+            forward, one CUDA-event window over all steps; the serial form
+            (copy, forward, copy per step) is reported beside it as
+            serial_value, and the measured H2D GB/s of the link beside both.
+  roofline  the tcgen05 conv/matmul kernels of the forward: every step is
+            timed alone (10 launches replayed from a CUDA graph, CUDA events
+            on the launching stream); the engine steps' share of those times
+            scaled to the timed forward gives their time inside it;
+            algorithmic int8 ops / that time vs the int8 tensor peak (the
+            larger of a live library int8 GEMM probe and 2x the measured
+            bf16 burst), plus the per-layer attainable roofline
+            (max of tensor and HBM floors per layer).
   qlinearconv_config2  BASELINE config 2 (one QLinearConv layer, NCHW in/out,
             requant R1): operator and kernel TOPS.
 
@@ -58,7 +64,7 @@ L2_FLUSH_BYTES = 256 << 20
 
 
 # DRAM bytes (read + write) of all tc_gemm_kernel launches of one batch-32
-# forward, from the ncu launch list in profiles/resnet50_b32_forward_launches.md
+# forward, summed over one ncu capture of the forward's launch list
 # (ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum).
 TC_TRAFFIC_BYTES = 468_700_000
 
@@ -150,10 +156,47 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------ CPU side
+def host_cpu_info():
+    """The host CPU as the reference arm sees it: model, logical and physical
+    cores, the AVX-512 / VNNI / AMX flags nnr's x64 dispatch keys on, and the
+    flags the C restatement was compiled with."""
+    model, flags, phys = None, set(), set()
+    cur = {}
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if ":" not in line:
+                if cur:
+                    phys.add((cur.get("physical id"), cur.get("core id")))
+                cur = {}
+                continue
+            k, v = (x.strip() for x in line.split(":", 1))
+            cur[k] = v
+            if k == "model name" and model is None:
+                model = v
+            if k == "flags" and not flags:
+                flags = set(v.split())
+        if cur:
+            phys.add((cur.get("physical id"), cur.get("core id")))
+    except OSError:
+        pass
+    want = ["avx2", "fma", "avx512f", "avx512bw", "avx512vl", "avx512_vnni", "avx512_bf16", "avx512_fp16",
+            "amx_int8", "amx_bf16"]
+    return {"model": model, "logical_cores": os.cpu_count(), "usable_cores": len(os.sched_getaffinity(0)),
+            "physical_cores": len(phys) or None, "isa_flags": [f for f in want if f in flags],
+            "compiler": "gcc -O3 -march=x86-64-v3 -ffp-contract=off -fopenmp (oracle/Makefile)"}
+
+
+def cpu_threads() -> int:
+    """All host threads this process may use, set explicitly: torchrun exports
+    OMP_NUM_THREADS=1 to its workers, which must not decide the baseline."""
+    return len(os.sched_getaffinity(0))
+
+
 def cpu_forward_fn(model, images):
     """One oracle forward of `images` images on the host cores (OpenMP)."""
     from nnr_b200 import resnet50
     from oracle import oracle as O
+    O.set_threads(cpu_threads())
     x = resnet50.input_batch(0, images)
     return (lambda: O.run_qmodel(model, x)), O.num_threads()
 
@@ -168,7 +211,8 @@ def cpu_baseline(model, seconds=10.0):
     dt = (time.perf_counter() - t0) / n
     return {"value": round(1.0 / dt, 3), "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"1 image per forward x {n} forwards ({dt * 1000:.0f} ms each): the C restatement of nnr's "
-                      "int8 operators (nnr's own int8 kernels need the absent Xbyak JIT)"}
+                      "int8 operators (nnr's own int8 kernels need the absent Xbyak JIT)",
+            "cpu": host_cpu_info()}
 
 
 def reference_arm(args, rank, world):
@@ -191,7 +235,8 @@ def reference_arm(args, rank, world):
             "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded numpy PCG64)",
             "config": {"workload": WORKLOAD, "sample": "1 image of the batch per step"},
             "cpu_baseline": {"value": round(val, 3), "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": "1 image per step, C restatement of nnr's int8 operators on the host cores"},
+                             "sample": "1 image per step, C restatement of nnr's int8 operators on the host cores",
+                             "cpu": host_cpu_info()},
             "e2e": {"value": round(val, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
@@ -207,6 +252,44 @@ def node_ops(model, i):
         return 2 * n * oh * ow * oc * w.shape[1] * w.shape[2] * w.shape[3]
     b = nd.attrs["b"]
     return 2 * model.shapes[nd.output][0] * b.shape[0] * b.shape[1]
+
+
+def node_bytes(model, net, t):
+    """Compulsory HBM bytes of engine step t: u8 input (or the fp32 image the
+    stem quantises), s8 weights, u8 output, plus the u8 residual of a fused
+    QLinearAdd."""
+    kind, j, ins, out, i = net.steps[t]
+    nd = model.nodes[i]
+    elem_in = 4 if ins[0] == "input" else 1
+    b = int(np.prod(model.shapes[ins[0]])) * elem_in + int(np.prod(model.shapes[out]))
+    b += nd.attrs["w"].size if nd.op == "QLinearConv" else nd.attrs["b"].size
+    if kind == "QConvAdd":
+        b += int(np.prod(model.shapes[ins[1]]))
+    return b
+
+
+def int8_peak_probe(torch, dev, n=8192, reps=10):
+    """Dense int8 tensor throughput of a large library GEMM (torch._int_mm,
+    cuBLASLt; a probe only, not on the hot path): best of `reps` 8192^3
+    multiplies, CUDA events."""
+    try:
+        a = torch.randint(-128, 127, (n, n), dtype=torch.int8, device=dev)
+        b = torch.randint(-128, 127, (n, n), dtype=torch.int8, device=dev).t()
+        for _ in range(3):
+            torch._int_mm(a, b)
+        best = float("inf")
+        for _ in range(reps):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            torch._int_mm(a, b)
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        return {"tops": round(2 * n ** 3 / (best / 1e3) / 1e12, 1), "shape": f"{n}^3 s8 x s8 -> s32",
+                "how": "torch._int_mm best of 10, CUDA events"}
+    except Exception as e:  # noqa: BLE001
+        return {"tops": None, "error": str(e)[:200]}
 
 
 def config2_qlinearconv(ops, W, torch, dev, stream, flush, steps=50):
@@ -359,12 +442,16 @@ def main():
         stream.synchronize()
         return sum(a.elapsed_time(b) for a, b in ev)
 
-    def node_times(reps=5):
-        """Device time of each engine step: 10 launches captured in a CUDA
-        graph, replayed `reps` times, CUDA events on the network's stream
-        (no host gaps between launches; L2 warm)."""
-        times = {}
-        for t_, i in tc_steps:
+    def step_times(reps=5):
+        """Device time of every step of the forward: 10 launches of the step
+        captured in a CUDA graph, replayed `reps` times, CUDA events on the
+        network's stream (no host gaps between launches; L2 warm). Only the
+        shares are used: scaled to the timed forward they give each step's
+        time inside it (the whole-forward graph overlaps each kernel's
+        prologue with its predecessor, so the isolated times add up to a
+        little more than the forward)."""
+        times = []
+        for t_ in range(len(net.steps)):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g, stream=stream):
                 for _ in range(10):
@@ -377,8 +464,23 @@ def main():
                     g.replay()
             e1.record(stream)
             stream.synchronize()
-            times[i] = e0.elapsed_time(e1) / (10 * reps)
+            times.append(e0.elapsed_time(e1) / (10 * reps))
         return times
+
+    def h2d_gbs(reps=10):
+        """Host-to-device bandwidth of this rank's pinned input batch (CUDA
+        events on the copy stream; the e2e line is bounded by this link)."""
+        buf = torch.empty_like(net.view("input"))
+        cs = torch.cuda.Stream(device=dev)
+        with torch.cuda.stream(cs):
+            buf.copy_(x_host, non_blocking=True)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(cs)
+            for _ in range(reps):
+                buf.copy_(x_host, non_blocking=True)
+            e1.record(cs)
+        e1.synchronize()
+        return x_np.nbytes * reps / (e0.elapsed_time(e1) / 1e3) / 1e9
 
     with ClockSampler(local) as clk:
         t_end = time.perf_counter() + 1.5  # reach load clocks (the GPU idles near 120 MHz)
@@ -406,7 +508,9 @@ def main():
         stream.synchronize()
         e2e_ms = pe0.elapsed_time(pe1)
         barrier()
-        ktimes = node_times()
+        stimes = step_times()
+        link_gbs = h2d_gbs()
+        int8_probe = int8_peak_probe(torch, dev) if rank == 0 else None
         c2 = config2_qlinearconv(ops, W, torch, dev, stream, flush) if rank == 0 else None
         rows = other_rows(ops, W, torch, dev, stream, flush) if rank == 0 else None
     assert ops.device_status() == 0
@@ -425,16 +529,34 @@ def main():
     except (OSError, ValueError):
         pass
     bf16 = peaks.get("bf16_tflops")
-    if bf16:
-        peak, peak_note = 2.0 * bf16, "2x measured bf16 burst (MEASURED_PEAKS.json): dense int8 runs at twice the bf16 rate"
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    two_bf16 = 2.0 * (bf16 or 1590.0)
+    # int8 peak: the larger of the live library int8 GEMM probe and twice the
+    # measured bf16 burst (dense int8 runs at twice the bf16 rate on B200);
+    # taking the larger keeps every fraction conservative
+    probe_tops = int8_probe["tops"] if int8_probe else None
+    if probe_tops and probe_tops > two_bf16:
+        peak, peak_note = probe_tops, "measured int8 GEMM probe (torch._int_mm, cuBLASLt), above 2x measured bf16"
     else:
-        peak, peak_note = 2.0 * 1590.0, "2x fallback bf16 1.59 PFLOP/s"
+        peak = two_bf16
+        peak_note = ("2x measured bf16 burst (MEASURED_PEAKS.json), above the measured int8 GEMM probe"
+                     if bf16 else "2x fallback bf16 1.59 PFLOP/s")
 
-    k_ms = sum(ktimes.values())
+    # per-step times inside the timed forward: isolated shares x the forward
+    share_scale = ms / sum(stimes)
+    in_fwd = [t_ * share_scale for t_ in stimes]
+    tc_time = {i: in_fwd[t_] for t_, i in tc_steps}
+    k_ms = sum(tc_time.values())
     k_ops = sum(node_ops(model, i) for i in tc_nodes)
     achieved = k_ops / (k_ms / 1e3) / 1e12
     three = [i for i in tc_nodes if model.nodes[i].op == "QLinearConv" and model.nodes[i].attrs["w"].shape[2] == 3]
-    three_tops = sum(node_ops(model, i) for i in three) / (sum(ktimes[i] for i in three) / 1e3) / 1e12
+    three_ms = sum(tc_time[i] for i in three)
+    three_tops = sum(node_ops(model, i) for i in three) / (three_ms / 1e3) / 1e12
+    # per-layer attainable time: the slower of the tensor floor and the HBM
+    # floor (u8 input + s8 weights + u8 output (+ u8 residual), each once)
+    att_ms = 0.0
+    for t_, i in tc_steps:
+        att_ms += max(node_ops(model, i) / (peak * 1e12), node_bytes(model, net, t_) / (hbm * 1e9)) * 1e3
     if c2:
         c2["kernel_frac_of_int8_peak"] = round(c2["kernel_tops"] / peak, 4)
 
@@ -450,16 +572,26 @@ def main():
                        "parallelism": f"dp{world} (batch-sharded replicas, no data-path collective)"},
             "e2e": {"value": round(e2e_val, 1), "unit": UNIT, "h2d_bytes_per_step": int(x_np.nbytes),
                     "d2h_bytes_per_step": int(np.prod(model.shapes["logits"]) * 4),
-                    "mode": "pipelined (DeviceNetwork.forward_many): H2D of step i overlaps step i-1's forward; "
-                            "one timed window over all steps, L2 flushed before each forward",
+                    "mode": "pipelined (DeviceNetwork.forward_many): H2D of step i into staging buffer i%2 overlaps "
+                            "step i-1's forward, which is the CUDA graph captured on its own staging buffer (no "
+                            "device-to-device input copy); one timed window over all steps, L2 flushed before "
+                            "each forward",
                     "serial_value": round(world * BATCH / (e2e_serial_ms / args.steps / 1e3), 1),
+                    "h2d_gbs_per_rank": round(link_gbs, 1),
+                    "link_bound_images_per_s": round(world * BATCH / (x_np.nbytes / (link_gbs * 1e9)), 1),
                     "serial_mode": "DeviceNetwork.forward: H2D, forward, D2H in sequence, per-step events"},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
                          "frac": round(achieved / peak, 4), "traffic": TC_TRAFFIC_BYTES,
                          "traffic_unit": "bytes per forward (DRAM read + write of all tc_gemm launches, one ncu capture)",
                          "kernel": "tc_gemm_kernel: all 53 QLinearConv (16 with the residual QLinearAdd fused) + the QLinearMatMul of one forward",
                          "kernel_ms_per_forward": round(k_ms, 4), "ops_per_forward": int(k_ops),
-                         "conv3x3_tops": round(three_tops, 1), "peak_source": peak_note},
+                         "kernel_ms_source": "timed forward x the tc steps' share of the isolated per-step times",
+                         "conv3x3_tops": round(three_tops, 1), "conv3x3_frac": round(three_tops / peak, 4),
+                         "conv3x3_ms_per_forward": round(three_ms, 4),
+                         "attainable_ms_per_forward": round(att_ms, 4),
+                         "attainable_frac": round(att_ms / k_ms, 4),
+                         "attainable_note": "sum over tc layers of max(ops / int8 peak, compulsory u8 bytes / HBM)",
+                         "peak_source": peak_note, "int8_probe": int8_probe, "hbm_gbs": hbm},
             "qlinearconv_config2": c2,
             "other_configs": rows,
             # steps + the stem's space-to-depth reorder + the input copies of

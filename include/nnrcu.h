@@ -184,7 +184,9 @@ int nnrcu_qlinearmatmul_run(nnrcu_op* op, const uint8_t* a, uint8_t* y, void* wo
  * rounded to 256) fail with NNRCU_ERR_INVALID. The first call on a device
  * looks up the array's device address, so make that first call before any
  * stream capture. Calls share the array: calls that overlap on the GPU race
- * and must be serialised by the caller. Same requant (R4) and results as
+ * and must be serialised by the caller. A non-NULL stream must belong to the
+ * current device (checked). Every error is returned before anything is
+ * queued on the stream. Same requant (R4) and results as
  * nnrcu_qlinearmatmul_create/_run. */
 #define NNRCU_NOALLOC_SCRATCH_BYTES (8u << 20)
 int nnrcu_qlinearmatmul_noalloc(const uint8_t* a, const int8_t* b, uint8_t* y, int m, int k, int n, float a_scale,

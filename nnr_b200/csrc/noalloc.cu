@@ -102,13 +102,37 @@ extern "C" int nnrcu_qlinearmatmul_noalloc(const uint8_t* a, const int8_t* b, ui
                      "bytes (use nnrcu_qlinearmatmul_create/_run instead)",
                      need, m, k, n, kScratchBytes);
 
+  // Everything that can fail runs before the first launch, so an error
+  // return leaves the caller's stream untouched: the stream's device, the
+  // per-device set-up (architecture check, status word), the scratch
+  // address and both tensor maps.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (st != nullptr) {
+    int cur = 0, sdev = 0;
+    NNRCU_CUDA(cudaGetDevice(&cur));
+    NNRCU_CUDA(cudaStreamGetDevice(st, &sdev));
+    if (sdev != cur)
+      return set_error(NNRCU_ERR_INVALID, "no-alloc QLinearMatMul: the stream belongs to device %d, the current device is %d",
+                       sdev, cur);
+  }
+  int* status = status_ptr();
+  if (!status) return NNRCU_ERR_CUDA;
   uint8_t* scratch = nullptr;
   int rc = scratch_address(&scratch);
   if (rc != NNRCU_OK) return rc;
   int8_t* bt = reinterpret_cast<int8_t*>(scratch);
   int32_t* colcorr = reinterpret_cast<int32_t*>(scratch + bt_bytes);
   int32_t* rowcorr = b_zp != 0 ? reinterpret_cast<int32_t*>(scratch + bt_bytes + col_bytes) : nullptr;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+
+  const int bn = pick_bn(m, n, 1, num_sms());
+  const int amode = k >= BKB ? A_TMA : A_GATHER;
+  CUtensorMap tmA{}, tmB{};
+  rc = encode_tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, bt, kpad, npad, kpad, BKB, bn);
+  if (rc != NNRCU_OK) return rc;
+  if (amode == A_TMA) {
+    rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, (uint64_t)m, k, BKB, BM);
+    if (rc != NNRCU_OK) return rc;
+  }
 
   dim3 tgrid(kpad / 32, npad / 32), tblock(32, 8);
   noalloc_pack_bt<<<tgrid, tblock, 0, st>>>(b, k, n, kpad, npad, bt);
@@ -120,15 +144,6 @@ extern "C" int nnrcu_qlinearmatmul_noalloc(const uint8_t* a, const int8_t* b, ui
     if (rc != NNRCU_OK) return rc;
   }
 
-  const int bn = pick_bn(m, n, 1, num_sms());
-  const int amode = k >= BKB ? A_TMA : A_GATHER;
-  CUtensorMap tmA{}, tmB{};
-  rc = encode_tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, bt, kpad, npad, kpad, BKB, bn);
-  if (rc != NNRCU_OK) return rc;
-  if (amode == A_TMA) {
-    rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, k, (uint64_t)m, k, BKB, BM);
-    if (rc != NNRCU_OK) return rc;
-  }
   GatherGeom g{};
   g.x = a;
   g.N = 1; g.H = 1; g.W = m;
@@ -145,7 +160,7 @@ extern "C" int nnrcu_qlinearmatmul_noalloc(const uint8_t* a, const int8_t* b, ui
   e.y_layout = 0;
   e.ldy = n;
   e.ohw = 1;
-  e.status = status_ptr();
+  e.status = status;
   TcLaunch L{};
   L.bn = bn; L.nplane = 1; L.amode = amode; L.epi = EPI_R4;
   L.m_tiles = (m + BM - 1) / BM;

@@ -323,38 +323,65 @@ class DeviceNetwork:
             out_host.copy_(self.view("logits"), non_blocking=True)
         return out_host
 
-    def forward_many(self, x_hosts, out_hosts, between=None):
-        """Pipelined forwards over a sequence of host batches: batch i+1's
-        host-to-device copy runs on a second stream (into one of two device
-        staging buffers) while batch i is computed; each forward then copies
-        its staged input into the network's input slot, runs, and copies its
-        logits to out_hosts[i]. `between` (optional) is enqueued on the
-        network's stream before each forward. Returns after enqueueing; the
-        caller synchronises self.stream."""
+    def _capture_staged(self):
+        """Two extra CUDA graphs of the forward, each reading its fp32 input
+        from its own staging buffer outside the arena (the arena's input slot
+        may be reused by later steps while the next batch is being copied in).
+        forward_many alternates between them, so no device-to-device copy of
+        the input is needed."""
+        from ._lib import call
         t = self.torch
-        if not hasattr(self, "_stage"):
-            xin = self.view("input")
-            self._stage = [t.empty_like(xin), t.empty_like(xin)]
-            self._copy_stream = t.cuda.Stream(device=self.dev)
-            self._staged = [t.cuda.Event(), t.cuda.Event()]
-            self._consumed = [t.cuda.Event(), t.cuda.Event()]
-        xin, logits = self.view("input"), self.view("logits")
+        xin = self.view("input")
+        self._stage = [t.empty_like(xin), t.empty_like(xin)]
+        self._stage_graphs = []
+        own = self.ptr["input"]
+        st = C.c_void_p(self.stream.cuda_stream)
+        try:
+            for buf in self._stage:
+                self.ptr["input"] = buf.data_ptr()
+                call("nnrcu_graph_begin", st)
+                try:
+                    self.run()
+                finally:
+                    g = C.c_void_p()
+                    call("nnrcu_graph_end", st, C.byref(g))
+                self._stage_graphs.append(g)
+        finally:
+            self.ptr["input"] = own
+        self._copy_stream = t.cuda.Stream(device=self.dev)
+        self._staged = [t.cuda.Event(), t.cuda.Event()]
+        self._consumed = [t.cuda.Event(), t.cuda.Event()]
+
+    def forward_many(self, x_hosts, out_hosts, between=None):
+        """Pipelined forwards over a sequence of host batches: batch i's
+        host-to-device copy runs on a second stream into staging buffer i % 2
+        while batch i-1 is computed; forward i is the CUDA graph captured on
+        that staging buffer, followed by the copy of its logits to
+        out_hosts[i]. `between` (optional) is enqueued on the network's
+        stream before each forward. Returns after enqueueing; the caller
+        synchronises self.stream."""
+        from ._lib import call
+        t = self.torch
+        if not hasattr(self, "_stage_graphs"):
+            self.run()  # module load and attribute set-up happen outside capture
+            self.stream.synchronize()
+            self._capture_staged()
+        logits = self.view("logits")
         cs = self._copy_stream
         cs.wait_stream(self.stream)  # (work already enqueued on the network's stream comes first)
         for i, (xh, oh) in enumerate(zip(x_hosts, out_hosts)):
             k = i & 1
             with t.cuda.stream(cs):
                 if i >= 2:
-                    cs.wait_event(self._consumed[k])   # forward i - 2 has read this buffer
+                    cs.wait_event(self._consumed[k])   # forward i - 2 has finished with this buffer
                 self._stage[k].copy_(xh, non_blocking=True)
                 self._staged[k].record(cs)
             with t.cuda.stream(self.stream):
                 self.stream.wait_event(self._staged[k])
-                xin.copy_(self._stage[k], non_blocking=True)
-                self._consumed[k].record(self.stream)
                 if between is not None:
                     between()
-                self.launch()
+                call("nnrcu_graph_launch", self._stage_graphs[k], C.c_void_p(self.stream.cuda_stream))
+                self._consumed[k].record(self.stream)
                 oh.copy_(logits, non_blocking=True)
         return out_hosts
 
@@ -363,6 +390,9 @@ class DeviceNetwork:
         if self.graph_exec is not None:
             lib.nnrcu_graph_destroy(self.graph_exec)
             self.graph_exec = None
+        for g in getattr(self, "_stage_graphs", []):
+            lib.nnrcu_graph_destroy(g)
+        self._stage_graphs = []
         for op in self.ops:
             if op is not None:
                 op.close()

@@ -325,6 +325,16 @@ int oracle_num_threads(void) {
 #endif
 }
 
+/* Sets the OpenMP thread count explicitly (callers use it so that an
+ * inherited OMP_NUM_THREADS, e.g. torchrun's 1, does not decide it). */
+void oracle_set_threads(int n) {
+#ifdef _OPENMP
+  if (n > 0) omp_set_num_threads(n);
+#else
+  (void)n;
+#endif
+}
+
 /* ------------------------------------------------------------------ QDQ glue (int8 networks) */
 
 static inline uint8_t sat_u8(int v) { return (uint8_t)(v < 0 ? 0 : (v > 255 ? 255 : v)); }

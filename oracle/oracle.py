@@ -179,6 +179,11 @@ def num_threads() -> int:
     return lib().oracle_num_threads()
 
 
+def set_threads(n: int) -> None:
+    """Sets the oracle's OpenMP thread count (overrides OMP_NUM_THREADS)."""
+    lib().oracle_set_threads(int(n))
+
+
 # ------------------------------------------------------------------ QDQ glue
 def quantize_u8(x, scale, zp):
     x = np.ascontiguousarray(x, np.float32)

@@ -62,3 +62,64 @@ def test_graph_replay_and_host_path(net_and_ref):
         assert np.array_equal(out.numpy(), net.view("logits").cpu().numpy())
     finally:
         n2.close()
+
+
+OP_TOL = 1e-4  # the north star's fp32 bound, per operator
+
+
+@pytest.fixture(scope="module")
+def bench_net_and_ref():
+    """The configuration bench.py times: batch 128 (rank 0's shard)."""
+    from nnr_b200 import fgraph, mobilenetv2 as M
+    model = M.build(batch=128)
+    x = M.input_batch(0, 128)
+    logits, ref = O.run_fmodel(model, x, keep=True)
+    net = fgraph.FloatNetwork(model, 0, reuse=False)
+    yield model, net, x, ref
+    net.close()
+
+
+def test_bench_batch_every_op_within_1e4(bench_net_and_ref):
+    """Each device step (Conv, Conv + fused residual Add, GlobalAveragePool,
+    Gemm) is fed the oracle's own input tensors and must reproduce the
+    oracle's output within 1e-4 relative L2: per-operator error, without the
+    compounding of 52 layers."""
+    from nnr_b200 import ops
+    model, net, _, ref = bench_net_and_ref
+    worst = (0.0, None)
+    for t, (kind, j, ins, out, i) in enumerate(net.steps):
+        for name in ins:
+            net.view(name).copy_(torch.from_numpy(ref[name]))
+        net.run_step(t)
+        net.stream.synchronize()
+        e = rel(net.view(out).cpu().numpy(), ref[out])
+        worst = max(worst, (e, f"{kind} {out}"))
+        assert e <= OP_TOL, (kind, out, e)
+    assert ops.device_status() == 0
+    print(f"worst per-op relative L2 error {worst[0]:.2e} at {worst[1]}")
+
+
+def test_bench_batch_whole_network(bench_net_and_ref):
+    """The same batch end to end through the captured graph (the bench's
+    launch path): every tensor within the compounded-network bound."""
+    from nnr_b200 import fgraph, ops
+    model, net, x, ref = bench_net_and_ref
+    net.view("input").copy_(torch.from_numpy(x))
+    net.run()
+    torch.cuda.synchronize()
+    worst = (0.0, None)
+    for nd in model.nodes:
+        if nd.output in net.fused_away:
+            continue
+        worst = max(worst, (rel(net.view(nd.output).cpu().numpy(), ref[nd.output]), nd.output))
+    print(f"batch 128: worst relative L2 error {worst[0]:.2e} at {worst[1]}")
+    assert worst[0] <= NET_TOL, worst
+    n2 = fgraph.FloatNetwork(model, 0)
+    try:
+        n2.capture()
+        out = n2.forward(torch.from_numpy(x).pin_memory())
+        n2.stream.synchronize()
+        assert ops.device_status() == 0
+        assert np.array_equal(out.numpy(), net.view("logits").cpu().numpy())
+    finally:
+        n2.close()

@@ -81,3 +81,44 @@ def test_resnet50_pipelined_forwards(cuda_dev, model4):
             assert torch.equal(o, ref)
     finally:
         net.close()
+
+
+@pytest.fixture(scope="module")
+def model32():
+    from nnr_b200 import resnet50
+    return resnet50.build(batch=32)
+
+
+def test_resnet50_bench_configuration_bit_exact(cuda_dev, model32):
+    """The configuration bench.py times: batch 32 (rank 0's shard of the
+    256-image batch), the planned arena with reuse, the captured CUDA graph.
+    Every intermediate tensor (arena without reuse, so each stays readable)
+    and the logits of the captured, reusing network are bit-exact against the
+    oracle."""
+    from nnr_b200 import graph, ops, resnet50
+    x = resnet50.input_batch(0, 32)
+    ref, tensors = O.run_qmodel(model32, x, keep=True)
+    net = graph.DeviceNetwork(model32, 0, reuse=False)
+    try:
+        net.view("input").copy_(torch.from_numpy(x))
+        net.run()
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        for nd in model32.nodes:
+            if nd.output == "logits" or nd.output in net.fused_away:
+                continue
+            got = net.view(nd.output).cpu().numpy()
+            want = tensors[nd.output]
+            assert np.array_equal(got, want), f"{nd.op} {nd.output}: {(got != want).sum()} of {want.size} differ"
+        assert np.array_equal(net.view("logits").cpu().numpy(), ref)
+    finally:
+        net.close()
+    bench_net = graph.DeviceNetwork(model32, 0)
+    try:
+        bench_net.capture()
+        out = bench_net.forward(torch.from_numpy(x).pin_memory())
+        bench_net.stream.synchronize()
+        assert ops.device_status() == 0
+        assert np.array_equal(out.numpy(), ref)
+    finally:
+        bench_net.close()
