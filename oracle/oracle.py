@@ -184,6 +184,24 @@ def set_threads(n: int) -> None:
     lib().oracle_set_threads(int(n))
 
 
+def round_bf16(x):
+    """fp32 -> bf16 -> fp32, round to nearest even (nnr's float32_to_bfloat16,
+    nnrconf.h:201-206, and the AVX-512 conversion it vectorises)."""
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    u = ((u + (((u >> 16) & 1) + 0x7FFF)) >> 16) << 16
+    return u.astype(np.uint32).view(np.float32)
+
+
+def matmul_f32_bf16_host(a, b):
+    """nnr's fp32 MatMul with a constant B on an AVX-512 BF16 host
+    (MatMul.cpp:128-152 packs B to bf16, :382-428 exec_f32_via_bf16 converts
+    A to bf16 and runs VDPBF16PS with fp32 accumulation): bf16(A) x bf16(B),
+    accumulated here in fp64. a [..., k], b [k, n]."""
+    a64 = round_bf16(a).astype(np.float64)
+    b64 = round_bf16(b).astype(np.float64)
+    return (a64 @ b64).astype(np.float32)
+
+
 # ------------------------------------------------------------------ QDQ glue
 def quantize_u8(x, scale, zp):
     x = np.ascontiguousarray(x, np.float32)

@@ -1,0 +1,13 @@
+// Forced include for nnr's Sigmoid.cpp only (oracle build of nnr, test
+// infrastructure). GCC 13 rejects that file's bf16/fp16 lambda, whose two
+// branches deduce float16_t and double; these overloads make exp() of a half
+// type return the half type, so both branches agree. With std::exp visible
+// beside them, float and double keep their own overloads (the only types
+// the oracle uses).
+#pragma once
+#include <cmath>
+#include "float16.h"
+#include "bfloat16.h"
+using std::exp;
+inline float16_t exp(float16_t v) { return float16_t(std::exp((float)v)); }
+inline bfloat16_t exp(bfloat16_t v) { return bfloat16_t(std::exp((float)v)); }
