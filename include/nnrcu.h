@@ -238,6 +238,11 @@ int nnrcu_dq_gap_q_u8_nhwc(const uint8_t* x, int n, int hw, int c, float x_scale
 int nnrcu_dequantize_linear_u8(const uint8_t* x, float scale, uint8_t zp, const float* bias, int rows, int cols,
                                float* y, void* stream);
 
+/* fp32 Add y = a + b with b repeating every `period` elements (period = total
+ * for a same-shape Add, the row length for a broadcast bias row); y may
+ * alias a (backend/cpu/binary_math.cpp:57-77, Add). */
+int nnrcu_add_f32(const float* a, const float* b, float* y, size_t total, size_t period, void* stream);
+
 /* GlobalAveragePool on fp32 NHWC [n, hw, c] -> [n, c] (kernel/pool.h:109-125). */
 int nnrcu_gap_f32_nhwc(const float* x, int n, int hw, int c, float* y, void* stream);
 

@@ -70,6 +70,7 @@ SIGNATURES = {
     "nnrcu_qlinearconv_set_padded_io": [P, I, I, I, I, I],
     "nnrcu_qlinearconv_run_quantize": [P, P, F, U8, P, P, P],
     "nnrcu_gap_f32_nhwc": [P, I, I, I, P, P],
+    "nnrcu_add_f32": [P, P, P, SZ, SZ, P],
     "nnrcu_qlinearmatmul_create": [I, I, I, F, U8, P, F, I8, F, U8, PP],
     "nnrcu_qlinearmatmul_run": [P, P, P, P, P],
     "nnrcu_qlinearmatmul_noalloc": [P, P, P, I, I, I, F, U8, F, I8, F, U8, P],

@@ -242,6 +242,15 @@ __global__ void dequant_bias_kernel(const uint8_t* __restrict x, float scale, fl
   }
 }
 
+// fp32 Add with the second operand repeating every `period` elements (a
+// same-shape tensor, or a trailing row vector such as a bias): one IEEE
+// addition per element, as binary_math.cpp:57-77 does on the host.
+__global__ void add_f32_kernel(const float* __restrict a, const float* __restrict b, long long period,
+                               long long total, float* __restrict y) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x)
+    y[i] = __fadd_rn(a[i], b[period == total ? i : i % period]);
+}
+
 // GlobalAveragePool on fp32 NHWC [n, hw, c] (kernel/pool.h:109-125): per
 // channel a sequential sum over the positions, times 1/spatial. One thread per
 // (image, channel): consecutive threads read consecutive channels.
@@ -362,6 +371,15 @@ int nnrcu_dequantize_linear_u8(const uint8_t* x, float scale, uint8_t zp, const 
   const long long total = (long long)rows * cols;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   dequant_bias_kernel<<<blocks_for(total, 256), 256, 0, st>>>(x, scale, (float)zp, bias, cols, total, y);
+  NNRCU_CUDA(cudaGetLastError());
+  return NNRCU_OK;
+}
+
+int nnrcu_add_f32(const float* a, const float* b, float* y, size_t total, size_t period, void* stream) {
+  if (!a || !b || !y || total == 0 || period == 0 || total % period != 0)
+    return set_error(NNRCU_ERR_INVALID, "nnrcu_add_f32: bad arguments");
+  add_f32_kernel<<<blocks_for((long long)total, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, b, (long long)period, (long long)total, y);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }

@@ -1,9 +1,8 @@
-// Forced include for nnr's Sigmoid.cpp only (oracle build of nnr, test
-// infrastructure). GCC 13 rejects that file's bf16/fp16 lambda, whose two
-// branches deduce float16_t and double; these overloads make exp() of a half
+// Forced include for nnr's Sigmoid.cpp only, when nnr is built with GCC 13,
+// which rejects that file's bf16/fp16 lambda: its two branches deduce
+// float16_t and double; these overloads make exp() of a half
 // type return the half type, so both branches agree. With std::exp visible
-// beside them, float and double keep their own overloads (the only types
-// the oracle uses).
+// beside them, float and double keep their own overloads.
 #pragma once
 #include <cmath>
 #include "float16.h"
