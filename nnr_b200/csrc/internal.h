@@ -49,7 +49,7 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
                    const uint64_t strides_bytes[2], const uint32_t box[3],
                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
-enum OpKind : int { OP_QCONV = 1, OP_QMATMUL = 2, OP_CONV_F32 = 3, OP_GEMM_F32 = 4, OP_DWCONV_F32 = 5 };
+enum OpKind : int { OP_QCONV = 1, OP_QMATMUL = 2, OP_CONV_F32 = 3, OP_GEMM_F32 = 4, OP_DWCONV_F32 = 5, OP_QDW = 6 };
 
 // One prepared operator: packed weights on the device plus everything the
 // launch needs. Created by nnrcu_*_create, consumed by nnrcu_*_run.
@@ -108,6 +108,11 @@ struct Op {
   int trans_a = 0;
   size_t ws_bytes = 0;
   int64_t num_ops = 0;
+  // split-K (tc_gemm.cuh EpiParams::ksplit): K ranges per tile, offset of
+  // the int32 partial blocks in the workspace, per-block counters (owned)
+  int ksplit = 1;
+  size_t sk_off = 0;
+  int* skcnt = nullptr;
 };
 
 // Launch of the tcgen05 engine (tc_launch.cu).
@@ -128,6 +133,13 @@ int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaSt
 // Picks the N tile (64/128/256) that minimises the estimated waves x tile cost.
 int pick_bn(int M, int N, int nplane, int num_sms);
 int num_sms();
+// Depthwise QLinearConv (qdw.cu).
+int qdw_create(const nnrcu_conv_desc& d, int oh, int ow, const int8_t* w_host, const float* w_scale, int n_w_scale,
+               const int8_t* w_zp, int n_w_zp, const int32_t* bias_host, float x_scale, uint8_t x_zp, float y_scale,
+               uint8_t y_zp, nnrcu_op** out);
+int qdw_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, cudaStream_t st);
+// Split-K of tile-starved convs (NNRCU_SPLITK=0 or 1 turns it off, 2..8 forces that many K ranges).
+bool splitk_enabled();
 
 // Auxiliary kernels (aux_kernels.cu).
 int launch_nchw_to_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int c, int h, int w, int cs, uint8_t fill,

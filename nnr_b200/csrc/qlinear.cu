@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <cstdlib>
 
 #include "internal.h"
 #include "tc_gemm.cuh"
@@ -62,10 +63,14 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   int oh = 0, ow = 0;
   int rc = conv_out_dims(d, &oh, &ow);
   if (rc != NNRCU_OK) return rc;
-  if (d.group != 1)
-    return set_error(NNRCU_ERR_UNSUPPORTED, "QLinearConv with group=%d is not implemented on the device", d.group);
   if (n_w_scale != 1 && n_w_scale != d.oc)
     return set_error(NNRCU_ERR_INVALID, "w_scale has %d entries (expected 1 or %d)", n_w_scale, d.oc);
+  if (d.group == d.c && d.oc == d.c && d.group > 1)  // depthwise: nnr's exec_dw_int8_nhwc (qdw.cu)
+    return qdw_create(d, oh, ow, w_host, w_scale, n_w_scale, w_zp, n_w_zp, bias_host, x_scale, x_zp, y_scale, y_zp,
+                      out);
+  if (d.group != 1)
+    return set_error(NNRCU_ERR_UNSUPPORTED, "grouped QLinearConv (group=%d, not depthwise) is not implemented on the device",
+                     d.group);
   for (int i = 0; i < n_w_zp; ++i)
     if (w_zp && w_zp[i] != 0)
       return set_error(NNRCU_ERR_UNSUPPORTED, "non-zero weight zero point (nnr's VNNI paths require symmetric weights)");
@@ -87,6 +92,10 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   op->npad = round_up(d.oc, 256);
   op->nplane = 1;
   op->bn = pick_bn(op->M, op->N, 1, num_sms());
+  if (const char* fb = std::getenv("NNRCU_BN")) {  // tuning override of the N tile
+    const int v = std::atoi(fb);
+    if (v == 64 || v == 128 || v == 256) op->bn = v;
+  }
   op->num_ops = 2LL * op->M * d.oc * (long long)op->K;
   op->x_zp = x_zp;
 
@@ -212,6 +221,33 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   if (op->explicit_im2col) op->ws_bytes = (size_t)op->M * op->kbytes;
   // (A_ROWS copies read up to BM + 8 pixels from a row start: slack at the end)
   if (op->s2d) op->ws_bytes = (size_t)d.n * op->s2d_hp * op->s2d_wp * 16 + (op->s2d_tpr ? ROWS_BYTES : 0);
+  // Split-K: a conv with fewer than half as many output tiles as SMs and a
+  // long K (the 3x3 and 1x1 convs of ResNet's last two stages at batch 32)
+  // gives each tile's K slabs to several CTAs; their int32 partial blocks go
+  // to the workspace and the last one to finish a block sums and
+  // requantises it (tc_gemm.cuh, EpiParams::ksplit).
+  {
+    const long long tiles = (long long)((op->M + BM - 1) / BM) * ((op->N + op->bn - 1) / op->bn);
+    const int sms = num_sms();
+    const bool shape_ok = op->kslab == 128 &&
+                          ((op->amode == A_TMA && op->num_kb >= 8) || (op->amode == A_IM2COL && op->num_kb >= 10));
+    // tuning override (NNRCU_SPLITK=<ranges>), else the rule below
+    const char* force = std::getenv("NNRCU_SPLITK");
+    const int forced = force ? std::atoi(force) : 0;
+    if (splitk_enabled() && shape_ok && (op->epi == EPI_R1 || op->epi == EPI_R2) && !op->s2d && !op->explicit_im2col &&
+        (tiles * 2 <= sms || forced >= 2)) {
+      const int ks = forced >= 2 ? std::min(forced, op->num_kb)
+                                 : std::min(8, std::min((int)(sms / tiles), op->num_kb / 4));
+      if (ks >= 2) {
+        op->ksplit = ks;
+        op->sk_off = round_up(op->ws_bytes, 256);
+        op->ws_bytes = op->sk_off + (size_t)ks * tiles * BM * op->bn * 4;
+        const size_t cnt_bytes = (size_t)tiles * 16 * sizeof(int);
+        NNRCU_TRY(cuda_check(cudaMalloc(reinterpret_cast<void**>(&op->skcnt), cnt_bytes), "cudaMalloc(split-K counters)"));
+        NNRCU_TRY(cuda_check(cudaMemset(op->skcnt, 0, cnt_bytes), "clear split-K counters"));
+      }
+    }
+  }
 
   // Pack B = W as [npad][kpad] K-major with k = (kh, kw, ic); padded channels,
   // taps and rows are zero. wsum feeds the x_zp compensation.
@@ -281,6 +317,11 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
 static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, void* stream, const uint8_t* res,
                      float res_scale, uint8_t res_zp, float out_scale, uint8_t out_zp, const float* xf = nullptr,
                      float q_scale = 0.0f, uint8_t q_zp = 0) {
+  if (op && op->kind == OP_QDW) {
+    if (!x || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
+    if (res || xf) return set_error(NNRCU_ERR_UNSUPPORTED, "depthwise QLinearConv: no fused add or quantisation");
+    return qdw_run(op, x, y, workspace, static_cast<cudaStream_t>(stream));
+  }
   if (!op || op->kind != OP_QCONV) return set_error(NNRCU_ERR_INVALID, "not a QLinearConv operator");
   if ((!x && !xf) || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
   if (xf && !op->s2d)
@@ -373,6 +414,11 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   e.ldy = d.oc;
   e.ohw = op->oh * op->ow;
   e.status = status_ptr();
+  if (op->ksplit > 1 && !res) {  // (the fused add keeps its own epilogue)
+    e.ksplit = op->ksplit;
+    e.skws = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + op->sk_off);
+    e.skcnt = op->skcnt;
+  }
   if (op->out_pad[0] | op->out_pad[1] | op->out_pad[2] | op->out_pad[3]) {
     if (res || xf) return set_error(NNRCU_ERR_UNSUPPORTED, "a padded output is available through nnrcu_qlinearconv_run only");
     e.opad = 1;
@@ -418,7 +464,8 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
 }
 
 int nnrcu_qlinearconv_input_padding(const nnrcu_op* op, int* pads) {
-  if (!op || op->kind != OP_QCONV || !pads) return set_error(NNRCU_ERR_INVALID, "not a QLinearConv operator");
+  if (!op || (op->kind != OP_QCONV && op->kind != OP_QDW) || !pads)
+    return set_error(NNRCU_ERR_INVALID, "not a QLinearConv operator");
   const bool padded = op->amode == A_SHIFT && op->d.in_layout == NNRCU_LAYOUT_NHWC;
   pads[0] = padded ? op->d.pad_top : 0;
   pads[1] = padded ? op->d.pad_left : 0;

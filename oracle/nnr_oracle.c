@@ -198,6 +198,51 @@ int oracle_qlinearconv(const uint8_t* x, int in_layout, int n, int c, int h, int
  * QLinearMatMul, a u8 [m,k], b s8 [k,n] row-major, y u8 [m,n].
  * R4: val = fma((float)acc, a_s*b_s/y_s, (float)y_zp); nearbyint; clamp [0,255].
  */
+/*
+ * Depthwise QLinearConv on u8 NHWC (group = c = oc), nnr's
+ * exec_dw_int8_nhwc (QLinearConv.cpp:425-531) with the kernel
+ * depthwise_int8_nhwc_avx512_direct (depthwise_int8_avx512.h:207-351):
+ * acc = sum (x - x_zp) * (w - w_zp) over the in-bounds taps (padding taps
+ * contribute (x_zp - x_zp) * w = 0), then R1 with the plain u8 bounds: nnr
+ * passes clamp_min, not the fused-Relu qmin, to this kernel (:502-507).
+ * cs = x_scale * w_scale[c], bias_f = (float)bias[c] * cs
+ * (QLinearConv_reshape.h:306-317). x [n,h,w,c], w [c,1,kh,kw], y [n,oh,ow,c].
+ * Every channel is computed (nnr's kernel skips the channels past the last
+ * whole group of 16).
+ */
+int oracle_qdwconv_u8_nhwc(const uint8_t* x, int n, int c, int h, int w, const int8_t* wt, int kh, int kw, int sh,
+                           int sw, int pt, int pl, int pb, int pr, int dh, int dw, const float* w_scale,
+                           int n_w_scale, int8_t w_zp, const int32_t* bias, float x_scale, uint8_t x_zp,
+                           float y_scale, uint8_t y_zp, uint8_t* y) {
+  const int oh = out_dim(h, pt, pb, kh, sh, dh), ow = out_dim(w, pl, pr, kw, sw, dw);
+  if (oh <= 0 || ow <= 0) return ORACLE_ERR;
+  const float inv_y = 1.0f / y_scale;
+#pragma omp parallel for schedule(static)
+  for (long long p = 0; p < (long long)n * oh * ow; ++p) {
+    const int img = (int)(p / ((long long)oh * ow));
+    const int r = (int)(p - (long long)img * oh * ow);
+    const int oy = r / ow, ox = r - oy * ow;
+    for (int ch = 0; ch < c; ++ch) {
+      int32_t acc = 0;
+      for (int ky = 0; ky < kh; ++ky) {
+        const int iy = oy * sh - pt + ky * dh;
+        if (iy < 0 || iy >= h) continue;
+        for (int kx = 0; kx < kw; ++kx) {
+          const int ix = ox * sw - pl + kx * dw;
+          if (ix < 0 || ix >= w) continue;
+          const int xv = (int)x[(((size_t)img * h + iy) * w + ix) * c + ch] - (int)x_zp;
+          const int wv = (int)wt[((size_t)ch * kh + ky) * kw + kx] - (int)w_zp;
+          acc = wrap_add(acc, wrap_mul(xv, wv));
+        }
+      }
+      const float cs = x_scale * (n_w_scale > 1 ? w_scale[ch] : w_scale[0]);
+      const float bf = bias ? (float)bias[ch] * cs : 0.0f;
+      y[(size_t)p * c + ch] = rq_r1(acc, cs, bf, inv_y, (float)y_zp, 0.0f, 255.0f);
+    }
+  }
+  return ORACLE_OK;
+}
+
 int oracle_qlinearmatmul(const uint8_t* a, const int8_t* b, int m, int k, int n, float a_scale, uint8_t a_zp,
                          float b_scale, int8_t b_zp, float y_scale, uint8_t y_zp, uint8_t* y) {
   if (m <= 0 || k <= 0 || n <= 0) return ORACLE_ERR;

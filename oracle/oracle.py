@@ -175,6 +175,49 @@ def ref_qlinearconv_direct(x, w, w_scale, bias, x_scale, x_zp, y_scale, y_zp, st
     return (y, raw) if want_raw else y
 
 
+def _dw_args(x, w, w_scale, bias, strides, pads, dilations):
+    x = np.ascontiguousarray(x, np.uint8)
+    w = np.ascontiguousarray(w, np.int8)
+    ws = np.ascontiguousarray(np.atleast_1d(w_scale), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.int32)
+    n, h, wd, c = x.shape
+    kh, kw = w.shape[2], w.shape[3]
+    oh, ow = out_hw(h, wd, kh, kw, strides, pads, dilations)
+    return x, w, ws, b, (n, c, h, wd, kh, kw, oh, ow)
+
+
+def qdwconv_u8_nhwc(x, w, w_scale, bias, x_scale, x_zp, y_scale, y_zp, w_zp=0, strides=(1, 1), pads=(0, 0, 0, 0),
+                    dilations=(1, 1)):
+    """Depthwise QLinearConv on u8 NHWC x [n,h,w,c], w [c,1,kh,kw] s8, the
+    restatement of nnr's exec_dw_int8_nhwc (nnr_oracle.c)."""
+    x, w, ws, b, (n, c, h, wd, kh, kw, oh, ow) = _dw_args(x, w, w_scale, bias, strides, pads, dilations)
+    y = np.empty((n, oh, ow, c), np.uint8)
+    rc = lib().oracle_qdwconv_u8_nhwc(_p(x), n, c, h, wd, _p(w), kh, kw, strides[0], strides[1], *pads,
+                                      dilations[0], dilations[1], _p(ws), ws.size, C.c_int8(w_zp), _p(b),
+                                      _f(x_scale), C.c_uint8(x_zp), _f(y_scale), C.c_uint8(y_zp), _p(y))
+    if rc != 0:
+        raise RuntimeError("oracle_qdwconv_u8_nhwc failed")
+    return y
+
+
+def ref_qdwconv_nhwc(x, w, w_scale, bias, x_scale, x_zp, y_scale, y_zp, w_zp=0, strides=(1, 1), pads=(0, 0, 0, 0),
+                     dilations=(1, 1), fill=0xAB):
+    """nnr's own AVX-512 depthwise int8 kernel (oracle/_ref), or None when
+    the harness is not built or the host lacks VNNI. Output bytes nnr does
+    not write (channels past the last group of 16) keep `fill`."""
+    r = ref_lib()
+    if r is None or not r.ref_has_vnni():
+        return None
+    x, w, ws, b, (n, c, h, wd, kh, kw, oh, ow) = _dw_args(x, w, w_scale, bias, strides, pads, dilations)
+    y = np.full((n, oh, ow, c), fill, np.uint8)
+    rc = r.ref_qdwconv_nhwc(_p(x), n, c, h, wd, _p(w), kh, kw, strides[0], strides[1], *pads, dilations[0],
+                            dilations[1], _p(ws), ws.size, C.c_int8(w_zp), _p(b), _f(x_scale), C.c_uint8(x_zp),
+                            _f(y_scale), C.c_uint8(y_zp), _p(y))
+    if rc != 0:
+        raise RuntimeError("ref_qdwconv_nhwc failed")
+    return y
+
+
 def num_threads() -> int:
     return lib().oracle_num_threads()
 

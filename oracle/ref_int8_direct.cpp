@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "backend/x64/conv_int8_direct_avx512.h"
+#include "backend/x64/depthwise_int8_avx512.h"
 
 extern "C" {
 
@@ -97,6 +98,50 @@ int ref_qlinearconv_direct(const uint8_t* x, int n, int c, int h, int w, const i
         const int32_t q = (int32_t)std::nearbyint(val * inv_y_scale) + (int32_t)y_zp;
         out[s] = (uint8_t)std::clamp(q, qmin, clamp_max);
       }
+    }
+  }
+  return 0;
+}
+
+// Depthwise QLinearConv through nnr's own Xbyak-free AVX-512 kernels, the
+// way exec_dw_int8_nhwc (QLinearConv.cpp:425-531) calls them: weights
+// repacked by repack_depthwise_weights, padding taps read from a buffer of
+// x_zp bytes, depthwise_int8_nhwc_avx512_direct for dilation 1 and the
+// indirection-buffer kernel otherwise (at most 5x5 taps there), with the
+// plain u8 clamp bounds nnr passes (:502-507). The per-channel constants
+// restate QLinearConv_reshape.h:306-317 (that class needs Xbyak). x [n,h,w,c]
+// u8, w [c,1,kh,kw] s8, y [n,oh,ow,c] u8; channels past the last whole group
+// of 16 are left as the caller filled them (nnr's kernels skip them).
+int ref_qdwconv_nhwc(const uint8_t* x, int n, int c, int h, int w, const int8_t* wt, int kh, int kw, int sh, int sw,
+                     int pt, int pl, int pb, int pr, int dh, int dw, const float* w_scale, int n_w_scale, int8_t w_zp,
+                     const int32_t* bias, float x_scale, uint8_t x_zp, float y_scale, uint8_t y_zp, uint8_t* y) {
+  if (!ref_has_vnni()) return -1;
+  const int oh = (h + pt + pb - (dh * (kh - 1) + 1)) / sh + 1, ow = (w + pl + pr - (dw * (kw - 1) + 1)) / sw + 1;
+  if (oh <= 0 || ow <= 0) return -1;
+  if ((dh != 1 || dw != 1) && kh * kw > 25) return -1;
+  std::vector<int8_t> wrep(nnr::int8::repack_depthwise_weights_size(c, kh, kw));
+  nnr::int8::repack_depthwise_weights(wrep.data(), wt, c, kh, kw);
+  std::vector<float> cs(c), bias_f(bias ? c : 0);
+  for (int o = 0; o < c; ++o) {
+    cs[o] = x_scale * (n_w_scale > 1 ? w_scale[o] : w_scale[0]);
+    if (bias) bias_f[o] = (float)bias[o] * cs[o];
+  }
+  std::vector<uint8_t> zero_buf((c + 15) & ~15, x_zp);
+  std::vector<const uint8_t*> ind((size_t)oh * ow * kh * kw);
+  const float inv_y = 1.0f / y_scale;
+  for (int img = 0; img < n; ++img) {
+    const uint8_t* xn = x + (size_t)img * h * w * c;
+    uint8_t* yn = y + (size_t)img * oh * ow * c;
+    if (dh == 1 && dw == 1) {
+      nnr::int8::depthwise_int8_nhwc_avx512_direct(yn, xn, wrep.data(), cs.data(), bias ? bias_f.data() : nullptr,
+                                                   zero_buf.data(), c, oh, ow, h, w, kh, kw, sh, sw, pt, pl, (int)x_zp,
+                                                   (int)w_zp, inv_y, (float)y_zp, 0.0f, 255.0f);
+    } else {
+      nnr::int8::build_depthwise_indirection(ind.data(), xn, zero_buf.data(), oh, ow, h, w, c, kh, kw, sh, sw, pt, pl,
+                                             dh, dw);
+      nnr::int8::depthwise_int8_nhwc_avx512_mt(yn, ind.data(), wrep.data(), cs.data(), bias ? bias_f.data() : nullptr,
+                                               c, oh, ow, kh * kw, (int)x_zp, (int)w_zp, inv_y, (float)y_zp, 0.0f,
+                                               255.0f);
     }
   }
   return 0;

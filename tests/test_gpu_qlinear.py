@@ -422,3 +422,54 @@ def test_padded_output_feeds_padded_input(cuda_dev):
     border[:, 1:h + 1, 1:w + 1] = False
     assert (b[border] == c1.y_zp).all()
     assert np.array_equal(out.cpu().numpy(), y2)
+
+
+# ------------------------------------------------------------------ depthwise (exec_dw_int8_nhwc)
+DW_SHAPES = [
+    # n, c, h, w, k, stride, pads, dilation, x_zp, w_zp, y_zp
+    (2, 32, 14, 14, 3, 1, (1, 1, 1, 1), 1, 37, 0, 5),
+    (4, 144, 28, 28, 3, 2, (1, 1, 1, 1), 1, 128, 0, 128),
+    (1, 96, 13, 11, 3, 2, (1, 0, 1, 0), 1, 131, -2, 200),
+    (2, 48, 9, 9, 5, 1, (2, 2, 2, 2), 2, 200, 0, 9),
+    (1, 20, 6, 7, 3, 1, (1, 1, 1, 1), 1, 10, 3, 5),   # C % 16 != 0: the per-element kernel
+]
+
+
+@pytest.mark.parametrize("shape", DW_SHAPES)
+@pytest.mark.parametrize("in_layout", ["NHWC", "NCHW"])
+@pytest.mark.parametrize("fused_relu", [False, True])
+def test_depthwise_bit_exact(cuda_dev, shape, in_layout, fused_relu):
+    """Depthwise QLinearConv (group = C) against the restatement of nnr's
+    exec_dw_int8_nhwc (pinned to nnr's kernels in test_oracle.py); a fused
+    Relu leaves the result unchanged, as in nnr's depthwise path."""
+    from nnr_b200 import ops
+    n, c, h, w, k, s, pads, d, xz, wz, yz = shape
+    rng = np.random.default_rng(c + 7 * h)
+    x = rng.integers(0, 256, size=(n, h, w, c)).astype(np.uint8)
+    wt = rng.integers(-127, 128, size=(c, 1, k, k)).astype(np.int8)
+    ws = rng.uniform(0.002, 0.01, size=c).astype(np.float32)
+    b = rng.integers(-2000, 2001, size=c).astype(np.int32)
+    want = O.qdwconv_u8_nhwc(x, wt, ws, b, 0.02, xz, 0.4, yz, w_zp=wz, strides=(s, s), pads=pads, dilations=(d, d))
+    op = ops.QLinearConv((n, c, h, w), wt, ws, np.int8(wz), b, 0.02, xz, 0.4, yz, strides=(s, s), pads=pads,
+                         dilations=(d, d), group=c, in_layout=in_layout, out_layout="NHWC", fused_relu=fused_relu)
+    xin = x if in_layout == "NHWC" else np.ascontiguousarray(x.transpose(0, 3, 1, 2))
+    y = op.exec(torch.from_numpy(xin).to(cuda_dev))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    got = y.cpu().numpy()
+    assert np.array_equal(got, want), f"{(got != want).sum()} of {want.size} differ"
+
+
+def test_depthwise_nchw_output_declined(cuda_dev):
+    """nnr takes its int8 depthwise kernel for NHWC outputs only; an NCHW
+    output is declined (NNRCU_ERR_UNSUPPORTED), as is a grouped conv that is
+    not depthwise."""
+    from nnr_b200 import ops
+    from nnr_b200._lib import NnrcuError
+    wt = np.ones((16, 1, 3, 3), np.int8)
+    with pytest.raises(NnrcuError, match="NHWC"):
+        ops.QLinearConv((1, 16, 8, 8), wt, np.float32(0.01), None, None, 0.1, 0, 0.1, 0, pads=(1, 1, 1, 1), group=16,
+                        in_layout="NHWC", out_layout="NCHW")
+    with pytest.raises(NnrcuError, match="grouped"):
+        ops.QLinearConv((1, 16, 8, 8), np.ones((16, 4, 3, 3), np.int8), np.float32(0.01), None, None, 0.1, 0, 0.1, 0,
+                        pads=(1, 1, 1, 1), group=4, in_layout="NHWC", out_layout="NHWC")

@@ -144,3 +144,58 @@ def test_gemm_f32_matches_numpy():
     c = rng.normal(size=(9, 5)).astype(np.float32)
     y = O.gemm_f32(a, b, c, alpha=0.5, beta=2.0, trans_b=1)
     assert np.allclose(y, 0.5 * a.astype(np.float64) @ b.T + 2.0 * c, rtol=1e-5, atol=1e-5)
+
+
+# ------------------------------------------------------------------ depthwise (exec_dw_int8_nhwc)
+DW_GOLDEN = sorted((Path(__file__).parent / "golden").glob("qdw_*.npz"))
+
+
+def test_dw_golden_fixtures_present():
+    assert len(DW_GOLDEN) >= 3
+
+
+@pytest.mark.parametrize("path", DW_GOLDEN, ids=lambda p: p.stem)
+def test_dw_oracle_matches_nnr_golden(path):
+    g = np.load(path)
+    s, p, d, xz, wz, yz = (int(v) for v in g["attrs"])
+    xs, ys = (float(v) for v in g["scales"])
+    y = O.qdwconv_u8_nhwc(g["x"], g["w"], g["w_scale"], g["bias"], xs, xz, ys, yz, w_zp=wz, strides=(s, s),
+                          pads=(p,) * 4, dilations=(d, d))
+    assert np.array_equal(y, g["y"]), f"{(y != g['y']).sum()} output bytes differ from nnr's depthwise kernel"
+
+
+@pytest.mark.skipif(not _ref_available(), reason="nnr's int8 kernels not built here or no VNNI")
+@pytest.mark.parametrize("case", [
+    # n, c, h, w, k, stride, pads, dilation, x_zp, w_zp, y_zp
+    (1, 32, 7, 9, 3, 1, (1, 1, 1, 1), 1, 0, 0, 0),
+    (2, 96, 13, 11, 3, 2, (1, 0, 1, 0), 1, 131, -2, 200),
+    (1, 16, 10, 10, 5, 1, (2, 2, 2, 2), 1, 255, 7, 37),
+    (1, 144, 14, 14, 3, 1, (2, 2, 2, 2), 2, 64, 0, 128),
+])
+def test_dw_oracle_matches_nnr_live(case):
+    n, c, h, w, k, s, pads, d, xz, wz, yz = case
+    rng = np.random.default_rng(c * 131 + h)
+    x = rng.integers(0, 256, size=(n, h, w, c)).astype(np.uint8)
+    wt = rng.integers(-127, 128, size=(c, 1, k, k)).astype(np.int8)
+    ws = rng.uniform(0.002, 0.01, size=c).astype(np.float32)
+    b = rng.integers(-2000, 2001, size=c).astype(np.int32)
+    kw = dict(w_zp=wz, strides=(s, s), pads=pads, dilations=(d, d))
+    want = O.ref_qdwconv_nhwc(x, wt, ws, b, 0.02, xz, 0.4, yz, **kw)
+    got = O.qdwconv_u8_nhwc(x, wt, ws, b, 0.02, xz, 0.4, yz, **kw)
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.skipif(not _ref_available(), reason="nnr's int8 kernels not built here or no VNNI")
+def test_dw_nnr_skips_ragged_channels():
+    """Reference defect, recorded: nnr's depthwise kernels loop over whole
+    groups of 16 channels (depthwise_int8_avx512.h:232), so with C % 16 != 0
+    the last channels are never written. The restatement (and the device)
+    compute every channel; the written ones agree."""
+    rng = np.random.default_rng(5)
+    x = rng.integers(0, 256, size=(1, 6, 6, 20)).astype(np.uint8)
+    wt = rng.integers(-127, 128, size=(20, 1, 3, 3)).astype(np.int8)
+    ws = np.full(20, 0.005, np.float32)
+    want = O.ref_qdwconv_nhwc(x, wt, ws, None, 0.02, 10, 0.4, 5, pads=(1, 1, 1, 1), fill=0xAB)
+    got = O.qdwconv_u8_nhwc(x, wt, ws, None, 0.02, 10, 0.4, 5, pads=(1, 1, 1, 1))
+    assert np.array_equal(got[..., :16], want[..., :16])
+    assert (want[..., 16:] == 0xAB).all()
