@@ -108,11 +108,6 @@ struct Op {
   int trans_a = 0;
   size_t ws_bytes = 0;
   int64_t num_ops = 0;
-  // split-K (tc_gemm.cuh EpiParams::ksplit): K ranges per tile, offset of
-  // the int32 partial blocks in the workspace, per-block counters (owned)
-  int ksplit = 1;
-  size_t sk_off = 0;
-  int* skcnt = nullptr;
 };
 
 // Launch of the tcgen05 engine (tc_launch.cu).
@@ -138,8 +133,7 @@ int qdw_create(const nnrcu_conv_desc& d, int oh, int ow, const int8_t* w_host, c
                const int8_t* w_zp, int n_w_zp, const int32_t* bias_host, float x_scale, uint8_t x_zp, float y_scale,
                uint8_t y_zp, nnrcu_op** out);
 int qdw_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, cudaStream_t st);
-// Split-K of tile-starved convs (NNRCU_SPLITK=0 or 1 turns it off, 2..8 forces that many K ranges).
-bool splitk_enabled();
+
 
 // Auxiliary kernels (aux_kernels.cu).
 int launch_nchw_to_nhwc_u8(const uint8_t* src, uint8_t* dst, int n, int c, int h, int w, int cs, uint8_t fill,

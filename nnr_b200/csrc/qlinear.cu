@@ -6,7 +6,6 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
-#include <cstdlib>
 
 #include "internal.h"
 #include "tc_gemm.cuh"
@@ -92,10 +91,6 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   op->npad = round_up(d.oc, 256);
   op->nplane = 1;
   op->bn = pick_bn(op->M, op->N, 1, num_sms());
-  if (const char* fb = std::getenv("NNRCU_BN")) {  // tuning override of the N tile
-    const int v = std::atoi(fb);
-    if (v == 64 || v == 128 || v == 256) op->bn = v;
-  }
   op->num_ops = 2LL * op->M * d.oc * (long long)op->K;
   op->x_zp = x_zp;
 
@@ -221,34 +216,6 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   if (op->explicit_im2col) op->ws_bytes = (size_t)op->M * op->kbytes;
   // (A_ROWS copies read up to BM + 8 pixels from a row start: slack at the end)
   if (op->s2d) op->ws_bytes = (size_t)d.n * op->s2d_hp * op->s2d_wp * 16 + (op->s2d_tpr ? ROWS_BYTES : 0);
-  // Split-K: a conv with fewer than half as many output tiles as SMs and a
-  // long K (the 3x3 and 1x1 convs of ResNet's last two stages at batch 32)
-  // gives each tile's K slabs to several CTAs; their int32 partial blocks go
-  // to the workspace and the last one to finish a block sums and
-  // requantises it (tc_gemm.cuh, EpiParams::ksplit).
-  {
-    const long long tiles = (long long)((op->M + BM - 1) / BM) * ((op->N + op->bn - 1) / op->bn);
-    const int sms = num_sms();
-    const bool shape_ok = op->kslab == 128 &&
-                          ((op->amode == A_TMA && op->num_kb >= 8) || (op->amode == A_IM2COL && op->num_kb >= 10));
-    // tuning override (NNRCU_SPLITK=<ranges>), else the rule below
-    const char* force = std::getenv("NNRCU_SPLITK");
-    const int forced = force ? std::atoi(force) : 0;
-    if (splitk_enabled() && shape_ok && (op->epi == EPI_R1 || op->epi == EPI_R2) && !op->s2d && !op->explicit_im2col &&
-        (tiles * 2 <= sms || forced >= 2)) {
-      const int ks = forced >= 2 ? std::min(forced, op->num_kb)
-                                 : std::min(8, std::min((int)(sms / tiles), op->num_kb / 4));
-      if (ks >= 2) {
-        op->ksplit = ks;
-        op->sk_off = round_up(op->ws_bytes, 256);
-        op->ws_bytes = op->sk_off + (size_t)ks * tiles * BM * op->bn * 4;
-        const size_t cnt_bytes = (size_t)tiles * 16 * sizeof(int);
-        NNRCU_TRY(cuda_check(cudaMalloc(reinterpret_cast<void**>(&op->skcnt), cnt_bytes), "cudaMalloc(split-K counters)"));
-        NNRCU_TRY(cuda_check(cudaMemset(op->skcnt, 0, cnt_bytes), "clear split-K counters"));
-      }
-    }
-  }
-
   // Pack B = W as [npad][kpad] K-major with k = (kh, kw, ic); padded channels,
   // taps and rows are zero. wsum feeds the x_zp compensation.
   std::vector<int8_t> B((size_t)op->npad * op->kpad_bytes, 0);
@@ -414,11 +381,6 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   e.ldy = d.oc;
   e.ohw = op->oh * op->ow;
   e.status = status_ptr();
-  if (op->ksplit > 1 && !res) {  // (the fused add keeps its own epilogue)
-    e.ksplit = op->ksplit;
-    e.skws = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + op->sk_off);
-    e.skcnt = op->skcnt;
-  }
   if (op->out_pad[0] | op->out_pad[1] | op->out_pad[2] | op->out_pad[3]) {
     if (res || xf) return set_error(NNRCU_ERR_UNSUPPORTED, "a padded output is available through nnrcu_qlinearconv_run only");
     e.opad = 1;

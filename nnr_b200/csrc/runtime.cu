@@ -98,11 +98,6 @@ bool pdl_enabled() {
   return on;
 }
 
-bool splitk_enabled() {  // read at operator creation, so it may change between creates
-  const char* v = std::getenv("NNRCU_SPLITK");
-  return !(v && (v[0] == '0' || v[0] == '1') && v[1] == 0);
-}
-
 bool shift_enabled() {
   // shifted-patch mode for stride-1 spatial QLinearConvs; NNRCU_SHIFT=0 turns it off
   // (read when an operator is created)
@@ -306,8 +301,7 @@ int nnrcu_op_num_ops(const nnrcu_op* op, int64_t* ops) {
 }
 int nnrcu_op_destroy(nnrcu_op* op) {
   if (!op) return NNRCU_OK;
-  void* bufs[] = {op->wB, op->colcorr, op->bias_i, op->cs_arr, op->bias_f, op->os, op->bias, op->cmat, op->w_dw,
-                  op->skcnt};
+  void* bufs[] = {op->wB, op->colcorr, op->bias_i, op->cs_arr, op->bias_f, op->os, op->bias, op->cmat, op->w_dw};
   int rc = NNRCU_OK;
   for (void* b : bufs)
     if (b && cudaFree(b) != cudaSuccess) rc = set_error(NNRCU_ERR_CUDA, "cudaFree failed in nnrcu_op_destroy");

@@ -157,15 +157,6 @@ struct EpiParams {
   // row img * o_hwp + oy * o_wp + ox + o_off (o_off = top * o_wp + left)
   int opad, o_w, o_hw, o_wp, o_hwp, o_off;
   int* status;             // device status word (first error wins)
-  // split-K (ksplit > 1): work item w is K range w % ksplit of tile w / ksplit.
-  // Every epilogue warp writes its 32 x HB int32 partial block to skws
-  // ([ksplit][tiles][BM][BN]); the warp that completes a block's count in
-  // skcnt ([tiles][16], zero between launches: the last one resets it) adds
-  // the other ranges' partials to its own (exact: wrapping int32 sums are
-  // order-independent) and requantises.
-  int ksplit;
-  int32_t* skws;
-  int* skcnt;
 };
 
 // NKBR > 0: the whole B operand (num_kb <= NKBR slabs of one N tile) stays
@@ -324,7 +315,7 @@ __device__ __forceinline__ float byte_to_float(uint32_t w, int j) {
 // The smem stage ring runs continuously across tiles, and the accumulator is
 // double-buffered in TMEM (2 x BN columns), so the epilogue of tile i overlaps
 // the loads and MMAs of tile i + 1.
-template <int BN, int NPLANE, int AMODE, int EPI, int KB, int NKBR = 0, int SK = 0>
+template <int BN, int NPLANE, int AMODE, int EPI, int KB, int NKBR = 0>
 __global__ void __launch_bounds__(Roles<AMODE, BN, EPI>::THREADS, 1)
 tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__ CUtensorMap tmA1,
                const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmY,
@@ -339,8 +330,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   constexpr int HB = BN / SPLIT;
   using Cfg = KernelCfg<BN, NPLANE, AMODE, EPI, KB, NKBR>;
   static_assert(NKBR == 0 || (NPLANE == 1 && KB != 16 && AMODE != A_GATHER), "resident B: int8, TMA-fed A");
-  static_assert(!SK || (NKBR == 0 && NPLANE == 1 && (AMODE == A_TMA || AMODE == A_IM2COL) && (EPI == EPI_R1 || EPI == EPI_R2)),
-                "split-K: int8, TMA/im2col-fed A, R1/R2 epilogue");
   static_assert(KB == BKB || AMODE != A_GATHER, "the gather producers fill 128-byte slabs");
   static_assert(AMODE != A_SHIFT || (NKBR > 0 && NPLANE == 1 && (KB == 64 || KB == 128)),
                 "shifted-patch mode: int8, resident B, 64/128-byte slabs");
@@ -378,10 +367,6 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int num_tiles = m_tiles * n_tiles;
-  // K ranges per tile: split-K instances (SK) only, so that the others keep
-  // their register budget
-  const int KS = (SK && e.ksplit > 1) ? e.ksplit : 1;
-  const int num_items = num_tiles * KS;
   if (threadIdx.x == 0) NNRCU_TRACE_AT(23, 15, 3);  // CTA start
   // per-column constants, one private copy per epilogue warp (no cross-warp sync)
   int32_t* s_ci = reinterpret_cast<int32_t*>(reinterpret_cast<uint8_t*>(full_bar) + Cfg::BAR_BYTES +
@@ -479,10 +464,8 @@ if constexpr (AMODE == A_ROWS) {
       const uint32_t tx_rows = (uint32_t)(8 / max(g.tpr, 1)) * ROWS_BYTES + B_BYTES;  // A_ROWS stage bytes
       bool aborted = false;
       int it = 0, tlt = 0;
-      for (int item = blockIdx.x; item < num_items && !aborted; item += gridDim.x, ++tlt) {
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x, ++tlt) {
         NNRCU_TRACE_AT(warp, tlt, 0);
-        const int tile = item / KS, ks = item - tile * KS;
-        const int kb_lo = ks * num_kb / KS, kb_hi = (ks + 1) * num_kb / KS;
         const int m0 = (tile / n_tiles) * BM, n0 = (tile % n_tiles) * BN;
         // im2col: input position of the tile's first output pixel
         int i_n = 0, i_h = 0, i_w = 0;
@@ -496,7 +479,7 @@ if constexpr (AMODE == A_ROWS) {
         }
         int r_mb = 0, r_nvr = 0, r_orow = 0, r_ow0 = 0;
         if (AMODE == A_ROWS) tile_rows(tile / n_tiles, r_mb, r_nvr, r_orow, r_ow0);
-        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
           if (R::NPROD > 1 && it % R::NPROD != pw) continue;
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
@@ -578,10 +561,7 @@ if constexpr (AMODE == A_ROWS) {
         fail(ST_TIMEOUT_FULL);
         aborted = true;
       }
-      for (int item = blockIdx.x; item < num_items && !aborted; item += gridDim.x, ++lt) {
-        const int tile = item / KS, ks = item - tile * KS;
-        const int kb_lo = ks * num_kb / KS, kb_hi = (ks + 1) * num_kb / KS;
-        (void)tile;
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x, ++lt) {
         const int acc = lt & 1;
         const uint32_t use_ph = (uint32_t)(lt >> 1) & 1u;
         if (!ptx::mbar_wait(&tempty_bar[acc], use_ph ^ 1u, abort_flag)) { fail(ST_TIMEOUT_ACCUM); aborted = true; break; }
@@ -612,12 +592,11 @@ if constexpr (AMODE == A_ROWS) {
           NNRCU_TRACE_AT(warp, lt, 2);
           continue;
         }
-        for (int kb = kb_lo; kb < kb_hi; ++kb, ++it) {
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!ptx::mbar_wait(&full_bar[s], ph, abort_flag)) { fail(ST_TIMEOUT_FULL); aborted = true; break; }
-          if (kb == kb_lo) NNRCU_TRACE_AT(warp, lt, 1);
-          const bool accum = kb != kb_lo;  // the first K step of a work item overwrites the accumulator
+          if (kb == 0) NNRCU_TRACE_AT(warp, lt, 1);
           ptx::tc_fence_after();
           // (stages filled by TMA are async-proxy writes already; the gather
           // producers fence their cp.async writes before arriving)
@@ -631,19 +610,19 @@ if constexpr (AMODE == A_ROWS) {
               // rows shifted by 16 bytes per tap (K-adjacent columns 16 B apart)
               const int tap0 = 2 * k, j = tap0 / g.tpr, kw0 = tap0 - j * g.tpr;
               ptx::mma_i8(d_tmem, ptx::umma_desc_interleaved(a_addr + j * ROWS_BYTES + kw0 * 16, 16, 128),
-                          ptx::umma_desc_interleaved(b_addr + k * 2 * (BN * 16), BN * 16, 128), idesc, (accum || k != 0));
+                          ptx::umma_desc_interleaved(b_addr + k * 2 * (BN * 16), BN * 16, 128), idesc, (kb | k) != 0);
             } else if constexpr (KB == 16) {
               // two 16-byte tap columns per K step
               ptx::mma_i8(d_tmem, ptx::umma_desc_interleaved(a_addr + k * 2 * (BM * 16), BM * 16, 128),
-                          ptx::umma_desc_interleaved(b_addr + k * 2 * (BN * 16), BN * 16, 128), idesc, (accum || k != 0));
+                          ptx::umma_desc_interleaved(b_addr + k * 2 * (BN * 16), BN * 16, 128), idesc, (kb | k) != 0);
             } else if constexpr (NPLANE == 1) {
               // stage descriptors plus the K offset (16-byte units)
               ptx::mma_i8(d_tmem, ptx::umma_desc_sw<KB>(a_addr) + (uint64_t)(koff >> 4),
-                          ptx::umma_desc_sw<KB>(b_addr) + (uint64_t)(koff >> 4), idesc, (accum || k != 0));
+                          ptx::umma_desc_sw<KB>(b_addr) + (uint64_t)(koff >> 4), idesc, (kb | k) != 0);
             } else {
               // hi*hi, hi*lo, lo*hi
               ptx::mma_f16(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff), ptx::umma_desc_sw<KB>(b_addr + koff), idesc,
-                           (accum || k != 0));
+                           (kb | k) != 0);
               ptx::mma_f16(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff),
                            ptx::umma_desc_sw<KB>(b_addr + B_BYTES + koff), idesc, 1u);
               ptx::mma_f16(d_tmem, ptx::umma_desc_sw<KB>(a_addr + A_BYTES + koff),
@@ -779,8 +758,7 @@ if constexpr (AMODE == A_ROWS) {
     };
     if (EPI == EPI_R2A && Cfg::RES_TMA && lane == 0 && (int)blockIdx.x < num_tiles) issue_res(blockIdx.x, 0);
     bool res_failed = false;
-    for (int item = blockIdx.x + group * gridDim.x; item < num_items; item += EG * gridDim.x, lt += EG) {
-      const int tile = item / KS, ks = item - tile * KS;
+    for (int tile = blockIdx.x + group * gridDim.x; tile < num_tiles; tile += EG * gridDim.x, lt += EG) {
       int m0 = 0, nvr = 0, orow = 0, ow0 = 0;
       tile_rows(tile / n_tiles, m0, nvr, orow, ow0);
       const int n0 = (tile % n_tiles) * BN;
@@ -1230,55 +1208,7 @@ if constexpr (AMODE == A_ROWS) {
       uint32_t va[CW], vb[CW];
       int tev = 0;
       bool released = false;
-      bool stored = true;  // this warp's block is (being) written
-      if (SK && KS > 1) {
-        // split-K: publish this K range's partial block, count it, and if it
-        // completes the block, sum all ranges and requantise
-        int32_t* const part = e.skws + ((size_t)ks * num_tiles + tile) * (BM * BN) + (size_t)row * BN;
-#pragma unroll 1
-        for (int c0 = col0; c0 < col0 + HB; c0 += CW) {
-          ptx::tmem_ld_async(t_addr + (uint32_t)c0, va);
-          ptx::tmem_wait_ld(va);
-          int4* p = reinterpret_cast<int4*>(part + c0);
-#pragma unroll
-          for (int j = 0; j < CW / 4; ++j)
-            p[j] = make_int4((int)va[4 * j], (int)va[4 * j + 1], (int)va[4 * j + 2], (int)va[4 * j + 3]);
-        }
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-          int* cnt = e.skcnt + (size_t)tile * 16 + wig;
-          last = atomicAdd(cnt, 1) == KS - 1;
-          if (last) *cnt = 0;  // ready for the next launch
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          __threadfence();
-#pragma unroll 1
-          for (int c0 = col0; c0 < col0 + HB; c0 += CW) {
-            ptx::tmem_ld_async(t_addr + (uint32_t)c0, va);
-            ptx::tmem_wait_ld(va);
-#pragma unroll 1
-            for (int o = 0; o < KS; ++o) {
-              if (o == ks) continue;
-              const int4* q = reinterpret_cast<const int4*>(e.skws + ((size_t)o * num_tiles + tile) * (BM * BN) +
-                                                            (size_t)row * BN + c0);
-#pragma unroll
-              for (int j = 0; j < CW / 4; ++j) {
-                const int4 w = __ldcg(q + j);
-                va[4 * j] += (uint32_t)w.x;
-                va[4 * j + 1] += (uint32_t)w.y;
-                va[4 * j + 2] += (uint32_t)w.z;
-                va[4 * j + 3] += (uint32_t)w.w;
-              }
-            }
-            chunk(c0, va);
-          }
-        } else {
-          stored = false;
-        }
-      } else if (fast && HB == CW) {
+      if (fast && HB == CW) {
         // one chunk per warp: the accumulator goes back to the MMA warp as
         // soon as it is in registers, so the next tiles' MMAs overlap this
         // requantisation
@@ -1335,7 +1265,7 @@ if constexpr (AMODE == A_ROWS) {
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&tempty_bar[acc]);
       }
-      if (Cfg::OUT_BLOCK > 0 && y_tma && stored) {
+      if (Cfg::OUT_BLOCK > 0 && y_tma) {
         // publish the staged block: rows >= M and columns >= N are clipped by the map
         ptx::fence_proxy_async_smem();
         __syncwarp();

@@ -8,10 +8,10 @@ namespace nnrcu {
 
 namespace {
 
-template <int BN, int NPLANE, int AMODE, int EPI, int KB = BKB, int NKBR = 0, int SK = 0>
+template <int BN, int NPLANE, int AMODE, int EPI, int KB = BKB, int NKBR = 0>
 int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
   using Cfg = KernelCfg<BN, NPLANE, AMODE, EPI, KB, NKBR>;
-  auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI, KB, NKBR, SK>;
+  auto kern = tc_gemm_kernel<BN, NPLANE, AMODE, EPI, KB, NKBR>;
   // The attribute is per function; setting it is cheap but not free, so do it
   // once per device.
   static unsigned long long configured = 0;
@@ -21,8 +21,7 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
     NNRCU_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     configured |= 1ull << dev;
   }
-  // work items: tiles, times the K ranges of a split-K launch
-  const long long tiles = (long long)L.m_tiles * L.n_tiles * ((SK && e.ksplit > 1) ? e.ksplit : 1);
+  const long long tiles = (long long)L.m_tiles * L.n_tiles;
   int grid = (int)std::min<long long>(tiles, (long long)num_sms());
   // resident B: each CTA keeps one N tile's weights, so its tiles must all
   // share that N tile (tile % n_tiles == blockIdx.x % n_tiles)
@@ -193,32 +192,12 @@ int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaSt
   if (L.amode == A_GATHER && ((reinterpret_cast<uintptr_t>(g.x) & 15) || (g.x2 && (reinterpret_cast<uintptr_t>(g.x2) & 15)) ||
                               (g.cbytes & 15)))
     return set_error(NNRCU_ERR_INVALID, "gathered operand must be 16-byte aligned with a 16-byte pixel stride");
-  if (e.ksplit > 1) {
-    // split-K instances: int8, 128-byte slabs, TMA or im2col A, R1/R2
-    if (!(L.amode == A_TMA || L.amode == A_IM2COL) || L.nplane != 1 || e.qres || L.kb_bytes != 128 ||
-        !(L.epi == EPI_R1 || L.epi == EPI_R2) || !e.skws || !e.skcnt)
-      return set_error(NNRCU_ERR_INVALID, "split-K needs an int8 TMA/im2col operand with 128-byte slabs, an R1/R2 "
-                                          "epilogue and its buffers");
-    const bool im = L.amode == A_IM2COL, r1 = L.epi == EPI_R1;
-#define NNRCU_SK(BNV)                                                                                  \
-  return im ? (r1 ? launch_one<BNV, 1, A_IM2COL, EPI_R1, 128, 0, 1>(L, g, e, stream)                 \
-                  : launch_one<BNV, 1, A_IM2COL, EPI_R2, 128, 0, 1>(L, g, e, stream))                \
-            : (r1 ? launch_one<BNV, 1, A_TMA, EPI_R1, 128, 0, 1>(L, g, e, stream)                    \
-                  : launch_one<BNV, 1, A_TMA, EPI_R2, 128, 0, 1>(L, g, e, stream))
-    switch (L.bn) {
-      case 64: NNRCU_SK(64);
-      case 128: NNRCU_SK(128);
-      case 256: NNRCU_SK(256);
-      default: return set_error(NNRCU_ERR_INVALID, "unsupported N tile %d", L.bn);
-    }
-#undef NNRCU_SK
-  }
   // an R2 requant with a fused add whose output and residual can move by
   // TMA (16-byte aligned NHWC rows) runs the residual-prefetching instance
   TcLaunch L2 = L;
   // Resident B: a single N tile whose K fits 9 slabs (3x3 convs over 64 or
   // 128 channels), im2col-fed, R2
-  if (e.ksplit <= 1 && L.n_tiles == 1 && L.num_kb <= 9 && L.amode == A_IM2COL && L.epi == EPI_R2 && L.nplane == 1 &&
+  if (L.n_tiles == 1 && L.num_kb <= 9 && L.amode == A_IM2COL && L.epi == EPI_R2 && L.nplane == 1 &&
       ((L.bn == 64 && L.kb_bytes == 64) || (L.bn == 128 && L.kb_bytes == 128))) {
     if (L.bn == 64) return launch_one<64, 1, A_IM2COL, EPI_R2, 64, 9>(L, g, e, stream);
     return launch_one<128, 1, A_IM2COL, EPI_R2, 128, 9>(L, g, e, stream);
