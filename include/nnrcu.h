@@ -215,6 +215,35 @@ int nnrcu_gemm_f32_create(int m, int n, int k, int trans_a, int trans_b, float a
                           float post_b, nnrcu_op** op);
 int nnrcu_gemm_f32_run(nnrcu_op* op, const float* a, float* y, void* workspace, void* stream);
 
+/* Precision of an fp32 Gemm / MatMul:
+ *   SPLIT_BF16: fp32 emulated as split bf16 (three products, ~2e-5 relative);
+ *   BF16: both operands rounded to bf16 (nearest even), one product each,
+ *         fp32 accumulation: nnr's own fp32 MatMul with a constant B on hosts
+ *         with AVX-512 BF16 (MatMul.cpp:128-152, :382-428 exec_f32_via_bf16),
+ *         so results follow that reference path. */
+#define NNRCU_PREC_SPLIT_BF16 0
+#define NNRCU_PREC_BF16 1
+int nnrcu_gemm_f32_create_ex(int m, int n, int k, int trans_a, int trans_b, float alpha, float beta,
+                             const float* b_host, const float* c_host, int c_rows, int post_op, float post_a,
+                             float post_b, int precision, nnrcu_op** op);
+
+/* ---------------------------------------------------------------- 16-bit Conv / Gemm (bf16 or fp16 I/O)
+ * Replace nnr's 16-bit I/O paths, which convert to fp32, compute in fp32,
+ * apply the post-op and round back (Conv_exec_entry.h:188-381, Gemm.cpp:
+ * 297-513): one kind::f16 product per multiply-add (exact in fp32), fp32
+ * accumulation and epilogue, the result rounded to the 16-bit type (nearest
+ * even). Tensors hold the raw 16-bit values; weights and bias too. */
+#define NNRCU_DT_BF16 1
+#define NNRCU_DT_F16 2
+int nnrcu_conv_half_create(const nnrcu_conv_desc* desc, int dtype, const uint16_t* w_host, const uint16_t* bias_host,
+                           nnrcu_op** op);
+int nnrcu_conv_half_run(nnrcu_op* op, const uint16_t* x, uint16_t* y, void* workspace, void* stream);
+/* alpha must be 1; C is a [n] row or a full [m, n] matrix (c_rows = 1 or m) of the 16-bit type */
+int nnrcu_gemm_half_create(int m, int n, int k, int trans_a, int trans_b, float alpha, float beta, int dtype,
+                           const uint16_t* b_host, const uint16_t* c_host, int c_rows, int post_op, float post_a,
+                           float post_b, nnrcu_op** op);
+int nnrcu_gemm_half_run(nnrcu_op* op, const uint16_t* a, uint16_t* y, void* workspace, void* stream);
+
 /* ---------------------------------------------------------------- QDQ glue of int8 networks
  * Device versions of the ops around QLinearConv/QLinearMatMul in a QDQ graph,
  * so that a whole int8 network stays on the device. Same float operation

@@ -71,6 +71,11 @@ SIGNATURES = {
     "nnrcu_qlinearconv_run_quantize": [P, P, F, U8, P, P, P],
     "nnrcu_gap_f32_nhwc": [P, I, I, I, P, P],
     "nnrcu_add_f32": [P, P, P, SZ, SZ, P],
+    "nnrcu_gemm_f32_create_ex": [I, I, I, I, I, F, F, P, P, I, I, F, F, I, PP],
+    "nnrcu_conv_half_create": [P, I, P, P, PP],
+    "nnrcu_conv_half_run": [P, P, P, P, P],
+    "nnrcu_gemm_half_create": [I, I, I, I, I, F, F, I, P, P, I, I, F, F, PP],
+    "nnrcu_gemm_half_run": [P, P, P, P, P],
     "nnrcu_qlinearmatmul_create": [I, I, I, F, U8, P, F, I8, F, U8, PP],
     "nnrcu_qlinearmatmul_run": [P, P, P, P, P],
     "nnrcu_qlinearmatmul_noalloc": [P, P, P, I, I, I, F, U8, F, I8, F, U8, P],

@@ -291,6 +291,10 @@ int nnrcu_gemm_f32_create(int m, int n, int k, int trans_a, int trans_b, float a
 }
 
 int nnrcu_gemm_f32_run(nnrcu_op* op, const float* a, float* y, void* workspace, void* stream) {
+  if (op && op->kind == OP_GEMM_F32_BF16) {
+    if (!a || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
+    return gemm_f32_bf16_run(op, a, y, workspace, static_cast<cudaStream_t>(stream));
+  }
   if (!op || op->kind != OP_GEMM_F32) return set_error(NNRCU_ERR_INVALID, "not a Gemm operator");
   if (!a || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
   if (!workspace) return set_error(NNRCU_ERR_INVALID, "workspace of %zu bytes required", op->ws_bytes);

@@ -49,7 +49,8 @@ int encode_tmap_3d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base
                    const uint64_t strides_bytes[2], const uint32_t box[3],
                    CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_NONE);
 
-enum OpKind : int { OP_QCONV = 1, OP_QMATMUL = 2, OP_CONV_F32 = 3, OP_GEMM_F32 = 4, OP_DWCONV_F32 = 5, OP_QDW = 6 };
+enum OpKind : int { OP_QCONV = 1, OP_QMATMUL = 2, OP_CONV_F32 = 3, OP_GEMM_F32 = 4, OP_DWCONV_F32 = 5, OP_QDW = 6, OP_CONV_HALF = 7,
+                   OP_GEMM_HALF = 8, OP_GEMM_F32_BF16 = 9 };
 
 // One prepared operator: packed weights on the device plus everything the
 // launch needs. Created by nnrcu_*_create, consumed by nnrcu_*_run.
@@ -107,6 +108,7 @@ struct Op {
   int c_rows = 0;
   int trans_a = 0;
   size_t ws_bytes = 0;
+  size_t out_off = 0;           // 16-bit ops: offset of the fp32 result in the workspace
   int64_t num_ops = 0;
 };
 
@@ -133,6 +135,8 @@ int qdw_create(const nnrcu_conv_desc& d, int oh, int ow, const int8_t* w_host, c
                const int8_t* w_zp, int n_w_zp, const int32_t* bias_host, float x_scale, uint8_t x_zp, float y_scale,
                uint8_t y_zp, nnrcu_op** out);
 int qdw_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace, cudaStream_t st);
+// fp32 Gemm with bf16-rounded operands (half.cu, NNRCU_PREC_BF16).
+int gemm_f32_bf16_run(nnrcu_op* op, const float* a, float* y, void* workspace, cudaStream_t st);
 
 
 // Auxiliary kernels (aux_kernels.cu).

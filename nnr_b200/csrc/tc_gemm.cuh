@@ -21,6 +21,8 @@
 // (SWIZZLE_128B) and the UMMA descriptors understand.
 //
 // NPLANE = 1: int8 (kind::i8, u8 activations x s8 weights, s32 accumulate).
+// NPLANE = 3 / 4: one bf16 / fp16 plane (kind::f16, f32 accumulate): the
+//             16-bit I/O variants, one exact product per multiply-add.
 // NPLANE = 2: fp32 emulated as split bf16 (kind::f16, f32 accumulate):
 //             a*b ~= a_hi*b_hi + a_hi*b_lo + a_lo*b_hi with x_hi = bf16(x),
 //             x_lo = bf16(x - x_hi); the dropped a_lo*b_lo term is < 2^-16
@@ -172,7 +174,8 @@ struct TileCfg {
   static constexpr int BRES_BYTES = NKBR * B_BYTES;
   static constexpr int PATCH_BYTES = PATCH ? ((BUDGET - BRES_BYTES) / 2) & ~1023 : 0;  // per patch buffer
   static constexpr int A_BYTES = PATCH ? PATCH_BYTES : BM * SLAB;  // 16 KB per plane (8 KB with 64-byte slabs)
-  static constexpr int STAGE_BYTES = NPLANE * (A_BYTES + (NKBR ? 0 : B_BYTES));
+  static constexpr int PL = NPLANE == 2 ? 2 : 1;  // shared-memory planes per operand
+  static constexpr int STAGE_BYTES = PL * (A_BYTES + (NKBR ? 0 : B_BYTES));
   // Epilogues stage each warp's 32-row output block for a TMA store: u8
   // always; fp32 (4 bytes per element) when that still leaves three stages.
   static constexpr int ESZ = EPI == EPI_F32 ? 4 : 1;
@@ -334,6 +337,8 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   static_assert(AMODE != A_SHIFT || (NKBR > 0 && NPLANE == 1 && (KB == 64 || KB == 128)),
                 "shifted-patch mode: int8, resident B, 64/128-byte slabs");
   constexpr int STAGES = Cfg::STAGES;
+  constexpr int PL = Cfg::PL;             // planes per operand (split-bf16: hi and lo)
+  constexpr bool HALF = NPLANE >= 2;      // 16-bit elements (kind::f16)
   constexpr int A_BYTES = Cfg::A_BYTES;
   constexpr int B_BYTES = Cfg::B_BYTES;
 
@@ -350,9 +355,9 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   // 1024-byte aligned base, derived by pointer arithmetic on the shared array
   // so that accesses through it stay shared-memory (not generic) accesses
   uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint8_t* sA = smem;                                        // [STAGES][NPLANE][A_BYTES]
-  uint8_t* sB = sA + STAGES * NPLANE * A_BYTES;              // [STAGES][NPLANE][B_BYTES], or [NKBR][B_BYTES]
-  uint8_t* sOut = sB + (NKBR ? Cfg::BRES_BYTES : STAGES * NPLANE * B_BYTES);  // u8 epilogue staging
+  uint8_t* sA = smem;                                        // [STAGES][PL][A_BYTES]
+  uint8_t* sB = sA + STAGES * PL * A_BYTES;                  // [STAGES][PL][B_BYTES], or [NKBR][B_BYTES]
+  uint8_t* sOut = sB + (NKBR ? Cfg::BRES_BYTES : STAGES * PL * B_BYTES);  // u8 epilogue staging
   uint8_t* sRes = sOut + Cfg::OUT_BYTES;                      // [2][8 warps][32 rows][HB] (EPI_R2A)
   // sOut: [OUT_BUFS][8 warps][32 rows][HB]
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(sRes + Cfg::RES_BYTES);
@@ -437,7 +442,7 @@ if constexpr (AMODE == A_ROWS) {
     const int pw = warp - R::TMA_WARP;  // this producer issues stages it with it % NPROD == pw
     if (lane == 0) {
       constexpr uint32_t tx =
-          AMODE == A_ROWS ? 0u : (AMODE != A_GATHER ? NPLANE * A_BYTES : 0) + (NKBR ? 0 : NPLANE * B_BYTES);
+          AMODE == A_ROWS ? 0u : (AMODE != A_GATHER ? PL * A_BYTES : 0) + (NKBR ? 0 : PL * B_BYTES);
       if (NKBR > 0 && pw == 0) {
         // this CTA's N tile's B, all K slabs, once per CTA (the grid is a
         // multiple of n_tiles, so a CTA's tiles all have N tile blockIdx.x % n_tiles)
@@ -485,9 +490,9 @@ if constexpr (AMODE == A_ROWS) {
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!ptx::mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag)) { fail(ST_TIMEOUT_EMPTY); aborted = true; break; }
           ptx::mbar_arrive_expect_tx(&full_bar[s], AMODE == A_ROWS ? tx_rows : tx);
-          uint8_t* a_st = sA + (size_t)s * NPLANE * A_BYTES;
-          uint8_t* b_st = sB + (size_t)s * NPLANE * B_BYTES;
-          const int kx = kb * KB / (NPLANE == 2 ? 2 : 1);  // element coordinate along K
+          uint8_t* a_st = sA + (size_t)s * PL * A_BYTES;
+          uint8_t* b_st = sB + (size_t)s * PL * B_BYTES;
+          const int kx = kb * KB / (HALF ? 2 : 1);  // element coordinate along K
           if constexpr (KB == 16) {
             // B: [tap][row][16 B] -> eight taps x BN rows x 16 B; A: one
             // hardware im2col copy (128 pixels x 16 B) per tap. Taps past the
@@ -516,7 +521,7 @@ if constexpr (AMODE == A_ROWS) {
             }
           } else {
           if (NKBR == 0)
-            for (int p = 0; p < NPLANE; ++p)
+            for (int p = 0; p < PL; ++p)
               ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
           if (AMODE == A_TMA) {
             ptx::tma_load_2d(a_st, &tmA0, &full_bar[s], kx, m0);
@@ -525,7 +530,7 @@ if constexpr (AMODE == A_ROWS) {
             // one K slab = 128 bytes of channels of a single filter tap
             const int kbyte = kb * KB;
             const int tap = kbyte / g.cbytes;
-            const int cc = (kbyte - tap * g.cbytes) / (NPLANE == 2 ? 2 : 1);
+            const int cc = (kbyte - tap * g.cbytes) / (HALF ? 2 : 1);
             const int kh = tap / g.KW, kw = tap - kh * g.KW;
             const uint16_t ow_off = (uint16_t)(kw * g.dw), oh_off = (uint16_t)(kh * g.dh);
             ptx::tma_load_im2col_4d(a_st, &tmA0, &full_bar[s], cc, i_w, i_h, i_n, ow_off, oh_off);
@@ -541,7 +546,10 @@ if constexpr (AMODE == A_ROWS) {
   } else if (warp == R::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = (NPLANE == 1) ? ptx::umma_idesc(2, 0, 1, BM, BN) : ptx::umma_idesc(1, 1, 1, BM, BN);
+      // s32 += u8 x s8; f32 += bf16 x bf16 (NPLANE 2, 3); f32 += f16 x f16 (NPLANE 4)
+      constexpr uint32_t idesc = (NPLANE == 1)   ? ptx::umma_idesc(2, 0, 1, BM, BN)
+                                 : (NPLANE == 4) ? ptx::umma_idesc(1, 0, 0, BM, BN)
+                                                 : ptx::umma_idesc(1, 1, 1, BM, BN);
       bool aborted = false;
       int it = 0, lt = 0;
       // A_SHIFT: per K step, the A view's start offset within a patch buffer (16-byte units)
@@ -600,8 +608,8 @@ if constexpr (AMODE == A_ROWS) {
           ptx::tc_fence_after();
           // (stages filled by TMA are async-proxy writes already; the gather
           // producers fence their cp.async writes before arriving)
-          const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * NPLANE * A_BYTES);
-          const uint32_t b_addr = ptx::smem_u32(NKBR ? sB + (size_t)kb * B_BYTES : sB + (size_t)s * NPLANE * B_BYTES);
+          const uint32_t a_addr = ptx::smem_u32(sA + (size_t)s * PL * A_BYTES);
+          const uint32_t b_addr = ptx::smem_u32(NKBR ? sB + (size_t)kb * B_BYTES : sB + (size_t)s * PL * B_BYTES);
 #pragma unroll
           for (int k = 0; k < Cfg::SLAB / 32; ++k) {
             const uint32_t koff = k * 32;
@@ -619,6 +627,10 @@ if constexpr (AMODE == A_ROWS) {
               // stage descriptors plus the K offset (16-byte units)
               ptx::mma_i8(d_tmem, ptx::umma_desc_sw<KB>(a_addr) + (uint64_t)(koff >> 4),
                           ptx::umma_desc_sw<KB>(b_addr) + (uint64_t)(koff >> 4), idesc, (kb | k) != 0);
+            } else if constexpr (NPLANE >= 3) {
+              // one 16-bit plane: one exact product per multiply-add
+              ptx::mma_f16(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff), ptx::umma_desc_sw<KB>(b_addr + koff), idesc,
+                           (kb | k) != 0);
             } else {
               // hi*hi, hi*lo, lo*hi
               ptx::mma_f16(d_tmem, ptx::umma_desc_sw<KB>(a_addr + koff), ptx::umma_desc_sw<KB>(b_addr + koff), idesc,
@@ -668,7 +680,7 @@ if constexpr (AMODE == A_ROWS) {
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           const bool ok = __all_sync(0xffffffffu, ptx::mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag));
           if (!ok) { fail(ST_TIMEOUT_EMPTY); aborted = true; break; }
-          uint8_t* const row_dst = row_dst0 + (size_t)s * NPLANE * A_BYTES;
+          uint8_t* const row_dst = row_dst0 + (size_t)s * PL * A_BYTES;
           int kbyte = kb * BKB;
           int tap = kbyte / g.cbytes;
           int cc = kbyte - tap * g.cbytes;

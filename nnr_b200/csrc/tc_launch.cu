@@ -132,6 +132,13 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
     }
     return set_error(NNRCU_ERR_INVALID, "no 64-byte-slab engine instance for amode %d epilogue %d", L.amode, L.epi);
   }
+  if (L.nplane == 3 || L.nplane == 4) {
+    // one bf16 (3) or fp16 (4) plane: 2-D TMA or gathered A, fp32 epilogue
+    if (L.epi != EPI_F32) return set_error(NNRCU_ERR_INVALID, "16-bit engine needs the fp32 epilogue");
+    if (L.nplane == 3)
+      return L.amode == A_TMA ? launch_one<BN, 3, A_TMA, EPI_F32>(L, g, e, st) : launch_one<BN, 3, A_GATHER, EPI_F32>(L, g, e, st);
+    return L.amode == A_TMA ? launch_one<BN, 4, A_TMA, EPI_F32>(L, g, e, st) : launch_one<BN, 4, A_GATHER, EPI_F32>(L, g, e, st);
+  }
   if (L.nplane == 2) {
     if (L.epi != EPI_F32) return set_error(NNRCU_ERR_INVALID, "split-bf16 engine needs the fp32 epilogue");
     if (L.amode == A_TMA) return launch_one<BN, 2, A_TMA, EPI_F32>(L, g, e, st);

@@ -246,3 +246,33 @@ def gap_f32(shape) -> bytes:
     g.node("GlobalAveragePool", ["x"], ["y"])
     g.output("y", P.FLOAT, (shape[0], shape[1], 1, 1))
     return g.model()
+
+
+def conv_half(x_shape, w_bits, b_bits, elem_type, strides=(1, 1), pads=(0, 0, 0, 0), post=None) -> bytes:
+    """x -> Conv [-> Relu] -> y on 16-bit tensors (elem_type FLOAT16 or
+    BFLOAT16; weights and bias given as uint16 bit patterns)."""
+    g = P.Graph("conv16")
+    g.input("x", elem_type, x_shape)
+    ins = ["x", g.init("w", np.asarray(w_bits, np.uint16), elem_type)]
+    if b_bits is not None:
+        ins.append(g.init("b", np.asarray(b_bits, np.uint16), elem_type))
+    kh, kw = w_bits.shape[2], w_bits.shape[3]
+    n, oc = x_shape[0], w_bits.shape[0]
+    oh = (x_shape[2] + pads[0] + pads[2] - kh) // strides[0] + 1
+    ow = (x_shape[3] + pads[1] + pads[3] - kw) // strides[1] + 1
+    y = g.node("Conv", ins, ["t" if post else "y"], kernel_shape=[kh, kw], strides=list(strides), pads=list(pads))
+    if post:
+        g.node(post, [y], ["y"])
+    g.output("y", elem_type, (n, oc, oh, ow))
+    return g.model()
+
+
+def gemm_half(m, k, n, b_bits, c_bits, elem_type, beta=1.0, trans_b=0) -> bytes:
+    g = P.Graph("gemm16")
+    g.input("a", elem_type, (m, k))
+    ins = ["a", g.init("B", np.asarray(b_bits, np.uint16), elem_type)]
+    if c_bits is not None:
+        ins.append(g.init("C", np.asarray(c_bits, np.uint16), elem_type))
+    g.node("Gemm", ins, ["y"], beta=float(beta), transB=int(trans_b))
+    g.output("y", elem_type, (m, n))
+    return g.model()

@@ -17,9 +17,9 @@ from typing import Dict, List, Sequence
 import numpy as np
 
 # TensorProto.DataType
-FLOAT, UINT8, INT8, INT32, INT64 = 1, 2, 3, 6, 7
+FLOAT, UINT8, INT8, INT32, INT64, FLOAT16, BFLOAT16 = 1, 2, 3, 6, 7, 10, 16
 _NP = {np.dtype(np.float32): FLOAT, np.dtype(np.uint8): UINT8, np.dtype(np.int8): INT8,
-       np.dtype(np.int32): INT32, np.dtype(np.int64): INT64}
+       np.dtype(np.int32): INT32, np.dtype(np.int64): INT64, np.dtype(np.float16): FLOAT16}
 # AttributeProto.AttributeType
 A_FLOAT, A_INT, A_STRING, A_FLOATS, A_INTS = 1, 2, 3, 6, 7
 
@@ -57,11 +57,12 @@ def _f32(fn: int, v: float) -> bytes:
     return _key(fn, 5) + struct.pack("<f", float(v))
 
 
-def tensor(name: str, arr: np.ndarray) -> bytes:
+def tensor(name: str, arr: np.ndarray, data_type: int = 0) -> bytes:
+    """data_type overrides the element type (BFLOAT16 for uint16 bit patterns)."""
     arr = np.ascontiguousarray(arr)
     dims = b"".join(_varint(int(d)) for d in arr.shape)
     out = _bytes(1, dims) if arr.ndim else b""
-    return out + _vint(2, _NP[arr.dtype]) + _str(8, name) + _bytes(9, arr.tobytes())
+    return out + _vint(2, data_type or _NP[arr.dtype]) + _str(8, name) + _bytes(9, arr.tobytes())
 
 
 def value_info(name: str, elem_type: int, shape: Sequence[int]) -> bytes:
@@ -103,8 +104,8 @@ class Graph:
         self.nodes.append(b)
         return outs[0]
 
-    def init(self, name: str, arr: np.ndarray) -> str:
-        self.inits.append(tensor(name, arr))
+    def init(self, name: str, arr: np.ndarray, data_type: int = 0) -> str:
+        self.inits.append(tensor(name, arr, data_type))
         return name
 
     def scalar(self, arr) -> str:

@@ -265,7 +265,9 @@ class Gemm(Operator):
     op_type = "Gemm"
 
     def __init__(self, m, b: np.ndarray, c=None, alpha=1.0, beta=1.0, trans_a=0, trans_b=0, post=None, post_a=0.0,
-                 post_b=0.0):
+                 post_b=0.0, precision: int = 0):
+        """precision: PREC_SPLIT_BF16 (fp32 emulation) or PREC_BF16 (nnr's
+        fp32 MatMul on AVX-512 BF16 hosts: bf16-rounded operands)."""
         super().__init__()
         b = np.ascontiguousarray(b, dtype=np.float32)
         n, k = (b.shape[0], b.shape[1]) if trans_b else (b.shape[1], b.shape[0])
@@ -276,9 +278,9 @@ class Gemm(Operator):
             c_rows = 1 if c_arr.size == n else (self.m if c_arr.size == self.m * n else -1)
             if c_rows < 0:
                 raise ValueError("Gemm C must be [n] or [m, n]")
-        call("nnrcu_gemm_f32_create", self.m, self.n, self.k, int(trans_a), int(trans_b), float(alpha), float(beta),
+        call("nnrcu_gemm_f32_create_ex", self.m, self.n, self.k, int(trans_a), int(trans_b), float(alpha), float(beta),
              b.ctypes.data_as(C.c_void_p), c_p, c_rows, _POSTS[post] if not isinstance(post, int) else post,
-             float(post_a), float(post_b), C.byref(self._op))
+             float(post_a), float(post_b), int(precision), C.byref(self._op))
 
     def exec(self, a, y=None, workspace=None, stream=None):
         if y is None:
@@ -293,5 +295,76 @@ class MatMul(Gemm):
     (MatMul.cpp:156-172)."""
     op_type = "MatMul"
 
-    def __init__(self, m, b: np.ndarray, post=None, post_a=0.0, post_b=0.0):
-        super().__init__(m, b, None, 1.0, 0.0, 0, 0, post, post_a, post_b)
+    def __init__(self, m, b: np.ndarray, post=None, post_a=0.0, post_b=0.0, precision: int = 0):
+        super().__init__(m, b, None, 1.0, 0.0, 0, 0, post, post_a, post_b, precision)
+
+
+PREC_SPLIT_BF16, PREC_BF16 = 0, 1
+DT_BF16, DT_F16 = 1, 2
+_HALF_TORCH = {DT_BF16: "bfloat16", DT_F16: "float16"}
+
+
+def _bits16(arr, dtype):
+    """Raw 16-bit values of a torch bf16/fp16 tensor or a numpy array
+    (float16, or uint16 bit patterns)."""
+    if arr is None:
+        return None
+    if isinstance(arr, torch.Tensor):
+        return arr.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    a = np.asarray(arr)
+    return np.ascontiguousarray(a.view(np.uint16) if a.dtype == np.float16 else a.astype(np.uint16))
+
+
+class ConvHalf(Operator):
+    """ONNX Conv on bf16 or fp16 tensors (nnr's 16-bit I/O path,
+    Conv_exec_entry.h:188-381): w and bias of the same type."""
+    op_type = "Conv"
+
+    def __init__(self, x_shape, w, bias=None, dtype=DT_BF16, strides=(1, 1), pads=(0, 0, 0, 0), dilations=(1, 1),
+                 in_layout="NCHW", out_layout="NCHW", post=None, post_a=0.0, post_b=0.0):
+        super().__init__()
+        wb = _bits16(w, dtype)
+        self.dtype = dtype
+        self.x_shape = tuple(int(v) for v in x_shape)
+        self.desc = conv_desc(self.x_shape, wb.shape, strides, pads, dilations, 1, in_layout, out_layout,
+                              post, post_a, post_b, 0)
+        bb = _bits16(bias, dtype)
+        call("nnrcu_conv_half_create", C.byref(self.desc), int(dtype), wb.ctypes.data_as(C.c_void_p),
+             None if bb is None else bb.ctypes.data_as(C.c_void_p), C.byref(self._op))
+        self._keep = (wb, bb)
+        n, c, h, wd = self.x_shape
+        oh, ow = conv_out_hw(h, wd, wb.shape[2], wb.shape[3], tuple(strides), tuple(pads), tuple(dilations))
+        oc = wb.shape[0]
+        self.y_shape = (n, oc, oh, ow) if out_layout == "NCHW" else (n, oh, ow, oc)
+
+    def exec(self, x, y=None, workspace=None, stream=None):
+        if y is None:
+            y = torch.empty(self.y_shape, dtype=getattr(torch, _HALF_TORCH[self.dtype]), device=x.device)
+        ws, ws_p = self._workspace(workspace, x.device)
+        call("nnrcu_conv_half_run", self._op, _ptr(x), _ptr(y), ws_p, C.c_void_p(_stream(stream)))
+        return y
+
+
+class GemmHalf(Operator):
+    """ONNX Gemm on bf16 or fp16 tensors with a constant B (Gemm.cpp:297-513)."""
+    op_type = "Gemm"
+
+    def __init__(self, m, b, c=None, dtype=DT_BF16, beta=1.0, trans_a=0, trans_b=0, post=None, post_a=0.0,
+                 post_b=0.0):
+        super().__init__()
+        bb = _bits16(b, dtype)
+        n, k = (bb.shape[0], bb.shape[1]) if trans_b else (bb.shape[1], bb.shape[0])
+        self.m, self.n, self.k, self.dtype = int(m), int(n), int(k), dtype
+        cb = _bits16(c, dtype)
+        c_rows = 0 if cb is None else (1 if cb.size == n else self.m)
+        call("nnrcu_gemm_half_create", self.m, self.n, self.k, int(trans_a), int(trans_b), 1.0, float(beta), int(dtype),
+             bb.ctypes.data_as(C.c_void_p), None if cb is None else cb.ctypes.data_as(C.c_void_p), c_rows,
+             _POSTS[post] if not isinstance(post, int) else post, float(post_a), float(post_b), C.byref(self._op))
+        self._keep = (bb, cb)
+
+    def exec(self, a, y=None, workspace=None, stream=None):
+        if y is None:
+            y = torch.empty((self.m, self.n), dtype=getattr(torch, _HALF_TORCH[self.dtype]), device=a.device)
+        ws, ws_p = self._workspace(workspace, a.device)
+        call("nnrcu_gemm_half_run", self._op, _ptr(a), _ptr(y), ws_p, C.c_void_p(_stream(stream)))
+        return y

@@ -17,7 +17,8 @@ import numpy as np
 LIB = Path(__file__).resolve().parent / "_ref" / "libnnr_cpu.so"
 
 # nnr data_type_t (nnr.h:21-58) -> numpy
-_DT = {1: np.float32, 2: np.float64, 5: np.int8, 7: np.int32, 8: np.int64, 9: np.uint8}
+_DT = {1: np.float32, 2: np.float64, 3: np.uint16, 4: np.uint16, 5: np.int8, 7: np.int32, 8: np.int64, 9: np.uint8}
+# (FLOAT16 and BFLOAT16 tensors are returned as their uint16 bit patterns)
 NHWC, BLOCKED_16 = 1, 3  # memory_layout_t
 
 _lib = None

@@ -49,7 +49,29 @@ CASES = {
     "gemm_bias": ("gemm", dict(m=64, k=96, n=80, c="row")),
     "gemm_trans_alpha_beta": ("gemm", dict(m=33, k=40, n=50, ta=1, tb=1, alpha=0.5, beta=2.0, c="full")),
     "matmul_batched": ("matmul", dict(a=[3, 17, 24], n=40)),
+    # 16-bit I/O (nnr converts to fp32, computes, rounds back): within one
+    # unit in the last place of the 16-bit result
+    "conv_bf16_relu": ("conv16", dict(x=[2, 16, 9, 9], oc=24, k=3, p=1, et=16, post="Relu")),
+    "conv_f16": ("conv16", dict(x=[1, 32, 8, 8], oc=16, k=1, p=0, et=10, post=None)),
+    "gemm_bf16": ("gemm16", dict(m=33, k=40, n=50, et=16)),
+    "gemm_f16": ("gemm16", dict(m=20, k=72, n=30, et=10)),
 }
+
+
+def to_bits16(x, et):
+    """fp32 -> bf16 (et 16, nearest even) or fp16 (et 10) bit patterns."""
+    x = np.ascontiguousarray(x, np.float32)
+    if et == 10:
+        return x.astype(np.float16).view(np.uint16)
+    u = x.view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def bits16_to_f32(b, et):
+    b = np.ascontiguousarray(b, np.uint16)
+    if et == 10:
+        return b.view(np.float16).astype(np.float32)
+    return (b.astype(np.uint32) << 16).view(np.float32)
 
 
 def inputs_for(name, kind, p):
@@ -86,6 +108,15 @@ def inputs_for(name, kind, p):
     if kind == "matmul":
         return {"a": rng.normal(0, 1, p["a"]).astype(f32),
                 "B": rng.normal(0, 0.1, (p["a"][-1], p["n"])).astype(f32)}
+    if kind == "conv16":
+        c = p["x"][1]
+        return {"x": to_bits16(rng.uniform(-1, 1, p["x"]), p["et"]),
+                "w": to_bits16(rng.normal(0, 0.2, (p["oc"], c, p["k"], p["k"])), p["et"]),
+                "b": to_bits16(rng.normal(0, 0.1, p["oc"]), p["et"])}
+    if kind == "gemm16":
+        return {"a": to_bits16(rng.normal(0, 1, (p["m"], p["k"])), p["et"]),
+                "B": to_bits16(rng.normal(0, 0.1, (p["k"], p["n"])), p["et"]),
+                "C": to_bits16(rng.normal(0, 0.1, p["n"]), p["et"])}
     raise ValueError(kind)
 
 
@@ -110,11 +141,16 @@ def model_for(kind, p, d) -> bytes:
                       trans_a=p.get("ta", 0), trans_b=p.get("tb", 0))
     if kind == "matmul":
         return M.matmul(p["a"], d["B"])
+    if kind == "conv16":
+        return M.conv_half(p["x"], d["w"], d["b"], p["et"], pads=(p["p"],) * 4, post=p["post"])
+    if kind == "gemm16":
+        return M.gemm_half(p["m"], p["k"], p["n"], d["B"], d["C"], p["et"])
     raise ValueError(kind)
 
 
 GRAPH_INPUTS = {"quantize": ["x"], "qlinearadd": ["a", "b"], "maxpool": ["x"], "dq_gap_q": ["x"],
-                "dequantize_add": ["x"], "conv": ["x", "r"], "gemm": ["a"], "matmul": ["a"]}
+                "dequantize_add": ["x"], "conv": ["x", "r"], "gemm": ["a"], "matmul": ["a"], "conv16": ["x"],
+                "gemm16": ["a"]}
 
 
 def run_nnr(name):

@@ -69,10 +69,32 @@ def oracle_for(kind, p, d):
         # the host has AVX-512 BF16 (the fixtures were made on one; the live
         # tests check it), where nnr computes fp32 MatMul as bf16 products
         return O.matmul_f32_bf16_host(d["a"], d["B"])
+    if kind in ("conv16", "gemm16"):
+        et = p["et"]
+        f = {k: G.bits16_to_f32(v, et) for k, v in d.items()}
+        if kind == "conv16":
+            ref = O.conv_f32(f["x"], f["w"], f["b"], pads=(p["p"],) * 4, post=POST[p["post"]])
+        else:
+            ref = O.gemm_f32(f["a"], f["B"], f["C"])
+        return G.to_bits16(ref, et)
     raise ValueError(kind)
 
 
-def check(kind, got, want, name):
+def ulp_close16(got_bits, want_bits, et):
+    """16-bit results within one unit in the last place (the fp32 sums before
+    the final rounding differ in order)."""
+    g = G.bits16_to_f32(got_bits, et).astype(np.float64)
+    w = G.bits16_to_f32(want_bits, et).astype(np.float64)
+    mant = 10 if et == 10 else 7
+    ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(w), 1e-30))) - mant)
+    return bool(np.all(np.abs(g - w) <= ulp * 1.0001 + 1e-30))
+
+
+def check(kind, got, want, name, p=None):
+    if kind in ("conv16", "gemm16"):
+        assert got.shape == want.shape
+        assert ulp_close16(got, want, p["et"]), f"{name}: 16-bit result off by more than one ulp"
+        return
     if got.dtype == np.uint8 or kind in ("dequantize_add",):
         assert got.shape == want.shape
         assert np.array_equal(got, want), f"{name}: {(got != want).sum()} of {want.size} differ from nnr"
@@ -91,7 +113,7 @@ def test_oracle_matches_nnr_fixture(path):
     p = json.loads(str(f["params"]))
     kind = p.pop("kind")
     d = {k: f[k] for k in f.files if k not in ("y", "params")}
-    check(kind, oracle_for(kind, p, d), f["y"], path.stem)
+    check(kind, oracle_for(kind, p, d), f["y"], path.stem, p)
 
 
 def host_has_bf16():
@@ -108,7 +130,7 @@ def test_oracle_matches_nnr_live(name):
     if kind == "matmul" and not host_has_bf16():
         pytest.skip("nnr's fp32 MatMul takes its bf16 path only on AVX-512 BF16 hosts")
     d, y = G.run_nnr(name)
-    check(kind, oracle_for(kind, p, d), y, name)
+    check(kind, oracle_for(kind, p, d), y, name, p)
 
 
 @live
