@@ -8,6 +8,7 @@
 #include <cstring>
 
 #include "backend/cpu/conv_shape.h"
+#include "cpu_features.h"
 #include "cuda_backend.h"
 
 namespace nnr::cuda {
@@ -17,6 +18,11 @@ namespace {
 constexpr uint8_t LAYOUT_DEVICE = LAYOUT_NCHW | LAYOUT_NHWC;
 
 int to_nnrcu(memory_layout_t l) { return l == memory_layout_t::NHWC ? NNRCU_LAYOUT_NHWC : NNRCU_LAYOUT_NCHW; }
+
+// 16-bit tensors: the nnrcu dtype, or 0 for other types
+int half_dtype(data_type_t t) {
+  return t == NNR_DATA_TYPE_BFLOAT16 ? NNRCU_DT_BF16 : (t == NNR_DATA_TYPE_FLOAT16 ? NNRCU_DT_F16 : 0);
+}
 
 bool is_const_tensor(context_t* ctx, const tensor_t* t) {
   if (!t) return false;
@@ -205,10 +211,12 @@ struct QLinearConv_cuda : cuda_op_t {
   }
 };
 
-// ------------------------------------------------------------------ fp32 Conv
+// ------------------------------------------------------------------ Conv (fp32, bf16, fp16)
 // Conv_operator (backend/cpu/Conv.cpp, Conv_reshape.h:17-380,
-// Conv_exec.h:1163-1192): dense convs as split-bf16 on the tensor cores,
+// Conv_exec.h:1163-1192): fp32 dense convs as split-bf16 on the tensor cores,
 // depthwise on CUDA cores; bias and the fused post-op in the epilogue.
+// bf16 / fp16 tensors (Conv_exec_entry.h:188-381: convert, fp32 conv, round
+// back) run on one 16-bit plane (dense convs only).
 struct Conv_cuda : cuda_op_t {
   conv_attrs_t a;
   int cpads[4] = {};
@@ -234,8 +242,11 @@ struct Conv_cuda : cuda_op_t {
     return device_layout_cost(layout, 4.0f * x->ndata, 4.0f * w->ndata, 4.0f * y->ndata);
   }
   bool device_ok() const override {
-    return inputs[0]->type == NNR_DATA_TYPE_FLOAT32 && inputs[0]->ndim == 4 && is_const_tensor(ctx, inputs[1]) &&
-           (inputs.size() < 3 || !inputs[2] || is_const_tensor(ctx, inputs[2]));
+    const data_type_t t = inputs[0]->type;
+    const bool half = half_dtype(t) != 0;
+    if (!(t == NNR_DATA_TYPE_FLOAT32 || (half && a.group == 1))) return false;
+    return inputs[0]->ndim == 4 && inputs[1]->type == t && is_const_tensor(ctx, inputs[1]) &&
+           (inputs.size() < 3 || !inputs[2] || (is_const_tensor(ctx, inputs[2]) && inputs[2]->type == t));
   }
   bool prepare_device(device_state_t& s) override {
     tensor_t *x = inputs[0], *w = inputs[1], *y = outputs[0];
@@ -247,25 +258,37 @@ struct Conv_cuda : cuda_op_t {
       return s.fail("Conv: fused post-op %.*s has no device epilogue", (int)fused_op->op_type.size(),
                     fused_op->op_type.data());
     h.reset();
-    if (!nnrcu_ok(s, nnrcu_conv_f32_create(&d, (const float*)w->data, b ? (const float*)b->data : nullptr, &h.op),
-                  "Conv"))
-      return false;
+    dtype = half_dtype(x->type);
+    const int rc = dtype ? nnrcu_conv_half_create(&d, dtype, (const uint16_t*)w->data,
+                                                  b ? (const uint16_t*)b->data : nullptr, &h.op)
+                         : nnrcu_conv_f32_create(&d, (const float*)w->data, b ? (const float*)b->data : nullptr, &h.op);
+    if (!nnrcu_ok(s, rc, "Conv")) return false;
     set_out_layout(s, y, y->format);
     return true;
   }
   size_t device_workspace() const override { return h.ws(); }
   bool run_device(device_state_t& s, void* stream) override {
+    if (dtype)
+      return nnrcu_ok(s,
+                      nnrcu_conv_half_run(h.op, (const uint16_t*)s.dev(inputs[0]), (uint16_t*)s.dev(outputs[0]),
+                                          s.workspace, stream),
+                      "Conv");
     return nnrcu_ok(s,
                     nnrcu_conv_f32_run(h.op, (const float*)s.dev(inputs[0]), (float*)s.dev(outputs[0]), nullptr,
                                        s.workspace, stream),
                     "Conv");
   }
+  int dtype = 0;
 };
 
-// ------------------------------------------------------------------ Gemm / MatMul (fp32)
+// ------------------------------------------------------------------ Gemm / MatMul (fp32, bf16, fp16)
 // Gemm_operator (backend/cpu/Gemm.cpp:40-294) with B (and C) initializers;
 // MatMul_operator (backend/cpu/MatMul.cpp:13-228) with a constant 2-D B, the
-// leading dims of A folded into M (:156-172).
+// leading dims of A folded into M (:156-172). bf16 / fp16 Gemm/MatMul run on
+// one 16-bit plane (Gemm.cpp:297-513; alpha 1). An fp32 MatMul follows the
+// precision nnr's own dispatch gives it on this host: with AVX-512 BF16 and a
+// constant B, bf16-rounded operands (MatMul.cpp:128-152, :424-428), else
+// fp32 (split-bf16). Unlike that nnr path, a fused post-op is applied.
 struct Gemm_cuda : cuda_op_t {
   bool matmul = false;
   float alpha = 1.0f, beta = 1.0f;
@@ -307,8 +330,13 @@ struct Gemm_cuda : cuda_op_t {
   }
   int64_t num_ops() const override { return 2LL * M * N * K; }
   bool device_ok() const override {
-    if (inputs[0]->type != NNR_DATA_TYPE_FLOAT32 || !is_const_tensor(ctx, inputs[1])) return false;
-    if (!matmul && inputs.size() > 2 && inputs[2] && !is_const_tensor(ctx, inputs[2])) return false;
+    const data_type_t t = inputs[0]->type;
+    const bool half = half_dtype(t) != 0;
+    if (!(t == NNR_DATA_TYPE_FLOAT32 || (half && alpha == 1.0f && !trans_a)) || inputs[1]->type != t ||
+        !is_const_tensor(ctx, inputs[1]))
+      return false;
+    if (!matmul && inputs.size() > 2 && inputs[2] && (!is_const_tensor(ctx, inputs[2]) || inputs[2]->type != t))
+      return false;
     return true;
   }
   bool prepare_device(device_state_t& s) override {
@@ -316,7 +344,7 @@ struct Gemm_cuda : cuda_op_t {
     std::vector<float> crow;
     const float* c = nullptr;
     int c_rows = 0;
-    if (C && C->ndata > 0) {
+    if (C && C->ndata > 0 && !half_dtype(inputs[0]->type)) {  // (16-bit C is handled below)
       if (C->ndata == (size_t)N) {
         c = (const float*)C->data, c_rows = 1;
       } else if (C->ndata == (size_t)M * N) {
@@ -332,9 +360,25 @@ struct Gemm_cuda : cuda_op_t {
     float pa = 0, pb = 0;
     if (!post_op_of(this, &post, &pa, &pb)) return s.fail("Gemm/MatMul: fused post-op has no device epilogue");
     h.reset();
+    dtype = half_dtype(inputs[0]->type);
+    if (dtype) {
+      const tensor_t* Ch = !matmul && inputs.size() > 2 ? inputs[2] : nullptr;
+      int rows = 0;
+      if (Ch && Ch->ndata > 0) rows = Ch->ndata == (size_t)N ? 1 : (Ch->ndata == (size_t)M * N ? M : -1);
+      if (rows < 0) return s.fail("Gemm: 16-bit C must be a [n] row or a full [m, n] matrix");
+      if (!nnrcu_ok(s,
+                    nnrcu_gemm_half_create(M, N, K, trans_a, trans_b, 1.0f, rows ? beta : 0.0f, dtype,
+                                           (const uint16_t*)inputs[1]->data,
+                                           rows ? (const uint16_t*)Ch->data : nullptr, rows, post, pa, pb, &h.op),
+                    "Gemm"))
+        return false;
+      set_out_layout(s, outputs[0], memory_layout_t::NCHW);
+      return true;
+    }
+    const int prec = matmul && has_avx512_bf16() ? NNRCU_PREC_BF16 : NNRCU_PREC_SPLIT_BF16;
     if (!nnrcu_ok(s,
-                  nnrcu_gemm_f32_create(M, N, K, trans_a, trans_b, alpha, c ? beta : 0.0f,
-                                        (const float*)inputs[1]->data, c, c_rows, post, pa, pb, &h.op),
+                  nnrcu_gemm_f32_create_ex(M, N, K, trans_a, trans_b, alpha, c ? beta : 0.0f,
+                                           (const float*)inputs[1]->data, c, c_rows, post, pa, pb, prec, &h.op),
                   "Gemm"))
       return false;
     set_out_layout(s, outputs[0], memory_layout_t::NCHW);
@@ -342,11 +386,17 @@ struct Gemm_cuda : cuda_op_t {
   }
   size_t device_workspace() const override { return h.ws(); }
   bool run_device(device_state_t& s, void* stream) override {
+    if (dtype)
+      return nnrcu_ok(s,
+                      nnrcu_gemm_half_run(h.op, (const uint16_t*)s.dev(inputs[0]), (uint16_t*)s.dev(outputs[0]),
+                                          s.workspace, stream),
+                      "Gemm");
     return nnrcu_ok(s,
                     nnrcu_gemm_f32_run(h.op, (const float*)s.dev(inputs[0]), (float*)s.dev(outputs[0]),
                                        s.workspace, stream),
                     "Gemm");
   }
+  int dtype = 0;
 };
 
 // ------------------------------------------------------------------ QLinearMatMul

@@ -19,7 +19,8 @@ from pathlib import Path
 import numpy as np
 
 LIB = Path(__file__).resolve().parent / "nnr_backend" / "libnnr_cuda.so"
-_DT = {1: np.float32, 2: np.float64, 5: np.int8, 7: np.int32, 8: np.int64, 9: np.uint8}
+_DT = {1: np.float32, 2: np.float64, 3: np.uint16, 4: np.uint16, 5: np.int8, 7: np.int32, 8: np.int64, 9: np.uint8}
+# (FLOAT16 and BFLOAT16 tensors are returned as their uint16 bit patterns)
 NCHW, NHWC = 0, 1
 STATS = ("runs", "graph_replays", "h2d_bytes", "d2h_bytes", "device_ops", "host_ops", "host_glue",
          "arena_bytes", "const_bytes", "slots")

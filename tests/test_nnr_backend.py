@@ -162,3 +162,49 @@ def test_unsupported_variant_fails_loudly(cuda_dev):
         assert net.error()
     finally:
         net.close()
+
+
+@pytest.mark.gpu
+def test_16bit_and_matmul_through_nnr(cuda_dev):
+    """bf16 / fp16 Conv and Gemm graphs through nnr on the device (nnr's
+    16-bit paths: fp32 compute, rounded back; within one ulp of the oracle
+    plus fp32 summation error), and an fp32 MatMul that follows nnr's own
+    precision on this host (bf16-rounded operands with AVX-512 BF16)."""
+    import importlib.util
+    from pathlib import Path
+
+    from nnr_b200 import onnx_models as M
+    from oracle import oracle as O
+    spec = importlib.util.spec_from_file_location("g", Path(__file__).parent / "golden" / "make_nnr_golden.py")
+    G = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(G)
+    rng = np.random.default_rng(11)
+    for et in (16, 10):
+        xb = G.to_bits16(rng.uniform(-1, 1, (2, 32, 10, 10)), et)
+        wb = G.to_bits16(rng.normal(0, 0.2, (48, 32, 3, 3)), et)
+        bb = G.to_bits16(rng.normal(0, 0.1, 48), et)
+        net = NC.NnrCudaModel(M.conv_half(xb.shape, wb, bb, et, pads=(1, 1, 1, 1), post="Relu"))
+        try:
+            assert [o for o, s, f, dev, fmt in net.active() if not dev] == []
+            net.set("x", xb)
+            net.run()
+            got = G.bits16_to_f32(net.get("y").view(np.uint16), et)
+            f = {k: G.bits16_to_f32(v, et) for k, v in (("x", xb), ("w", wb), ("b", bb))}
+            ref = G.bits16_to_f32(G.to_bits16(O.conv_f32(f["x"], f["w"], f["b"], pads=(1, 1, 1, 1), post=1), et), et)
+            tol = np.exp2(np.floor(np.log2(np.maximum(np.abs(ref), 1e-30))) - (10 if et == 10 else 7))
+            absum = O.conv_f32(np.abs(f["x"]), np.abs(f["w"]), np.abs(f["b"]), pads=(1, 1, 1, 1))
+            assert np.all(np.abs(got - ref) <= tol * 1.0001 + 1e-5 * absum)
+        finally:
+            net.close()
+    a = rng.normal(0, 1, (40, 96)).astype(np.float32)
+    b = rng.normal(0, 0.1, (96, 70)).astype(np.float32)
+    net = NC.NnrCudaModel(M.matmul(a.shape, b))
+    try:
+        net.set("a", a)
+        net.run()
+        got = net.get("y")
+        want = O.matmul_f32_bf16_host(a, b) if "avx512_bf16" in Path("/proc/cpuinfo").read_text() \
+            else O.gemm_f32(a, b, None, beta=0.0)
+        assert rel(got, want) <= 1e-5
+    finally:
+        net.close()
