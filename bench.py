@@ -34,9 +34,11 @@ one captured CUDA graph.
   qlinearconv_config2  BASELINE config 2 (one QLinearConv layer, NCHW in/out,
             requant R1): operator and kernel TOPS.
 
---impl reference runs nnr's int8 path on the host cores: the C restatement of
-its operators (nnr's int8 kernels need the absent Xbyak JIT and cannot be
-built here), one image of the batch per step.
+--impl reference runs nnr's own CPU runtime (compiled from its sources into
+oracle/_ref) on the same QDQ graph at batch 32 on all host threads. nnr's int8
+QLinearConv/QLinearMatMul need the absent Xbyak JIT, so nnr runs the QDQ convs
+on its fake-quant float path; without the runtime it falls back to the C
+restatement of nnr's int8 operators.
 """
 from __future__ import annotations
 
@@ -201,26 +203,112 @@ def cpu_forward_fn(model, images):
     return (lambda: O.run_qmodel(model, x)), O.num_threads()
 
 
+NNR_SAMPLE_NOTE = ("nnr's own loader, graph passes and run loop (oracle/_ref/libnnr_cpu.so, compiled from the nnr "
+                   "sources) on the config-4 QDQ ONNX graph. nnr's int8 QLinearConv/QLinearMatMul need the absent "
+                   "Xbyak JIT, so its QDQ convs run as DequantizeLinear -> fp32 Conv -> QuantizeLinear (nnr's "
+                   "fake-quant float path) and the residual adds as QLinearAdd. Memory planner and nChw16c layout "
+                   "off: with them on nnr is slower and its logits are wrong on this graph.")
+
+
+def nnr_cpu_forward_fn(model, batch):
+    """One forward of nnr's own CPU runtime on the config-4 QDQ graph, or None
+    when the runtime was not built."""
+    from nnr_b200 import onnx_models, resnet50
+    from oracle import nnr_ref as R
+    if not R.available():
+        return None
+    R.set_threads(cpu_threads())
+    net = R.NnrModel(onnx_models.resnet50_qdq(model), memory_planning=False, no_blocked=True)
+    net.set("input", resnet50.input_batch(0, batch))
+
+    def fn():
+        net.run()
+    return fn
+
+
 def cpu_baseline(model, seconds=10.0):
-    fn, cores = cpu_forward_fn(model, 1)
-    fn()
-    n, t0 = 0, time.perf_counter()
-    while time.perf_counter() - t0 < seconds:
+    """The reference CPU timing beside the GPU line: nnr's own runtime on a
+    bounded sample (4 images per forward, about `seconds` of CPU work), and
+    the C restatement of nnr's int8 operators as a second figure."""
+    from nnr_b200 import resnet50
+    out = {}
+    fn = nnr_cpu_forward_fn(resnet50.build(batch=4), 4)
+    if fn is not None:
         fn()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            fn()
+            n += 1
+        dt = (time.perf_counter() - t0) / n
+        out = {"value": round(4.0 / dt, 3), "unit": UNIT, "cores": cpu_threads(), "kind": "reference",
+               "sample": f"4 images per forward x {n} forwards ({dt * 1000:.0f} ms each). " + NNR_SAMPLE_NOTE}
+    pfn, cores = cpu_forward_fn(model, 1)
+    pfn()
+    n, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < seconds / 2:
+        pfn()
         n += 1
     dt = (time.perf_counter() - t0) / n
-    return {"value": round(1.0 / dt, 3), "unit": UNIT, "cores": cores, "kind": "port",
+    port = {"value": round(1.0 / dt, 3), "unit": UNIT, "cores": cores, "kind": "port",
             "sample": f"1 image per forward x {n} forwards ({dt * 1000:.0f} ms each): the C restatement of nnr's "
-                      "int8 operators (nnr's own int8 kernels need the absent Xbyak JIT)",
-            "cpu": host_cpu_info()}
+                      "int8 operators (the oracle), exact int8 arithmetic"}
+    if not out:
+        out = port
+    else:
+        out["port"] = port
+    out["cpu"] = host_cpu_info()
+    return out
+
+
+def nnr_cpu_other_configs(seconds=3.0):
+    """nnr's own CPU runtime on BASELINE configs 1, 3 (fp32 Gemm) and 5
+    (MobileNetV2, an 8-image sample; memory planner and nChw16c layout off,
+    as nnr's logits are wrong with them on), all host threads: the CPU
+    figures beside the GPU operator timings."""
+    from nnr_b200 import mobilenetv2, onnx_models as M, workloads as W
+    from oracle import nnr_ref as R
+    if not R.available():
+        return None
+    R.set_threads(cpu_threads())
+
+    def timed(net):
+        net.run()
+        n, t0 = 0, time.perf_counter()
+        while time.perf_counter() - t0 < seconds:
+            net.run()
+            n += 1
+        return (time.perf_counter() - t0) / n * 1e3
+    c1 = W.config1_conv_relu()
+    n1 = R.NnrModel(M.conv(c1.x.shape, c1.w, c1.bias, pads=c1.pads, post="Relu"))
+    n1.set("x", c1.x)
+    c3 = W.config3_matmul()
+    n3 = R.NnrModel(M.gemm(4096, 768, 3072, c3.b_f32, c3.c_f32))
+    n3.set("a", c3.a_f32)
+    mb = mobilenetv2.build(batch=8)
+    n5 = R.NnrModel(M.mobilenetv2(mb), memory_planning=False, no_blocked=True)
+    n5.set("input", mobilenetv2.input_batch(0, 8))
+    ms1, ms3, ms5 = timed(n1), timed(n3), timed(n5)
+    return {"cores": cpu_threads(), "kind": "reference",
+            "config1_conv_relu_ms": round(ms1, 4), "config3_gemm_fp32_ms": round(ms3, 3),
+            "config5_mobilenetv2_images_per_s": round(8 / ms5 * 1e3, 2),
+            "note": "nnr's CPU runtime compiled from its sources (oracle/_ref/libnnr_cpu.so)"}
 
 
 def reference_arm(args, rank, world):
+    """nnr's own CPU runtime on the GPU arm's config (batch 32 per step), all
+    host threads; the C restatement when the runtime was not built."""
     if rank != 0:
         return 0
     from nnr_b200 import resnet50
     model = resnet50.build(batch=BATCH)
-    fn, cores = cpu_forward_fn(model, 1)
+    fn = nnr_cpu_forward_fn(model, BATCH)
+    if fn is not None:
+        kind, cores, per_step = "reference", cpu_threads(), BATCH
+        sample = f"the whole batch of {BATCH} per step. " + NNR_SAMPLE_NOTE
+    else:
+        fn, cores = cpu_forward_fn(model, 1)
+        kind, per_step = "port", 1
+        sample = "1 image of the batch per step, C restatement of nnr's int8 operators on the host cores"
     for _ in range(args.warmup):
         fn()
     times = []
@@ -229,13 +317,13 @@ def reference_arm(args, rank, world):
         fn()
         times.append(time.perf_counter() - t0)
     ms = 1000 * sum(times) / len(times)
-    val = 1000.0 / ms
+    val = per_step * 1000.0 / ms
     line = {"metric": METRIC, "value": round(val, 3), "unit": UNIT, "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u8", "data": "synthetic (seeded numpy PCG64)",
-            "config": {"workload": WORKLOAD, "sample": "1 image of the batch per step"},
-            "cpu_baseline": {"value": round(val, 3), "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": "1 image per step, C restatement of nnr's int8 operators on the host cores",
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 (fake-quant)" if kind == "reference" else "u8",
+            "data": "synthetic (seeded numpy PCG64)",
+            "config": {"workload": WORKLOAD, "sample": sample},
+            "cpu_baseline": {"value": round(val, 3), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample,
                              "cpu": host_cpu_info()},
             "e2e": {"value": round(val, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -601,6 +689,8 @@ def main():
         }
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(model)
+            if rows is not None:
+                rows["cpu_nnr"] = nnr_cpu_other_configs()
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
