@@ -178,7 +178,11 @@ struct QLinearConv_cuda : cuda_op_t {
     return device_layout_cost(layout, (float)x->ndata, (float)w->ndata, (float)y->ndata);
   }
   bool device_ok() const override {
-    return inputs[0]->type == NNR_DATA_TYPE_UINT8 && inputs[3]->type == NNR_DATA_TYPE_INT8 && inputs[0]->ndim == 4;
+    // u8 activations, s8 weights, fp32 scales (s8 activations and other
+    // scale types are declined: nnr's arithmetic differs there)
+    return inputs[0]->type == NNR_DATA_TYPE_UINT8 && inputs[3]->type == NNR_DATA_TYPE_INT8 && inputs[0]->ndim == 4 &&
+           inputs[1]->type == NNR_DATA_TYPE_FLOAT32 && inputs[4]->type == NNR_DATA_TYPE_FLOAT32 &&
+           inputs[6]->type == NNR_DATA_TYPE_FLOAT32;
   }
   bool prepare_device(device_state_t& s) override {
     tensor_t *x = inputs[0], *w = inputs[3], *y = outputs[0];
@@ -425,8 +429,13 @@ struct QLinearMatMul_cuda : cuda_op_t {
   }
   int64_t num_ops() const override { return 2LL * M * N * K; }
   bool device_ok() const override {
+    // u8 output from u8 x s8 with fp32 scales: the R4 path. nnr computes the
+    // combined scale in fp16 for fp16 scales (QLinearMatMul.cpp:123-133) and
+    // has an s8-output branch (:185-196); both are declined.
     return inputs[0]->type == NNR_DATA_TYPE_UINT8 && inputs[3]->type == NNR_DATA_TYPE_INT8 &&
-           is_const_tensor(ctx, inputs[3]) && inputs[4]->ndata == 1;
+           is_const_tensor(ctx, inputs[3]) && inputs[4]->ndata == 1 && inputs[1]->type == NNR_DATA_TYPE_FLOAT32 &&
+           inputs[4]->type == NNR_DATA_TYPE_FLOAT32 && inputs[6]->type == NNR_DATA_TYPE_FLOAT32 &&
+           outputs[0]->type == NNR_DATA_TYPE_UINT8;
   }
   bool prepare_device(device_state_t& s) override {
     h.reset();

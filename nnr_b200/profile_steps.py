@@ -13,6 +13,12 @@
         replays the captured whole-network graph 3 times and nothing else
         (a target for an ncu launch list of one forward: skip the first 58
         launches, capture the next 58).
+
+    python -m nnr_b200.profile_steps --op gemm_f32 --repeat 3
+        launches one BASELINE operator alone (after one untimed launch):
+        gemm_f32 / qmatmul (config 3), conv_f32 (config 1), gemm_bf16 (the
+        config-3 shape on bf16 tensors), qdw (an int8 depthwise QLinearConv
+        over 32 x 56 x 56 x 144); prints its CUDA-event time per launch.
 """
 from __future__ import annotations
 
@@ -40,6 +46,53 @@ def step_ops(model, node_index: int) -> int:
     return 0
 
 
+def op_target(name: str, repeat: int) -> int:
+    """Launches one operator `repeat` times (plus one untimed launch first)
+    with inputs resident on cuda:0 and reports its time per launch."""
+    import numpy as np
+    import torch
+    from . import ops, workloads as W
+    ops.init(0)
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(0)
+    if name in ("gemm_f32", "qmatmul", "gemm_bf16"):
+        c3 = W.config3_matmul()
+        if name == "gemm_f32":
+            op, x = ops.Gemm(4096, c3.b_f32, c3.c_f32), torch.from_numpy(c3.a_f32).to(dev)
+        elif name == "qmatmul":
+            op = ops.QLinearMatMul(4096, c3.b_s8, c3.a_scale, c3.a_zp, c3.b_scale, c3.b_zp, c3.y_scale, c3.y_zp)
+            x = torch.from_numpy(c3.a_u8).to(dev)
+        else:
+            op = ops.GemmHalf(4096, torch.from_numpy(c3.b_f32).to(torch.bfloat16), torch.from_numpy(c3.c_f32).to(
+                torch.bfloat16), dtype=ops.DT_BF16)
+            x = torch.from_numpy(c3.a_f32).to(dev).to(torch.bfloat16)
+        flops = 2 * 4096 * 768 * 3072
+    elif name == "conv_f32":
+        c1 = W.config1_conv_relu()
+        op = ops.Conv(c1.x.shape, c1.w, c1.bias, pads=c1.pads, post="Relu")
+        x = torch.from_numpy(c1.x).to(dev)
+        flops = 2 * 64 * 56 * 56 * 64 * 9
+    else:
+        n, h, w, c = 32, 56, 56, 144
+        wt = rng.integers(-127, 128, (c, 1, 3, 3)).astype(np.int8)
+        op = ops.QLinearConv((n, c, h, w), wt, np.full(c, 0.005, np.float32), None, None, 0.02, 128, 0.4, 128,
+                             pads=(1, 1, 1, 1), group=c, in_layout="NHWC", out_layout="NHWC")
+        x = torch.from_numpy(rng.integers(0, 256, (n, h, w, c)).astype(np.uint8)).to(dev)
+        flops = 2 * n * h * w * c * 9
+    op.exec(x)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(repeat):
+        op.exec(x)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / repeat
+    print(json.dumps({"op": name, "us_per_launch": round(us, 2), "tops": round(flops / us / 1e6, 1),
+                      "status": ops.device_status()}))
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--model", default="resnet50", choices=["resnet50", "mobilenetv2"])
@@ -48,10 +101,13 @@ def main(argv=None) -> int:
     ap.add_argument("--repeat", type=int, default=3)
     ap.add_argument("--json", default=None)
     ap.add_argument("--forward", type=int, default=0, help="replay the whole forward graph this many times")
+    ap.add_argument("--op", default=None, choices=["gemm_f32", "qmatmul", "conv_f32", "gemm_bf16", "qdw"])
     a = ap.parse_args(argv)
 
     import torch
     from . import graph, resnet50
+    if a.op:
+        return op_target(a.op, a.repeat)
 
     if a.model == "resnet50":
         a.batch = a.batch or 32

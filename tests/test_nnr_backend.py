@@ -208,3 +208,28 @@ def test_16bit_and_matmul_through_nnr(cuda_dev):
         assert rel(got, want) <= 1e-5
     finally:
         net.close()
+
+
+@pytest.mark.gpu
+def test_s8_activation_qlinearconv_declined_loudly(cuda_dev):
+    """A QDQ Conv on s8 activations fuses to a QLinearConv that the device
+    does not implement (its requant and padding differ from the u8 path):
+    the run fails with a message instead of computing something else."""
+    from nnr_b200 import onnx_pb as P
+    g = P.Graph("qconv_s8")
+    g.input("x", P.INT8, (1, 8, 6, 6))
+    g.node("DequantizeLinear", ["x", g.scalar(np.float32(0.1)), g.scalar(np.int8(0))], ["xd"])
+    g.init("w", np.ones((8, 8, 3, 3), np.int8))
+    g.node("DequantizeLinear", ["w", g.scalar(np.float32(0.01)), g.scalar(np.int8(0))], ["wd"])
+    g.node("Conv", ["xd", "wd"], ["c"], kernel_shape=[3, 3], pads=[1, 1, 1, 1])
+    g.node("QuantizeLinear", ["c", g.scalar(np.float32(0.2)), g.scalar(np.int8(0))], ["y"])
+    g.output("y", P.INT8, (1, 8, 6, 6))
+    net = NC.NnrCudaModel(g.model())
+    try:
+        assert [n[0] for n in net.active()] == ["QLinearConv"]
+        net.set("x", np.zeros((1, 8, 6, 6), np.int8))
+        with pytest.raises(RuntimeError):
+            net.run()
+        assert "not supported on the device" in net.error()
+    finally:
+        net.close()
