@@ -298,6 +298,18 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t 
   }
 }
 
+// R3's scalar tail (the first-layer kernel's NCHW remainder pixels):
+// f = fma(float(acc), cs, bias_f); q = int(rne(f * inv_y)) + y_zp with the x86
+// conversion (out-of-range values become INT_MIN); integer clamp to [qmin, 255].
+__device__ __forceinline__ uint32_t requant_r3_tail(int32_t raw, int32_t ci, float f1, float f2, const EpiParams& e) {
+  const int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci);
+  const float f = __fmaf_rn(__int2float_rn(acc), f1, f2);
+  int32_t q = (int32_t)((uint32_t)ptx::cvt_rne_x86(__fmul_rn(f, e.inv_y)) + (uint32_t)e.yzp);
+  q = max(q, (int32_t)e.qmin_f);
+  q = min(q, (int32_t)e.qmax_f);
+  return (uint32_t)q;
+}
+
 // Low bytes of four words packed into one (byte j from word j).
 __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
@@ -851,6 +863,9 @@ if constexpr (AMODE == A_ROWS) {
       if (EPI == EPI_R4 && e.rowcorr && mvalid) rowc = e.rowcorr[m];
       int img = 0, pix = 0;
       if (e.y_layout == 1 && mvalid) { img = m / e.ohw; pix = m - img * e.ohw; }
+      // R3 with an NCHW output: the last OW % 16 pixels of each output row take
+      // the first-layer kernel's scalar tail sequence
+      const bool r3_tail = EPI == EPI_R3 && e.y_layout == 1 && mvalid && (pix % g.OW) >= (g.OW & ~15);
       int mst = m;  // row of the output buffer
       if (e.opad) {
         const int im = m / e.o_hw, r = m - im * e.o_hw, oy = r / e.o_w;
@@ -1015,6 +1030,10 @@ if constexpr (AMODE == A_ROWS) {
               q[j + 1] = requant_u8<EPI>((int32_t)v[j + 1], ci4.y, rowc, a4.y, b4.y, e);
               q[j + 2] = requant_u8<EPI>((int32_t)v[j + 2], ci4.z, rowc, a4.z, b4.z, e);
               q[j + 3] = requant_u8<EPI>((int32_t)v[j + 3], ci4.w, rowc, a4.w, b4.w, e);
+            }
+            if (EPI == EPI_R3 && r3_tail) {
+#pragma unroll
+              for (int j = 0; j < CW; ++j) q[j] = requant_r3_tail((int32_t)v[j], s_ci[pc + j], s_f1[pc + j], s_f2[pc + j], e);
             }
           }
           if (scalar_add) {

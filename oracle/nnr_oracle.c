@@ -11,7 +11,8 @@
  *     sequences, selected the way nnr's x64 VNNI dispatch selects them:
  *       R1 QLinearConv.cpp:616-646          (exec_direct_int8)
  *       R2 backend/x64/jit_conv_int8_ukernel.cpp:950-965 (packed NR48 / NR16)
- *       R3 backend/x64/conv_first_layer_int8_avx512.h:262-270 (stem)
+ *       R3 backend/x64/conv_first_layer_int8_avx512.h:262-270 (stem; NCHW
+ *          outputs use R1 for each row's last ow % 16 pixels, :301-309)
  *     with the constants of QLinearConv_reshape.h:287-337.
  *   - QLinearMatMul: exact int32 sum of (a - a_zp)(b - b_zp) and the R4
  *     requant of QLinearMatMul.cpp:134,188-198.
@@ -102,6 +103,19 @@ static inline uint8_t rq_r3(int32_t acc, float cs, float bias_f, float inv_y, fl
   return (uint8_t)(int32_t)nearbyintf(f);
 }
 
+/* R3's scalar tail: f = fma((float)acc, cs, bias_f); q = (int32)rne(f * inv_y)
+ * + y_zp (x86 conversion: out-of-range values become INT_MIN); clamp to
+ * [qmin, hi] in integers. (conv_first_layer_int8_avx512.h:301-309) */
+static inline uint8_t rq_r3_tail(int32_t acc, float cs, float bias_f, float inv_y, int32_t yzp, int32_t qmin,
+                                 int32_t qmax) {
+  const float r = nearbyintf(fmaf((float)acc, cs, bias_f) * inv_y);
+  int32_t q = (r >= -2147483648.0f && r < 2147483648.0f) ? (int32_t)r : INT32_MIN;
+  q = wrap_add(q, yzp);
+  if (q < qmin) q = qmin;
+  if (q > qmax) q = qmax;
+  return (uint8_t)q;
+}
+
 /*
  * QLinearConv, u8 x / s8 w / u8 y, group 1, w_zp = 0.
  * x: in_layout 0 = NCHW [n,c,h,w], 1 = NHWC [n,h,w,c]; y likewise per out_layout.
@@ -179,6 +193,11 @@ int oracle_qlinearconv(const uint8_t* x, int in_layout, int n, int c, int h, int
             q = rq_r1(acc, cs[o], bf[o], inv_y, (float)y_zp, (float)qmin, (float)hi);
           else if (formula == RQ_R2)
             q = rq_r2(acc, bias ? bias[o] : 0, os[o], rq_lo, rq_hi, y_zp);
+          else if (out_layout == 0 && ox >= ow / 16 * 16)
+            /* the first-layer kernel's NCHW scalar tail (the last ow % 16
+             * pixels of a row): f*cs+bs contracted, rne(f * inv_y) + y_zp,
+             * integer clamp (conv_first_layer_int8_avx512.h:301-309) */
+            q = rq_r3_tail(acc, cs[o], bf[o], inv_y, y_zp, qmin, hi);
           else
             q = rq_r3(acc, cs[o], bf[o], inv_y, (float)y_zp, (float)qmin, (float)hi);
           const size_t oi = out_layout == 1 ? ((size_t)p * oc + o)

@@ -55,6 +55,7 @@ def ref_lib():
     if _ref is None and REF.exists():
         _ref = C.CDLL(str(REF))
         _ref.ref_qlinearconv_direct.restype = C.c_int
+        _ref.ref_qconv_first_layer.restype = C.c_int
         _ref.ref_has_vnni.restype = C.c_int
         _ref.ref_get_threads.restype = C.c_int
     return _ref
@@ -173,6 +174,29 @@ def ref_qlinearconv_direct(x, w, w_scale, bias, x_scale, x_zp, y_scale, y_zp, st
     if rc != 0:
         return None
     return (y, raw) if want_raw else y
+
+
+def ref_qconv_first_layer(x, w, w_scale, bias, x_scale, x_zp, y_scale, y_zp, strides=(1, 1), pads=(0, 0),
+                          has_post=False, out_layout="NCHW"):
+    """nnr's first-layer int8 conv (the R3 stem kernel, its own AVX-512 VNNI
+    code) on NCHW u8 input with at most 4 channels and symmetric pads
+    (pad_h, pad_w). Returns None when the harness is absent or the host lacks
+    VNNI."""
+    r = ref_lib()
+    if r is None or not r.ref_has_vnni():
+        return None
+    x = np.ascontiguousarray(x, np.uint8)
+    w = np.ascontiguousarray(w, np.int8)
+    n, c, h, wd = x.shape
+    oc, _, kh, kw = w.shape
+    oh, ow = out_hw(h, wd, kh, kw, strides, (pads[0], pads[1], pads[0], pads[1]), (1, 1))
+    ws = np.ascontiguousarray(np.atleast_1d(w_scale), np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.int32)
+    y = np.empty((n, oc, oh, ow) if out_layout == "NCHW" else (n, oh, ow, oc), np.uint8)
+    rc = r.ref_qconv_first_layer(_p(x), n, c, h, wd, _p(w), oc, kh, kw, strides[0], strides[1], pads[0], pads[1],
+                                 _p(ws), ws.size, _p(b), _f(x_scale), C.c_uint8(x_zp), _f(y_scale), C.c_uint8(y_zp),
+                                 int(bool(has_post)), int(out_layout == "NHWC"), _p(y))
+    return None if rc != 0 else y
 
 
 def _dw_args(x, w, w_scale, bias, strides, pads, dilations):

@@ -21,6 +21,7 @@
 
 #include "backend/x64/conv_int8_direct_avx512.h"
 #include "backend/x64/depthwise_int8_avx512.h"
+#include "backend/x64/conv_first_layer_int8_avx512.h"
 
 extern "C" {
 
@@ -143,6 +144,35 @@ int ref_qdwconv_nhwc(const uint8_t* x, int n, int c, int h, int w, const int8_t*
                                                c, oh, ow, kh * kw, (int)x_zp, (int)w_zp, inv_y, (float)y_zp, 0.0f,
                                                255.0f);
     }
+  }
+  return 0;
+}
+
+// nnr's first-layer int8 conv (R3), as exec_first_layer_int8 calls it
+// (backend/cpu/QLinearConv.cpp:661-698): NCHW u8 x [n, c <= 4, h, w], OIHW s8
+// w, symmetric pads (ph, pw), NCHW or NHWC u8 y. The requant (vector body
+// and, for NCHW outputs, the scalar tail of each row's last oW % 16 pixels)
+// is nnr's own code in conv_first_layer_int8_avx512.h.
+int ref_qconv_first_layer(const uint8_t* x, int n, int c, int h, int w, const int8_t* wt, int oc, int kh, int kw,
+                          int sh, int sw, int ph, int pw, const float* w_scale, int n_w_scale, const int32_t* bias,
+                          float x_scale, uint8_t x_zp, float y_scale, uint8_t y_zp, int has_post, int out_nhwc,
+                          uint8_t* y) {
+  if (!ref_has_vnni() || c < 1 || c > 4) return -1;
+  const int oh = (h + 2 * ph - kh) / sh + 1, ow = (w + 2 * pw - kw) / sw + 1;
+  if (oh <= 0 || ow <= 0) return -1;
+  std::vector<int8_t> wpk(nnr::pack_weights_first_layer_int8_size(oc, c, kh, kw));
+  nnr::pack_weights_first_layer_int8(wpk.data(), wt, oc, c, kh, kw);
+  std::vector<int32_t> wsum(oc);
+  nnr::compute_weight_sums_first_layer_int8(wsum.data(), wt, oc, c, kh, kw);
+  // v.qmin / v.clamp_max of QLinearConv.cpp:419 for a u8 output
+  const int32_t qmin = has_post ? std::max(0, (int)y_zp) : 0, qmax = 255;
+  const float inv_y = 1.0f / y_scale;
+  for (int img = 0; img < n; img++) {
+    if (!nnr::conv_first_layer_int8_avx512(y + (size_t)img * oc * oh * ow, x + (size_t)img * c * h * w, wpk.data(),
+                                           wsum.data(), bias, w_scale, n_w_scale, x_scale, inv_y, (int32_t)x_zp,
+                                           (int32_t)y_zp, qmin, qmax, c, h, w, oc, oh, ow, kh, kw, sh, sw, ph, pw,
+                                           out_nhwc != 0))
+      return -1;
   }
   return 0;
 }

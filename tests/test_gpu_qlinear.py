@@ -4,6 +4,8 @@ Integer outputs must be bit-exact (nnr's tensor_equal compares integer
 tensors exactly, src/nnr.cpp:503-606). Every call goes through the C ABI
 (libnnrcu.so) via nnr_b200.ops.
 """
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
@@ -100,6 +102,28 @@ def test_stem_auto_r3(cuda_dev):
     y, _ = run_qconv(cuda_dev, case, in_layout="NCHW", out_layout="NHWC", requant=0)
     ref = oracle_qconv(case, O.R3, out_layout="NHWC")
     assert np.array_equal(y, ref)
+
+
+FIRST_GOLDEN = sorted((Path(__file__).parent / "golden").glob("qfirst_*.npz"))
+
+
+@pytest.mark.parametrize("path", FIRST_GOLDEN, ids=lambda p: p.stem)
+def test_first_layer_matches_nnr_golden(cuda_dev, path):
+    """The stem formula picked automatically (R3) against nnr's own
+    first-layer kernel output, NCHW outputs including the scalar tail of each
+    row's last OW % 16 pixels."""
+    from nnr_b200 import ops
+    g = np.load(path)
+    s, p, xz, yz, post, nhwc = (int(v) for v in g["attrs"])
+    xs, ys = (float(v) for v in g["scales"])
+    op = ops.QLinearConv(g["x"].shape, g["w"], g["w_scale"], None, g["bias"], xs, xz, ys, yz, strides=(s, s),
+                         pads=(p,) * 4, in_layout="NCHW", out_layout="NHWC" if nhwc else "NCHW",
+                         fused_relu=bool(post), requant=0)
+    y = op.exec(torch.from_numpy(g["x"]).to(cuda_dev))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    got = y.cpu().numpy()
+    assert np.array_equal(got, g["y"]), f"{(got != g['y']).sum()} bytes differ from nnr's first-layer kernel"
 
 
 S2D_SHAPES = [

@@ -199,3 +199,48 @@ def test_dw_nnr_skips_ragged_channels():
     got = O.qdwconv_u8_nhwc(x, wt, ws, None, 0.02, 10, 0.4, 5, pads=(1, 1, 1, 1))
     assert np.array_equal(got[..., :16], want[..., :16])
     assert (want[..., 16:] == 0xAB).all()
+
+
+# ------------------------------------------------------------------ first layer (R3, exec_first_layer_int8)
+FIRST_GOLDEN = sorted((Path(__file__).parent / "golden").glob("qfirst_*.npz"))
+
+
+def test_first_layer_golden_fixtures_present():
+    assert len(FIRST_GOLDEN) >= 4
+
+
+def _r3_oracle(x, w, ws, b, xs, xz, ys, yz, s, p, post, lay):
+    return O.qlinearconv(x, w, ws, b, xs, xz, ys, yz, strides=(s, s), pads=(p,) * 4, formula=O.R3, has_post=post,
+                         out_layout=lay)
+
+
+@pytest.mark.parametrize("path", FIRST_GOLDEN, ids=lambda p: p.stem)
+def test_r3_oracle_matches_nnr_golden(path):
+    """R3 with its NCHW scalar tail against nnr's first-layer kernel output."""
+    g = np.load(path)
+    s, p, xz, yz, post, nhwc = (int(v) for v in g["attrs"])
+    xs, ys = (float(v) for v in g["scales"])
+    y = _r3_oracle(g["x"], g["w"], g["w_scale"], g["bias"], xs, xz, ys, yz, s, p, bool(post),
+                   "NHWC" if nhwc else "NCHW")
+    assert np.array_equal(y, g["y"]), f"{(y != g['y']).sum()} output bytes differ from nnr's first-layer kernel"
+
+
+@pytest.mark.skipif(not _ref_available(), reason="nnr's int8 kernels not built here or no VNNI")
+@pytest.mark.parametrize("case", [
+    # n, c, h, w, oc, k, stride, pad, x_zp, y_zp, y_scale, post, out layout
+    (1, 3, 224, 224, 64, 7, 2, 3, 128, 0, 0.05, True, "NCHW"),
+    (2, 3, 50, 37, 40, 7, 2, 3, 3, 201, 0.3, False, "NCHW"),
+    (1, 4, 19, 23, 16, 5, 1, 2, 77, 50, 0.2, True, "NHWC"),
+    (1, 2, 9, 31, 33, 3, 2, 0, 255, 255, 0.7, False, "NCHW"),
+])
+def test_r3_oracle_matches_nnr_live(case):
+    n, c, h, w, oc, k, s, p, xz, yz, ys, post, lay = case
+    rng = np.random.default_rng(oc * 7 + h)
+    x = rng.integers(0, 256, size=(n, c, h, w)).astype(np.uint8)
+    wt = rng.integers(-127, 128, size=(oc, c, k, k)).astype(np.int8)
+    ws = rng.uniform(0.002, 0.01, size=oc).astype(np.float32)
+    b = rng.integers(-5000, 5001, size=oc).astype(np.int32)
+    want = O.ref_qconv_first_layer(x, wt, ws, b, 0.02, xz, ys, yz, strides=(s, s), pads=(p, p), has_post=post,
+                                   out_layout=lay)
+    got = _r3_oracle(x, wt, ws, b, 0.02, xz, ys, yz, s, p, post, lay)
+    assert np.array_equal(got, want), f"{(got != want).sum()} bytes differ"
