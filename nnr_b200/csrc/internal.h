@@ -25,6 +25,7 @@ int cuda_check(cudaError_t e, const char* what);
 // (on unless the environment sets NNRCU_PDL=0).
 bool pdl_enabled();
 bool shift_enabled();
+bool r2_sat_enabled();
 
 // Device address of this device's status word (set up once per device).
 int* status_ptr();

@@ -376,6 +376,7 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   e.colcorr = op->colcorr; e.bias_i = op->bias_i; e.cs = op->cs_arr; e.bias_f = op->bias_f; e.os = op->os;
   e.inv_y = op->inv_y; e.yzp_f = op->yzp_f; e.qmin_f = op->qmin_f; e.qmax_f = op->qmax_f;
   e.rq_lo = op->rq_lo; e.rq_hi = op->rq_hi; e.yzp = op->yzp;
+  e.r2_sat = r2_sat_enabled() && op->yzp == 0 && op->rq_lo == 0.0f && op->rq_hi == 255.0f;
   e.y = y;
   e.y_layout = d.out_layout == NNRCU_LAYOUT_NCHW ? 1 : 0;
   e.ldy = d.oc;

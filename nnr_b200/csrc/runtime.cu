@@ -105,6 +105,12 @@ bool shift_enabled() {
   return !(v && v[0] == '0');
 }
 
+bool r2_sat_enabled() {
+  // R2 epilogue with y_zp = 0 as one saturating conversion; NNRCU_R2SAT=0 turns it off
+  const char* v = std::getenv("NNRCU_R2SAT");
+  return !(v && v[0] == '0');
+}
+
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   int dev = 0;

@@ -52,7 +52,10 @@ enum : int { A_TMA = 0, A_GATHER = 1, A_IM2COL = 2, A_ROWS = 3, A_SHIFT = 4 };
 constexpr int ROWS_BYTES = (128 + 8) * 16;  // one A_ROWS copy: BM + 8 pixels of 16 bytes
 // EPI_R2A: the R2 requant followed by a fused QLinearAdd whose residual
 // tiles are TMA-prefetched one tile ahead (u8 row-major output via TMA store).
-enum : int { EPI_R1 = 1, EPI_R2 = 2, EPI_R3 = 3, EPI_R4 = 4, EPI_R2A = 5, EPI_F32 = 10 };
+// EPI_R3N: R3 with an NCHW output, whose last OW % 16 pixels of each output
+// row take the first-layer kernel's scalar tail sequence (a separate
+// instance, so that the NHWC stem keeps its register budget).
+enum : int { EPI_R1 = 1, EPI_R2 = 2, EPI_R3 = 3, EPI_R4 = 4, EPI_R2A = 5, EPI_R3N = 6, EPI_F32 = 10 };
 enum : int { ACT_NONE = 0, ACT_RELU = 1, ACT_CLIP = 2, ACT_HARDSWISH = 3, ACT_SIGMOID = 4, ACT_LEAKYRELU = 5,
              ACT_TANH = 6 };
 enum : int { ST_OK = 0, ST_TIMEOUT_FULL = 1, ST_TIMEOUT_EMPTY = 2, ST_TIMEOUT_ACCUM = 3, ST_SMEM = 4 };
@@ -137,6 +140,7 @@ struct EpiParams {
   float rq_lo, rq_hi;                  // R2 clamp bounds (lo - y_zp, hi - y_zp)
   float combined;                      // R4 scalar scale a_s*b_s/y_s
   int yzp;                             // R2 integer zero point
+  int r2_sat;                          // R2 bounds are [0, 255] with y_zp = 0: one saturating conversion
   // Fused QLinearAdd after the requant (u8 epilogues): y = QLinearAdd(q, qres)
   // with qres laid out like y. Same float sequence as the standalone op.
   const uint8_t* qres;                 // residual operand b, or null
@@ -279,7 +283,7 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t 
     // f lies in [-y_zp, 255 - y_zp] (integral bounds), so rne(f) + y_zp is
     // already in [0, 255]: the unsigned saturation of the reference is a no-op
     return __float_as_uint(r2_magic(raw, ci, f1, e)) + (uint32_t)e.yzp;
-  } else if constexpr (EPI == EPI_R3) {
+  } else if constexpr (EPI == EPI_R3 || EPI == EPI_R3N) {
     // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); min(hi) then max(qmin); rne
     // (the clamp bounds are integers in [0, 255], so rne commutes with the clamp)
     int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci);
@@ -298,13 +302,20 @@ __device__ __forceinline__ uint32_t requant_u8(int32_t raw, int32_t ci, int32_t 
   }
 }
 
-// R3's scalar tail (the first-layer kernel's NCHW remainder pixels):
-// f = fma(float(acc), cs, bias_f); q = int(rne(f * inv_y)) + y_zp with the x86
-// conversion (out-of-range values become INT_MIN); integer clamp to [qmin, 255].
-__device__ __forceinline__ uint32_t requant_r3_tail(int32_t raw, int32_t ci, float f1, float f2, const EpiParams& e) {
+// R3 for one output row: the vector body
+//   f = fma(float(acc), cs, bias_f); q = rne(clamp(fma(f, inv_y, y_zp), qmin, 255))
+// or, for the first-layer kernel's NCHW remainder pixels (tail), its scalar
+//   q = clamp(int(rne(f * inv_y)) + y_zp, qmin, 255)
+// with the x86 conversion (out-of-range values become INT_MIN). add_f / add_i
+// place y_zp before or after the rounding; the clamp bounds are integers, so
+// clamping after the rounding equals the body's clamp before it, and the
+// saturating conversion keeps huge values at the upper bound there.
+__device__ __forceinline__ uint32_t requant_r3_row(int32_t raw, int32_t ci, float f1, float f2, float add_f,
+                                                   int32_t add_i, bool tail, const EpiParams& e) {
   const int32_t acc = (int32_t)((uint32_t)raw + (uint32_t)ci);
-  const float f = __fmaf_rn(__int2float_rn(acc), f1, f2);
-  int32_t q = (int32_t)((uint32_t)ptx::cvt_rne_x86(__fmul_rn(f, e.inv_y)) + (uint32_t)e.yzp);
+  const float g = __fmaf_rn(__fmaf_rn(__int2float_rn(acc), f1, f2), e.inv_y, add_f);
+  int32_t q = tail ? ptx::cvt_rne_x86(g) : __float2int_rn(g);
+  q = (int32_t)((uint32_t)q + (uint32_t)add_i);
   q = max(q, (int32_t)e.qmin_f);
   q = min(q, (int32_t)e.qmax_f);
   return (uint32_t)q;
@@ -769,6 +780,7 @@ if constexpr (AMODE == A_ROWS) {
     const float kp_ca = __fsub_rn(e.yzp_f, RND_MAGIC);
     const uint32_t kp_yzp = (uint32_t)e.yzp;
     const bool kp_ovf = e.qa_ovf != 0;
+    const bool kp_sat = e.r2_sat != 0;
     const bool shift_direct = e.y_layout == 0 && (e.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0;
     const bool direct = AMODE == A_SHIFT || e.opad != 0;  // lean path stores rows straight to HBM
     // EPI_R2A: TMA load of this warp's 32 x HB residual block of tile t into buffer buf
@@ -865,7 +877,9 @@ if constexpr (AMODE == A_ROWS) {
       if (e.y_layout == 1 && mvalid) { img = m / e.ohw; pix = m - img * e.ohw; }
       // R3 with an NCHW output: the last OW % 16 pixels of each output row take
       // the first-layer kernel's scalar tail sequence
-      const bool r3_tail = EPI == EPI_R3 && e.y_layout == 1 && mvalid && (pix % g.OW) >= (g.OW & ~15);
+      const bool r3_tail = EPI == EPI_R3N && e.y_layout == 1 && mvalid && (pix % g.OW) >= (g.OW & ~15);
+      const float r3_add_f = r3_tail ? 0.0f : e.yzp_f;  // y_zp added before the rounding (body) ...
+      const int32_t r3_add_i = r3_tail ? e.yzp : 0;     // ... or after it (tail)
       int mst = m;  // row of the output buffer
       if (e.opad) {
         const int im = m / e.o_hw, r = m - im * e.o_hw, oy = r / e.o_w;
@@ -1020,6 +1034,17 @@ if constexpr (AMODE == A_ROWS) {
 #pragma unroll
               for (int j = 0; j < CW; ++j) q[j] = __float_as_uint(t[j]) + (uint32_t)e.yzp;
             }
+          } else if constexpr (EPI == EPI_R3N) {
+#pragma unroll
+            for (int j = 0; j < CW; j += 4) {
+              const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
+              const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
+              const float4 b4 = *reinterpret_cast<const float4*>(s_f2 + pc + j);
+              q[j + 0] = requant_r3_row((int32_t)v[j + 0], ci4.x, a4.x, b4.x, r3_add_f, r3_add_i, r3_tail, e);
+              q[j + 1] = requant_r3_row((int32_t)v[j + 1], ci4.y, a4.y, b4.y, r3_add_f, r3_add_i, r3_tail, e);
+              q[j + 2] = requant_r3_row((int32_t)v[j + 2], ci4.z, a4.z, b4.z, r3_add_f, r3_add_i, r3_tail, e);
+              q[j + 3] = requant_r3_row((int32_t)v[j + 3], ci4.w, a4.w, b4.w, r3_add_f, r3_add_i, r3_tail, e);
+            }
           } else {
 #pragma unroll
             for (int j = 0; j < CW; j += 4) {
@@ -1030,10 +1055,6 @@ if constexpr (AMODE == A_ROWS) {
               q[j + 1] = requant_u8<EPI>((int32_t)v[j + 1], ci4.y, rowc, a4.y, b4.y, e);
               q[j + 2] = requant_u8<EPI>((int32_t)v[j + 2], ci4.z, rowc, a4.z, b4.z, e);
               q[j + 3] = requant_u8<EPI>((int32_t)v[j + 3], ci4.w, rowc, a4.w, b4.w, e);
-            }
-            if (EPI == EPI_R3 && r3_tail) {
-#pragma unroll
-              for (int j = 0; j < CW; ++j) q[j] = requant_r3_tail((int32_t)v[j], s_ci[pc + j], s_f1[pc + j], s_f2[pc + j], e);
             }
           }
           if (scalar_add) {
@@ -1110,6 +1131,30 @@ if constexpr (AMODE == A_ROWS) {
             for (int k = 0; k < CW / 16; ++k) rq[k] = __ldg(rp + k);
           }
           if constexpr (EPI == EPI_R2 || EPI == EPI_R2A) {
+            // R2 with y_zp = 0 and the full u8 range (every Relu output):
+            // clamp(rne(f), 0, 255) is one saturating conversion
+            bool sat_done = false;
+            if constexpr (EPI == EPI_R2) {
+              if (kp_sat) {
+#pragma unroll
+                for (int j = 0; j < CW; j += 4) {
+                  const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
+                  const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
+                  const float2 f0 = __fmul2_rn(make_float2(__int2float_rn((int32_t)(v[j + 0] + (uint32_t)ci4.x)),
+                                                           __int2float_rn((int32_t)(v[j + 1] + (uint32_t)ci4.y))),
+                                               make_float2(a4.x, a4.y));
+                  const float2 f1 = __fmul2_rn(make_float2(__int2float_rn((int32_t)(v[j + 2] + (uint32_t)ci4.z)),
+                                                           __int2float_rn((int32_t)(v[j + 3] + (uint32_t)ci4.w))),
+                                               make_float2(a4.z, a4.w));
+                  q[j + 0] = ptx::cvt_rni_sat_u8(f0.x);
+                  q[j + 1] = ptx::cvt_rni_sat_u8(f0.y);
+                  q[j + 2] = ptx::cvt_rni_sat_u8(f1.x);
+                  q[j + 3] = ptx::cvt_rni_sat_u8(f1.y);
+                }
+                sat_done = true;
+              }
+            }
+            if (!sat_done) {
             float2 t[CW / 2];  // RND_MAGIC + rne(f), f = clamp(float(acc + bias) * os)
 #pragma unroll
             for (int j = 0; j < CW; j += 4) {
@@ -1184,7 +1229,8 @@ if constexpr (AMODE == A_ROWS) {
                 q[j + 1] = __float_as_uint(t[j / 2].y) + kp_yzp;
               }
             }
-          } else if constexpr (EPI == EPI_R3) {
+            }
+          } else if constexpr (EPI == EPI_R3 || EPI == EPI_R3N) {
             // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); clamp; rne
             const float2 iy = make_float2(e.inv_y, e.inv_y), yz = make_float2(e.yzp_f, e.yzp_f);
             const uint32_t qmin_u = (uint32_t)e.qmin_f;

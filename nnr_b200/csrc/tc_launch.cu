@@ -102,11 +102,13 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
         if (L.epi == EPI_R1) return launch_one<BN, 1, A_ROWS, EPI_R1, 16>(L, g, e, st);
         if (L.epi == EPI_R2) return launch_one<BN, 1, A_ROWS, EPI_R2, 16>(L, g, e, st);
         if (L.epi == EPI_R3) return launch_one<BN, 1, A_ROWS, EPI_R3, 16>(L, g, e, st);
+        if (L.epi == EPI_R3N) return launch_one<BN, 1, A_ROWS, EPI_R3N, 16>(L, g, e, st);
       }
       if (L.nplane == 1 && L.amode == A_IM2COL) {
         if (L.epi == EPI_R1) return launch_one<BN, 1, A_IM2COL, EPI_R1, 16>(L, g, e, st);
         if (L.epi == EPI_R2) return launch_one<BN, 1, A_IM2COL, EPI_R2, 16>(L, g, e, st);
         if (L.epi == EPI_R3) return launch_one<BN, 1, A_IM2COL, EPI_R3, 16>(L, g, e, st);
+        if (L.epi == EPI_R3N) return launch_one<BN, 1, A_IM2COL, EPI_R3N, 16>(L, g, e, st);
       }
     }
     return set_error(NNRCU_ERR_INVALID, "no 16-byte-tap engine instance for bn %d amode %d epilogue %d", BN, L.amode,
@@ -128,6 +130,7 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
       if (L.epi == EPI_R1) return launch_one<BN, 1, A_TMA, EPI_R1, 64>(L, g, e, st);
       if (L.epi == EPI_R2) return launch_one<BN, 1, A_TMA, EPI_R2, 64>(L, g, e, st);
       if (L.epi == EPI_R3) return launch_one<BN, 1, A_TMA, EPI_R3, 64>(L, g, e, st);
+      if (L.epi == EPI_R3N) return launch_one<BN, 1, A_TMA, EPI_R3N, 64>(L, g, e, st);
       if (L.epi == EPI_R4) return launch_one<BN, 1, A_TMA, EPI_R4, 64>(L, g, e, st);
     }
     return set_error(NNRCU_ERR_INVALID, "no 64-byte-slab engine instance for amode %d epilogue %d", L.amode, L.epi);
@@ -164,6 +167,7 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
       case EPI_R1: return launch_one<BN, 1, A_GATHER, EPI_R1>(L, g, e, st);
       case EPI_R2: return launch_one<BN, 1, A_GATHER, EPI_R2>(L, g, e, st);
       case EPI_R3: return launch_one<BN, 1, A_GATHER, EPI_R3>(L, g, e, st);
+      case EPI_R3N: return launch_one<BN, 1, A_GATHER, EPI_R3N>(L, g, e, st);
       case EPI_R4: return launch_one<BN, 1, A_GATHER, EPI_R4>(L, g, e, st);
       default: break;
     }
@@ -202,6 +206,7 @@ int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaSt
   // an R2 requant with a fused add whose output and residual can move by
   // TMA (16-byte aligned NHWC rows) runs the residual-prefetching instance
   TcLaunch L2 = L;
+  if (L.epi == EPI_R3 && e.y_layout == 1) L2.epi = EPI_R3N;
   // Resident B: a single N tile whose K fits 9 slabs (3x3 convs over 64 or
   // 128 channels), im2col-fed, R2
   if (L.n_tiles == 1 && L.num_kb <= 9 && L.amode == A_IM2COL && L.epi == EPI_R2 && L.nplane == 1 &&

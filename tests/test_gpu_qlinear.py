@@ -275,6 +275,23 @@ def test_conv_with_fused_residual_add(cuda_dev, shape):
     assert np.array_equal(y.cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("kind", ["1x1", "3x3", "shift"])
+@pytest.mark.parametrize("y_scale", [1e-7, 0.05, 3.0])
+def test_r2_zero_point_zero(cuda_dev, kind, y_scale):
+    """R2 with y_zp = 0 (every Relu output) runs as one saturating conversion
+    per value: rounding ties, both saturation ends and huge values agree with
+    the clamp-then-round reference, fused Relu or not."""
+    rng = np.random.default_rng(int(y_scale * 1e3) + len(kind))
+    k, p = (1, 0) if kind == "1x1" else (3, 1)
+    h = 56 if kind == "shift" else 13
+    case = W.random_qconv(rng, 2, 64, h, h, 128, k, k, (1, 1), (p,) * 4, x_zp=17, y_zp=0)
+    case.y_scale = y_scale
+    for relu in (False, True):
+        y, _ = run_qconv(cuda_dev, case, O.R2, "NHWC", "NHWC", fused_relu=relu)
+        ref = oracle_qconv(case, O.R2, "NHWC", fused_relu=relu)
+        assert np.array_equal(y, ref), f"relu {relu}: {(y != ref).sum()} / {y.size} mismatches"
+
+
 @pytest.mark.parametrize("kind", ["1x1", "3x3"])
 def test_saturating_scales(cuda_dev, kind):
     """Tiny output scales: R2 values far outside [0, 255] (the clamp before the
