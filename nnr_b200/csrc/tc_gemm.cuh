@@ -1234,20 +1234,39 @@ if constexpr (AMODE == A_ROWS) {
             // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); clamp; rne
             const float2 iy = make_float2(e.inv_y, e.inv_y), yz = make_float2(e.yzp_f, e.yzp_f);
             const uint32_t qmin_u = (uint32_t)e.qmin_f;
+            auto r3_quads = [&](auto has_qmin) {
 #pragma unroll
-            for (int j = 0; j < CW; j += 2) {
-              const int2 ci2 = *reinterpret_cast<const int2*>(s_ci + pc + j);
-              const float2 a2 = *reinterpret_cast<const float2*>(s_f1 + pc + j);
-              const float2 b2 = *reinterpret_cast<const float2*>(s_f2 + pc + j);
-              float2 f = __ffma2_rn(make_float2(__int2float_rn((int32_t)(v[j] + (uint32_t)ci2.x)),
-                                                __int2float_rn((int32_t)(v[j + 1] + (uint32_t)ci2.y))),
-                                    a2, b2);
-              f = __ffma2_rn(f, iy, yz);
-              // the upper bound is 255: rne + clamp to [0, 255] in one
-              // conversion, then the lower bound (y_zp under a fused Relu)
-              q[j] = max(ptx::cvt_rni_sat_u8(f.x), qmin_u);
-              q[j + 1] = max(ptx::cvt_rni_sat_u8(f.y), qmin_u);
-            }
+              for (int j = 0; j < CW; j += 4) {
+                const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
+                const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
+                const float4 b4 = *reinterpret_cast<const float4*>(s_f2 + pc + j);
+                float2 f0 = __ffma2_rn(make_float2(__int2float_rn((int32_t)(v[j] + (uint32_t)ci4.x)),
+                                                   __int2float_rn((int32_t)(v[j + 1] + (uint32_t)ci4.y))),
+                                       make_float2(a4.x, a4.y), make_float2(b4.x, b4.y));
+                float2 f1 = __ffma2_rn(make_float2(__int2float_rn((int32_t)(v[j + 2] + (uint32_t)ci4.z)),
+                                                   __int2float_rn((int32_t)(v[j + 3] + (uint32_t)ci4.w))),
+                                       make_float2(a4.z, a4.w), make_float2(b4.z, b4.w));
+                f0 = __ffma2_rn(f0, iy, yz);
+                f1 = __ffma2_rn(f1, iy, yz);
+                // the upper bound is 255: rne + clamp to [0, 255] in one
+                // conversion, then the lower bound (y_zp under a fused Relu;
+                // nothing to do when it is 0)
+                q[j] = ptx::cvt_rni_sat_u8(f0.x);
+                q[j + 1] = ptx::cvt_rni_sat_u8(f0.y);
+                q[j + 2] = ptx::cvt_rni_sat_u8(f1.x);
+                q[j + 3] = ptx::cvt_rni_sat_u8(f1.y);
+                if constexpr (decltype(has_qmin)::value) {
+                  q[j] = max(q[j], qmin_u);
+                  q[j + 1] = max(q[j + 1], qmin_u);
+                  q[j + 2] = max(q[j + 2], qmin_u);
+                  q[j + 3] = max(q[j + 3], qmin_u);
+                }
+              }
+            };
+            if (qmin_u != 0)
+              r3_quads(std::true_type{});
+            else
+              r3_quads(std::false_type{});
           } else {
 #pragma unroll
             for (int j = 0; j < CW; j += 4) {
