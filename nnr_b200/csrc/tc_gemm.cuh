@@ -628,6 +628,7 @@ if constexpr (AMODE == A_ROWS) {
           const uint32_t ph = (uint32_t)(it / STAGES) & 1u;
           if (!ptx::mbar_wait(&full_bar[s], ph, abort_flag)) { fail(ST_TIMEOUT_FULL); aborted = true; break; }
           if (kb == 0) NNRCU_TRACE_AT(warp, lt, 1);
+          if (kb < 8) NNRCU_TRACE2_AT(warp, lt, 2 * kb);
           ptx::tc_fence_after();
           // (stages filled by TMA are async-proxy writes already; the gather
           // producers fence their cp.async writes before arriving)
@@ -664,6 +665,7 @@ if constexpr (AMODE == A_ROWS) {
                            ptx::umma_desc_sw<KB>(b_addr + koff), idesc, 1u);
             }
           }
+          if (kb < 8) NNRCU_TRACE2_AT(warp, lt, 2 * kb + 1);
           ptx::mma_commit(&empty_bar[s]);
         }
         if (!aborted) ptx::mma_commit(&tfull_bar[acc]);  // fires when this tile's MMAs have completed
