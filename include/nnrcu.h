@@ -227,6 +227,18 @@ int nnrcu_gemm_f32_create_ex(int m, int n, int k, int trans_a, int trans_b, floa
                              const float* b_host, const float* c_host, int c_rows, int post_op, float post_a,
                              float post_b, int precision, nnrcu_op** op);
 
+/* MatMul with both operands computed at run time (nnr's MatMul_operator with
+ * a non-initializer B, MatMul.cpp:32-94 shapes and broadcast strides,
+ * :194-228 exec): for b in [0, batch),
+ *   Y[b] = A[a_batch_stride * b] (m x k) x B[b_batch_stride * b] (k x n)
+ * row-major, strides in elements (0 broadcasts), Y batches contiguous, plus a
+ * post-op. Each batch is split into bf16 hi/lo planes in the workspace
+ * (nnrcu_matmul_f32_workspace bytes) and runs on the split-bf16 engine. */
+int nnrcu_matmul_f32_workspace(int m, int n, int k, size_t* bytes);
+int nnrcu_matmul_f32_run(const float* a, const float* b, float* y, int batch, int m, int n, int k,
+                         long long a_batch_stride, long long b_batch_stride, int post_op, float post_a, float post_b,
+                         void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------- 16-bit Conv / Gemm (bf16 or fp16 I/O)
  * Replace nnr's 16-bit I/O paths, which convert to fp32, compute in fp32,
  * apply the post-op and round back (Conv_exec_entry.h:188-381, Gemm.cpp:

@@ -341,4 +341,93 @@ int nnrcu_gemm_f32_run(nnrcu_op* op, const float* a, float* y, void* workspace, 
   return tc_launch(L, g, e, st);
 }
 
+namespace {
+struct MatmulGeom {
+  int cs, kbytes, kpad_bytes, num_kb, npad;
+  size_t a_plane, b_plane;
+};
+MatmulGeom matmul_geom(int m, int n, int k) {
+  MatmulGeom g;
+  g.cs = round_up(k, 8);  // bf16 elements per operand row
+  g.kbytes = g.cs * 2;
+  g.kpad_bytes = round_up(g.kbytes, BKB);
+  g.num_kb = g.kpad_bytes / BKB;
+  g.npad = round_up(n, 256);
+  g.a_plane = round_up_sz((size_t)m * g.cs * 2, 256);
+  g.b_plane = round_up_sz((size_t)g.npad * g.cs * 2, 256);
+  return g;
+}
+}  // namespace
+
+int nnrcu_matmul_f32_workspace(int m, int n, int k, size_t* bytes) {
+  if (!bytes || m <= 0 || n <= 0 || k <= 0) return set_error(NNRCU_ERR_INVALID, "MatMul dims must be positive");
+  const MatmulGeom g = matmul_geom(m, n, k);
+  *bytes = 2 * g.a_plane + 2 * g.b_plane;
+  return NNRCU_OK;
+}
+
+int nnrcu_matmul_f32_run(const float* a, const float* b, float* y, int batch, int m, int n, int k,
+                         long long a_batch_stride, long long b_batch_stride, int post_op, float post_a, float post_b,
+                         void* workspace, size_t workspace_bytes, void* stream) {
+  if (!a || !b || !y || !workspace) return set_error(NNRCU_ERR_INVALID, "NULL argument");
+  if (batch <= 0 || m <= 0 || n <= 0 || k <= 0 || a_batch_stride < 0 || b_batch_stride < 0)
+    return set_error(NNRCU_ERR_INVALID, "MatMul: dims must be positive and strides non-negative");
+  const MatmulGeom mg = matmul_geom(m, n, k);
+  if (workspace_bytes < 2 * mg.a_plane + 2 * mg.b_plane)
+    return set_error(NNRCU_ERR_INVALID, "MatMul workspace of %zu bytes required", 2 * mg.a_plane + 2 * mg.b_plane);
+  nnrcu_op post{};  // carries the mapped post-op only
+  int rc = map_post(post_op, post_a, post_b, &post);
+  if (rc != NNRCU_OK) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint16_t* ahi = reinterpret_cast<uint16_t*>(ws);
+  uint16_t* alo = reinterpret_cast<uint16_t*>(ws + mg.a_plane);
+  uint16_t* bhi = reinterpret_cast<uint16_t*>(ws + 2 * mg.a_plane);  // [2][npad][cs]: hi rows, then lo rows
+  uint16_t* blo = bhi + (size_t)mg.npad * mg.cs;
+  const int amode = mg.kbytes >= BKB ? A_TMA : A_GATHER;
+  const int bn = pick_bn(m, n, 2, num_sms());
+  CUtensorMap tmA0{}, tmA1{}, tmB{};
+  if (amode == A_TMA) {
+    rc = encode_tmap_2d(&tmA0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, ahi, mg.cs, m, mg.cs * 2, BKB / 2, BM);
+    if (rc != NNRCU_OK) return rc;
+    rc = encode_tmap_2d(&tmA1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, alo, mg.cs, m, mg.cs * 2, BKB / 2, BM);
+    if (rc != NNRCU_OK) return rc;
+  }
+  // B planes: rows past n are never written; they only feed output columns
+  // past n, which are not stored. K past cs is the map's zero fill.
+  rc = encode_tmap_2d(&tmB, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bhi, mg.cs, (uint64_t)2 * mg.npad, mg.cs * 2, BKB / 2, bn);
+  if (rc != NNRCU_OK) return rc;
+  GatherGeom g{};
+  g.x = reinterpret_cast<const uint8_t*>(ahi);
+  g.x2 = reinterpret_cast<const uint8_t*>(alo);
+  g.N = 1; g.H = 1; g.W = m;
+  g.cbytes = mg.cs * 2;
+  g.OH = 1; g.OW = m; g.KH = 1; g.KW = 1; g.sh = 1; g.sw = 1; g.ph = 0; g.pw = 0; g.dh = 1; g.dw = 1;
+  g.kbytes = mg.kbytes;
+  EpiParams e{};
+  e.M = m; e.N = n;
+  e.act = post.act; e.act_a = post.act_a; e.act_b = post.act_b;
+  e.y_layout = 0;
+  e.ldy = n;
+  e.ohw = 1;
+  e.status = status_ptr();
+  TcLaunch L{};
+  L.bn = bn; L.nplane = 2; L.amode = amode; L.epi = EPI_F32;
+  L.m_tiles = (m + BM - 1) / BM;
+  L.n_tiles = (n + bn - 1) / bn;
+  L.tmA0 = &tmA0; L.tmA1 = &tmA1; L.tmB = &tmB;
+  L.b_plane_rows = mg.npad;
+  L.num_kb = mg.num_kb;
+  for (int bi = 0; bi < batch; ++bi) {
+    // (a broadcast operand is split once)
+    if (bi == 0 || a_batch_stride)
+      if ((rc = launch_split_bf16_rows(a + a_batch_stride * bi, 0, ahi, alo, m, k, mg.cs, st)) != NNRCU_OK) return rc;
+    if (bi == 0 || b_batch_stride)
+      if ((rc = launch_split_bf16_rows(b + b_batch_stride * bi, 1, bhi, blo, n, k, mg.cs, st)) != NNRCU_OK) return rc;
+    e.y = y + (size_t)bi * m * n;
+    if ((rc = tc_launch(L, g, e, st)) != NNRCU_OK) return rc;
+  }
+  return NNRCU_OK;
+}
+
 }  // extern "C"

@@ -312,8 +312,58 @@ struct Gemm_cuda : cuda_op_t {
     layout_mask = LAYOUT_NCHW;
     return true;
   }
+  // MatMul whose B is computed at run time (or batched): nnr's shapes and
+  // broadcast strides (MatMul.cpp:32-94), one offset pair per output batch
+  bool dyn = false;
+  int dm = 0, dn = 0, dk = 0;
+  std::vector<std::pair<long long, long long>> offs;
+  size_t dws = 0;
+  int dpost = 0;
+  float dpa = 0, dpb = 0;
+  bool infer_dynamic() {
+    const tensor_t *A = inputs[0], *B = inputs[1];
+    std::vector<int> ad(A->dims, A->dims + A->ndim), bd(B->dims, B->dims + B->ndim);
+    if (A->ndim == 1) ad = {1, A->dims[0]};
+    if (B->ndim == 1) bd = {B->dims[0], 1};
+    if (ad.size() < 2 || bd.size() < 2 || ad.back() != bd[bd.size() - 2]) return false;
+    const int nd = (int)std::max(ad.size(), bd.size()), nb = nd - 2;
+    std::vector<int> dims(nd);
+    dm = ad[ad.size() - 2], dk = ad.back(), dn = bd.back();
+    dims[nd - 2] = dm, dims[nd - 1] = dn;
+    for (int i = 3; i <= nd; ++i) {
+      const int ai = (int)ad.size() - i, bi = (int)bd.size() - i;
+      const int al = ai < 0 ? 1 : ad[ai], bl = bi < 0 ? 1 : bd[bi];
+      if (al != bl && al > 1 && bl > 1) return false;
+      dims[nd - i] = std::max(al, bl);
+    }
+    std::vector<long long> as(nb, 0), bs(nb, 0);
+    long long sa = (long long)dm * dk, sb = (long long)dk * dn;
+    for (int i = nb - 1; i >= 0; --i) {
+      const int ai = i - (nb - ((int)ad.size() - 2)), bi = i - (nb - ((int)bd.size() - 2));
+      if (ai >= 0 && ad[ai] > 1) as[i] = sa, sa *= ad[ai];
+      if (bi >= 0 && bd[bi] > 1) bs[i] = sb, sb *= bd[bi];
+    }
+    long long total = 1;
+    for (int i = 0; i < nb; ++i) total *= dims[i];
+    offs.clear();
+    std::vector<int> idx(nb, 0);
+    for (long long t = 0; t < total; ++t) {
+      long long ao = 0, bo = 0;
+      for (int i = 0; i < nb; ++i) ao += idx[i] * as[i], bo += idx[i] * bs[i];
+      offs.emplace_back(ao, bo);
+      for (int i = nb - 1; i >= 0; --i) {
+        if (++idx[i] < dims[i]) break;
+        idx[i] = 0;
+      }
+    }
+    M = dm, N = dn, K = dk;
+    return outputs[0]->reshape({dims.data(), (size_t)nd}, A->type);
+  }
+  bool device_input(int idx) const override { return idx == 0 || (dyn && idx == 1); }
   bool infer_shape() override {
     const tensor_t *A = inputs[0], *B = inputs[1];
+    dyn = matmul && !(B->ndim == 2 && A->ndim >= 2 && is_const_tensor(ctx, B));
+    if (dyn) return infer_dynamic();
     if (B->ndim != 2 || A->ndim < 2) return false;
     if (matmul) {
       K = A->dims[A->ndim - 1];
@@ -332,9 +382,10 @@ struct Gemm_cuda : cuda_op_t {
     const int dims[2] = {M, N};
     return outputs[0]->reshape({dims, 2}, A->type);
   }
-  int64_t num_ops() const override { return 2LL * M * N * K; }
+  int64_t num_ops() const override { return 2LL * M * N * K * (dyn ? (int64_t)offs.size() : 1); }
   bool device_ok() const override {
     const data_type_t t = inputs[0]->type;
+    if (dyn) return t == NNR_DATA_TYPE_FLOAT32 && inputs[1]->type == t;
     const bool half = half_dtype(t) != 0;
     if (!(t == NNR_DATA_TYPE_FLOAT32 || (half && alpha == 1.0f && !trans_a)) || inputs[1]->type != t ||
         !is_const_tensor(ctx, inputs[1]))
@@ -344,6 +395,12 @@ struct Gemm_cuda : cuda_op_t {
     return true;
   }
   bool prepare_device(device_state_t& s) override {
+    if (dyn) {
+      if (!post_op_of(this, &dpost, &dpa, &dpb)) return s.fail("MatMul: fused post-op has no device epilogue");
+      if (!nnrcu_ok(s, nnrcu_matmul_f32_workspace(dm, dn, dk, &dws), "MatMul")) return false;
+      set_out_layout(s, outputs[0], memory_layout_t::NCHW);
+      return true;
+    }
     const tensor_t* C = !matmul && inputs.size() > 2 ? inputs[2] : nullptr;
     std::vector<float> crow;
     const float* c = nullptr;
@@ -388,8 +445,30 @@ struct Gemm_cuda : cuda_op_t {
     set_out_layout(s, outputs[0], memory_layout_t::NCHW);
     return true;
   }
-  size_t device_workspace() const override { return h.ws(); }
+  size_t device_workspace() const override { return dyn ? dws : h.ws(); }
   bool run_device(device_state_t& s, void* stream) override {
+    if (dyn) {
+      // runs of output batches whose A and B offsets advance by fixed strides: one call each
+      const float* a = (const float*)s.dev(inputs[0]);
+      const float* b = (const float*)s.dev(inputs[1]);
+      float* y = (float*)s.dev(outputs[0]);
+      size_t i = 0;
+      while (i < offs.size()) {
+        size_t j = i + 1;
+        const long long sa = j < offs.size() ? offs[j].first - offs[i].first : 0;
+        const long long sb = j < offs.size() ? offs[j].second - offs[i].second : 0;
+        while (j < offs.size() && sa >= 0 && sb >= 0 && offs[j].first - offs[j - 1].first == sa &&
+               offs[j].second - offs[j - 1].second == sb)
+          ++j;
+        if (!nnrcu_ok(s,
+                      nnrcu_matmul_f32_run(a + offs[i].first, b + offs[i].second, y + i * (size_t)dm * dn, (int)(j - i),
+                                           dm, dn, dk, sa, sb, dpost, dpa, dpb, s.workspace, dws, stream),
+                      "MatMul"))
+          return false;
+        i = j;
+      }
+      return true;
+    }
     if (dtype)
       return nnrcu_ok(s,
                       nnrcu_gemm_half_run(h.op, (const uint16_t*)s.dev(inputs[0]), (uint16_t*)s.dev(outputs[0]),

@@ -186,6 +186,21 @@ def matmul(a_shape, b) -> bytes:
     return g.model()
 
 
+def matmul_dynamic(a_shape, b_shape, y_shape, post=None) -> bytes:
+    """a, b -> MatMul(a, b) [-> Relu] -> y, both operands graph inputs (nnr's
+    MatMul with a run-time B)."""
+    g = P.Graph("matmul_dyn")
+    g.input("a", P.FLOAT, a_shape)
+    g.input("b", P.FLOAT, b_shape)
+    if post:
+        g.node("MatMul", ["a", "b"], ["m"])
+        g.node(post, ["m"], ["y"])
+    else:
+        g.node("MatMul", ["a", "b"], ["y"])
+    g.output("y", P.FLOAT, y_shape)
+    return g.model()
+
+
 def quantize(shape, scale, zp) -> bytes:
     g = P.Graph("q")
     g.input("x", P.FLOAT, shape)

@@ -299,6 +299,67 @@ class MatMul(Gemm):
         super().__init__(m, b, None, 1.0, 0.0, 0, 0, post, post_a, post_b, precision)
 
 
+def matmul_broadcast(a_shape, b_shape):
+    """nnr's MatMul shapes (MatMul.cpp:32-94): a 1-D A is [1, k], a 1-D B
+    [k, 1] (the unit dims are kept in the output), batch dims broadcast
+    numpy-style. Returns (out_shape, m, n, k, [(a_off, b_off)] per output
+    batch in row-major order, offsets in elements)."""
+    ad = [1, a_shape[0]] if len(a_shape) == 1 else list(a_shape)
+    bd = [b_shape[0], 1] if len(b_shape) == 1 else list(b_shape)
+    if ad[-1] != bd[-2]:
+        raise ValueError(f"MatMul: inner dims {ad[-1]} and {bd[-2]} differ")
+    nd = max(len(ad), len(bd))
+    m, k, n = ad[-2], ad[-1], bd[-1]
+    dims = [0] * nd
+    dims[-2], dims[-1] = m, n
+    for i in range(3, nd + 1):
+        al = ad[-i] if i <= len(ad) else 1
+        bl = bd[-i] if i <= len(bd) else 1
+        if al != bl and al > 1 and bl > 1:
+            raise ValueError("MatMul: batch dims do not broadcast")
+        dims[-i] = max(al, bl)
+    nb = nd - 2
+    a_str, b_str = [0] * nb, [0] * nb
+    sa, sb = m * k, k * n
+    for i in range(nb - 1, -1, -1):
+        ai, bi = i - (nb - (len(ad) - 2)), i - (nb - (len(bd) - 2))
+        if ai >= 0 and ad[ai] > 1:
+            a_str[i], sa = sa, sa * ad[ai]
+        if bi >= 0 and bd[bi] > 1:
+            b_str[i], sb = sb, sb * bd[bi]
+    offs = []
+    for idx in np.ndindex(*dims[:nb]) if nb else [()]:
+        offs.append((sum(i * s for i, s in zip(idx, a_str)), sum(i * s for i, s in zip(idx, b_str))))
+    return tuple(dims), m, n, k, offs
+
+
+def matmul_f32(a: torch.Tensor, b: torch.Tensor, post=None, post_a=0.0, post_b=0.0, stream=None) -> torch.Tensor:
+    """ONNX MatMul of two fp32 device tensors computed at run time (nnr's
+    MatMul_operator with a non-initializer B), through nnrcu_matmul_f32_run.
+    Runs of output batches whose A and B offsets advance by fixed strides go
+    to one call."""
+    a, b = a.contiguous(), b.contiguous()
+    shape, m, n, k, offs = matmul_broadcast(tuple(a.shape), tuple(b.shape))
+    y = torch.empty(shape, dtype=torch.float32, device=a.device)
+    ws_bytes = C.c_size_t()
+    call("nnrcu_matmul_f32_workspace", m, n, k, C.byref(ws_bytes))
+    ws = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=a.device)
+    code = _POSTS[post] if not isinstance(post, int) else post
+    i = 0
+    while i < len(offs):
+        j = i + 1
+        sa = offs[j][0] - offs[i][0] if j < len(offs) else 0
+        sb = offs[j][1] - offs[i][1] if j < len(offs) else 0
+        while j < len(offs) and offs[j][0] - offs[j - 1][0] == sa and offs[j][1] - offs[j - 1][1] == sb \
+                and sa >= 0 and sb >= 0:
+            j += 1
+        call("nnrcu_matmul_f32_run", C.c_void_p(a.data_ptr() + 4 * offs[i][0]), C.c_void_p(b.data_ptr() + 4 * offs[i][1]),
+             C.c_void_p(y.data_ptr() + 4 * i * m * n), j - i, m, n, k, sa, sb, code, float(post_a), float(post_b),
+             C.c_void_p(ws.data_ptr()), ws_bytes.value, C.c_void_p(_stream(stream)))
+        i = j
+    return y
+
+
 PREC_SPLIT_BF16, PREC_BF16 = 0, 1
 DT_BF16, DT_F16 = 1, 2
 _HALF_TORCH = {DT_BF16: "bfloat16", DT_F16: "float16"}
