@@ -465,10 +465,28 @@ def other_rows(ops, W, torch, dev, stream, flush, steps=30):
     mnet.view("input").copy_(torch.from_numpy(mobilenetv2.input_batch(0, 128)))
     mnet.capture()
     ms5 = timed(lambda: mnet.launch())
+    # its depthwise 3x3 convs (CUDA cores, HBM bound): each step alone, inputs
+    # far above L2 at batch 128; algorithmic bytes = input + output + weights
+    dw_ms, dw_bytes, dw_best = 0.0, 0, None
+    for t, (kind, j, ins, out, i) in enumerate(mnet.steps):
+        nd = mb.nodes[i]
+        if nd.op != "Conv" or nd.attrs.get("group", 1) == 1:
+            continue
+        ms = timed(lambda: mnet.run_step(t, stream.cuda_stream))
+        nbytes = 4 * (int(np.prod(mb.shapes[ins[0]])) + int(np.prod(mb.shapes[out])) + nd.attrs["w"].size)
+        dw_ms += ms
+        dw_bytes += nbytes
+        gbs = nbytes / ms / 1e6
+        if dw_best is None or gbs > dw_best[1]:
+            dw_best = (out, gbs)
     mnet.close()
     del mnet
     return {"config5_mobilenetv2_fp32": {"images_per_s": round(128 / ms5 * 1e3, 1), "ms_per_128": round(ms5, 4),
                                          "tflops": round(2 * mb.macs_per_image() * 128 / ms5 / 1e9, 1)},
+            "config5_depthwise_f32": {"ms_per_128": round(dw_ms, 4), "gb_per_s": round(dw_bytes / dw_ms / 1e6, 1),
+                                      "best_layer": dw_best[0], "best_gb_per_s": round(dw_best[1], 1),
+                                      "bytes": dw_bytes, "how": "every depthwise step of the forward alone, "
+                                      "CUDA events; bytes = fp32 input + output + weights"},
             "config1_conv_relu_fp32": {"ms": round(ms1, 5), "tflops": round(f1 / ms1 / 1e9, 1)},
             "config3_gemm_fp32": {"ms": round(ms3, 5), "tflops": round(f3 / ms3 / 1e9, 1)},
             "config3_qlinearmatmul": {"ms": round(msq, 5), "tops": round(f3 / msq / 1e9, 1)},
@@ -618,6 +636,8 @@ def main():
         pass
     bf16 = peaks.get("bf16_tflops")
     hbm = peaks.get("hbm_gbs") or 6650.0
+    if rows and "config5_depthwise_f32" in rows:
+        rows["config5_depthwise_f32"]["frac_of_hbm"] = round(rows["config5_depthwise_f32"]["gb_per_s"] / hbm, 4)
     two_bf16 = 2.0 * (bf16 or 1590.0)
     # int8 peak: the larger of the live library int8 GEMM probe and twice the
     # measured bf16 burst (dense int8 runs at twice the bf16 rate on B200);
