@@ -351,15 +351,21 @@ class DeviceNetwork:
         self._copy_stream = t.cuda.Stream(device=self.dev)
         self._staged = [t.cuda.Event(), t.cuda.Event()]
         self._consumed = [t.cuda.Event(), t.cuda.Event()]
+        self._d2h_stream = t.cuda.Stream(device=self.dev)
+        logits = self.view("logits")
+        self._logits = [t.empty_like(logits), t.empty_like(logits)]
+        self._kept = [t.cuda.Event(), t.cuda.Event()]
+        self._read = [t.cuda.Event(), t.cuda.Event()]
 
     def forward_many(self, x_hosts, out_hosts, between=None):
         """Pipelined forwards over a sequence of host batches: batch i's
         host-to-device copy runs on a second stream into staging buffer i % 2
         while batch i-1 is computed; forward i is the CUDA graph captured on
-        that staging buffer, followed by the copy of its logits to
-        out_hosts[i]. `between` (optional) is enqueued on the network's
-        stream before each forward. Returns after enqueueing; the caller
-        synchronises self.stream."""
+        that staging buffer; its logits are copied to one of two device
+        buffers and from there to out_hosts[i] on a third stream.
+        `between` (optional) is enqueued on the network's stream before each
+        forward. Returns after enqueueing, with self.stream ordered after the
+        last host copy; the caller synchronises self.stream."""
         from ._lib import call
         t = self.torch
         if not hasattr(self, "_stage_graphs"):
@@ -367,7 +373,7 @@ class DeviceNetwork:
             self.stream.synchronize()
             self._capture_staged()
         logits = self.view("logits")
-        cs = self._copy_stream
+        cs, ds = self._copy_stream, self._d2h_stream
         cs.wait_stream(self.stream)  # (work already enqueued on the network's stream comes first)
         for i, (xh, oh) in enumerate(zip(x_hosts, out_hosts)):
             k = i & 1
@@ -382,7 +388,17 @@ class DeviceNetwork:
                     between()
                 call("nnrcu_graph_launch", self._stage_graphs[k], C.c_void_p(self.stream.cuda_stream))
                 self._consumed[k].record(self.stream)
-                oh.copy_(logits, non_blocking=True)
+                # the logits leave through a device copy of their own, so that
+                # the next forward does not queue behind the device-to-host copy
+                if i >= 2:
+                    self.stream.wait_event(self._read[k])  # logits i - 2 have reached the host
+                self._logits[k].copy_(logits, non_blocking=True)
+                self._kept[k].record(self.stream)
+            with t.cuda.stream(ds):
+                ds.wait_event(self._kept[k])
+                oh.copy_(self._logits[k], non_blocking=True)
+                self._read[k].record(ds)
+        self.stream.wait_stream(ds)
         return out_hosts
 
     def close(self):
