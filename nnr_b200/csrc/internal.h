@@ -87,6 +87,7 @@ struct Op {
   int s2d_tpr = 0;              // A_ROWS: taps per s2d kernel row in K (0: hardware im2col instead)
   // device buffers (owned)
   void* wB = nullptr;
+  void* wBimg = nullptr;       // int8 B as per-(N tile, K slab) shared-memory images (bulk-copied)
   int32_t* colcorr = nullptr;
   int32_t* bias_i = nullptr;
   float* cs_arr = nullptr;
@@ -130,6 +131,11 @@ struct EpiParams;
 int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream);
 // Picks the N tile (64/128/256) that minimises the estimated waves x tile cost.
 int pick_bn(int M, int N, int nplane, int num_sms);
+// Lays B (through its tensor map: box kb_bytes x bn) out as the shared-memory
+// image of every (N tile, K slab), in that order, into out
+// (n_tiles * num_kb * bn * kb_bytes bytes). Synchronous.
+int pack_b_images(const CUtensorMap* tmB, int bn, int kb_bytes, int n_tiles, int num_kb, void* out);
+bool bimg_enabled();
 int num_sms();
 // Depthwise QLinearConv (qdw.cu).
 int qdw_create(const nnrcu_conv_desc& d, int oh, int ow, const int8_t* w_host, const float* w_scale, int n_w_scale,

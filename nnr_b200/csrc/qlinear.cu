@@ -51,6 +51,19 @@ int conv_out_dims(const nnrcu_conv_desc& d, int* oh, int* ow) {
 
 using namespace nnrcu;
 
+namespace nnrcu {
+// The int8 weights as shared-memory images per (N tile, K slab), read by the
+// engine with one contiguous bulk copy per slab (a tensor-map load moves a
+// 128-byte box row per few cycles; a 256-row B slab cost as much as the A
+// slab it multiplies).
+static int make_b_images(Op* op, int kslab) {
+  const int n_tiles = (op->N + op->bn - 1) / op->bn;
+  const size_t bytes = (size_t)n_tiles * op->num_kb * op->bn * kslab;
+  NNRCU_CUDA(cudaMalloc(&op->wBimg, bytes));
+  return pack_b_images(&op->tmB, op->bn, kslab, n_tiles, op->num_kb, op->wBimg);
+}
+}  // namespace nnrcu
+
 extern "C" {
 
 int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, const float* w_scale, int n_w_scale,
@@ -274,6 +287,7 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
     NNRCU_TRY(encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, op->kpad_bytes, op->npad, op->kpad_bytes,
                              op->kslab, op->bn,
                              op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
+    NNRCU_TRY(make_b_images(op, op->kslab));
   }
   *out = op;
   return NNRCU_OK;
@@ -336,6 +350,7 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
     if (rc != NNRCU_OK) return rc;
   }
   GatherGeom g{};
+  g.wb = bimg_enabled() ? static_cast<const uint8_t*>(op->wBimg) : nullptr;
   g.x = xin;
   g.x2 = nullptr;
   // a spatially pre-padded input is convolved with zero pads
@@ -516,6 +531,7 @@ int nnrcu_qlinearmatmul_create(int m, int k, int n, float a_scale, uint8_t a_zp,
   NNRCU_TRY(upload(&op->colcorr, colcorr));
   NNRCU_TRY(encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, op->kpad_bytes, op->npad, op->kpad_bytes,
                            BKB, op->bn));
+  NNRCU_TRY(make_b_images(op, BKB));
   *out = op;
   return NNRCU_OK;
 }
@@ -546,6 +562,7 @@ int nnrcu_qlinearmatmul_run(nnrcu_op* op, const uint8_t* a, uint8_t* y, void* wo
     if (rc != NNRCU_OK) return rc;
   }
   GatherGeom g{};
+  g.wb = bimg_enabled() ? static_cast<const uint8_t*>(op->wBimg) : nullptr;
   g.x = ain;
   g.N = 1; g.H = 1; g.W = op->M;
   g.cbytes = op->cs;

@@ -105,6 +105,12 @@ bool shift_enabled() {
   return !(v && v[0] == '0');
 }
 
+bool bimg_enabled() {
+  // int8 engine: B from shared-memory images by plain bulk copies; NNRCU_BIMG=0 keeps the tensor-map loads
+  const char* v = std::getenv("NNRCU_BIMG");
+  return !(v && v[0] == '0');
+}
+
 bool r2_sat_enabled() {
   // R2 epilogue with y_zp = 0 as one saturating conversion; NNRCU_R2SAT=0 turns it off
   const char* v = std::getenv("NNRCU_R2SAT");
@@ -307,7 +313,7 @@ int nnrcu_op_num_ops(const nnrcu_op* op, int64_t* ops) {
 }
 int nnrcu_op_destroy(nnrcu_op* op) {
   if (!op) return NNRCU_OK;
-  void* bufs[] = {op->wB, op->colcorr, op->bias_i, op->cs_arr, op->bias_f, op->os, op->bias, op->cmat, op->w_dw};
+  void* bufs[] = {op->wB, op->wBimg, op->colcorr, op->bias_i, op->cs_arr, op->bias_f, op->os, op->bias, op->cmat, op->w_dw};
   int rc = NNRCU_OK;
   for (void* b : bufs)
     if (b && cudaFree(b) != cudaSuccess) rc = set_error(NNRCU_ERR_CUDA, "cudaFree failed in nnrcu_op_destroy");

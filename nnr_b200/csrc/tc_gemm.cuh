@@ -74,7 +74,27 @@ __device__ unsigned long long g_trace2[2 * 24 * 4 * 16];
   do {                                                                                  \
     if (blockIdx.x < 2 && (t) < 4 && (ev) < 16) g_trace2[((blockIdx.x * 24 + (w)) * 4 + (t)) * 16 + (ev)] = clock64(); \
   } while (0)
+// per launch (trace_seq): earliest CTA start, latest CTA end, earliest CTA
+// end, latest CTA start, in globaltimer ns
+__device__ unsigned long long g_span[256 * 4];
+#define NNRCU_SPAN_BEGIN() const unsigned long long span_t0 = ptx::globaltimer()
+#define NNRCU_SPAN_END()                                                                       \
+  do {                                                                                         \
+    if (threadIdx.x == 0 && e.trace_seq >= 0 && e.trace_seq < 256) {                            \
+      const unsigned long long t1 = ptx::globaltimer();                                        \
+      atomicMin(&g_span[e.trace_seq * 4 + 0], span_t0);                                        \
+      atomicMax(&g_span[e.trace_seq * 4 + 1], t1);                                             \
+      atomicMin(&g_span[e.trace_seq * 4 + 2], t1);                                             \
+      atomicMax(&g_span[e.trace_seq * 4 + 3], span_t0);                                        \
+    }                                                                                          \
+  } while (0)
 #else
+#define NNRCU_SPAN_BEGIN() \
+  do {                     \
+  } while (0)
+#define NNRCU_SPAN_END() \
+  do {                   \
+  } while (0)
 #define NNRCU_TRACE2_AT(w, t, ev) \
   do {                            \
   } while (0)
@@ -163,6 +183,7 @@ struct EpiParams {
   // row img * o_hwp + oy * o_wp + ox + o_off (o_off = top * o_wp + left)
   int opad, o_w, o_hw, o_wp, o_hwp, o_off;
   int* status;             // device status word (first error wins)
+  int trace_seq;           // trace builds: this launch's slot in g_span
 };
 
 // NKBR > 0: the whole B operand (num_kb <= NKBR slabs of one N tile) stays
@@ -365,6 +386,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   constexpr int A_BYTES = Cfg::A_BYTES;
   constexpr int B_BYTES = Cfg::B_BYTES;
 
+  NNRCU_SPAN_BEGIN();
   extern __shared__ uint8_t smem_raw[];
   {
     // the launch must provide this instance's whole layout (checked before any shared access)
@@ -471,7 +493,12 @@ if constexpr (AMODE == A_ROWS) {
         // multiple of n_tiles, so a CTA's tiles all have N tile blockIdx.x % n_tiles)
         const int bn0 = (int)(blockIdx.x % n_tiles) * BN;
         ptx::mbar_arrive_expect_tx(bres_bar, (uint32_t)(num_kb * B_BYTES));
-        for (int kb = 0; kb < num_kb; ++kb) ptx::tma_load_2d(sB + (size_t)kb * B_BYTES, &tmB, bres_bar, kb * KB, bn0);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (g.wb)  // the slab's shared-memory image: one plain bulk copy
+            ptx::bulk_load(sB + (size_t)kb * B_BYTES, g.wb + ((size_t)(bn0 / BN) * num_kb + kb) * B_BYTES, B_BYTES, bres_bar);
+          else
+            ptx::tma_load_2d(sB + (size_t)kb * B_BYTES, &tmB, bres_bar, kb * KB, bn0);
+        }
       }
       if constexpr (AMODE == A_SHIFT) {
         // one patch per tile: each K slab's rows [m0, m0 + prows) of the padded input
@@ -543,9 +570,16 @@ if constexpr (AMODE == A_ROWS) {
             }
             }
           } else {
-          if (NKBR == 0)
-            for (int p = 0; p < PL; ++p)
-              ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
+          if (NKBR == 0) {
+            if (NPLANE == 1 && g.wb) {
+              // B's shared-memory image for (N tile, K slab): one contiguous
+              // bulk copy instead of BN tensor-map rows
+              ptx::bulk_load(b_st, g.wb + ((size_t)(n0 / BN) * num_kb + kb) * B_BYTES, B_BYTES, &full_bar[s]);
+            } else {
+              for (int p = 0; p < PL; ++p)
+                ptx::tma_load_2d(b_st + p * B_BYTES, &tmB, &full_bar[s], kx, p * b_plane_rows + n0);
+            }
+          }
           if (AMODE == A_TMA) {
             ptx::tma_load_2d(a_st, &tmA0, &full_bar[s], kx, m0);
             if (NPLANE == 2) ptx::tma_load_2d(a_st + A_BYTES, &tmA1, &full_bar[s], kx, m0);
@@ -1395,6 +1429,7 @@ if constexpr (AMODE == A_ROWS) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
+  NNRCU_SPAN_END();
 }
 
 }  // namespace nnrcu

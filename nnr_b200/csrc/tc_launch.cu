@@ -8,6 +8,34 @@ namespace nnrcu {
 
 namespace {
 
+// One (N tile, K slab) box of B per block: loaded by the tensor map (so the
+// shared-memory swizzle is exactly the one the engine's loads produce), then
+// written out as a contiguous image.
+__global__ void pack_b_images_kernel(const __grid_constant__ CUtensorMap tmB, int bn, int kb, int num_kb,
+                                     uint8_t* __restrict out, int* status) {
+  extern __shared__ uint8_t raw[];
+  __shared__ uint64_t bar;
+  uint8_t* sm = raw + ((1024u - (ptx::smem_u32(raw) & 1023u)) & 1023u);
+  const uint32_t bytes = (uint32_t)(bn * kb);
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(&bar, 1);
+    ptx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    ptx::mbar_arrive_expect_tx(&bar, bytes);
+    ptx::tma_load_2d(sm, &tmB, &bar, (int)blockIdx.y * kb, (int)blockIdx.x * bn);
+  }
+  if (!ptx::mbar_wait(&bar, 0u)) {
+    if (threadIdx.x == 0) record_status(status, ST_TIMEOUT_FULL);
+    ptx::settle_ns(200000);
+    return;
+  }
+  uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)blockIdx.x * num_kb + blockIdx.y) * bytes);
+  const uint4* src = reinterpret_cast<const uint4*>(sm);
+  for (uint32_t i = threadIdx.x; i < bytes / 16; i += blockDim.x) dst[i] = src[i];
+}
+
 template <int BN, int NPLANE, int AMODE, int EPI, int KB = BKB, int NKBR = 0>
 int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
   using Cfg = KernelCfg<BN, NPLANE, AMODE, EPI, KB, NKBR>;
@@ -196,7 +224,43 @@ extern "C" int nnrcu_trace2_read(void* host, size_t bytes) {
 }
 #endif
 
-int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaStream_t stream) {
+#ifdef NNRCU_TRACE
+static int g_span_next = 0;
+extern "C" int nnrcu_span_reset(void) {
+  // slots restart at 0 (for the next capture); spans are cleared to (max, 0, max, 0)
+  g_span_next = 0;
+  static unsigned long long init[256 * 4];
+  for (int i = 0; i < 256; ++i) init[i * 4] = init[i * 4 + 2] = ~0ull, init[i * 4 + 1] = init[i * 4 + 3] = 0;
+  NNRCU_CUDA(cudaMemcpyToSymbol(g_span, init, sizeof(init)));
+  return NNRCU_OK;
+}
+extern "C" int nnrcu_span_read(void* host, size_t bytes) {
+  NNRCU_CUDA(cudaDeviceSynchronize());
+  NNRCU_CUDA(cudaMemcpyFromSymbol(host, g_span, bytes < sizeof(g_span) ? bytes : sizeof(g_span)));
+  return NNRCU_OK;
+}
+#endif
+
+int pack_b_images(const CUtensorMap* tmB, int bn, int kb_bytes, int n_tiles, int num_kb, void* out) {
+  const int smem = bn * kb_bytes + 1024;
+  NNRCU_CUDA(cudaFuncSetAttribute(pack_b_images_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  pack_b_images_kernel<<<dim3(n_tiles, num_kb), 256, smem>>>(*tmB, bn, kb_bytes, num_kb, static_cast<uint8_t*>(out),
+                                                              status_ptr());
+  NNRCU_CUDA(cudaGetLastError());
+  NNRCU_CUDA(cudaDeviceSynchronize());
+  int st = 0;
+  NNRCU_CUDA(cudaMemcpy(&st, status_ptr(), sizeof(int), cudaMemcpyDeviceToHost));
+  if (st) return set_error(NNRCU_ERR_CUDA, "packing the weight images timed out (status %d)", st);
+  return NNRCU_OK;
+}
+
+int tc_launch(const TcLaunch& L, const GatherGeom& g, const EpiParams& e_in, cudaStream_t stream) {
+  EpiParams e = e_in;
+#ifdef NNRCU_TRACE
+  e.trace_seq = g_span_next++;
+#else
+  e.trace_seq = -1;
+#endif
   if (L.m_tiles <= 0 || L.n_tiles <= 0 || L.num_kb <= 0) return NNRCU_OK;
   if ((long long)L.m_tiles * L.n_tiles > 0x7fffffffLL)
     return set_error(NNRCU_ERR_INVALID, "too many tiles (%d x %d)", L.m_tiles, L.n_tiles);
