@@ -356,6 +356,42 @@ def node_bytes(model, net, t):
     return b
 
 
+def nnr_plugin_e2e(model, x_np, steps, device, flush, torch):
+    """The same forward through nnr's own application path with the CUDA
+    backend (libnnr_cuda.so: nnr's loader, fusion passes and run loop,
+    preferred_backend = CUDA): the batch sits in nnr's own input tensor
+    (host memory, filled in place), and every step is run() (upload, the
+    replayed device graph, download) plus reading the logits; host wall
+    clock around each step, L2 flushed before it."""
+    from nnr_b200 import nnr_cuda as NC, onnx_models as M
+    if not NC.available():
+        return {"unavailable": "libnnr_cuda.so not built"}
+    net = NC.NnrCudaModel(M.resnet50_qdq(model), device=device)
+    try:
+        net.input_array("input")[...] = x_np
+        for _ in range(3):
+            net.run()
+            net.get("logits")
+        ts = []
+        for _ in range(steps):
+            flush.zero_()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            net.run()
+            net.get("logits")
+            ts.append(time.perf_counter() - t0)
+        st = net.stats()
+    finally:
+        net.close()
+    ms = statistics.median(ts) * 1e3
+    return {"value": round(x_np.shape[0] / ms * 1e3, 1), "unit": UNIT, "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": int(x_np.nbytes), "d2h_bytes_per_step": int(x_np.shape[0] * 1000 * 4),
+            "n_gpus": 1, "graph_replays": st.get("graph_replays"), "device_ops": st.get("device_ops"),
+            "host_ops": st.get("host_ops"),
+            "mode": "nnr context_t::run() with the CUDA backend (nnr's memory planner off: its run() clears every "
+                    "planned host slot each call), graph inputs/outputs page-locked, median of per-step wall clock"}
+
+
 def int8_peak_probe(torch, dev, n=8192, reps=10):
     """Dense int8 tensor throughput of a large library GEMM (torch._int_mm,
     cuBLASLt; a probe only, not on the hot path): best of `reps` 8192^3
@@ -619,6 +655,7 @@ def main():
         int8_probe = int8_peak_probe(torch, dev) if rank == 0 else None
         c2 = config2_qlinearconv(ops, W, torch, dev, stream, flush) if rank == 0 else None
         rows = other_rows(ops, W, torch, dev, stream, flush) if rank == 0 else None
+        plugin = nnr_plugin_e2e(model, x_np, args.steps, local, flush, torch) if rank == 0 else None
     assert ops.device_status() == 0
 
     t = torch.tensor([dev_ms, e2e_ms, e2e_serial_ms], dtype=torch.float64, device=dev)
@@ -687,7 +724,8 @@ def main():
                     "serial_value": round(world * BATCH / (e2e_serial_ms / args.steps / 1e3), 1),
                     "h2d_gbs_per_rank": round(link_gbs, 1),
                     "link_bound_images_per_s": round(world * BATCH / (x_np.nbytes / (link_gbs * 1e9)), 1),
-                    "serial_mode": "DeviceNetwork.forward: H2D, forward, D2H in sequence, per-step events"},
+                    "serial_mode": "DeviceNetwork.forward: H2D, forward, D2H in sequence, per-step events",
+                    "nnr_plugin": plugin},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(peak, 1), "unit": "TOPS",
                          "frac": round(achieved / peak, 4), "traffic": TC_TRAFFIC_BYTES,
                          "traffic_unit": "bytes per forward (DRAM read + write of all tc_gemm launches, one ncu capture)",

@@ -101,6 +101,11 @@ int nnrcu_free(void* ptr);
 int nnrcu_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
 int nnrcu_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
 int nnrcu_memset(void* dst, int value, size_t bytes, void* stream);
+/* Page-lock an existing host buffer (a graph input or output that nnr owns)
+ * so that copies from and to it run at the link's rate and asynchronously;
+ * a buffer already registered is accepted. nnrcu_host_unregister undoes it. */
+int nnrcu_host_register(void* ptr, size_t bytes);
+int nnrcu_host_unregister(void* ptr);
 /* Stream capture of a run loop into one CUDA graph (replaces nnr's
  * exec_steps loop, src/nnr.cpp:908-1051, for a fixed batch). */
 int nnrcu_graph_begin(void* stream);

@@ -56,6 +56,8 @@ SIGNATURES = {
     "nnrcu_memcpy_h2d": [P, P, SZ, P],
     "nnrcu_memcpy_d2h": [P, P, SZ, P],
     "nnrcu_memset": [P, I, SZ, P],
+    "nnrcu_host_register": [P, SZ],
+    "nnrcu_host_unregister": [P],
     "nnrcu_graph_begin": [P],
     "nnrcu_graph_end": [P, PP],
     "nnrcu_graph_launch": [P, P],

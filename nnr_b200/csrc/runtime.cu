@@ -277,6 +277,20 @@ int nnrcu_memset(void* dst, int value, size_t bytes, void* stream) {
   NNRCU_CUDA(cudaMemsetAsync(dst, value, bytes, static_cast<cudaStream_t>(stream)));
   return NNRCU_OK;
 }
+int nnrcu_host_register(void* ptr, size_t bytes) {
+  if (!ptr || !bytes) return set_error(NNRCU_ERR_INVALID, "NULL or empty host buffer");
+  const cudaError_t e = cudaHostRegister(ptr, bytes, cudaHostRegisterDefault);
+  if (e == cudaErrorHostMemoryAlreadyRegistered) {
+    (void)cudaGetLastError();
+    return NNRCU_OK;
+  }
+  NNRCU_CUDA(e);
+  return NNRCU_OK;
+}
+int nnrcu_host_unregister(void* ptr) {
+  NNRCU_CUDA(cudaHostUnregister(ptr));
+  return NNRCU_OK;
+}
 int nnrcu_graph_begin(void* stream) {
   NNRCU_CUDA(cudaStreamBeginCapture(static_cast<cudaStream_t>(stream), cudaStreamCaptureModeThreadLocal));
   return NNRCU_OK;

@@ -55,6 +55,17 @@ int nnrcuda_set_input(void* h, const char* name, const void* data, size_t bytes)
   return 0;
 }
 
+// A graph input's own host buffer (nnr's tensor_t::data) and its size: an
+// application may fill it in place instead of passing a copy to
+// nnrcuda_set_input (nnr's own applications write tensor data directly).
+int nnrcuda_input_buffer(void* h, const char* name, void** data, size_t* bytes) {
+  tensor_t* t = static_cast<context_t*>(h)->search_tensor(name);
+  if (!t || !t->data || !data || !bytes) return -1;
+  *data = t->data;
+  *bytes = t->ndata * data_type_sizeof(t);
+  return 0;
+}
+
 int nnrcuda_run(void* h) { return static_cast<context_t*>(h)->run() ? 0 : -1; }
 
 int nnrcuda_tensor_info(void* h, const char* name, int* dims, int* ndim, int* type, int* format) {

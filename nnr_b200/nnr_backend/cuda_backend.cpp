@@ -83,6 +83,8 @@ void device_state_t::invalidate() {
   }
   if (arena) nnrcu_free(arena);
   if (workspace) nnrcu_free(workspace);
+  for (void* p : pinned) nnrcu_host_unregister(p);
+  pinned.clear();
   for (auto& [t, p] : consts) nnrcu_free(p);
   arena = workspace = nullptr;
   arena_bytes = workspace_bytes = 0;
@@ -239,6 +241,22 @@ bool device_state_t::setup() {
     }
     if (host_reads) downloads[producer[c]].push_back(c);
   }
+
+  // graph inputs uploaded and graph outputs downloaded every run: page-lock
+  // their host buffers (nnr's own allocations), so that those copies run at
+  // the link's rate instead of through pageable staging
+  auto pin = [&](tensor_t* c) {
+    const size_t b = tensor_bytes(c);
+    if (!c->data || b < (1u << 16)) return;  // (small buffers gain nothing)
+    if (std::find(pinned.begin(), pinned.end(), c->data) != pinned.end()) return;
+    if (nnrcu_host_register(c->data, b) == NNRCU_OK) pinned.push_back(c->data);
+  };
+  for (auto& [op, list] : uploads)
+    for (auto* c : list)
+      if (graph_in.count(c)) pin(c);
+  for (auto& [op, list] : downloads)
+    for (auto* c : list)
+      if (graph_out.count(c)) pin(c);
 
   // arena: one slot per distinct host buffer (nnr's memory plan), the
   // largest tensor that uses it deciding its size

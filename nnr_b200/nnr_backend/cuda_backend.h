@@ -84,6 +84,7 @@ struct device_state_t {
   std::unordered_map<const operator_t*, std::vector<tensor_t*>> uploads;  // H2D before an op
   std::unordered_map<const operator_t*, std::vector<tensor_t*>> downloads; // D2H after an op
   std::vector<cuda_op_t*> order;  // CUDA operators in execution order
+  std::vector<void*> pinned;      // page-locked host buffers of graph inputs / outputs
   bool all_device = false;
 
   // graph mode

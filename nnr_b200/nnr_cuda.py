@@ -44,6 +44,7 @@ def lib() -> C.CDLL:
         _lib.nnrcuda_run.argtypes = [C.c_void_p]
         _lib.nnrcuda_num_nodes.argtypes = [C.c_void_p]
         _lib.nnrcuda_set_input.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]
+        _lib.nnrcuda_input_buffer.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(C.c_void_p), C.POINTER(C.c_size_t)]
         _lib.nnrcuda_get.argtypes = [C.c_void_p, C.c_char_p, C.c_void_p, C.c_size_t]
         _lib.nnrcuda_tensor_info.argtypes = [C.c_void_p, C.c_char_p, C.POINTER(C.c_int), C.POINTER(C.c_int),
                                              C.POINTER(C.c_int), C.POINTER(C.c_int)]
@@ -57,7 +58,12 @@ def lib() -> C.CDLL:
 class NnrCudaModel:
     """One nnr context on one GPU with preferred_backend = CUDA."""
 
-    def __init__(self, model: bytes, device: int = 0, memory_planning: bool = True, graphs: bool = True):
+    def __init__(self, model: bytes, device: int = 0, memory_planning: bool = False, graphs: bool = True):
+        """memory_planning: nnr's host memory planner. With the graph on the
+        device, the plan only decides which tensors share a device slot,
+        while nnr's run() still clears every planned host slot on each call
+        (memory_planner.cpp zero_pool: ~15 ms per ResNet-50 batch of 32), so
+        it is off by default here."""
         self._buf = model  # nnr's tensors may alias the proto buffer: keep it alive
         self.h = lib().nnrcuda_load(model, len(model), device, int(memory_planning), int(graphs))
         if not self.h:
@@ -72,6 +78,16 @@ class NnrCudaModel:
         arr = np.ascontiguousarray(arr)
         if lib().nnrcuda_set_input(self.h, name.encode(), arr.ctypes.data, arr.nbytes) != 0:
             raise RuntimeError(f"nnr: cannot set input {name}")
+
+    def input_array(self, name: str) -> np.ndarray:
+        """A writable numpy view of a graph input's own host buffer (filled in
+        place, no copy through set()); valid until the model is closed."""
+        shape, ty, _ = self.info(name)
+        ptr, nbytes = C.c_void_p(), C.c_size_t()
+        if lib().nnrcuda_input_buffer(self.h, name.encode(), C.byref(ptr), C.byref(nbytes)) != 0:
+            raise KeyError(name)
+        buf = (C.c_uint8 * nbytes.value).from_address(ptr.value)
+        return np.frombuffer(buf, dtype=_DT[ty]).reshape(shape)
 
     def run(self) -> None:
         if lib().nnrcuda_run(self.h) != 0:

@@ -70,15 +70,17 @@ def test_mobilenetv2_graph_on_device():
 
 # ------------------------------------------------------------------ on the device
 @pytest.mark.gpu
-@pytest.mark.parametrize("batch", [2, 32])
-def test_resnet50_through_nnr_bit_exact(cuda_dev, batch):
+@pytest.mark.parametrize("batch,planning", [(2, True), (32, True), (32, False)])
+def test_resnet50_through_nnr_bit_exact(cuda_dev, batch, planning):
     """nnr's run loop on the device gives the oracle's logits exactly, in the
-    eager first run, the captured second run and replayed runs."""
+    eager first run, the captured second run and replayed runs, with nnr's
+    memory planner (device slots keyed by its planned host buffers) and
+    without it."""
     from nnr_b200 import onnx_models as M
     from nnr_b200 import resnet50
     from oracle import oracle as O
     model = resnet50.build(batch=batch)
-    net = NC.NnrCudaModel(M.resnet50_qdq(model))
+    net = NC.NnrCudaModel(M.resnet50_qdq(model), memory_planning=planning)
     try:
         for i in range(4):
             x = resnet50.input_batch(batch * i, batch)
