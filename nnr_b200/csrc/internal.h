@@ -136,6 +136,8 @@ int pick_bn(int M, int N, int nplane, int num_sms);
 // (n_tiles * num_kb * bn * kb_bytes bytes). Synchronous.
 int pack_b_images(const CUtensorMap* tmB, int bn, int kb_bytes, int n_tiles, int num_kb, void* out);
 bool bimg_enabled();
+bool xrows_enabled();
+bool xrows_map_ok();
 int num_sms();
 // Depthwise QLinearConv (qdw.cu).
 int qdw_create(const nnrcu_conv_desc& d, int oh, int ow, const int8_t* w_host, const float* w_scale, int n_w_scale,

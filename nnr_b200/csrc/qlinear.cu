@@ -192,6 +192,15 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
     op->kbytes = taps * 16;
     op->kpad_bytes = op->num_kb * 128;
     op->bn = std::min(op->bn, 128);
+    // four taps per kernel row: 64-byte kernel rows through an overlapping-row
+    // tensor map (A_XROWS), if the driver accepts that map
+    if (op->s2d_tpr == 4 && xrows_enabled() && xrows_map_ok()) {
+      op->amode = A_XROWS;
+      op->kslab = 64;
+      op->num_kb = op->s2d_kh;
+      op->kbytes = op->s2d_kh * 64;
+      op->kpad_bytes = round_up(op->kbytes, BKB);
+    }
   }
   // Shifted-patch mode (A_SHIFT in tc_gemm.cuh): stride-1 spatial convs over
   // whole 64/128-byte channel slabs whose K slabs (at most 9) fit a resident
@@ -241,7 +250,11 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
       for (int y = 0; y < d.kh; ++y)
         for (int x = 0; x < d.kw; ++x) {
           const int8_t v = w_host[(((size_t)o * d.c + ic) * d.kh + y) * d.kw + x];
-          if (op->s2d) {
+          if (op->s2d && op->amode == A_XROWS) {
+            // K-major [npad][kpad]: s2d tap (ky, kx) at (ky * 4 + kx) * 16
+            const int ry = y + 2 * op->s2d_pt - d.pad_top, rx = x + 2 * op->s2d_pl - d.pad_left;
+            B[(size_t)o * op->kpad_bytes + (size_t)((ry >> 1) * 4 + (rx >> 1)) * 16 + ((ry & 1) * 2 + (rx & 1)) * d.c + ic] = v;
+          } else if (op->s2d) {
             // per (N tile, K slab) the stage's smem image [8 taps][bn rows][16 B]:
             // s2d tap (ky, kx), byte (dy * 2 + dx) * C + ic
             const int ry = y + 2 * op->s2d_pt - d.pad_top, rx = x + 2 * op->s2d_pl - d.pad_left;
@@ -283,7 +296,7 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   NNRCU_TRY(upload(&op->cs_arr, csv));
   NNRCU_TRY(upload(&op->bias_f, bias_f));
   NNRCU_TRY(upload(&op->os, osv));
-  if (!op->s2d) {  // (the s2d weights are read by plain bulk copies)
+  if (!op->s2d || op->amode == A_XROWS) {  // (A_ROWS s2d weights are read by plain bulk copies)
     NNRCU_TRY(encode_tmap_2d(&op->tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, wB, op->kpad_bytes, op->npad, op->kpad_bytes,
                              op->kslab, op->bn,
                              op->kslab == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B));
@@ -367,7 +380,16 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
     g.sh = g.sw = 1; g.ph = g.pw = 0; g.dh = g.dw = 1;
     g.tpr = op->s2d_tpr;
     g.wb = static_cast<const uint8_t*>(op->wB);
-    if (!op->s2d_tpr) {
+    if (op->amode == A_XROWS) {
+      // rows 16 bytes apart, 64 bytes wide: row p = s2d pixels p .. p + 3.
+      // Every pixel starts a row; the last rows reach up to 48 bytes past the
+      // image into the workspace's slack (taps past the kernel width have
+      // zero weights, and real taps never leave the image)
+      g.wb = bimg_enabled() ? static_cast<const uint8_t*>(op->wBimg) : nullptr;
+      int rc = encode_tmap_2d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, xin, 64, (uint64_t)g.N * g.H * g.W, 16, 64, BM,
+                              CU_TENSOR_MAP_SWIZZLE_64B);
+      if (rc != NNRCU_OK) return rc;
+    } else if (!op->s2d_tpr) {
       int rc = encode_tmap_im2col(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, xin, g.N, g.H, g.W, 16, 0, 0, 0, 0, g.KH,
                                   g.KW, 1, 1, 1, 1, 16);
       if (rc != NNRCU_OK) return rc;
@@ -427,7 +449,8 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
 
   TcLaunch L{};
   L.bn = op->bn; L.nplane = 1; L.amode = op->amode; L.epi = op->epi;
-  L.m_tiles = op->amode == A_ROWS ? d.n * op->oh * ((op->ow + BM - 1) / BM) : (op->M + BM - 1) / BM;
+  L.m_tiles = (op->amode == A_ROWS || op->amode == A_XROWS) ? d.n * op->oh * ((op->ow + BM - 1) / BM)
+                                                            : (op->M + BM - 1) / BM;
   if (op->amode == A_SHIFT) {
     // GEMM rows = padded-grid positions up to the last output pixel
     e.M = ((d.n - 1) * g.H + op->oh - 1) * g.W + op->ow;

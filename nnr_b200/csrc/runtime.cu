@@ -105,6 +105,30 @@ bool shift_enabled() {
   return !(v && v[0] == '0');
 }
 
+bool xrows_enabled() {
+  // space-to-depth convs as 64-byte kernel rows (A_XROWS); NNRCU_XROWS=0 keeps A_ROWS
+  const char* v = std::getenv("NNRCU_XROWS");
+  return !(v && v[0] == '0');
+}
+
+bool xrows_map_ok() {
+  // whether the driver encodes a tensor map whose 64-byte rows are 16 bytes
+  // apart (checked once per process on a scratch allocation)
+  static int ok = -1;
+  if (ok < 0) {
+    void* p = nullptr;
+    ok = 0;
+    if (cudaMalloc(&p, 1 << 20) == cudaSuccess) {
+      CUtensorMap m{};
+      ok = encode_tmap_2d(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, p, 64, (1 << 16) - 3, 16, 64, 128,
+                          CU_TENSOR_MAP_SWIZZLE_64B) == NNRCU_OK;
+      cudaFree(p);
+    }
+    (void)cudaGetLastError();
+  }
+  return ok == 1;
+}
+
 bool bimg_enabled() {
   // int8 engine: B from shared-memory images by plain bulk copies; NNRCU_BIMG=0 keeps the tensor-map loads
   const char* v = std::getenv("NNRCU_BIMG");

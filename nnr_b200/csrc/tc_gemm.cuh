@@ -48,7 +48,12 @@ namespace nnrcu {
 // once, and every tap is a view of it starting at a shifted row. The 64/128-
 // byte swizzle is a function of the shared-memory address, so a view may
 // start at any row of the swizzled patch. B is resident.
-enum : int { A_TMA = 0, A_GATHER = 1, A_IM2COL = 2, A_ROWS = 3, A_SHIFT = 4 };
+// A_XROWS: the same space-to-depth convs with 4 taps per kernel row, read
+// as 64-byte rows: a 2-D tensor map over the s2d image whose rows are 16
+// bytes apart (row p = taps p .. p + 3 of one s2d row), so that one K slab is
+// one kernel row of a tile in the 64-byte swizzled layout (a swizzled MMA
+// operand instead of the 16-byte-interleaved one of A_ROWS).
+enum : int { A_TMA = 0, A_GATHER = 1, A_IM2COL = 2, A_ROWS = 3, A_SHIFT = 4, A_XROWS = 5 };
 constexpr int ROWS_BYTES = (128 + 8) * 16;  // one A_ROWS copy: BM + 8 pixels of 16 bytes
 // EPI_R2A: the R2 requant followed by a fused QLinearAdd whose residual
 // tiles are TMA-prefetched one tile ahead (u8 row-major output via TMA store).
@@ -463,7 +468,7 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   // Output rows of an M tile: mb = first GEMM row, nvr = valid rows; A_ROWS
   // tiles also give the output row (image * OH + oh) and first column ow0.
   auto tile_rows = [&](const int mt, int& mb, int& nvr, int& orow, int& ow0) {
-if constexpr (AMODE == A_ROWS) {
+if constexpr (AMODE == A_ROWS || AMODE == A_XROWS) {
       const int owt = (g.OW + BM - 1) / BM;
       orow = mt / owt;
       ow0 = (mt - orow * owt) * BM;
@@ -533,7 +538,7 @@ if constexpr (AMODE == A_ROWS) {
           i_w = (p - oh * g.OW) * g.sw - g.pw;
         }
         int r_mb = 0, r_nvr = 0, r_orow = 0, r_ow0 = 0;
-        if (AMODE == A_ROWS) tile_rows(tile / n_tiles, r_mb, r_nvr, r_orow, r_ow0);
+        if (AMODE == A_ROWS || AMODE == A_XROWS) tile_rows(tile / n_tiles, r_mb, r_nvr, r_orow, r_ow0);
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           if (R::NPROD > 1 && it % R::NPROD != pw) continue;
           const int s = it % STAGES;
@@ -583,6 +588,10 @@ if constexpr (AMODE == A_ROWS) {
           if (AMODE == A_TMA) {
             ptx::tma_load_2d(a_st, &tmA0, &full_bar[s], kx, m0);
             if (NPLANE == 2) ptx::tma_load_2d(a_st + A_BYTES, &tmA1, &full_bar[s], kx, m0);
+          } else if (AMODE == A_XROWS) {
+            // kernel row kb of the tile's output row: 128 consecutive 64-byte rows
+            const int img = r_orow / g.OH, oh = r_orow - img * g.OH;
+            ptx::tma_load_2d(a_st, &tmA0, &full_bar[s], 0, ((img * g.H + oh + kb) * g.W + r_ow0));
           } else if (AMODE == A_IM2COL) {
             // one K slab = 128 bytes of channels of a single filter tap
             const int kbyte = kb * KB;
@@ -1147,7 +1156,7 @@ if constexpr (AMODE == A_ROWS) {
         if (direct)
           fast = shift_direct && n0 + BN <= e.N && e.qres == nullptr;
         else
-          fast = y_tma && (AMODE == A_ROWS || m0 + BM <= e.M) && n0 + BN <= e.N &&
+          fast = y_tma && (AMODE == A_ROWS || AMODE == A_XROWS || m0 + BM <= e.M) && n0 + BN <= e.N &&
                (EPI == EPI_R2A ? (long long)(m0 + BM) * e.N <= e.qa_vec_end : e.qres == nullptr);
       }
       auto chunk_fast = [&](const int c0, uint32_t (&v)[CW]) {
@@ -1409,7 +1418,7 @@ if constexpr (AMODE == A_ROWS) {
             for (int h = 0; h < Cfg::ROW_BYTES / SEG; ++h)
               if (n0 + col0 + h * SEGE < e.N) {
                 // A_ROWS: map [rows][OW][N], pixels past OW are clipped
-                if (AMODE == A_ROWS)
+                if (AMODE == A_ROWS || AMODE == A_XROWS)
                   ptx::tma_store_3d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEGE, ow0 + eq * 32, orow);
                 else
                   ptx::tma_store_2d(&tmY, stg + h * (32 * SEG), n0 + col0 + h * SEGE, m0 + eq * 32);

@@ -58,7 +58,7 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
   // warp's staged 32 x BN block (coalesced rows instead of per-lane pieces).
   CUtensorMap tmY{};
   int y_tma = 0;
-  if (AMODE == A_ROWS && EPI != EPI_F32 && e.y_layout == 0 && !e.opad && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
+  if ((AMODE == A_ROWS || AMODE == A_XROWS) && EPI != EPI_F32 && e.y_layout == 0 && !e.opad && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
       (e.ldy & 15) == 0) {
     // [output rows][OW][N]: a warp's 32 pixels of one output row, clipped at OW
     const int seg = Cfg::OUT_SEG;
@@ -70,7 +70,7 @@ int launch_one(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cudaS
                                        : (seg == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B));
     if (rc != NNRCU_OK) return rc;
     y_tma = 1;
-  } else if (AMODE != A_ROWS && AMODE != A_SHIFT && EPI != EPI_F32 && e.y_layout == 0 && !e.opad && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
+  } else if (AMODE != A_ROWS && AMODE != A_XROWS && AMODE != A_SHIFT && EPI != EPI_F32 && e.y_layout == 0 && !e.opad && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0 &&
              (e.ldy & 15) == 0) {
     const int seg = Cfg::OUT_SEG;
     int rc = encode_tmap_2d(&tmY, CU_TENSOR_MAP_DATA_TYPE_UINT8, e.y, (uint64_t)e.N, (uint64_t)e.M, (uint64_t)e.ldy,
@@ -151,6 +151,16 @@ int dispatch_bn(const TcLaunch& L, const GatherGeom& g, const EpiParams& e, cuda
     if (L.nplane != 1 || L.amode == A_GATHER)
       return set_error(NNRCU_ERR_INVALID, "64-byte K slabs need int8 or split-bf16 with a TMA-fed A operand");
     if (L.epi == EPI_R2A && L.amode == A_TMA) return launch_one<BN, 1, A_TMA, EPI_R2A, 64>(L, g, e, st);
+    if (L.amode == A_XROWS) {
+      // space-to-depth convs as 64-byte kernel rows (N tile <= 128)
+      if constexpr (BN <= 128) {
+        if (L.epi == EPI_R1) return launch_one<BN, 1, A_XROWS, EPI_R1, 64>(L, g, e, st);
+        if (L.epi == EPI_R2) return launch_one<BN, 1, A_XROWS, EPI_R2, 64>(L, g, e, st);
+        if (L.epi == EPI_R3) return launch_one<BN, 1, A_XROWS, EPI_R3, 64>(L, g, e, st);
+        if (L.epi == EPI_R3N) return launch_one<BN, 1, A_XROWS, EPI_R3N, 64>(L, g, e, st);
+      }
+      return set_error(NNRCU_ERR_INVALID, "no 64-byte-row s2d instance for bn %d epilogue %d", BN, L.epi);
+    }
     if (L.amode == A_IM2COL) {
       if (L.epi == EPI_R1) return launch_one<BN, 1, A_IM2COL, EPI_R1, 64>(L, g, e, st);
       if (L.epi == EPI_R2) return launch_one<BN, 1, A_IM2COL, EPI_R2, 64>(L, g, e, st);
