@@ -88,19 +88,11 @@ def dist_env():
 
 def load_model(batch, rank, world, barrier):
     """Rank 0 builds the seeded model once and shares it with the other ranks
-    through a file (the build includes a float calibration pass on the CPU)."""
-    from nnr_b200 import resnet50
-    if world == 1:
-        return resnet50.build(batch=batch)
+    (the build includes a float calibration pass on the CPU)."""
+    from nnr_b200 import replicas, resnet50
     port = os.environ.get("MASTER_PORT", "0")
-    path = Path(os.environ.get("TMPDIR", "/tmp")) / f"nnrcu_resnet50_s3_b{batch}_{port}.pkl"
-    if rank == 0:
-        m = resnet50.build(batch=batch)
-        tmp = path.with_suffix(".tmp")
-        tmp.write_bytes(pickle.dumps(m))
-        os.replace(tmp, path)
-    barrier()
-    return pickle.loads(path.read_bytes())
+    return replicas.build_once(lambda: resnet50.build(batch=batch), f"resnet50_s3_b{batch}_{port}", rank, world,
+                               barrier)
 
 
 # ------------------------------------------------------------------ clocks
@@ -552,7 +544,8 @@ def main():
 
     model = load_model(BATCH, rank, world, barrier)
     net = graph.DeviceNetwork(model, local)
-    x_np = resnet50.input_batch(BATCH * rank, BATCH)
+    from nnr_b200 import replicas
+    x_np = resnet50.input_batch(replicas.shard_offset(rank, BATCH), BATCH)
     x_host = torch.from_numpy(x_np).pin_memory()
     out_host = torch.empty(model.shapes["logits"], dtype=torch.float32).pin_memory()
     x_host2 = torch.from_numpy(resnet50.input_batch(BATCH * (rank + world), BATCH)).pin_memory()
@@ -658,13 +651,11 @@ def main():
         plugin = nnr_plugin_e2e(model, x_np, args.steps, local, flush, torch) if rank == 0 else None
     assert ops.device_status() == 0
 
-    t = torch.tensor([dev_ms, e2e_ms, e2e_serial_ms], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    dev_ms, e2e_ms, e2e_serial_ms = t.tolist()
+    dev_ms, e2e_ms, e2e_serial_ms = replicas.max_over_ranks([dev_ms, e2e_ms, e2e_serial_ms], world,
+                                                            dist if world > 1 else None, dev)
     ms = dev_ms / args.steps
-    value = world * BATCH / (ms / 1e3)
-    e2e_val = world * BATCH / (e2e_ms / args.steps / 1e3)
+    value = replicas.job_rate(BATCH, world, ms)
+    e2e_val = replicas.job_rate(BATCH, world, e2e_ms / args.steps)
 
     peaks = {}
     try:
