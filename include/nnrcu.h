@@ -240,6 +240,13 @@ int nnrcu_gemm_f32_create_ex(int m, int n, int k, int trans_a, int trans_b, floa
  * post-op. Each batch is split into bf16 hi/lo planes in the workspace
  * (nnrcu_matmul_f32_workspace bytes) and runs on the split-bf16 engine. */
 int nnrcu_matmul_f32_workspace(int m, int n, int k, size_t* bytes);
+/* The same for bf16 / fp16 tensors (dtype NNRCU_DT_*; nnr's 16-bit MatMul
+ * converts to fp32, multiplies and rounds back): one kind::f16 product per
+ * multiply-add, fp32 sums, the result rounded to the type (nearest even). */
+int nnrcu_matmul_half_workspace(int m, int n, int k, size_t* bytes);
+int nnrcu_matmul_half_run(const uint16_t* a, const uint16_t* b, uint16_t* y, int batch, int m, int n, int k,
+                          long long a_batch_stride, long long b_batch_stride, int dtype, int post_op, float post_a,
+                          float post_b, void* workspace, size_t workspace_bytes, void* stream);
 int nnrcu_matmul_f32_run(const float* a, const float* b, float* y, int batch, int m, int n, int k,
                          long long a_batch_stride, long long b_batch_stride, int post_op, float post_a, float post_b,
                          void* workspace, size_t workspace_bytes, void* stream);

@@ -76,6 +76,8 @@ SIGNATURES = {
     "nnrcu_gemm_f32_create_ex": [I, I, I, I, I, F, F, P, P, I, I, F, F, I, PP],
     "nnrcu_matmul_f32_workspace": [I, I, I, C.POINTER(C.c_size_t)],
     "nnrcu_matmul_f32_run": [P, P, P, I, I, I, I, C.c_longlong, C.c_longlong, I, F, F, P, SZ, P],
+    "nnrcu_matmul_half_workspace": [I, I, I, C.POINTER(C.c_size_t)],
+    "nnrcu_matmul_half_run": [P, P, P, I, I, I, I, C.c_longlong, C.c_longlong, I, I, F, F, P, SZ, P],
     "nnrcu_conv_half_create": [P, I, P, P, PP],
     "nnrcu_conv_half_run": [P, P, P, P, P],
     "nnrcu_gemm_half_create": [I, I, I, I, I, F, F, I, P, P, I, I, F, F, PP],

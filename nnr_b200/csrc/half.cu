@@ -402,6 +402,90 @@ int nnrcu_gemm_f32_create_ex(int m, int n, int k, int trans_a, int trans_b, floa
   return NNRCU_OK;
 }
 
+// MatMul of two 16-bit device tensors computed at run time (nnr's MatMul
+// with a non-initializer B on bf16 / fp16 tensors: MatMul.cpp:32-94 shapes,
+// exec_f16_as_f32 and its bf16 twin convert to fp32, multiply, round back).
+// Per batch: A rows and B's columns (transposed) to K-major 16-bit planes,
+// one kind::f16 engine launch into an fp32 buffer, rounding to the type.
+namespace {
+struct HalfMM {
+  int cs, kbytes, kpad_bytes, num_kb, npad;
+  size_t a_plane, b_plane, y32;
+};
+HalfMM half_mm_geom(int m, int n, int k) {
+  HalfMM g;
+  g.cs = round_up(k, 8);
+  g.kbytes = g.cs * 2;
+  g.kpad_bytes = round_up(g.kbytes, BKB);
+  g.num_kb = g.kpad_bytes / BKB;
+  g.npad = round_up(n, 256);
+  g.a_plane = round_up_sz((size_t)m * g.cs * 2, 256);
+  g.b_plane = round_up_sz((size_t)g.npad * g.cs * 2, 256);
+  g.y32 = round_up_sz((size_t)m * n * 4, 256);
+  return g;
+}
+}  // namespace
+
+int nnrcu_matmul_half_workspace(int m, int n, int k, size_t* bytes) {
+  if (!bytes || m <= 0 || n <= 0 || k <= 0) return set_error(NNRCU_ERR_INVALID, "MatMul dims must be positive");
+  const HalfMM g = half_mm_geom(m, n, k);
+  *bytes = g.a_plane + g.b_plane + g.y32;
+  return NNRCU_OK;
+}
+
+int nnrcu_matmul_half_run(const uint16_t* a, const uint16_t* b, uint16_t* y, int batch, int m, int n, int k,
+                          long long a_batch_stride, long long b_batch_stride, int dtype, int post_op, float post_a,
+                          float post_b, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!a || !b || !y || !workspace) return set_error(NNRCU_ERR_INVALID, "NULL argument");
+  if (dtype != NNRCU_DT_BF16 && dtype != NNRCU_DT_F16) return set_error(NNRCU_ERR_INVALID, "dtype must be bf16 or fp16");
+  if (batch <= 0 || m <= 0 || n <= 0 || k <= 0 || a_batch_stride < 0 || b_batch_stride < 0)
+    return set_error(NNRCU_ERR_INVALID, "MatMul: dims must be positive and strides non-negative");
+  const HalfMM hg = half_mm_geom(m, n, k);
+  if (workspace_bytes < hg.a_plane + hg.b_plane + hg.y32)
+    return set_error(NNRCU_ERR_INVALID, "MatMul workspace of %zu bytes required", hg.a_plane + hg.b_plane + hg.y32);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  uint16_t* ap = reinterpret_cast<uint16_t*>(ws);
+  uint16_t* bp = reinterpret_cast<uint16_t*>(ws + hg.a_plane);
+  float* y32 = reinterpret_cast<float*>(ws + hg.a_plane + hg.b_plane);
+  nnrcu_op op{};  // the launch geometry only (no device buffers of its own)
+  op.M = m; op.N = n; op.K = k;
+  op.nplane = dtype == NNRCU_DT_BF16 ? 3 : 4;
+  op.epi = EPI_F32;
+  op.cs = hg.cs;
+  op.kbytes = hg.kbytes;
+  op.kpad_bytes = hg.kpad_bytes;
+  op.num_kb = hg.num_kb;
+  op.npad = hg.npad;
+  op.bn = pick_bn(m, n, 1, num_sms());
+  op.amode = op.kbytes >= BKB ? A_TMA : A_GATHER;
+  int rc = map_post_half(post_op, post_a, post_b, &op);
+  if (rc != NNRCU_OK) return rc;
+  // B rows past n are never written; they only feed output columns past n
+  rc = encode_tmap_2d(&op.tmB, tmap_type(op.nplane), bp, hg.cs, (uint64_t)hg.npad, (uint64_t)hg.cs * 2, BKB / 2,
+                      op.bn, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc != NNRCU_OK) return rc;
+  GatherGeom g{};
+  g.N = 1; g.H = 1; g.W = m; g.OH = 1; g.OW = m; g.KH = 1; g.KW = 1;
+  g.sh = 1; g.sw = 1; g.ph = 0; g.pw = 0; g.dh = 1; g.dw = 1;
+  for (int bi = 0; bi < batch; ++bi) {
+    if (bi == 0 || a_batch_stride) {
+      rows_to_half_kernel<<<blocks((long long)m * hg.cs, 256), 256, 0, st>>>(a + a_batch_stride * bi, 0, 0, ap, m, k,
+                                                                            hg.cs);
+      NNRCU_CUDA(cudaGetLastError());
+    }
+    if (bi == 0 || b_batch_stride) {
+      // B [k][n] read as the transposed rows of [n][cs]
+      rows_to_half_kernel<<<blocks((long long)n * hg.cs, 256), 256, 0, st>>>(b + b_batch_stride * bi, 0, 1, bp, n, k,
+                                                                            hg.cs);
+      NNRCU_CUDA(cudaGetLastError());
+    }
+    if ((rc = half_launch(&op, ap, m, g, y32, 0, n, 1, st)) != NNRCU_OK) return rc;
+    if ((rc = to_half(y32, y + (size_t)bi * m * n, (size_t)m * n, dtype, st)) != NNRCU_OK) return rc;
+  }
+  return NNRCU_OK;
+}
+
 }  // extern "C"
 
 namespace nnrcu {

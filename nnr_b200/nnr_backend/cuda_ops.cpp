@@ -385,7 +385,7 @@ struct Gemm_cuda : cuda_op_t {
   int64_t num_ops() const override { return 2LL * M * N * K * (dyn ? (int64_t)offs.size() : 1); }
   bool device_ok() const override {
     const data_type_t t = inputs[0]->type;
-    if (dyn) return t == NNR_DATA_TYPE_FLOAT32 && inputs[1]->type == t;
+    if (dyn) return (t == NNR_DATA_TYPE_FLOAT32 || half_dtype(t) != 0) && inputs[1]->type == t;
     const bool half = half_dtype(t) != 0;
     if (!(t == NNR_DATA_TYPE_FLOAT32 || (half && alpha == 1.0f && !trans_a)) || inputs[1]->type != t ||
         !is_const_tensor(ctx, inputs[1]))
@@ -397,7 +397,10 @@ struct Gemm_cuda : cuda_op_t {
   bool prepare_device(device_state_t& s) override {
     if (dyn) {
       if (!post_op_of(this, &dpost, &dpa, &dpb)) return s.fail("MatMul: fused post-op has no device epilogue");
-      if (!nnrcu_ok(s, nnrcu_matmul_f32_workspace(dm, dn, dk, &dws), "MatMul")) return false;
+      dtype = half_dtype(inputs[0]->type);
+      if (!nnrcu_ok(s, dtype ? nnrcu_matmul_half_workspace(dm, dn, dk, &dws) : nnrcu_matmul_f32_workspace(dm, dn, dk, &dws),
+                    "MatMul"))
+        return false;
       set_out_layout(s, outputs[0], memory_layout_t::NCHW);
       return true;
     }
@@ -460,11 +463,18 @@ struct Gemm_cuda : cuda_op_t {
         while (j < offs.size() && sa >= 0 && sb >= 0 && offs[j].first - offs[j - 1].first == sa &&
                offs[j].second - offs[j - 1].second == sb)
           ++j;
-        if (!nnrcu_ok(s,
-                      nnrcu_matmul_f32_run(a + offs[i].first, b + offs[i].second, y + i * (size_t)dm * dn, (int)(j - i),
-                                           dm, dn, dk, sa, sb, dpost, dpa, dpb, s.workspace, dws, stream),
-                      "MatMul"))
-          return false;
+        int rc;
+        if (dtype) {
+          const uint16_t* ah = (const uint16_t*)s.dev(inputs[0]);
+          const uint16_t* bh = (const uint16_t*)s.dev(inputs[1]);
+          rc = nnrcu_matmul_half_run(ah + offs[i].first, bh + offs[i].second,
+                                     (uint16_t*)s.dev(outputs[0]) + i * (size_t)dm * dn, (int)(j - i), dm, dn, dk, sa,
+                                     sb, dtype, dpost, dpa, dpb, s.workspace, dws, stream);
+        } else {
+          rc = nnrcu_matmul_f32_run(a + offs[i].first, b + offs[i].second, y + i * (size_t)dm * dn, (int)(j - i), dm,
+                                    dn, dk, sa, sb, dpost, dpa, dpb, s.workspace, dws, stream);
+        }
+        if (!nnrcu_ok(s, rc, "MatMul")) return false;
         i = j;
       }
       return true;

@@ -186,18 +186,19 @@ def matmul(a_shape, b) -> bytes:
     return g.model()
 
 
-def matmul_dynamic(a_shape, b_shape, y_shape, post=None) -> bytes:
+def matmul_dynamic(a_shape, b_shape, y_shape, post=None, elem=None) -> bytes:
     """a, b -> MatMul(a, b) [-> Relu] -> y, both operands graph inputs (nnr's
-    MatMul with a run-time B)."""
+    MatMul with a run-time B); elem: the tensor type (FLOAT by default)."""
+    elem = P.FLOAT if elem is None else elem
     g = P.Graph("matmul_dyn")
-    g.input("a", P.FLOAT, a_shape)
-    g.input("b", P.FLOAT, b_shape)
+    g.input("a", elem, a_shape)
+    g.input("b", elem, b_shape)
     if post:
         g.node("MatMul", ["a", "b"], ["m"])
         g.node(post, ["m"], ["y"])
     else:
         g.node("MatMul", ["a", "b"], ["y"])
-    g.output("y", P.FLOAT, y_shape)
+    g.output("y", elem, y_shape)
     return g.model()
 
 

@@ -360,6 +360,27 @@ def matmul_f32(a: torch.Tensor, b: torch.Tensor, post=None, post_a=0.0, post_b=0
     return y
 
 
+def matmul_half(a: torch.Tensor, b: torch.Tensor, post=None, post_a=0.0, post_b=0.0, stream=None) -> torch.Tensor:
+    """matmul_f32 for two bf16 (or two fp16) device tensors (nnr's 16-bit
+    MatMul: fp32 products and sums, the result rounded to the type), through
+    nnrcu_matmul_half_run."""
+    if a.dtype != b.dtype or a.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError("matmul_half: two bf16 or two fp16 tensors")
+    dtype = DT_BF16 if a.dtype == torch.bfloat16 else DT_F16
+    a, b = a.contiguous(), b.contiguous()
+    shape, m, n, k, offs = matmul_broadcast(tuple(a.shape), tuple(b.shape))
+    y = torch.empty(shape, dtype=a.dtype, device=a.device)
+    ws_bytes = C.c_size_t()
+    call("nnrcu_matmul_half_workspace", m, n, k, C.byref(ws_bytes))
+    ws = torch.empty(max(ws_bytes.value, 1), dtype=torch.uint8, device=a.device)
+    code = _POSTS[post] if not isinstance(post, int) else post
+    for i, (ao, bo) in enumerate(offs):
+        call("nnrcu_matmul_half_run", C.c_void_p(a.data_ptr() + 2 * ao), C.c_void_p(b.data_ptr() + 2 * bo),
+             C.c_void_p(y.data_ptr() + 2 * i * m * n), 1, m, n, k, 0, 0, dtype, code, float(post_a), float(post_b),
+             C.c_void_p(ws.data_ptr()), ws_bytes.value, C.c_void_p(_stream(stream)))
+    return y
+
+
 PREC_SPLIT_BF16, PREC_BF16 = 0, 1
 DT_BF16, DT_F16 = 1, 2
 _HALF_TORCH = {DT_BF16: "bfloat16", DT_F16: "float16"}
