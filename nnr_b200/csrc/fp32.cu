@@ -79,8 +79,16 @@ int nnrcu_conv_f32_create(const nnrcu_conv_desc* desc, const float* w_host, cons
   int rc = conv_out_dims(d, &oh, &ow);
   if (rc != NNRCU_OK) return rc;
   const bool depthwise = d.group == d.c && d.group == d.oc && d.group > 1;
-  if (d.group != 1 && !depthwise)
-    return set_error(NNRCU_ERR_UNSUPPORTED, "grouped fp32 Conv (group=%d) is not implemented on the device", d.group);
+  if (d.group != 1 && !depthwise) {
+    if (d.c % d.group || d.oc % d.group)
+      return set_error(NNRCU_ERR_INVALID, "group %d does not divide channels %d / %d", d.group, d.c, d.oc);
+    const std::vector<float> dense = grouped_to_dense(w_host, d.oc, d.c, d.group, d.kh, d.kw);
+    nnrcu_conv_desc d1 = d;
+    d1.group = 1;
+    rc = nnrcu_conv_f32_create(&d1, dense.data(), bias_host, out);
+    if (rc == NNRCU_OK) (*out)->num_ops /= d.group;
+    return rc;
+  }
   if (depthwise && (d.c % 4) != 0)
     return set_error(NNRCU_ERR_UNSUPPORTED, "depthwise Conv needs channels %% 4 == 0 (got %d)", d.c);
 

@@ -227,8 +227,16 @@ int nnrcu_conv_half_create(const nnrcu_conv_desc* desc, int dtype, const uint16_
   int oh = 0, ow = 0;
   int rc = conv_out_dims(d, &oh, &ow);
   if (rc != NNRCU_OK) return rc;
-  if (d.group != 1)
-    return set_error(NNRCU_ERR_UNSUPPORTED, "16-bit Conv with group=%d is not implemented on the device", d.group);
+  if (d.group != 1) {
+    if (d.c % d.group || d.oc % d.group)
+      return set_error(NNRCU_ERR_INVALID, "group %d does not divide channels %d / %d", d.group, d.c, d.oc);
+    const std::vector<uint16_t> dense = grouped_to_dense(w_host, d.oc, d.c, d.group, d.kh, d.kw);
+    nnrcu_conv_desc d1 = d;
+    d1.group = 1;
+    rc = nnrcu_conv_half_create(&d1, dtype, dense.data(), bias_host, out);
+    if (rc == NNRCU_OK) (*out)->num_ops /= d.group;
+    return rc;
+  }
   nnrcu_op* op = new nnrcu_op();
   NNRCU_TRY(cuda_check(cudaGetDevice(&op->device), "cudaGetDevice"));
   op->kind = OP_CONV_HALF;

@@ -24,6 +24,23 @@ int cuda_check(cudaError_t e, const char* what);
 // Whether engine kernels are launched with programmatic dependent launch
 // (on unless the environment sets NNRCU_PDL=0).
 bool pdl_enabled();
+
+// Grouped conv weights [oc][c / g][kh][kw] as the block-diagonal dense
+// weights [oc][c][kh][kw] of the same conv (zeros between the groups): a
+// grouped Conv / QLinearConv runs as a group-1 conv whose extra products are
+// exact zeros (nnr's grouped path computes each group's sums on their own).
+template <typename T>
+std::vector<T> grouped_to_dense(const T* w, int oc, int c, int g, int kh, int kw) {
+  const int cg = c / g, og = oc / g, taps = kh * kw;
+  std::vector<T> d((size_t)oc * c * taps, T(0));
+  for (int o = 0; o < oc; ++o) {
+    const int gi = o / og;
+    for (int ic = 0; ic < cg; ++ic)
+      for (int t = 0; t < taps; ++t)
+        d[((size_t)o * c + gi * cg + ic) * taps + t] = w[((size_t)o * cg + ic) * taps + t];
+  }
+  return d;
+}
 bool shift_enabled();
 bool r2_sat_enabled();
 

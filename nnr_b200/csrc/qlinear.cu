@@ -80,9 +80,21 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   if (d.group == d.c && d.oc == d.c && d.group > 1)  // depthwise: nnr's exec_dw_int8_nhwc (qdw.cu)
     return qdw_create(d, oh, ow, w_host, w_scale, n_w_scale, w_zp, n_w_zp, bias_host, x_scale, x_zp, y_scale, y_zp,
                       out);
-  if (d.group != 1)
-    return set_error(NNRCU_ERR_UNSUPPORTED, "grouped QLinearConv (group=%d, not depthwise) is not implemented on the device",
-                     d.group);
+  if (d.group != 1) {
+    if (d.c % d.group || d.oc % d.group)
+      return set_error(NNRCU_ERR_INVALID, "group %d does not divide channels %d / %d", d.group, d.c, d.oc);
+    const std::vector<int8_t> dense = grouped_to_dense(w_host, d.oc, d.c, d.group, d.kh, d.kw);
+    nnrcu_conv_desc d1 = d;
+    d1.group = 1;
+    // nnr runs grouped int8 convs on its VNNI im2col path (the direct and
+    // packed paths take group 1 only), whose requant is R1
+    // (QLinearConv.cpp:1171-1185, QLinearConv_reshape.h:212-222)
+    if (d1.requant == NNRCU_RQ_AUTO) d1.requant = NNRCU_RQ_R1;
+    rc = nnrcu_qlinearconv_create(&d1, dense.data(), w_scale, n_w_scale, w_zp, n_w_zp, bias_host, x_scale, x_zp,
+                                  y_scale, y_zp, out);
+    if (rc == NNRCU_OK) (*out)->num_ops /= d.group;
+    return rc;
+  }
   for (int i = 0; i < n_w_zp; ++i)
     if (w_zp && w_zp[i] != 0)
       return set_error(NNRCU_ERR_UNSUPPORTED, "non-zero weight zero point (nnr's VNNI paths require symmetric weights)");

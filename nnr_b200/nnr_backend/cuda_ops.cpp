@@ -248,7 +248,7 @@ struct Conv_cuda : cuda_op_t {
   bool device_ok() const override {
     const data_type_t t = inputs[0]->type;
     const bool half = half_dtype(t) != 0;
-    if (!(t == NNR_DATA_TYPE_FLOAT32 || (half && a.group == 1))) return false;
+    if (!(t == NNR_DATA_TYPE_FLOAT32 || half)) return false;
     return inputs[0]->ndim == 4 && inputs[1]->type == t && is_const_tensor(ctx, inputs[1]) &&
            (inputs.size() < 3 || !inputs[2] || (is_const_tensor(ctx, inputs[2]) && inputs[2]->type == t));
   }

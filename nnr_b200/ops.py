@@ -403,12 +403,12 @@ class ConvHalf(Operator):
     op_type = "Conv"
 
     def __init__(self, x_shape, w, bias=None, dtype=DT_BF16, strides=(1, 1), pads=(0, 0, 0, 0), dilations=(1, 1),
-                 in_layout="NCHW", out_layout="NCHW", post=None, post_a=0.0, post_b=0.0):
+                 in_layout="NCHW", out_layout="NCHW", post=None, post_a=0.0, post_b=0.0, group=1):
         super().__init__()
         wb = _bits16(w, dtype)
         self.dtype = dtype
         self.x_shape = tuple(int(v) for v in x_shape)
-        self.desc = conv_desc(self.x_shape, wb.shape, strides, pads, dilations, 1, in_layout, out_layout,
+        self.desc = conv_desc(self.x_shape, wb.shape, strides, pads, dilations, group, in_layout, out_layout,
                               post, post_a, post_b, 0)
         bb = _bits16(bias, dtype)
         call("nnrcu_conv_half_create", C.byref(self.desc), int(dtype), wb.ctypes.data_as(C.c_void_p),

@@ -66,24 +66,27 @@ def test_qlinearconv_rejects_bad_descriptors(bad):
 
 
 def test_qlinearconv_unsupported_cases_are_reported():
-    """group != 1 and non-zero weight zero points are declined with
-    NNRCU_ERR_UNSUPPORTED (nnr's registry then keeps the CPU operator)."""
+    """Non-zero weight zero points (grouped or not) are declined with
+    NNRCU_ERR_UNSUPPORTED (nnr's registry then keeps the CPU operator); a
+    group count that does not divide the channels is NNRCU_ERR_INVALID."""
     import numpy as np
     from nnr_b200 import _lib
     w = np.zeros(8 * 8 * 3 * 3, np.int8)
     s = np.ones(1, np.float32)
     op = C.c_void_p()
-    d = _desc(group=2)
+    d = _desc(group=3)
     rc = _lib.lib.nnrcu_qlinearconv_create(C.byref(d), w.ctypes.data_as(C.c_void_p), s.ctypes.data_as(C.c_void_p),
                                            1, None, 0, None, 0.02, 128, 0.05, 128, C.byref(op))
-    assert rc == -2
+    assert rc == -1
+    assert "group" in _lib.last_error()
     zp = np.ones(8, np.int8)
-    d = _desc()
-    rc = _lib.lib.nnrcu_qlinearconv_create(C.byref(d), w.ctypes.data_as(C.c_void_p), s.ctypes.data_as(C.c_void_p),
-                                           1, zp.ctypes.data_as(C.c_void_p), 8, None, 0.02, 128, 0.05, 128,
-                                           C.byref(op))
-    assert rc == -2
-    assert "zero point" in _lib.last_error()
+    for g in (1, 2):
+        d = _desc(group=g)
+        rc = _lib.lib.nnrcu_qlinearconv_create(C.byref(d), w.ctypes.data_as(C.c_void_p),
+                                               s.ctypes.data_as(C.c_void_p), 1, zp.ctypes.data_as(C.c_void_p), 8,
+                                               None, 0.02, 128, 0.05, 128, C.byref(op))
+        assert rc == -2
+        assert "zero point" in _lib.last_error()
 
 
 def test_null_arguments():

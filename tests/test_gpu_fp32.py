@@ -88,6 +88,24 @@ def test_depthwise_clip(cuda_dev, s, layout, hw):
     assert rel_err(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("shape", [(2, 64, 14, 14, 128, 3, 1, 4), (1, 128, 9, 11, 64, 3, 2, 32),
+                                   (1, 32, 7, 7, 64, 3, 1, 32)])
+@pytest.mark.parametrize("layout", ["NCHW", "NHWC"])
+def test_grouped_conv(cuda_dev, shape, layout):
+    """Grouped (not depthwise) fp32 Conv + Relu against the fp64 grouped
+    restatement (nnr's grouped im2col path computes each group on its own)."""
+    n, c, h, w_, oc, k, s, g = shape
+    rng = np.random.default_rng(oc + g)
+    x = rng.normal(0, 1, size=(n, c, h, w_)).astype(np.float32)
+    w = rng.normal(0, 0.2, size=(oc, c // g, k, k)).astype(np.float32)
+    b = rng.normal(0, 0.1, size=oc).astype(np.float32)
+    p = k // 2
+    xin = x if layout == "NCHW" else np.ascontiguousarray(x.transpose(0, 2, 3, 1))
+    y = run_conv(cuda_dev, xin, w, b, layout, layout, strides=(s, s), pads=(p,) * 4, group=g, post="Relu")
+    ref = O.conv_f32(x, w, b, strides=(s, s), pads=(p,) * 4, group=g, post=1, out_layout=layout)
+    assert rel_err(y, ref) <= TOL
+
+
 def test_conv_residual_add(cuda_dev):
     """Projection conv followed by the residual Add (MobileNetV2 block output)."""
     rng = np.random.default_rng(9)

@@ -89,6 +89,32 @@ def test_conv_half(cuda_dev, dtype, shape, post):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("shape", [((2, 64, 14, 14), 128, 3, 1, 1, 4, "NHWC"), ((1, 128, 9, 11), 64, 3, 2, 1, 32, "NCHW")])
+def test_grouped_conv_half(cuda_dev, dtype, shape):
+    """Grouped (not depthwise) 16-bit Conv + Relu: the fp32 sums of each
+    group, rounded once to the 16-bit type."""
+    from nnr_b200 import ops
+    xs, oc, k, s, p, g, lay = shape
+    et = ET[dtype]
+    rng = np.random.default_rng(oc + g)
+    xb = G.to_bits16(rng.uniform(-1, 1, xs), et)
+    wb = G.to_bits16(rng.normal(0, 0.2, (oc, xs[1] // g, k, k)), et)
+    bb = G.to_bits16(rng.normal(0, 0.1, oc), et)
+    kw = dict(strides=(s, s), pads=(p,) * 4, group=g, in_layout="NCHW", out_layout=lay)
+    ref = O.conv_f32(G.bits16_to_f32(xb, et), G.bits16_to_f32(wb, et), G.bits16_to_f32(bb, et), post=1, **kw)
+    want = G.to_bits16(ref, et)
+    f = {k: np.abs(G.bits16_to_f32(v, et)) for k, v in (("x", xb), ("w", wb), ("b", bb))}
+    abs_sum = O.conv_f32(f["x"], f["w"], f["b"], **kw)
+    op = ops.ConvHalf(xs, wb, bb, dtype=ops.DT_BF16 if dtype == "bf16" else ops.DT_F16, strides=(s, s),
+                      pads=(p,) * 4, in_layout=lay, out_layout=lay, post="Relu", group=g)
+    xin = xb if lay == "NCHW" else np.ascontiguousarray(xb.transpose(0, 2, 3, 1))
+    y = op.exec(dev16(xin, cuda_dev))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    assert ulp_ok(host_bits(y), want, et, abs_sum) == 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
 @pytest.mark.parametrize("m,k,n,c,trans_b", [(200, 192, 300, "row", 0), (64, 768, 256, "full", 1),
                                              (33, 40, 50, None, 0), (4096, 768, 3072, "row", 0)])
 def test_gemm_half(cuda_dev, dtype, m, k, n, c, trans_b):

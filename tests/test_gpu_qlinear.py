@@ -503,14 +503,48 @@ def test_depthwise_bit_exact(cuda_dev, shape, in_layout, fused_relu):
 
 def test_depthwise_nchw_output_declined(cuda_dev):
     """nnr takes its int8 depthwise kernel for NHWC outputs only; an NCHW
-    output is declined (NNRCU_ERR_UNSUPPORTED), as is a grouped conv that is
-    not depthwise."""
+    output is declined (NNRCU_ERR_UNSUPPORTED)."""
     from nnr_b200 import ops
     from nnr_b200._lib import NnrcuError
     wt = np.ones((16, 1, 3, 3), np.int8)
     with pytest.raises(NnrcuError, match="NHWC"):
         ops.QLinearConv((1, 16, 8, 8), wt, np.float32(0.01), None, None, 0.1, 0, 0.1, 0, pads=(1, 1, 1, 1), group=16,
                         in_layout="NHWC", out_layout="NCHW")
-    with pytest.raises(NnrcuError, match="grouped"):
-        ops.QLinearConv((1, 16, 8, 8), np.ones((16, 4, 3, 3), np.int8), np.float32(0.01), None, None, 0.1, 0, 0.1, 0,
-                        pads=(1, 1, 1, 1), group=4, in_layout="NHWC", out_layout="NHWC")
+
+
+@pytest.mark.parametrize("shape", [
+    # n, c, h, w, oc, k, stride, group
+    (2, 64, 14, 14, 128, 3, 1, 4),      # 4 groups of 16 -> 32
+    (1, 128, 9, 11, 64, 3, 2, 32),      # 32 groups (ResNeXt-like), stride 2
+    (2, 24, 8, 8, 48, 1, 1, 3),         # 1x1, 3 groups
+    (1, 32, 7, 7, 64, 3, 1, 32),        # group = C with a channel multiplier of 2 (not depthwise)
+])
+@pytest.mark.parametrize("layouts", [("NCHW", "NCHW"), ("NHWC", "NHWC")])
+@pytest.mark.parametrize("x_zp", [0, 111])
+def test_grouped_qlinearconv(cuda_dev, shape, layouts, x_zp):
+    """Grouped (not depthwise) QLinearConv: nnr's VNNI im2col path, R1, per
+    group. Reference: the oracle per group on the group's input and output
+    channels, concatenated."""
+    n, c, h, w, oc, k, s, g = shape
+    rng = np.random.default_rng(c + oc + g)
+    x = rng.integers(0, 256, size=(n, c, h, w)).astype(np.uint8)
+    wt = rng.integers(-127, 128, size=(oc, c // g, k, k)).astype(np.int8)
+    ws = rng.uniform(0.002, 0.01, size=oc).astype(np.float32)
+    b = rng.integers(-2000, 2001, size=oc).astype(np.int32)
+    p = k // 2
+    cg, og = c // g, oc // g
+    parts = [O.qlinearconv(x[:, i * cg:(i + 1) * cg], wt[i * og:(i + 1) * og], ws[i * og:(i + 1) * og],
+                           b[i * og:(i + 1) * og], 0.02, x_zp, 0.3, 9, strides=(s, s), pads=(p,) * 4, formula=O.R1)
+             for i in range(g)]
+    ref = np.concatenate(parts, axis=1)
+    from nnr_b200 import ops
+    op = ops.QLinearConv((n, c, h, w), wt, ws, None, b, 0.02, x_zp, 0.3, 9, strides=(s, s), pads=(p,) * 4, group=g,
+                         in_layout=layouts[0], out_layout=layouts[1])
+    xin = x if layouts[0] == "NCHW" else _to_nhwc(x)
+    y = op.exec(torch.from_numpy(np.ascontiguousarray(xin)).to(cuda_dev))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    got = y.cpu().numpy()
+    if layouts[1] == "NHWC":
+        got = got.transpose(0, 3, 1, 2)
+    assert np.array_equal(got, ref), f"{(got != ref).sum()} of {ref.size} differ"
