@@ -3,6 +3,8 @@
 // depthwise fp32 convolution (CUDA cores, NHWC, 128-bit channel vectors).
 #include <algorithm>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <type_traits>
 
 #include "internal.h"
 #include "tc_gemm.cuh"
@@ -355,35 +357,64 @@ __global__ void transpose_kernel(const T* __restrict src, T* __restrict dst, int
   }
 }
 
+// Depthwise I/O types: 0 = fp32, 1 = bf16, 2 = fp16. A 4-channel vector is a
+// float4 or a uint2 of four 16-bit values; 16-bit tensors are widened to fp32
+// on load and rounded to nearest even on store, the way nnr's 16-bit Conv
+// converts around its fp32 kernels (Conv_exec_entry.h:188-381).
+template <int IO>
+struct Vec4IO {
+  using T = std::conditional_t<IO == 0, float, uint16_t>;     // element
+  using V = std::conditional_t<IO == 0, float4, uint2>;       // 4-channel vector
+  static __device__ __forceinline__ float h2f(uint32_t b) {
+    if constexpr (IO == 1) return __uint_as_float(b << 16);
+    else return __half2float(__ushort_as_half((unsigned short)b));
+  }
+  static __device__ __forceinline__ uint32_t f2h(float v) {
+    if constexpr (IO == 1) return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    else return __half_as_ushort(__float2half_rn(v));
+  }
+  static __device__ __forceinline__ float4 cvt(const V& u) {
+    if constexpr (IO == 0) return u;
+    else return make_float4(h2f(u.x & 0xFFFFu), h2f(u.x >> 16), h2f(u.y & 0xFFFFu), h2f(u.y >> 16));
+  }
+  static __device__ __forceinline__ V pack(float4 v) {
+    if constexpr (IO == 0) return v;
+    else return make_uint2(f2h(v.x) | (f2h(v.y) << 16), f2h(v.z) | (f2h(v.w) << 16));
+  }
+};
+
 // Depthwise fp32 conv, NHWC in/out. Each thread produces 4 consecutive
 // channels (one float4) of one output pixel; weights are [kh][kw][c].
 // Depthwise fp32 conv on NHWC (Conv_depthwise.h:11). One block per output
 // row (image, oy); threads over (ox, 4-channel vector), so consecutive threads
 // read consecutive channels of one pixel. Bias, post-op and residual fused.
-template <int ACT>
-__global__ void depthwise_f32_kernel(const float* __restrict x, const float* __restrict w, const float* __restrict bias,
-                                     float* __restrict y, const float* __restrict residual, int h, int wd, int c,
+template <int ACT, int IO = 0>
+__global__ void depthwise_f32_kernel(const typename Vec4IO<IO>::T* __restrict x, const float* __restrict w,
+                                     const float* __restrict bias, typename Vec4IO<IO>::T* __restrict y,
+                                     const typename Vec4IO<IO>::T* __restrict residual, int h, int wd, int c,
                                      int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int dh, int dw,
                                      int act, float act_a, float act_b) {
   const int c4 = c >> 2;
   const int row = blockIdx.x;  // img * oh + oy
   const int img = row / oh, oy = row - img * oh;
-  const float4* xin = reinterpret_cast<const float4*>(x) + (size_t)img * h * wd * c4;
+  using IOT = Vec4IO<IO>;
+  using VT = typename IOT::V;
+  const VT* xin = reinterpret_cast<const VT*>(x) + (size_t)img * h * wd * c4;
   const float4* w4 = reinterpret_cast<const float4*>(w);
-  float4* out = reinterpret_cast<float4*>(y) + (size_t)row * ow * c4;
-  const float4* res = residual ? reinterpret_cast<const float4*>(residual) + (size_t)row * ow * c4 : nullptr;
+  VT* out = reinterpret_cast<VT*>(y) + (size_t)row * ow * c4;
+  const VT* res = residual ? reinterpret_cast<const VT*>(residual) + (size_t)row * ow * c4 : nullptr;
   for (int t = threadIdx.x; t < ow * c4; t += blockDim.x) {
     const int ox = t / c4, cv = t - ox * c4;
     float4 acc = bias ? reinterpret_cast<const float4*>(bias)[cv] : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int ky = 0; ky < kh; ++ky) {
       const int iy = oy * sh - ph + ky * dh;
       if ((unsigned)iy >= (unsigned)h) continue;
-      const float4* xr = xin + (size_t)iy * wd * c4 + cv;
+      const VT* xr = xin + (size_t)iy * wd * c4 + cv;
       const float4* wr = w4 + (size_t)ky * kw * c4 + cv;
       for (int kx = 0; kx < kw; ++kx) {
         const int ix = ox * sw - pw + kx * dw;
         if ((unsigned)ix >= (unsigned)wd) continue;
-        const float4 xv = xr[(size_t)ix * c4];
+        const float4 xv = IOT::cvt(xr[(size_t)ix * c4]);
         const float4 wv = wr[(size_t)kx * c4];
         acc.x = fmaf(xv.x, wv.x, acc.x);
         acc.y = fmaf(xv.y, wv.y, acc.y);
@@ -399,10 +430,10 @@ __global__ void depthwise_f32_kernel(const float* __restrict x, const float* __r
       else if constexpr (ACT != ACT_NONE) o[u] = apply_act(o[u], act, act_a, act_b);
     }
     if (res) {
-      const float4 rr = res[t];
+      const float4 rr = IOT::cvt(res[t]);
       o[0] += rr.x; o[1] += rr.y; o[2] += rr.z; o[3] += rr.w;
     }
-    out[t] = make_float4(o[0], o[1], o[2], o[3]);
+    out[t] = IOT::pack(make_float4(o[0], o[1], o[2], o[3]));
   }
 }
 
@@ -412,18 +443,22 @@ __global__ void depthwise_f32_kernel(const float* __restrict x, const float* __r
 // (all loads in flight together). One block per output row.
 // (stride 2: three blocks per SM, 85 registers a thread, measured 1.3-1.4x
 // faster than two on the MobileNetV2 stride-2 shapes)
-template <int ACT, int SW>
-__global__ void __launch_bounds__(256, SW == 2 ? 3 : 2) dw3x3_f32_kernel(const float* __restrict x, const float* __restrict w, const float* __restrict bias,
-                                 float* __restrict y, const float* __restrict residual, int h, int wd, int c, int oh,
+template <int ACT, int SW, int IO = 0>
+__global__ void __launch_bounds__(256, SW == 2 ? 3 : 2)
+    dw3x3_f32_kernel(const typename Vec4IO<IO>::T* __restrict x, const float* __restrict w,
+                     const float* __restrict bias, typename Vec4IO<IO>::T* __restrict y,
+                     const typename Vec4IO<IO>::T* __restrict residual, int h, int wd, int c, int oh,
                                  int ow, int ph, int pw, int act, float act_a, float act_b) {
   constexpr int OXT = SW == 1 ? 4 : 2, NC = (OXT - 1) * SW + 3;
   const int c4 = c >> 2;
   const int row = blockIdx.x;
   const int img = row / oh, oy = row - img * oh;
-  const float4* xin = reinterpret_cast<const float4*>(x) + (size_t)img * h * wd * c4;
+  using IOT = Vec4IO<IO>;
+  using VT = typename IOT::V;
+  const VT* xin = reinterpret_cast<const VT*>(x) + (size_t)img * h * wd * c4;
   const float4* w4 = reinterpret_cast<const float4*>(w);
-  float4* out = reinterpret_cast<float4*>(y) + (size_t)row * ow * c4;
-  const float4* res = residual ? reinterpret_cast<const float4*>(residual) + (size_t)row * ow * c4 : nullptr;
+  VT* out = reinterpret_cast<VT*>(y) + (size_t)row * ow * c4;
+  const VT* res = residual ? reinterpret_cast<const VT*>(residual) + (size_t)row * ow * c4 : nullptr;
   const int groups = (ow + OXT - 1) / OXT;
   const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int t = threadIdx.x; t < groups * c4; t += blockDim.x) {
@@ -434,11 +469,11 @@ __global__ void __launch_bounds__(256, SW == 2 ? 3 : 2) dw3x3_f32_kernel(const f
     for (int ky = 0; ky < 3; ++ky) {
       const int iy = oy * SW - ph + ky;
       const bool vy = (unsigned)iy < (unsigned)h;
-      const float4* xr = xin + (size_t)(vy ? iy : 0) * wd * c4 + cv;
+      const VT* xr = xin + (size_t)(vy ? iy : 0) * wd * c4 + cv;
 #pragma unroll
       for (int j = 0; j < NC; ++j) {
         const int ix = ox0 * SW - pw + j;
-        xv[ky][j] = (vy && (unsigned)ix < (unsigned)wd) ? xr[(size_t)ix * c4] : z;
+        xv[ky][j] = (vy && (unsigned)ix < (unsigned)wd) ? IOT::cvt(xr[(size_t)ix * c4]) : z;
       }
     }
     const float4 b4 = bias ? reinterpret_cast<const float4*>(bias)[cv] : z;
@@ -473,10 +508,10 @@ __global__ void __launch_bounds__(256, SW == 2 ? 3 : 2) dw3x3_f32_kernel(const f
       }
       const size_t oi = (size_t)(ox0 + o) * c4 + cv;
       if (res) {
-        const float4 rr = res[oi];
+        const float4 rr = IOT::cvt(res[oi]);
         r[0] += rr.x; r[1] += rr.y; r[2] += rr.z; r[3] += rr.w;
       }
-      out[oi] = make_float4(r[0], r[1], r[2], r[3]);
+      out[oi] = IOT::pack(make_float4(r[0], r[1], r[2], r[3]));
     }
   }
 }
@@ -786,12 +821,17 @@ int launch_transpose_generic(const void* src, void* dst, int n, int c, int hw, i
   return NNRCU_OK;
 }
 
-int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const float* residual, cudaStream_t st) {
+template <int IO>
+int launch_depthwise(const Op& op, const void* x_v, void* y_v, const void* residual_v, cudaStream_t st) {
+  using T = typename Vec4IO<IO>::T;
+  const T* x_nhwc = static_cast<const T*>(x_v);
+  T* y = static_cast<T*>(y_v);
+  const T* residual = static_cast<const T*>(residual_v);
   const nnrcu_conv_desc& d = op.d;
   const int rows = d.n * op.oh;
   const int threads = std::min(256, std::max(32, (op.ow * (d.c / 4) + 31) / 32 * 32));
 #define NNRCU_DW(A)                                                                                                   \
-  depthwise_f32_kernel<A><<<rows, threads, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh,      \
+  depthwise_f32_kernel<A, IO><<<rows, threads, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh,      \
                                                     op.ow, d.kh, d.kw, d.stride_h, d.stride_w, d.pad_top, d.pad_left,  \
                                                     d.dil_h, d.dil_w, op.act, op.act_a, op.act_b)
   if (d.kh == 3 && d.kw == 3 && d.dil_h == 1 && d.dil_w == 1 && d.stride_h == d.stride_w &&
@@ -800,7 +840,7 @@ int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const floa
     const int groups = (op.ow + oxt - 1) / oxt;
     const int th = std::min(256, std::max(32, (groups * (d.c / 4) + 31) / 32 * 32));
 #define NNRCU_DW3(A, S)                                                                                                 \
-  dw3x3_f32_kernel<A, S><<<rows, th, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh, op.ow,     \
+  dw3x3_f32_kernel<A, S, IO><<<rows, th, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh, op.ow,     \
                                               d.pad_top, d.pad_left, op.act, op.act_a, op.act_b)
 #define NNRCU_DW3S(A) \
   if (d.stride_h == 1) NNRCU_DW3(A, 1); else NNRCU_DW3(A, 2)
@@ -824,6 +864,15 @@ int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const floa
 #undef NNRCU_DW
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
+}
+
+int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const float* residual, cudaStream_t st) {
+  return launch_depthwise<0>(op, x_nhwc, y, residual, st);
+}
+
+int launch_depthwise_half(const Op& op, const uint16_t* x_nhwc, uint16_t* y, int dtype, cudaStream_t st) {
+  return dtype == NNRCU_DT_BF16 ? launch_depthwise<1>(op, x_nhwc, y, nullptr, st)
+                                : launch_depthwise<2>(op, x_nhwc, y, nullptr, st);
 }
 
 }  // namespace nnrcu

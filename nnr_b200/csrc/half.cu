@@ -227,6 +227,37 @@ int nnrcu_conv_half_create(const nnrcu_conv_desc* desc, int dtype, const uint16_
   int oh = 0, ow = 0;
   int rc = conv_out_dims(d, &oh, &ow);
   if (rc != NNRCU_OK) return rc;
+  // depthwise with whole 4-channel vectors: the fp32 depthwise kernels with
+  // 16-bit loads and stores (nnr widens 16-bit tensors around its fp32
+  // depthwise conv, Conv_exec_entry.h:188-381, Conv_depthwise.h:11)
+  if (d.group == d.c && d.group == d.oc && d.group > 1 && d.c % 4 == 0) {
+    nnrcu_op* op = new nnrcu_op();
+    NNRCU_TRY(cuda_check(cudaGetDevice(&op->device), "cudaGetDevice"));
+    op->kind = OP_CONV_HALF;
+    op->d = d;
+    op->oh = oh;
+    op->ow = ow;
+    op->M = d.n * oh * ow;
+    op->N = d.oc;
+    op->K = d.kh * d.kw;
+    op->num_ops = 2LL * op->M * d.oc * (long long)op->K;
+    op->nplane = dtype == NNRCU_DT_BF16 ? 3 : 4;
+    NNRCU_TRY(map_post_half(d.post_op, d.post_a, d.post_b, op));
+    std::vector<float> w((size_t)d.kh * d.kw * d.c);
+    for (int ch = 0; ch < d.c; ++ch)
+      for (int t = 0; t < d.kh * d.kw; ++t) w[(size_t)t * d.c + ch] = half_to_float_host(w_host[(size_t)ch * d.kh * d.kw + t], dtype);
+    NNRCU_TRY(upload_f32(&op->w_dw, w));
+    if (bias_host) {
+      std::vector<float> b(d.oc);
+      for (int i = 0; i < d.oc; ++i) b[i] = half_to_float_host(bias_host[i], dtype);
+      NNRCU_TRY(upload_f32(&op->bias, b));
+    }
+    // workspace: the NHWC copy of an NCHW input, then the NHWC result of an NCHW output
+    op->out_off = d.in_layout == NNRCU_LAYOUT_NCHW ? round_up_sz((size_t)d.n * d.h * d.w * d.c * 2, 256) : 0;
+    op->ws_bytes = op->out_off + (d.out_layout == NNRCU_LAYOUT_NCHW ? (size_t)op->M * d.oc * 2 : 0);
+    *out = op;
+    return NNRCU_OK;
+  }
   if (d.group != 1) {
     if (d.c % d.group || d.oc % d.group)
       return set_error(NNRCU_ERR_INVALID, "group %d does not divide channels %d / %d", d.group, d.c, d.oc);
@@ -282,9 +313,24 @@ int nnrcu_conv_half_create(const nnrcu_conv_desc* desc, int dtype, const uint16_
 int nnrcu_conv_half_run(nnrcu_op* op, const uint16_t* x, uint16_t* y, void* workspace, void* stream) {
   if (!op || op->kind != OP_CONV_HALF) return set_error(NNRCU_ERR_INVALID, "not a 16-bit Conv operator");
   if (!x || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
-  if (!workspace) return set_error(NNRCU_ERR_INVALID, "workspace of %zu bytes required", op->ws_bytes);
+  if (op->ws_bytes && !workspace) return set_error(NNRCU_ERR_INVALID, "workspace of %zu bytes required", op->ws_bytes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const nnrcu_conv_desc& d = op->d;
+  const int dtype = op->nplane == 3 ? NNRCU_DT_BF16 : NNRCU_DT_F16;
+  if (op->w_dw) {  // depthwise
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const uint16_t* xin = x;
+    if (d.in_layout == NNRCU_LAYOUT_NCHW) {
+      int rc = launch_transpose_generic(x, ws, d.n, d.c, d.h * d.w, 2, 1, st);
+      if (rc != NNRCU_OK) return rc;
+      xin = reinterpret_cast<const uint16_t*>(ws);
+    }
+    if (d.out_layout == NNRCU_LAYOUT_NHWC) return launch_depthwise_half(*op, xin, y, dtype, st);
+    uint16_t* tmp = reinterpret_cast<uint16_t*>(ws + op->out_off);
+    int rc = launch_depthwise_half(*op, xin, tmp, dtype, st);
+    if (rc != NNRCU_OK) return rc;
+    return launch_transpose_generic(tmp, y, d.n, d.oc, op->oh * op->ow, 2, 0, st);
+  }
   uint16_t* a = static_cast<uint16_t*>(workspace);
   float* y32 = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + op->out_off);
   const long long total = (long long)d.n * d.h * d.w * op->cs;
@@ -298,7 +344,7 @@ int nnrcu_conv_half_run(nnrcu_op* op, const uint16_t* x, uint16_t* y, void* work
   int rc = half_launch(op, a, d.n * d.h * d.w, g, y32, d.out_layout == NNRCU_LAYOUT_NCHW ? 1 : 0, d.oc,
                        op->oh * op->ow, st);
   if (rc != NNRCU_OK) return rc;
-  return to_half(y32, y, (size_t)op->M * d.oc, op->nplane == 3 ? NNRCU_DT_BF16 : NNRCU_DT_F16, st);
+  return to_half(y32, y, (size_t)op->M * d.oc, dtype, st);
 }
 
 int nnrcu_gemm_half_create(int m, int n, int k, int trans_a, int trans_b, float alpha, float beta, int dtype,

@@ -115,6 +115,41 @@ def test_grouped_conv_half(cuda_dev, dtype, shape):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("shape", [((2, 32, 17, 15), 3, 1, 1, 1, "NHWC", "NHWC"), ((2, 48, 16, 16), 3, 2, 1, 1, "NCHW", "NHWC"),
+                                   ((1, 20, 11, 9), 5, 1, 2, 1, "NHWC", "NCHW"), ((1, 16, 12, 12), 3, 1, 2, 2, "NCHW", "NCHW"),
+                                   ((1, 6, 8, 8), 3, 1, 1, 1, "NHWC", "NHWC")])
+@pytest.mark.parametrize("post", [None, "Clip"])
+def test_depthwise_conv_half(cuda_dev, dtype, shape, post):
+    """16-bit depthwise Conv (group = C): fp32 sums of the widened values,
+    rounded once (C % 4 != 0 takes the block-diagonal dense path)."""
+    from nnr_b200 import ops
+    xs, k, s, p, dil, lin, lout = shape
+    c = xs[1]
+    et = ET[dtype]
+    rng = np.random.default_rng(c * 3 + k)
+    xb = G.to_bits16(rng.uniform(-1, 1, xs), et)
+    wb = G.to_bits16(rng.normal(0, 0.3, (c, 1, k, k)), et)
+    bb = G.to_bits16(rng.normal(0, 0.1, c), et)
+    pa, pb = (0.0, 0.5) if post == "Clip" else (0.0, 0.0)
+    kw = dict(strides=(s, s), pads=(p,) * 4, dilations=(dil, dil), group=c, in_layout="NCHW", out_layout=lout)
+    ref = O.conv_f32(G.bits16_to_f32(xb, et), G.bits16_to_f32(wb, et), G.bits16_to_f32(bb, et), post=POST[post],
+                     post_a=pa, post_b=pb, **kw)
+    want = G.to_bits16(ref, et)
+    f = {k: np.abs(G.bits16_to_f32(v, et)) for k, v in (("x", xb), ("w", wb), ("b", bb))}
+    abs_sum = O.conv_f32(f["x"], f["w"], f["b"], **kw)
+    op = ops.ConvHalf(xs, wb, bb, dtype=ops.DT_BF16 if dtype == "bf16" else ops.DT_F16, strides=(s, s),
+                      pads=(p,) * 4, dilations=(dil, dil), in_layout=lin, out_layout=lout, post=post, post_a=pa,
+                      post_b=pb, group=c)
+    xin = xb if lin == "NCHW" else np.ascontiguousarray(xb.transpose(0, 2, 3, 1))
+    y = op.exec(dev16(xin, cuda_dev))
+    torch.cuda.synchronize()
+    assert ops.device_status() == 0
+    got = host_bits(y)
+    assert got.shape == want.shape
+    assert ulp_ok(got, want, et, abs_sum) == 0
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
 @pytest.mark.parametrize("m,k,n,c,trans_b", [(200, 192, 300, "row", 0), (64, 768, 256, "full", 1),
                                              (33, 40, 50, None, 0), (4096, 768, 3072, "row", 0)])
 def test_gemm_half(cuda_dev, dtype, m, k, n, c, trans_b):
