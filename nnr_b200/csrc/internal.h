@@ -43,7 +43,6 @@ std::vector<T> grouped_to_dense(const T* w, int oc, int c, int g, int kh, int kw
 }
 bool shift_enabled();
 bool r2_sat_enabled();
-bool acc_magic_enabled();
 
 // Device address of this device's status word (set up once per device).
 int* status_ptr();
@@ -118,7 +117,6 @@ struct Op {
   // requant scalars
   float inv_y = 0, yzp_f = 0, qmin_f = 0, qmax_f = 0, rq_lo = 0, rq_hi = 0, combined = 0;
   int yzp = 0;
-  int acc_small = 0;            // every corrected int8 accumulator is in (-2^22, 2^22)
   float y_scale = 0;
   int x_zp = 0;
   int a_zp = 0, b_zp = 0;

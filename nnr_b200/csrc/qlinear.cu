@@ -256,12 +256,8 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   std::vector<int32_t> colcorr(d.oc), bias_i(d.oc, 0);
   std::vector<float> csv(d.oc), bias_f(d.oc, 0.0f), osv(d.oc);
   const float inv_y = 1.0f / y_scale;  // QLinearConv.cpp:420 / QLinearConv_reshape.h:291
-  // bound on |acc - x_zp * sum(w) + bias| over all u8 inputs, per column
-  const int64_t xdev = std::max<int64_t>(x_zp, 255 - (int64_t)x_zp);
-  int64_t acc_bound = 0;
   for (int o = 0; o < d.oc; ++o) {
     int32_t wsum = 0;
-    int64_t wabs = 0;
     for (int ic = 0; ic < d.c; ++ic)
       for (int y = 0; y < d.kh; ++y)
         for (int x = 0; x < d.kw; ++x) {
@@ -282,11 +278,8 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
             B[(size_t)o * op->kpad_bytes + (size_t)(y * d.kw + x) * tap_stride + ic] = v;
           }
           wsum += v;
-          wabs += v < 0 ? -(int64_t)v : (int64_t)v;
         }
     colcorr[o] = (int32_t)(0u - (uint32_t)x_zp * (uint32_t)wsum);
-    const int64_t bcol = xdev * wabs + (bias_host ? std::llabs((long long)bias_host[o]) : 0);
-    acc_bound = std::max(acc_bound, bcol);
     const float ws = n_w_scale > 1 ? w_scale[o] : w_scale[0];
     csv[o] = x_scale * ws;                                   // combined scale
     if (bias_host) {
@@ -305,7 +298,6 @@ int nnrcu_qlinearconv_create(const nnrcu_conv_desc* desc, const int8_t* w_host, 
   op->rq_hi = (float)hi - (float)y_zp;
   op->yzp = y_zp;
   op->y_scale = y_scale;
-  op->acc_small = acc_bound < (int64_t(1) << 22);
 
   void* wB = nullptr;
   NNRCU_TRY(cuda_check(cudaMalloc(&wB, B.size()), "cudaMalloc(weights)"));
@@ -434,7 +426,6 @@ static int qconv_run(nnrcu_op* op, const uint8_t* x, uint8_t* y, void* workspace
   e.inv_y = op->inv_y; e.yzp_f = op->yzp_f; e.qmin_f = op->qmin_f; e.qmax_f = op->qmax_f;
   e.rq_lo = op->rq_lo; e.rq_hi = op->rq_hi; e.yzp = op->yzp;
   e.r2_sat = r2_sat_enabled() && op->yzp == 0 && op->rq_lo == 0.0f && op->rq_hi == 255.0f;
-  e.acc_small = acc_magic_enabled() && op->acc_small;
   e.y = y;
   e.y_layout = d.out_layout == NNRCU_LAYOUT_NCHW ? 1 : 0;
   e.ldy = d.oc;

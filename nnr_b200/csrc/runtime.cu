@@ -141,13 +141,6 @@ bool r2_sat_enabled() {
   return !(v && v[0] == '0');
 }
 
-bool acc_magic_enabled() {
-  // accumulators below 2^22 converted to float by an exact bit-pattern add
-  // instead of a conversion instruction; NNRCU_ACCMAGIC=0 turns it off
-  const char* v = std::getenv("NNRCU_ACCMAGIC");
-  return !(v && v[0] == '0');
-}
-
 int encode_tmap_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
                    uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   int dev = 0;

@@ -166,7 +166,6 @@ struct EpiParams {
   float combined;                      // R4 scalar scale a_s*b_s/y_s
   int yzp;                             // R2 integer zero point
   int r2_sat;                          // R2 bounds are [0, 255] with y_zp = 0: one saturating conversion
-  int acc_small;                       // every corrected accumulator (acc + column correction + bias) is in (-2^22, 2^22)
   // Fused QLinearAdd after the requant (u8 epilogues): y = QLinearAdd(q, qres)
   // with qres laid out like y. Same float sequence as the standalone op.
   const uint8_t* qres;                 // residual operand b, or null
@@ -288,21 +287,6 @@ __device__ __forceinline__ float r2_magic(int32_t raw, int32_t ci, float os, flo
 }
 __device__ __forceinline__ float r2_magic(int32_t raw, int32_t ci, float os, const EpiParams& e) {
   return r2_magic(raw, ci, os, e.rq_lo, e.rq_hi);
-}
-
-// float(raw + ci) for two accumulators. MC: |raw + ci| < 2^22, so the bit
-// pattern 0x4B400000 + (raw + ci) is the float 1.5 * 2^23 + (raw + ci) and
-// subtracting 1.5 * 2^23 gives the exact integer (the same value the
-// round-to-nearest conversion gives, since it is exact there too).
-template <bool MC>
-__device__ __forceinline__ float2 acc_to_f2(uint32_t v0, int32_t c0, uint32_t v1, int32_t c1) {
-  if constexpr (MC) {
-    return __fadd2_rn(make_float2(__uint_as_float(v0 + (uint32_t)c0 + 0x4B400000u),
-                                  __uint_as_float(v1 + (uint32_t)c1 + 0x4B400000u)),
-                      make_float2(-RND_MAGIC, -RND_MAGIC));
-  } else {
-    return make_float2(__int2float_rn((int32_t)(v0 + (uint32_t)c0)), __int2float_rn((int32_t)(v1 + (uint32_t)c1)));
-  }
 }
 
 // Requantise one int32 accumulator to u8 with the formula EPI selects; the
@@ -842,7 +826,6 @@ if constexpr (AMODE == A_ROWS || AMODE == A_XROWS) {
     const uint32_t kp_yzp = (uint32_t)e.yzp;
     const bool kp_ovf = e.qa_ovf != 0;
     const bool kp_sat = e.r2_sat != 0;
-    const bool kp_mc = e.acc_small != 0;
     const bool shift_direct = e.y_layout == 0 && (e.ldy & 15) == 0 && (reinterpret_cast<uintptr_t>(e.y) & 15) == 0;
     const bool direct = AMODE == A_SHIFT || e.opad != 0;  // lean path stores rows straight to HBM
     // EPI_R2A: TMA load of this warp's 32 x HB residual block of tile t into buffer buf
@@ -1193,11 +1176,6 @@ if constexpr (AMODE == A_ROWS || AMODE == A_XROWS) {
             for (int k = 0; k < CW / 16; ++k) rq[k] = __ldg(rp + k);
           }
           if constexpr (EPI == EPI_R2 || EPI == EPI_R2A) {
-            // (kp_mc: every corrected accumulator is below 2^22 in magnitude, so its
-            // float is an integer add into a 1.5 * 2^23 bit pattern and one packed
-            // subtraction, both exact, instead of two conversions)
-            auto r2_body = [&](auto mc) {
-            constexpr bool MC = decltype(mc)::value;
             // R2 with y_zp = 0 and the full u8 range (every Relu output):
             // clamp(rne(f), 0, 255) is one saturating conversion
             bool sat_done = false;
@@ -1207,9 +1185,11 @@ if constexpr (AMODE == A_ROWS || AMODE == A_XROWS) {
                 for (int j = 0; j < CW; j += 4) {
                   const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
                   const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
-                  const float2 f0 = __fmul2_rn(acc_to_f2<MC>(v[j + 0], ci4.x, v[j + 1], ci4.y),
+                  const float2 f0 = __fmul2_rn(make_float2(__int2float_rn((int32_t)(v[j + 0] + (uint32_t)ci4.x)),
+                                                           __int2float_rn((int32_t)(v[j + 1] + (uint32_t)ci4.y))),
                                                make_float2(a4.x, a4.y));
-                  const float2 f1 = __fmul2_rn(acc_to_f2<MC>(v[j + 2], ci4.z, v[j + 3], ci4.w),
+                  const float2 f1 = __fmul2_rn(make_float2(__int2float_rn((int32_t)(v[j + 2] + (uint32_t)ci4.z)),
+                                                           __int2float_rn((int32_t)(v[j + 3] + (uint32_t)ci4.w))),
                                                make_float2(a4.z, a4.w));
                   q[j + 0] = ptx::cvt_rni_sat_u8(f0.x);
                   q[j + 1] = ptx::cvt_rni_sat_u8(f0.y);
@@ -1225,9 +1205,11 @@ if constexpr (AMODE == A_ROWS || AMODE == A_XROWS) {
             for (int j = 0; j < CW; j += 4) {
               const int4 ci4 = *reinterpret_cast<const int4*>(s_ci + pc + j);
               const float4 a4 = *reinterpret_cast<const float4*>(s_f1 + pc + j);
-              float2 f0 = __fmul2_rn(acc_to_f2<MC>(v[j + 0], ci4.x, v[j + 1], ci4.y),
+              float2 f0 = __fmul2_rn(make_float2(__int2float_rn((int32_t)(v[j + 0] + (uint32_t)ci4.x)),
+                                                 __int2float_rn((int32_t)(v[j + 1] + (uint32_t)ci4.y))),
                                      make_float2(a4.x, a4.y));
-              float2 f1 = __fmul2_rn(acc_to_f2<MC>(v[j + 2], ci4.z, v[j + 3], ci4.w),
+              float2 f1 = __fmul2_rn(make_float2(__int2float_rn((int32_t)(v[j + 2] + (uint32_t)ci4.z)),
+                                                 __int2float_rn((int32_t)(v[j + 3] + (uint32_t)ci4.w))),
                                      make_float2(a4.z, a4.w));
               f0.x = fminf(fmaxf(f0.x, kp_lo), kp_hi);
               f0.y = fminf(fmaxf(f0.y, kp_lo), kp_hi);
@@ -1293,11 +1275,6 @@ if constexpr (AMODE == A_ROWS || AMODE == A_XROWS) {
               }
             }
             }
-            };
-            if (kp_mc)
-              r2_body(std::true_type{});
-            else
-              r2_body(std::false_type{});
           } else if constexpr (EPI == EPI_R3 || EPI == EPI_R3N) {
             // f = fma(float(acc), cs, bias_f); f = fma(f, inv_y, y_zp); clamp; rne
             const float2 iy = make_float2(e.inv_y, e.inv_y), yz = make_float2(e.yzp_f, e.yzp_f);
