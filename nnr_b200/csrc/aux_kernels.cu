@@ -39,8 +39,11 @@ __global__ void nchw_to_nhwc_u8_kernel(const uint8_t* __restrict src, uint8_t* _
 // words along channels. The destination may be spatially padded
 // ([n][hp][wp][cs], pixel (y, x) stored at (y + pt, x + pl)); its border is
 // filled by the caller.
+// border != 0: the grid has one more block column (the last blockIdx.x),
+// which writes the fill into the border pixels of its 64 channels.
 __global__ void nchw_to_nhwc_u8_vec_kernel(const uint8_t* __restrict src, uint8_t* __restrict dst, int c, int w,
-                                           int hw, int hp, int wp, int pt, int pl, int cs, uint8_t fill) {
+                                           int hw, int hp, int wp, int pt, int pl, int cs, uint8_t fill,
+                                           int border = 0) {
   __shared__ uint8_t tile[64][128 + 4];
   const int img = blockIdx.z;
   const int p0 = blockIdx.x * 128;
@@ -48,6 +51,30 @@ __global__ void nchw_to_nhwc_u8_vec_kernel(const uint8_t* __restrict src, uint8_
   const uint8_t* s = src + (size_t)img * c * hw;
   uint8_t* d = dst + (size_t)img * hp * wp * cs;
   const uint32_t fill4 = 0x01010101u * fill;
+  if (border && blockIdx.x == gridDim.x - 1) {
+    // border pixels: the top pt and bottom rows whole, then the left pl and
+    // right wp - w - pl columns of the h interior rows
+    const int h = hw / w, pb = hp - h - pt, pr = wp - w - pl;
+    const int n_tb = (pt + pb) * wp, side = pl + pr;
+    const int nb = n_tb + h * side;
+    const int cw = min(64, cs - c0) / 4;  // words of this block's channels
+    for (int idx = threadIdx.x; idx < nb * 16; idx += blockDim.x) {
+      const int bp = idx >> 4, wd = idx & 15;
+      if (wd >= cw) continue;
+      int y, x;
+      if (bp < n_tb) {
+        const int r = bp / wp;
+        y = r < pt ? r : h + r;  // rows pt .. pt + h - 1 are interior
+        x = bp - r * wp;
+      } else {
+        const int q = bp - n_tb, r = q / side, j = q - r * side;
+        y = pt + r;
+        x = j < pl ? j : w + j;
+      }
+      *reinterpret_cast<uint32_t*>(d + ((size_t)y * wp + x) * cs + c0 + wd * 4) = fill4;
+    }
+    return;
+  }
   for (int idx = threadIdx.x; idx < 64 * 32; idx += blockDim.x) {
     const int ch = idx >> 5, wd = idx & 31;
     const int p = p0 + wd * 4;
@@ -690,9 +717,10 @@ int launch_nchw_to_nhwc_u8_padded(const uint8_t* src, uint8_t* dst, int n, int c
   const int hp = h + pt + pb, wp = w + pl + pr;
   if ((h * w) % 4 != 0 || cs % 4 != 0 || (reinterpret_cast<uintptr_t>(src) & 3) || (reinterpret_cast<uintptr_t>(dst) & 3))
     return set_error(NNRCU_ERR_INVALID, "padded reorder needs h*w %% 4 == 0 and 4-byte aligned buffers");
-  NNRCU_CUDA(cudaMemsetAsync(dst, fill, (size_t)n * hp * wp * cs, st));
-  dim3 grid((h * w + 127) / 128, (cs + 63) / 64, n);
-  nchw_to_nhwc_u8_vec_kernel<<<grid, 256, 0, st>>>(src, dst, c, w, h * w, hp, wp, pt, pl, cs, fill);
+  // the interior by 128-pixel tiles, the border (x_zp) by one extra block column
+  const int border = (hp * wp != h * w) ? 1 : 0;
+  dim3 grid((h * w + 127) / 128 + border, (cs + 63) / 64, n);
+  nchw_to_nhwc_u8_vec_kernel<<<grid, 256, 0, st>>>(src, dst, c, w, h * w, hp, wp, pt, pl, cs, fill, border);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }
