@@ -210,6 +210,28 @@ int nnrcu_conv_f32_create(const nnrcu_conv_desc* desc, const float* w_host, cons
 int nnrcu_conv_f32_run(nnrcu_op* op, const float* x, float* y, const float* residual, void* workspace,
                        void* stream);
 
+/* Depthwise -> 1x1 chains without the fp32 round trip. A dense fp32 Conv runs
+ * on the tensor cores from two bf16 planes of its input (hi = bf16(x),
+ * lo = bf16(x - hi), NHWC with a padded channel stride cs), which
+ * nnrcu_conv_f32_run makes with a split pass over x. When x is the output of
+ * an fp32 depthwise Conv with no other consumer (MobileNet's depthwise ->
+ * projection pairs, Conv_depthwise.h:11 feeding Conv_exec.h:760-829), the
+ * depthwise conv can write those planes itself:
+ *   nnrcu_conv_f32_plane_stride  the channel stride cs of a 1x1 stride-1 NHWC
+ *                                fp32 Conv's planes (NNRCU_ERR_UNSUPPORTED for
+ *                                any other Conv: it splits its input itself);
+ *   nnrcu_conv_f32_run_to_planes a depthwise fp32 Conv (NHWC in and out) whose
+ *                                result goes to y_hi / y_lo ([n*oh*ow][cs]
+ *                                uint16 each, channels oc .. cs-1 zero);
+ *   nnrcu_conv_f32_run_planes    the 1x1 Conv on such planes (no workspace).
+ * The consumer's result is bit-identical to running both convs with
+ * nnrcu_conv_f32_run. */
+int nnrcu_conv_f32_plane_stride(const nnrcu_op* op, int* cs);
+int nnrcu_conv_f32_run_to_planes(nnrcu_op* op, const float* x, uint16_t* y_hi, uint16_t* y_lo, int cs,
+                                 void* stream);
+int nnrcu_conv_f32_run_planes(nnrcu_op* op, const uint16_t* x_hi, const uint16_t* x_lo, float* y,
+                              const float* residual, void* stream);
+
 /* ---------------------------------------------------------------- fp32 Gemm / MatMul
  * Y[m,n] = alpha * op(A)[m,k] * op(B)[k,n] + beta * C, B a constant initializer
  * (prepacked, Gemm.cpp:72-103), C NULL or a [n] row vector or a full [m,n] matrix

@@ -87,6 +87,9 @@ SIGNATURES = {
     "nnrcu_qlinearmatmul_noalloc": [P, P, P, I, I, I, F, U8, F, I8, F, U8, P],
     "nnrcu_conv_f32_create": [C.POINTER(ConvDesc), P, P, PP],
     "nnrcu_conv_f32_run": [P, P, P, P, P, P],
+    "nnrcu_conv_f32_plane_stride": [P, C.POINTER(C.c_int)],
+    "nnrcu_conv_f32_run_to_planes": [P, P, P, P, C.c_int, P],
+    "nnrcu_conv_f32_run_planes": [P, P, P, P, P, P],
     "nnrcu_gemm_f32_create": [I, I, I, I, I, F, F, P, P, I, I, F, F, PP],
     "nnrcu_gemm_f32_run": [P, P, P, P, P],
     "nnrcu_quantize_linear_u8": [P, P, I, I, I, I, F, U8, I, I, P],

@@ -388,10 +388,11 @@ __global__ void transpose_kernel(const T* __restrict src, T* __restrict dst, int
 // float4 or a uint2 of four 16-bit values; 16-bit tensors are widened to fp32
 // on load and rounded to nearest even on store, the way nnr's 16-bit Conv
 // converts around its fp32 kernels (Conv_exec_entry.h:188-381).
+// IO 3: fp32 input, and the output written as two bf16 planes (PlaneOut).
 template <int IO>
 struct Vec4IO {
-  using T = std::conditional_t<IO == 0, float, uint16_t>;     // element
-  using V = std::conditional_t<IO == 0, float4, uint2>;       // 4-channel vector
+  using T = std::conditional_t<IO == 0 || IO == 3, float, uint16_t>;     // element
+  using V = std::conditional_t<IO == 0 || IO == 3, float4, uint2>;       // 4-channel vector
   static __device__ __forceinline__ float h2f(uint32_t b) {
     if constexpr (IO == 1) return __uint_as_float(b << 16);
     else return __half2float(__ushort_as_half((unsigned short)b));
@@ -401,14 +402,46 @@ struct Vec4IO {
     else return __half_as_ushort(__float2half_rn(v));
   }
   static __device__ __forceinline__ float4 cvt(const V& u) {
-    if constexpr (IO == 0) return u;
+    if constexpr (IO == 0 || IO == 3) return u;
     else return make_float4(h2f(u.x & 0xFFFFu), h2f(u.x >> 16), h2f(u.y & 0xFFFFu), h2f(u.y >> 16));
   }
   static __device__ __forceinline__ V pack(float4 v) {
-    if constexpr (IO == 0) return v;
+    if constexpr (IO == 0 || IO == 3) return v;
     else return make_uint2(f2h(v.x) | (f2h(v.y) << 16), f2h(v.z) | (f2h(v.w) << 16));
   }
 };
+
+// Output of a depthwise conv as the split-bf16 operand of the dense conv
+// that consumes it: hi = bf16(v), lo = bf16(v - hi), NHWC with channel
+// stride cs4 * 4 (channels c .. cs - 1 zero), the layout and values the
+// consumer's own split (split_bf16_nhwc_kernel) would produce from the fp32
+// tensor.
+struct PlaneOut {
+  uint2* hi;
+  uint2* lo;
+  int cs4;
+};
+
+__device__ __forceinline__ void store_planes(const PlaneOut& po, size_t pixel, int cv, const float (&r)[4]) {
+  uint16_t h[4], l[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) split_bf16(r[u], h[u], l[u]);
+  const size_t i = pixel * po.cs4 + cv;
+  po.hi[i] = make_uint2(h[0] | ((uint32_t)h[1] << 16), h[2] | ((uint32_t)h[3] << 16));
+  po.lo[i] = make_uint2(l[0] | ((uint32_t)l[1] << 16), l[2] | ((uint32_t)l[3] << 16));
+}
+
+// the padding channels [c4, cs4) of one output row's pixels
+__device__ __forceinline__ void zero_plane_pad(const PlaneOut& po, size_t pixel0, int ow, int c4) {
+  const int pad = po.cs4 - c4;
+  if (pad <= 0) return;
+  for (int t = threadIdx.x; t < ow * pad; t += blockDim.x) {
+    const int ox = t / pad, cv = c4 + (t - ox * pad);
+    const size_t i = (pixel0 + ox) * po.cs4 + cv;
+    po.hi[i] = make_uint2(0u, 0u);
+    po.lo[i] = make_uint2(0u, 0u);
+  }
+}
 
 // Depthwise fp32 conv, NHWC in/out. Each thread produces 4 consecutive
 // channels (one float4) of one output pixel; weights are [kh][kw][c].
@@ -420,7 +453,7 @@ __global__ void depthwise_f32_kernel(const typename Vec4IO<IO>::T* __restrict x,
                                      const float* __restrict bias, typename Vec4IO<IO>::T* __restrict y,
                                      const typename Vec4IO<IO>::T* __restrict residual, int h, int wd, int c,
                                      int oh, int ow, int kh, int kw, int sh, int sw, int ph, int pw, int dh, int dw,
-                                     int act, float act_a, float act_b) {
+                                     int act, float act_a, float act_b, PlaneOut po) {
   const int c4 = c >> 2;
   const int row = blockIdx.x;  // img * oh + oy
   const int img = row / oh, oy = row - img * oh;
@@ -460,8 +493,10 @@ __global__ void depthwise_f32_kernel(const typename Vec4IO<IO>::T* __restrict x,
       const float4 rr = IOT::cvt(res[t]);
       o[0] += rr.x; o[1] += rr.y; o[2] += rr.z; o[3] += rr.w;
     }
-    out[t] = IOT::pack(make_float4(o[0], o[1], o[2], o[3]));
+    if constexpr (IO == 3) store_planes(po, (size_t)row * ow + ox, cv, o);
+    else out[t] = IOT::pack(make_float4(o[0], o[1], o[2], o[3]));
   }
+  if constexpr (IO == 3) zero_plane_pad(po, (size_t)row * ow, ow, c4);
 }
 
 // 3x3 depthwise fp32 conv (stride SW, dilation 1) on NHWC: each thread makes
@@ -475,7 +510,7 @@ __global__ void __launch_bounds__(256, SW == 2 ? 3 : 2)
     dw3x3_f32_kernel(const typename Vec4IO<IO>::T* __restrict x, const float* __restrict w,
                      const float* __restrict bias, typename Vec4IO<IO>::T* __restrict y,
                      const typename Vec4IO<IO>::T* __restrict residual, int h, int wd, int c, int oh,
-                                 int ow, int ph, int pw, int act, float act_a, float act_b) {
+                                 int ow, int ph, int pw, int act, float act_a, float act_b, PlaneOut po) {
   constexpr int OXT = SW == 1 ? 4 : 2, NC = (OXT - 1) * SW + 3;
   const int c4 = c >> 2;
   const int row = blockIdx.x;
@@ -538,9 +573,11 @@ __global__ void __launch_bounds__(256, SW == 2 ? 3 : 2)
         const float4 rr = IOT::cvt(res[oi]);
         r[0] += rr.x; r[1] += rr.y; r[2] += rr.z; r[3] += rr.w;
       }
-      out[oi] = IOT::pack(make_float4(r[0], r[1], r[2], r[3]));
+      if constexpr (IO == 3) store_planes(po, (size_t)row * ow + ox0 + o, cv, r);
+      else out[oi] = IOT::pack(make_float4(r[0], r[1], r[2], r[3]));
     }
   }
+  if constexpr (IO == 3) zero_plane_pad(po, (size_t)row * ow, ow, c4);
 }
 
 // Explicit im2col for fp32 small-channel convs, written as split bf16:
@@ -850,7 +887,8 @@ int launch_transpose_generic(const void* src, void* dst, int n, int c, int hw, i
 }
 
 template <int IO>
-int launch_depthwise(const Op& op, const void* x_v, void* y_v, const void* residual_v, cudaStream_t st) {
+int launch_depthwise(const Op& op, const void* x_v, void* y_v, const void* residual_v, cudaStream_t st,
+                     PlaneOut po = PlaneOut{}) {
   using T = typename Vec4IO<IO>::T;
   const T* x_nhwc = static_cast<const T*>(x_v);
   T* y = static_cast<T*>(y_v);
@@ -861,7 +899,7 @@ int launch_depthwise(const Op& op, const void* x_v, void* y_v, const void* resid
 #define NNRCU_DW(A)                                                                                                   \
   depthwise_f32_kernel<A, IO><<<rows, threads, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh,      \
                                                     op.ow, d.kh, d.kw, d.stride_h, d.stride_w, d.pad_top, d.pad_left,  \
-                                                    d.dil_h, d.dil_w, op.act, op.act_a, op.act_b)
+                                                    d.dil_h, d.dil_w, op.act, op.act_a, op.act_b, po)
   if (d.kh == 3 && d.kw == 3 && d.dil_h == 1 && d.dil_w == 1 && d.stride_h == d.stride_w &&
       (d.stride_h == 1 || d.stride_h == 2)) {
     const int oxt = d.stride_h == 1 ? 4 : 2;  // outputs per thread (the kernel's OXT)
@@ -869,7 +907,7 @@ int launch_depthwise(const Op& op, const void* x_v, void* y_v, const void* resid
     const int th = std::min(256, std::max(32, (groups * (d.c / 4) + 31) / 32 * 32));
 #define NNRCU_DW3(A, S)                                                                                                 \
   dw3x3_f32_kernel<A, S, IO><<<rows, th, 0, st>>>(x_nhwc, op.w_dw, op.bias, y, residual, d.h, d.w, d.c, op.oh, op.ow,     \
-                                              d.pad_top, d.pad_left, op.act, op.act_a, op.act_b)
+                                              d.pad_top, d.pad_left, op.act, op.act_a, op.act_b, po)
 #define NNRCU_DW3S(A) \
   if (d.stride_h == 1) NNRCU_DW3(A, 1); else NNRCU_DW3(A, 2)
     switch (op.act) {
@@ -896,6 +934,12 @@ int launch_depthwise(const Op& op, const void* x_v, void* y_v, const void* resid
 
 int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const float* residual, cudaStream_t st) {
   return launch_depthwise<0>(op, x_nhwc, y, residual, st);
+}
+
+int launch_depthwise_f32_planes(const Op& op, const float* x_nhwc, uint16_t* hi, uint16_t* lo, int cs,
+                                cudaStream_t st) {
+  PlaneOut po{reinterpret_cast<uint2*>(hi), reinterpret_cast<uint2*>(lo), cs / 4};
+  return launch_depthwise<3>(op, x_nhwc, nullptr, nullptr, st, po);
 }
 
 int launch_depthwise_half(const Op& op, const uint16_t* x_nhwc, uint16_t* y, int dtype, cudaStream_t st) {

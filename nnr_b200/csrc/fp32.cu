@@ -168,6 +168,9 @@ int nnrcu_conv_f32_create(const nnrcu_conv_desc* desc, const float* w_host, cons
   return NNRCU_OK;
 }
 
+static int conv_f32_planes(nnrcu_op* op, const uint16_t* hi, const uint16_t* lo, float* y, const float* residual,
+                           cudaStream_t st);
+
 int nnrcu_conv_f32_run(nnrcu_op* op, const float* x, float* y, const float* residual, void* workspace, void* stream) {
   if (!op || (op->kind != OP_CONV_F32 && op->kind != OP_DWCONV_F32))
     return set_error(NNRCU_ERR_INVALID, "not an fp32 Conv operator");
@@ -205,6 +208,15 @@ int nnrcu_conv_f32_run(nnrcu_op* op, const float* x, float* y, const float* resi
                                           d.dil_w, op->cs, st)
                : launch_split_bf16_nhwc(x, d.in_layout == NNRCU_LAYOUT_NCHW, hi, lo, d.n, d.c, d.h, d.w, op->cs, st);
   if (rc != NNRCU_OK) return rc;
+  return conv_f32_planes(op, hi, lo, y, residual, st);
+}
+
+// The split-bf16 GEMM of a dense fp32 Conv over A planes already split
+// (hi / lo, NHWC with channel stride op->cs, or the explicit im2col rows).
+static int conv_f32_planes(nnrcu_op* op, const uint16_t* hi, const uint16_t* lo, float* y, const float* residual,
+                           cudaStream_t st) {
+  const nnrcu_conv_desc& d = op->d;
+  int rc = NNRCU_OK;
   CUtensorMap tmA0{}, tmA1{};
   if (op->amode == A_TMA) {
     // rows: input pixels (1x1) or output pixels (explicit im2col)
@@ -254,6 +266,38 @@ int nnrcu_conv_f32_run(nnrcu_op* op, const float* x, float* y, const float* resi
   L.num_kb = op->num_kb;
   L.kb_bytes = op->kslab;
   return tc_launch(L, g, e, st);
+}
+
+int nnrcu_conv_f32_plane_stride(const nnrcu_op* op, int* cs) {
+  if (!op || !cs) return set_error(NNRCU_ERR_INVALID, "NULL argument");
+  if (op->kind != OP_CONV_F32 || op->explicit_im2col || op->amode != A_TMA || op->d.in_layout != NNRCU_LAYOUT_NHWC)
+    return set_error(NNRCU_ERR_UNSUPPORTED, "only a 1x1 stride-1 NHWC fp32 Conv reads pre-split planes");
+  *cs = op->cs;
+  return NNRCU_OK;
+}
+
+int nnrcu_conv_f32_run_planes(nnrcu_op* op, const uint16_t* x_hi, const uint16_t* x_lo, float* y,
+                              const float* residual, void* stream) {
+  int cs = 0;
+  int rc = nnrcu_conv_f32_plane_stride(op, &cs);
+  if (rc != NNRCU_OK) return rc;
+  if (!x_hi || !x_lo || !y) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
+  if ((reinterpret_cast<uintptr_t>(x_hi) | reinterpret_cast<uintptr_t>(x_lo)) & 15)
+    return set_error(NNRCU_ERR_INVALID, "the planes must be 16-byte aligned");
+  return conv_f32_planes(op, x_hi, x_lo, y, residual, static_cast<cudaStream_t>(stream));
+}
+
+int nnrcu_conv_f32_run_to_planes(nnrcu_op* op, const float* x, uint16_t* y_hi, uint16_t* y_lo, int cs,
+                                 void* stream) {
+  if (!op || op->kind != OP_DWCONV_F32) return set_error(NNRCU_ERR_INVALID, "not an fp32 depthwise Conv operator");
+  if (!x || !y_hi || !y_lo) return set_error(NNRCU_ERR_INVALID, "NULL tensor");
+  if (op->d.in_layout != NNRCU_LAYOUT_NHWC || op->d.out_layout != NNRCU_LAYOUT_NHWC)
+    return set_error(NNRCU_ERR_UNSUPPORTED, "planes output needs NHWC input and output");
+  if (cs < op->d.oc || cs % 4 != 0)
+    return set_error(NNRCU_ERR_INVALID, "plane channel stride %d must be a multiple of 4 and >= %d", cs, op->d.oc);
+  if ((reinterpret_cast<uintptr_t>(y_hi) | reinterpret_cast<uintptr_t>(y_lo)) & 7)
+    return set_error(NNRCU_ERR_INVALID, "the planes must be 8-byte aligned");
+  return launch_depthwise_f32_planes(*op, x, y_hi, y_lo, cs, static_cast<cudaStream_t>(stream));
 }
 
 int nnrcu_gemm_f32_create(int m, int n, int k, int trans_a, int trans_b, float alpha, float beta, const float* b_host,

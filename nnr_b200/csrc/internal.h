@@ -197,6 +197,8 @@ int launch_rowcorr_u8(const uint8_t* a, int m, int k, int lda, int b_zp, int32_t
 int launch_transpose_generic(const void* src, void* dst, int n, int c, int hw, int elem, int to_nhwc,
                              cudaStream_t st);
 int launch_depthwise_f32(const Op& op, const float* x_nhwc, float* y, const float* residual, cudaStream_t st);
+int launch_depthwise_f32_planes(const Op& op, const float* x_nhwc, uint16_t* hi, uint16_t* lo, int cs,
+                                cudaStream_t st);
 // 16-bit NHWC depthwise (dtype NNRCU_DT_BF16 / NNRCU_DT_F16): fp32 sums, rounded once
 int launch_depthwise_half(const Op& op, const uint16_t* x_nhwc, uint16_t* y, int dtype, cudaStream_t st);
 

@@ -8,6 +8,12 @@ the unfused Conv -> Add computes it), GlobalAveragePool and the FC Gemm run
 through the C ABI on one stream, in node order, with all tensors and
 workspaces in one planned arena; capture() records the forward into one CUDA
 graph.
+
+With split_links (the default), a depthwise Conv whose output feeds only a
+1x1 projection writes that output directly as the projection's split-bf16
+operand planes (nnrcu_conv_f32_run_to_planes / _run_planes), so the fp32
+tensor between them is never stored and re-split; the projection's result
+is bit-identical. Such a tensor has no fp32 view (plane_links lists them).
 """
 from __future__ import annotations
 
@@ -20,7 +26,7 @@ from .graph import ALIGN, Interval, check_plan, plan_arena
 
 
 class FloatNetwork:
-    def __init__(self, model, device: int = 0, reuse: bool = True, fuse_add: bool = True):
+    def __init__(self, model, device: int = 0, reuse: bool = True, fuse_add: bool = True, split_links: bool = True):
         import torch
         from . import ops
 
@@ -46,6 +52,7 @@ class FloatNetwork:
             self.ops.append(op)
             self.ws.append(op.workspace_size() if op is not None else 0)
         self._schedule(fuse_add)
+        self._link_planes(split_links)
         self._plan(reuse)
         self.stream = torch.cuda.Stream(device=self.dev)
         self.graph_exec = None
@@ -78,7 +85,37 @@ class FloatNetwork:
                 self.steps.append((nd.op, j, list(nd.inputs), nd.output, j))
         self.fused_away = {nodes[i].output for i in fused}
 
+    def _link_planes(self, enabled: bool):
+        """plane_links[t] = cs for each depthwise output t consumed only by a
+        1x1 Conv that reads pre-split planes with channel stride cs."""
+        from ._lib import lib
+        self.plane_links: Dict[str, int] = {}
+        if not enabled:
+            return
+        uses: Dict[str, list] = {}
+        for t, (_, _, ins, _, _) in enumerate(self.steps):
+            for k, x in enumerate(ins):
+                uses.setdefault(x, []).append((t, k))
+        nodes = self.model.nodes
+        for kind, _, _, out, i in self.steps:
+            if kind != "Conv" or nodes[i].attrs["group"] == 1 or len(uses.get(out, [])) != 1:
+                continue
+            t, k = uses[out][0]
+            ckind, _, _, _, ci = self.steps[t]
+            if ckind not in ("Conv", "ConvAdd") or k != 0:
+                continue
+            cs = C.c_int()
+            if lib.nnrcu_conv_f32_plane_stride(self.ops[ci]._op, C.byref(cs)) == 0:
+                self.plane_links[out] = cs.value
+                self.ws[ci] = 0  # reads the planes: no split workspace
+
+    def _plane_bytes(self, name: str) -> int:
+        n, h, w, _ = self.model.shapes[name]
+        return (n * h * w * self.plane_links[name] * 2 + ALIGN - 1) // ALIGN * ALIGN
+
     def _nbytes(self, name: str) -> int:
+        if name in self.plane_links:
+            return 2 * self._plane_bytes(name)  # hi plane, then lo plane
         return int(np.prod(self.model.shapes[name])) * 4
 
     def _plan(self, reuse: bool):
@@ -102,6 +139,8 @@ class FloatNetwork:
         self.ptr = {k: base + v for k, v in self.offsets.items()}
 
     def view(self, name: str):
+        if name in self.plane_links:
+            raise KeyError(f"{name} is stored as split-bf16 planes (split_links=False keeps it fp32)")
         off = self.offsets[name]
         return self.arena[off:off + self._nbytes(name)].view(self.torch.float32).view(self.model.shapes[name])
 
@@ -117,7 +156,16 @@ class FloatNetwork:
         ws = C.c_void_p(P[f"ws{i}"]) if self.ws[i] else None
         if kind in ("Conv", "ConvAdd"):
             res = C.c_void_p(P[ins[1]]) if kind == "ConvAdd" else None
-            call("nnrcu_conv_f32_run", self.ops[i]._op, C.c_void_p(P[ins[0]]), C.c_void_p(P[out]), res, ws, st)
+            if out in self.plane_links:
+                pb = self._plane_bytes(out)
+                call("nnrcu_conv_f32_run_to_planes", self.ops[i]._op, C.c_void_p(P[ins[0]]), C.c_void_p(P[out]),
+                     C.c_void_p(P[out] + pb), self.plane_links[out], st)
+            elif ins[0] in self.plane_links:
+                pb = self._plane_bytes(ins[0])
+                call("nnrcu_conv_f32_run_planes", self.ops[i]._op, C.c_void_p(P[ins[0]]), C.c_void_p(P[ins[0]] + pb),
+                     C.c_void_p(P[out]), res, st)
+            else:
+                call("nnrcu_conv_f32_run", self.ops[i]._op, C.c_void_p(P[ins[0]]), C.c_void_p(P[out]), res, ws, st)
         elif kind == "GlobalAveragePool":
             n, h, w, c = m.shapes[ins[0]]
             call("nnrcu_gap_f32_nhwc", C.c_void_p(P[ins[0]]), n, h * w, c, C.c_void_p(P[out]), st)

@@ -106,6 +106,60 @@ def test_grouped_conv(cuda_dev, shape, layout):
     assert rel_err(y, ref) <= TOL
 
 
+@pytest.mark.parametrize("c,oc,hw,s,k", [(40, 24, 15, 1, 3), (96, 24, 28, 2, 3), (64, 32, 9, 1, 5), (144, 144, 14, 1, 3)])
+def test_depthwise_to_planes_chain(cuda_dev, c, oc, hw, s, k):
+    """Depthwise -> 1x1 through pre-split planes (nnrcu_conv_f32_run_to_planes
+    then nnrcu_conv_f32_run_planes) is bit-identical to the two convs through
+    nnrcu_conv_f32_run, including channel counts that need padded planes, and
+    twice in a row over the same planes buffer (poisoned first)."""
+    import ctypes as C
+    from nnr_b200 import ops
+    from nnr_b200._lib import call
+    rng = np.random.default_rng(c + oc + hw)
+    n = 3
+    x = rng.uniform(-1, 1, size=(n, hw, hw, c)).astype(np.float32)
+    wd = rng.normal(0, 0.3, size=(c, 1, k, k)).astype(np.float32)
+    bd = rng.normal(0, 0.1, size=c).astype(np.float32)
+    wp = rng.normal(0, 0.2, size=(oc, c, 1, 1)).astype(np.float32)
+    bp = rng.normal(0, 0.1, size=oc).astype(np.float32)
+    p = k // 2
+    dw = ops.Conv((n, c, hw, hw), wd, bd, strides=(s, s), pads=(p,) * 4, group=c, in_layout="NHWC",
+                  out_layout="NHWC", post="Clip", post_a=0.0, post_b=6.0)
+    oh = (hw + 2 * p - k) // s + 1
+    pj = ops.Conv((n, c, oh, oh), wp, bp, in_layout="NHWC", out_layout="NHWC")
+    xd = torch.from_numpy(x).to(cuda_dev)
+    mid = dw.exec(xd)
+    want = pj.exec(mid).cpu().numpy()
+    cs = C.c_int()
+    call("nnrcu_conv_f32_plane_stride", pj._op, C.byref(cs))
+    assert cs.value >= c and cs.value % 8 == 0
+    pix = n * oh * oh
+    planes = torch.empty(2 * pix * cs.value, dtype=torch.int16, device=cuda_dev)
+    y = torch.empty_like(torch.from_numpy(want)).to(cuda_dev)
+    st = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    for _ in range(2):
+        planes.fill_(-1)  # NaN bit patterns in every padding channel unless they are rewritten
+        y.fill_(float("nan"))
+        hi, lo = planes.data_ptr(), planes.data_ptr() + pix * cs.value * 2
+        call("nnrcu_conv_f32_run_to_planes", dw._op, C.c_void_p(xd.data_ptr()), C.c_void_p(hi), C.c_void_p(lo),
+             cs.value, st)
+        call("nnrcu_conv_f32_run_planes", pj._op, C.c_void_p(hi), C.c_void_p(lo), C.c_void_p(y.data_ptr()), None, st)
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        got = y.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+
+
+def test_planes_declined_for_non_1x1(cuda_dev):
+    import ctypes as C
+    from nnr_b200 import ops
+    from nnr_b200._lib import lib
+    w = np.zeros((16, 16, 3, 3), np.float32)
+    op = ops.Conv((1, 16, 8, 8), w, None, pads=(1, 1, 1, 1), in_layout="NHWC", out_layout="NHWC")
+    cs = C.c_int()
+    assert lib.nnrcu_conv_f32_plane_stride(op._op, C.byref(cs)) == -2
+
+
 def test_conv_residual_add(cuda_dev):
     """Projection conv followed by the residual Add (MobileNetV2 block output)."""
     rng = np.random.default_rng(9)

@@ -27,7 +27,7 @@ def net_and_ref():
     from nnr_b200 import fgraph, mobilenetv2 as M
     model = M.build(batch=2)
     x = M.input_batch(0, 2)
-    net = fgraph.FloatNetwork(model, 0, reuse=False)
+    net = fgraph.FloatNetwork(model, 0, reuse=False, split_links=False)
     net.view("input").copy_(torch.from_numpy(x))
     net.run()
     torch.cuda.synchronize()
@@ -48,6 +48,28 @@ def test_every_tensor_close(net_and_ref):
         worst = max(worst, (e, nd.output))
     print(f"worst relative L2 error {worst[0]:.2e} at {worst[1]}")
     assert worst[0] <= NET_TOL, worst
+
+
+def test_split_links_bit_identical(net_and_ref):
+    """The network with its depthwise -> projection pairs linked through
+    split-bf16 planes computes every remaining tensor bit-identically."""
+    from nnr_b200 import fgraph, ops
+    model, net, x, _ = net_and_ref
+    n2 = fgraph.FloatNetwork(model, 0, reuse=False)
+    try:
+        assert len(n2.plane_links) == 17  # one per inverted-residual block
+        n2.view("input").copy_(torch.from_numpy(x))
+        n2.run()
+        torch.cuda.synchronize()
+        assert ops.device_status() == 0
+        for nd in model.nodes:
+            if nd.output in net.fused_away or nd.output in n2.plane_links:
+                continue
+            a = n2.view(nd.output).cpu().numpy()
+            b = net.view(nd.output).cpu().numpy()
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), nd.output
+    finally:
+        n2.close()
 
 
 def test_graph_replay_and_host_path(net_and_ref):
@@ -74,7 +96,7 @@ def bench_net_and_ref():
     model = M.build(batch=128)
     x = M.input_batch(0, 128)
     logits, ref = O.run_fmodel(model, x, keep=True)
-    net = fgraph.FloatNetwork(model, 0, reuse=False)
+    net = fgraph.FloatNetwork(model, 0, reuse=False, split_links=False)
     yield model, net, x, ref
     net.close()
 
