@@ -501,7 +501,12 @@ def other_rows(ops, W, torch, dev, stream, flush, steps=30):
         if nd.op != "Conv" or nd.attrs.get("group", 1) == 1:
             continue
         ms = timed(lambda: mnet.run_step(t, stream.cuda_stream))
-        nbytes = 4 * (int(np.prod(mb.shapes[ins[0]])) + int(np.prod(mb.shapes[out])) + nd.attrs["w"].size)
+        # (an output linked to its projection is written as two bf16 planes
+        # with the projection's padded channel stride: counted as written)
+        n_out = int(np.prod(mb.shapes[out]))
+        if out in mnet.plane_links:
+            n_out = n_out // mb.shapes[out][3] * mnet.plane_links[out]
+        nbytes = 4 * (int(np.prod(mb.shapes[ins[0]])) + n_out + nd.attrs["w"].size)
         dw_ms += ms
         dw_bytes += nbytes
         gbs = nbytes / ms / 1e6
@@ -514,7 +519,8 @@ def other_rows(ops, W, torch, dev, stream, flush, steps=30):
             "config5_depthwise_f32": {"ms_per_128": round(dw_ms, 4), "gb_per_s": round(dw_bytes / dw_ms / 1e6, 1),
                                       "best_layer": dw_best[0], "best_gb_per_s": round(dw_best[1], 1),
                                       "bytes": dw_bytes, "how": "every depthwise step of the forward alone, "
-                                      "CUDA events; bytes = fp32 input + output + weights"},
+                                      "CUDA events; bytes = fp32 input + output (fp32, or the two bf16 planes "
+                                      "a linked projection reads) + weights"},
             "config1_conv_relu_fp32": {"ms": round(ms1, 5), "tflops": round(f1 / ms1 / 1e9, 1)},
             "config3_gemm_fp32": {"ms": round(ms3, 5), "tflops": round(f3 / ms3 / 1e9, 1)},
             "config3_qlinearmatmul": {"ms": round(msq, 5), "tops": round(f3 / msq / 1e9, 1)},
