@@ -296,6 +296,23 @@ __global__ void split_bf16_nhwc_kernel(const float* __restrict src, int src_nchw
   }
 }
 
+// NHWC fp32 [pixels][c] -> planes [pixels][cs], c and cs multiples of 4:
+// one 4-channel vector per thread (zeros past c).
+__global__ void split_bf16_nhwc_vec_kernel(const float4* __restrict src, uint2* __restrict hi, uint2* __restrict lo,
+                                           unsigned total4, unsigned c4, unsigned cs4) {
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < total4; i += gridDim.x * blockDim.x) {
+    const unsigned p = i / cs4, cv = i - p * cs4;
+    const float4 v = cv < c4 ? src[(size_t)p * c4 + cv] : make_float4(0.f, 0.f, 0.f, 0.f);
+    uint16_t h0, l0, h1, l1, h2, l2, h3, l3;
+    split_bf16(v.x, h0, l0);
+    split_bf16(v.y, h1, l1);
+    split_bf16(v.z, h2, l2);
+    split_bf16(v.w, h3, l3);
+    hi[i] = make_uint2(h0 | ((uint32_t)h1 << 16), h2 | ((uint32_t)h3 << 16));
+    lo[i] = make_uint2(l0 | ((uint32_t)l1 << 16), l2 | ((uint32_t)l3 << 16));
+  }
+}
+
 // Tiled NCHW -> NHWC split for fp32 inputs: coalesced reads along pixels,
 // coalesced writes along channels.
 __global__ void split_bf16_nchw_tiled_kernel(const float* __restrict src, uint16_t* __restrict hi,
@@ -584,10 +601,14 @@ __global__ void __launch_bounds__(256, SW == 2 ? 3 : 2)
 // row m (output pixel) holds k = (kh, kw, ic) for k < KH*KW*C, zeros up to kp;
 // hi = bf16(x), lo = bf16(x - hi). One thread per output pixel, 8 elements
 // (16 bytes) per store.
+// (C, KH, KW, KP nonzero: a compile-time shape, e.g. MobileNet's 3-channel
+// 3x3 stem, so the tap / channel index arithmetic folds away)
+template <int C_, int KH_, int KW_, int KP_>
 __global__ void im2col_split_bf16_kernel(const float* __restrict x, int nchw, uint16_t* __restrict hi,
-                                         uint16_t* __restrict lo, long long m_total, int c, int h, int w, int oh,
-                                         int ow, int kh, int kw, int sh, int sw, int pt, int pl, int dh, int dw,
-                                         int kp) {
+                                         uint16_t* __restrict lo, long long m_total, int c_rt, int h, int w, int oh,
+                                         int ow, int kh_rt, int kw_rt, int sh, int sw, int pt, int pl, int dh, int dw,
+                                         int kp_rt) {
+  const int c = C_ ? C_ : c_rt, kh = KH_ ? KH_ : kh_rt, kw = KW_ ? KW_ : kw_rt, kp = KP_ ? KP_ : kp_rt;
   for (long long m = blockIdx.x * (long long)blockDim.x + threadIdx.x; m < m_total;
        m += (long long)gridDim.x * blockDim.x) {
     const int ox = (int)(m % ow);
@@ -597,6 +618,7 @@ __global__ void im2col_split_bf16_kernel(const float* __restrict x, int nchw, ui
     const int kd = kh * kw * c;
     uint4* hrow = reinterpret_cast<uint4*>(hi + m * kp);
     uint4* lrow = reinterpret_cast<uint4*>(lo + m * kp);
+#pragma unroll
     for (int k0 = 0; k0 < kp; k0 += 8) {
       uint32_t hw_[4], lw_[4];
 #pragma unroll
@@ -832,6 +854,13 @@ int launch_split_bf16_nhwc(const float* src, int src_nchw, uint16_t* hi, uint16_
     split_bf16_rows_vec_kernel<<<grid_for(n4, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(src),
                                                                    reinterpret_cast<uint2*>(hi),
                                                                    reinterpret_cast<uint2*>(lo), n4);
+  } else if ((c % 4) == 0 && (cs % 4) == 0 && (long long)n * hw * (cs / 4) < (1LL << 31) &&
+             (reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    const unsigned total4 = (unsigned)((long long)n * hw * (cs / 4));
+    split_bf16_nhwc_vec_kernel<<<grid_for(total4, 256), 256, 0, st>>>(reinterpret_cast<const float4*>(src),
+                                                                       reinterpret_cast<uint2*>(hi),
+                                                                       reinterpret_cast<uint2*>(lo), total4,
+                                                                       (unsigned)(c / 4), (unsigned)(cs / 4));
   } else {
     const long long pixels = (long long)n * hw;
     split_bf16_nhwc_kernel<<<grid_for(pixels * cs, 256), 256, 0, st>>>(src, 0, hi, lo, pixels, c, hw, cs);
@@ -846,8 +875,12 @@ int launch_im2col_split_bf16(const float* x, int nchw, uint16_t* hi, uint16_t* l
   if (kp % 8 != 0 || (reinterpret_cast<uintptr_t>(hi) & 15) || (reinterpret_cast<uintptr_t>(lo) & 15))
     return set_error(NNRCU_ERR_INVALID, "im2col split: kp %% 8 and 16-byte aligned planes required");
   const long long m = (long long)n * oh * ow;
-  im2col_split_bf16_kernel<<<grid_for(m, 256), 256, 0, st>>>(x, nchw, hi, lo, m, c, h, w, oh, ow, kh, kw, sh, sw, pt,
-                                                             pl, dh, dw, kp);
+  if (c == 3 && kh == 3 && kw == 3 && kp == 32)
+    im2col_split_bf16_kernel<3, 3, 3, 32><<<grid_for(m, 256), 256, 0, st>>>(x, nchw, hi, lo, m, c, h, w, oh, ow, kh,
+                                                                          kw, sh, sw, pt, pl, dh, dw, kp);
+  else
+    im2col_split_bf16_kernel<0, 0, 0, 0><<<grid_for(m, 256), 256, 0, st>>>(x, nchw, hi, lo, m, c, h, w, oh, ow, kh,
+                                                                        kw, sh, sw, pt, pl, dh, dw, kp);
   NNRCU_CUDA(cudaGetLastError());
   return NNRCU_OK;
 }
