@@ -473,6 +473,8 @@ DW_SHAPES = [
     (1, 96, 13, 11, 3, 2, (1, 0, 1, 0), 1, 131, -2, 200),
     (2, 48, 9, 9, 5, 1, (2, 2, 2, 2), 2, 200, 0, 9),
     (1, 20, 6, 7, 3, 1, (1, 1, 1, 1), 1, 10, 3, 5),   # C % 16 != 0: the per-element kernel
+    (3, 64, 10, 12, 3, 1, (0, 1, 1, 0), 1, 255, 0, 0),  # asymmetric pads, x_zp 255 (dp4a kernel)
+    (1, 16, 5, 5, 7, 1, (3, 3, 3, 3), 1, 0, 0, 128),    # 49 taps: 13 groups of four, x_zp 0
 ]
 
 
