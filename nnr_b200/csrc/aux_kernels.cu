@@ -517,18 +517,20 @@ __global__ void depthwise_f32_kernel(const typename Vec4IO<IO>::T* __restrict x,
 }
 
 // 3x3 depthwise fp32 conv (stride SW, dilation 1) on NHWC: each thread makes
-// OXT consecutive outputs along x (4 at stride 1, 2 at stride 2) for one
-// 4-channel vector, with the input vectors they share loaded once, up front
-// (all loads in flight together). One block per output row.
-// (stride 2: three blocks per SM, 85 registers a thread, measured 1.3-1.4x
-// faster than two on the MobileNetV2 stride-2 shapes)
+// two consecutive outputs along x for one 4-channel vector, with the input
+// vectors they share loaded once, up front (all loads in flight together).
+// One block per output row; three blocks per SM (85 registers a thread).
+// Measured on the MobileNetV2 shapes: at stride 2, 1.3-1.4x faster than two
+// blocks per SM; at stride 1, the batch-128 forward took 2.36 ms against 2.43
+// with four outputs a thread at two blocks per SM and 2.55 with one output at
+// four blocks per SM.
 template <int ACT, int SW, int IO = 0>
-__global__ void __launch_bounds__(256, SW == 2 ? 3 : 2)
+__global__ void __launch_bounds__(256, 3)
     dw3x3_f32_kernel(const typename Vec4IO<IO>::T* __restrict x, const float* __restrict w,
                      const float* __restrict bias, typename Vec4IO<IO>::T* __restrict y,
                      const typename Vec4IO<IO>::T* __restrict residual, int h, int wd, int c, int oh,
                                  int ow, int ph, int pw, int act, float act_a, float act_b, PlaneOut po) {
-  constexpr int OXT = SW == 1 ? 4 : 2, NC = (OXT - 1) * SW + 3;
+  constexpr int OXT = 2, NC = (OXT - 1) * SW + 3;
   const int c4 = c >> 2;
   const int row = blockIdx.x;
   const int img = row / oh, oy = row - img * oh;
@@ -935,7 +937,7 @@ int launch_depthwise(const Op& op, const void* x_v, void* y_v, const void* resid
                                                     d.dil_h, d.dil_w, op.act, op.act_a, op.act_b, po)
   if (d.kh == 3 && d.kw == 3 && d.dil_h == 1 && d.dil_w == 1 && d.stride_h == d.stride_w &&
       (d.stride_h == 1 || d.stride_h == 2)) {
-    const int oxt = d.stride_h == 1 ? 4 : 2;  // outputs per thread (the kernel's OXT)
+    const int oxt = 2;  // outputs per thread (the kernel's OXT)
     const int groups = (op.ow + oxt - 1) / oxt;
     const int th = std::min(256, std::max(32, (groups * (d.c / 4) + 31) / 32 * 32));
 #define NNRCU_DW3(A, S)                                                                                                 \
