@@ -463,6 +463,21 @@ tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA0, const __grid_constant__
   // launch it overlaps the previous kernel's tail; every read of activations
   // and every write of outputs comes after this wait.
   ptx::pdl_launch_dependents();
+  if (NKBR > 0 && warp == R::TMA_WARP && lane == 0) {
+    // this CTA's N tile's B, all K slabs, once per CTA (the grid is a
+    // multiple of n_tiles, so a CTA's tiles all have N tile blockIdx.x %
+    // n_tiles). B is a constant operand (the weights), written by no
+    // kernel, so its copy starts before the wait for the previous kernel.
+    const int bn0 = (int)(blockIdx.x % n_tiles) * BN;
+    ptx::mbar_arrive_expect_tx(bres_bar, (uint32_t)(num_kb * Cfg::B_BYTES));
+    for (int kb = 0; kb < num_kb; ++kb) {
+      if (g.wb)  // the slab's shared-memory image: one plain bulk copy
+        ptx::bulk_load(sB + (size_t)kb * Cfg::B_BYTES, g.wb + ((size_t)(bn0 / BN) * num_kb + kb) * Cfg::B_BYTES,
+                       Cfg::B_BYTES, bres_bar);
+      else
+        ptx::tma_load_2d(sB + (size_t)kb * Cfg::B_BYTES, &tmB, bres_bar, kb * KB, bn0);
+    }
+  }
   ptx::pdl_wait();
 
   // Output rows of an M tile: mb = first GEMM row, nvr = valid rows; A_ROWS
@@ -493,18 +508,6 @@ if constexpr (AMODE == A_ROWS || AMODE == A_XROWS) {
     if (lane == 0) {
       constexpr uint32_t tx =
           AMODE == A_ROWS ? 0u : (AMODE != A_GATHER ? PL * A_BYTES : 0) + (NKBR ? 0 : PL * B_BYTES);
-      if (NKBR > 0 && pw == 0) {
-        // this CTA's N tile's B, all K slabs, once per CTA (the grid is a
-        // multiple of n_tiles, so a CTA's tiles all have N tile blockIdx.x % n_tiles)
-        const int bn0 = (int)(blockIdx.x % n_tiles) * BN;
-        ptx::mbar_arrive_expect_tx(bres_bar, (uint32_t)(num_kb * B_BYTES));
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (g.wb)  // the slab's shared-memory image: one plain bulk copy
-            ptx::bulk_load(sB + (size_t)kb * B_BYTES, g.wb + ((size_t)(bn0 / BN) * num_kb + kb) * B_BYTES, B_BYTES, bres_bar);
-          else
-            ptx::tma_load_2d(sB + (size_t)kb * B_BYTES, &tmB, bres_bar, kb * KB, bn0);
-        }
-      }
       if constexpr (AMODE == A_SHIFT) {
         // one patch per tile: each K slab's rows [m0, m0 + prows) of the padded input
         const int nslab = g.cbytes / KB;
