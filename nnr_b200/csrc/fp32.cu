@@ -135,7 +135,11 @@ int nnrcu_conv_f32_create(const nnrcu_conv_desc* desc, const float* w_host, cons
   op->kpad_bytes = round_up(op->kbytes, op->kslab);
   op->num_kb = op->kpad_bytes / op->kslab;
   op->npad = round_up(d.oc, 256);
-  op->bn = pick_bn(op->M, op->N, 2, num_sms());
+  // N tile 64 for every split-bf16 conv: on MobileNetV2 (N 16-1280) the
+  // batch-128 forward took 2.30 ms against 2.36 with pick_bn's choice and
+  // 2.35 with 128 wherever N > 64 (the fp32 epilogue, not the A re-reads,
+  // sets the tile cost)
+  op->bn = 64;
   op->amode = (one_by_one && op->kbytes >= op->kslab) ? A_TMA : A_GATHER;
   // hardware im2col (TMA) when a pixel is whole 128-byte slabs of bf16 (C a
   // multiple of 64); its zero fill is the fp32 padding value
